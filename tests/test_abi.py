@@ -1,0 +1,63 @@
+"""The C-ABI library loads and exports every symbol include/vbs_b200.h
+declares; the ops table has the reference's layout. No GPU compute."""
+import ctypes as C
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "vbs_b200.h").read_text()
+    names = set(re.findall(r"VBS_API\s+[\w\s\*]*?\b(vbs_\w+)\s*\(", text))
+    names |= set(re.findall(r"VBS_API\s+const\s+vbs_backend_ops_t\s+(g_vbs_cuda_backend)", text))
+    return sorted(names)
+
+
+def test_header_declares_boundary():
+    names = declared_symbols()
+    assert "g_vbs_cuda_backend" in names and "vbs_cuda_last_error" in names
+    assert len(names) >= 25
+
+
+def test_library_exports_all_declared(vbs):
+    L = vbs.lib()
+    for n in declared_symbols():
+        assert hasattr(L, n), f"{n} declared in include/vbs_b200.h but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(vbs.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.split()[1] in "TDBR"}
+    assert set(declared_symbols()) <= exported
+
+
+def test_ops_table_layout(vbs):
+    # 14 pointer-sized fields, in the order of include/vbs_backend.h:64-99
+    assert C.sizeof(vbs.OpsTable) == 14 * C.sizeof(C.c_void_p)
+    assert C.sizeof(vbs.Device) == 128 + 8 + 8 + 8 + 8   # name, type (+pad), two u64, handle
+    assert C.sizeof(vbs.Buffer) == 4 * 8
+    assert C.sizeof(vbs.Arg) == 24
+    o = vbs.ops()
+    for name, _ in vbs.OpsTable._fields_[:-1]:
+        assert C.cast(getattr(o, name), C.c_void_p).value, f"{name} is NULL"
+    assert not o.launch_persistent_kernel
+
+
+def test_init_without_gpu_reports_reason(vbs):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert vbs.ops().init() is False
+    assert vbs.last_error() != "ok"
+
+
+def test_version_names_blackwell_features(vbs):
+    v = vbs.lib().vbs_cu_version().decode()
+    for feat in ("sm_100a", "cp.async.bulk", "mbarrier"):
+        assert feat in v
+
+
+def test_sources_use_tma_and_no_multicast():
+    src = "".join(p.read_text() for p in (ROOT / "verum-bespoke-singularity_b200" / "csrc").glob("*.cu*"))
+    assert "cp.async.bulk" in src
+    assert "multicast::cluster" not in src

@@ -1,0 +1,537 @@
+"""Python host binding of libvbs_b200.so (the sm_100a decode backend).
+
+The C ABI is include/vbs_b200.h. This module mirrors it with ctypes so the
+tests and the benchmark drive the library exactly as the reference engine
+would: through the `g_vbs_cuda_backend` ops table (the reference's
+vbs_backend_ops_t, include/vbs_backend.h:64-99 of the reference) and through
+the vbs_cu_* extension entry points. PyTorch is used only to own device
+memory and streams; no tensor math runs in PyTorch.
+
+There is no CPU fallback: `lib()` raises when the shared library is missing
+or cannot be loaded, and every entry point that fails raises VbsError with
+the backend's latched message.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import struct
+import subprocess
+from dataclasses import dataclass, field
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libvbs_b200.so"
+
+# GGML type ids (include/vbs_gguf.h:13-48 of the reference)
+F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K, Q8_K = 0, 1, 2, 3, 8, 12, 14, 15
+TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q4_1: "Q4_1", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+# op kinds (include/vbs_graph.h:12-24 of the reference)
+(OP_EMBEDDING, OP_LINEAR, OP_NORMALIZE, OP_ATTENTION, OP_ROTARY, OP_ACTIVATION, OP_ELEMENTWISE,
+ OP_STATE_SPACE, OP_CONVOLUTION, OP_CACHE, OP_PROJECTION) = range(11)
+ARG_BUFFER, ARG_SCALAR = 0, 1
+
+MV_ACCUMULATE, MV_PORTABLE = 1, 2
+DEC_STRICT, DEC_NO_GRAPH, DEC_NO_PDL = 1, 2, 4
+
+
+class VbsError(RuntimeError):
+    """A backend call failed; the message is the backend's latched error."""
+
+
+def row_bytes(type_id: int, cols: int) -> int:
+    e, b = BLOCK[type_id]
+    if cols % e:
+        raise ValueError(f"{cols} columns are not whole {e}-element blocks")
+    return cols // e * b
+
+
+# ---------------------------------------------------------------------------
+# ctypes mirror of the reference ops-table types
+# ---------------------------------------------------------------------------
+class Device(C.Structure):
+    _fields_ = [("name", C.c_char * 128), ("type", C.c_int), ("max_working_set_bytes", C.c_uint64),
+                ("max_buffer_bytes", C.c_uint64), ("internal_handle", C.c_void_p)]
+
+
+class Buffer(C.Structure):
+    _fields_ = [("internal_handle", C.c_void_p), ("host_ptr", C.c_void_p), ("size", C.c_size_t),
+                ("device", C.POINTER(Device))]
+
+
+class Arg(C.Structure):
+    _fields_ = [("tag", C.c_int), ("value", C.c_void_p), ("size", C.c_size_t)]
+
+
+class PrimPipeline(C.Structure):
+    _fields_ = [("native", C.c_void_p), ("kind", C.c_int)]
+
+
+_P_DEV = C.POINTER(Device)
+_P_BUF = C.POINTER(Buffer)
+
+
+class OpsTable(C.Structure):
+    _fields_ = [
+        ("init", C.CFUNCTYPE(C.c_bool)),
+        ("get_device_count", C.CFUNCTYPE(C.c_size_t)),
+        ("get_device", C.CFUNCTYPE(_P_DEV, C.c_size_t)),
+        ("alloc_buffer", C.CFUNCTYPE(_P_BUF, _P_DEV, C.c_size_t, C.c_bool)),
+        ("free_buffer", C.CFUNCTYPE(None, _P_BUF)),
+        ("copy_to_device", C.CFUNCTYPE(C.c_bool, _P_BUF, C.c_void_p, C.c_size_t)),
+        ("copy_to_host", C.CFUNCTYPE(C.c_bool, C.c_void_p, _P_BUF, C.c_size_t)),
+        ("compile_linear_pipeline", C.CFUNCTYPE(C.c_void_p, _P_DEV, C.c_int, C.c_char_p, C.c_size_t)),
+        ("compile_embed_pipeline", C.CFUNCTYPE(C.c_void_p, _P_DEV, C.c_int, C.c_char_p, C.c_size_t)),
+        ("compile_primitive_pipeline", C.CFUNCTYPE(C.c_void_p, _P_DEV, C.c_int, C.c_char_p, C.c_size_t)),
+        ("dispatch_linear_tile", C.CFUNCTYPE(C.c_bool, _P_DEV, C.c_void_p, _P_BUF, _P_BUF, C.c_size_t, _P_BUF, _P_BUF,
+                                             C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_bool)),
+        ("dispatch_primitive", C.CFUNCTYPE(C.c_bool, _P_DEV, C.c_void_p, C.POINTER(Arg), C.c_size_t, C.c_size_t,
+                                           C.c_size_t)),
+        ("synchronize_device", C.CFUNCTYPE(None, _P_DEV)),
+        ("launch_persistent_kernel", C.c_void_p),
+    ]
+
+
+class ModelDesc(C.Structure):
+    """vbs_cu_model_t (include/vbs_b200.h)."""
+    _fields_ = [
+        ("n_layers", C.c_uint32), ("dim", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+        ("head_dim", C.c_uint32), ("ffn", C.c_uint32), ("vocab", C.c_uint32),
+        ("eps", C.c_float), ("theta", C.c_float),
+        ("embd_type", C.c_int), ("out_type", C.c_int),
+        ("embd", C.c_void_p), ("out", C.c_void_p), ("out_norm", C.c_void_p),
+        ("attn_norm", C.POINTER(C.c_void_p)), ("ffn_norm", C.POINTER(C.c_void_p)),
+        ("wq", C.POINTER(C.c_void_p)), ("wk", C.POINTER(C.c_void_p)), ("wv", C.POINTER(C.c_void_p)),
+        ("wo", C.POINTER(C.c_void_p)), ("wgate", C.POINTER(C.c_void_p)), ("wup", C.POINTER(C.c_void_p)),
+        ("wdown", C.POINTER(C.c_void_p)),
+        ("tq", C.POINTER(C.c_int)), ("tk", C.POINTER(C.c_int)), ("tv", C.POINTER(C.c_int)),
+        ("to", C.POINTER(C.c_int)), ("tgate", C.POINTER(C.c_int)), ("tup", C.POINTER(C.c_int)),
+        ("tdown", C.POINTER(C.c_int)),
+        ("vocab_full", C.c_uint32), ("vocab_offset", C.c_uint32),
+    ]
+
+
+_LIB = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile libvbs_b200.so in place (nvcc, sm_100a). Returns its path."""
+    if force or not LIB_PATH.exists():
+        subprocess.run(["make", "-C", str(PKG_DIR), "-j8"], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    """The loaded library; raises when it is missing (no fallback exists)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise VbsError(f"{LIB_PATH} is not built; run build() (make -C {PKG_DIR})")
+    L = C.CDLL(str(LIB_PATH))
+    vp, u32, u64, i32, f32, sz = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_size_t
+    sig = {
+        "vbs_cuda_last_error": (C.c_char_p, []),
+        "vbs_cu_status": (i32, []),
+        "vbs_cu_clear_error": (None, []),
+        "vbs_cu_version": (C.c_char_p, []),
+        "vbs_cu_kernel_launches": (u64, []),
+        "vbs_cu_dequant": (i32, [i32, vp, vp, u64, vp]),
+        "vbs_cu_matvec": (i32, [i32, vp, vp, vp, u32, u32, u32, u32, vp]),
+        "vbs_cu_ffn_gate_up": (i32, [i32, vp, vp, vp, vp, f32, vp, u32, u32, vp]),
+        "vbs_cu_attention": (i32, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, f32, u32, u64, vp]),
+        "vbs_cu_synth": (i32, [i32, vp, u64, u64, u64, u64, u64, u64, f32, vp]),
+        "vbs_cu_decoder_create": (vp, [C.POINTER(ModelDesc), u32, u32, C.c_char_p, sz]),
+        "vbs_cu_decoder_destroy": (None, [vp]),
+        "vbs_cu_decoder_forward": (i32, [vp, C.POINTER(u32), sz, C.POINTER(f32)]),
+        "vbs_cu_decoder_reset": (None, [vp]),
+        "vbs_cu_decoder_generate": (i32, [vp, C.POINTER(u32), sz, u32, C.POINTER(u32)]),
+        "vbs_cu_decoder_enqueue_steps": (i32, [vp, u32]),
+        "vbs_cu_decoder_set_position": (i32, [vp, u32, u32]),
+        "vbs_cu_decoder_position": (u32, [vp]),
+        "vbs_cu_decoder_stream": (vp, [vp]),
+        "vbs_cu_decoder_logits_device": (vp, [vp]),
+        "vbs_cu_decoder_kernels_per_step": (u32, [vp]),
+        "vbs_cu_tp_unique_id": (i32, [vp]),
+        "vbs_cu_tp_init": (i32, [i32, i32, vp]),
+        "vbs_cu_tp_finalize": (i32, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = L
+    return L
+
+
+def last_error() -> str:
+    return lib().vbs_cuda_last_error().decode()
+
+
+def clear_error() -> None:
+    lib().vbs_cu_clear_error()
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise VbsError(f"{what}: {last_error()}")
+
+
+def ops() -> OpsTable:
+    """The drop-in ops table g_vbs_cuda_backend."""
+    return OpsTable.in_dll(lib(), "g_vbs_cuda_backend")
+
+
+def kernel_launches() -> int:
+    return int(lib().vbs_cu_kernel_launches())
+
+
+# ---------------------------------------------------------------------------
+# thin wrappers over the extension entry points (device pointers as ints)
+# ---------------------------------------------------------------------------
+def dequant(type_id: int, w_ptr: int, out_ptr: int, n_elems: int, stream: int = 0) -> None:
+    check(lib().vbs_cu_dequant(type_id, w_ptr, out_ptr, n_elems, stream or None), "vbs_cu_dequant")
+
+
+def matvec(type_id, w_ptr, x_ptr, y_ptr, rows, cols, batch=1, flags=0, stream=0) -> None:
+    check(lib().vbs_cu_matvec(type_id, w_ptr, x_ptr, y_ptr, rows, cols, batch, flags, stream or None), "vbs_cu_matvec")
+
+
+def ffn_gate_up(type_id, wg_ptr, wu_ptr, x_ptr, norm_ptr, eps, h_ptr, rows, cols, stream=0) -> None:
+    check(lib().vbs_cu_ffn_gate_up(type_id, wg_ptr, wu_ptr, x_ptr, norm_ptr or None, eps, h_ptr, rows, cols,
+                                   stream or None), "vbs_cu_ffn_gate_up")
+
+
+def attention(q, kc, vc, out, seq_len, layer, max_ctx, nqh, nkh, hd, scale, batch=1, kv_batch_stride=0, stream=0):
+    check(lib().vbs_cu_attention(q, kc, vc, out, seq_len, layer, max_ctx, nqh, nkh, hd, scale, batch,
+                                 kv_batch_stride, stream or None), "vbs_cu_attention")
+
+
+def synth(type_id, dst_ptr, rows, cols, seed, scale, row0=0, col0=0, full_cols=None, stream=0) -> None:
+    check(lib().vbs_cu_synth(type_id, dst_ptr, rows, cols, row0, col0, full_cols or cols, seed, scale,
+                             stream or None), "vbs_cu_synth")
+
+
+def synth_scale(std: float) -> float:
+    """Float scale that gives the Irwin-Hall(4) synthesizer a standard deviation `std`."""
+    return float(struct.unpack("<f", struct.pack("<f", std / ((65536.0 * 65536.0 - 1.0) / 3.0) ** 0.5))[0])
+
+
+# ---------------------------------------------------------------------------
+# models resident on the device
+# ---------------------------------------------------------------------------
+@dataclass
+class LlamaShape:
+    n_layers: int
+    dim: int
+    n_heads: int
+    n_kv_heads: int
+    ffn: int
+    vocab: int
+    eps: float = 1e-5
+    theta: float = 10000.0
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+
+@dataclass
+class DeviceModel:
+    """Weights on the device (torch uint8/float32 tensors own the memory)
+    plus the vbs_cu_model_t that points at them."""
+    shape: LlamaShape
+    types: dict
+    tensors: dict = field(default_factory=dict)
+    desc: ModelDesc | None = None
+    _keep: list = field(default_factory=list)
+    tp_rank: int = 0
+    tp_world: int = 1
+
+    def weight_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.tensors.values())
+
+    def make_desc(self) -> ModelDesc:
+        s, T = self.shape, self.tensors
+        n = s.n_layers
+        P = C.c_void_p * n
+        I = C.c_int * n
+        lw = lambda key: P(*[T[f"blk.{l}.{key}"].data_ptr() for l in range(n)])
+        lt = lambda key: I(*[self.types[key]] * n)
+        arrs = dict(attn_norm=lw("attn_norm"), ffn_norm=lw("ffn_norm"), wq=lw("attn_q"), wk=lw("attn_k"),
+                    wv=lw("attn_v"), wo=lw("attn_output"), wgate=lw("ffn_gate"), wup=lw("ffn_up"),
+                    wdown=lw("ffn_down"), tq=lt("attn_q"), tk=lt("attn_k"), tv=lt("attn_v"),
+                    to=lt("attn_output"), tgate=lt("ffn_gate"), tup=lt("ffn_up"), tdown=lt("ffn_down"))
+        self._keep = list(arrs.values())
+        d = ModelDesc()
+        d.n_layers, d.dim, d.n_heads, d.n_kv_heads = n, s.dim, s.n_heads // self.tp_world, s.n_kv_heads // self.tp_world
+        d.head_dim, d.ffn, d.vocab = s.head_dim, s.ffn // self.tp_world, s.vocab // self.tp_world
+        d.eps, d.theta = s.eps, s.theta
+        d.embd_type, d.out_type = self.types["token_embd"], self.types["output"]
+        d.embd, d.out, d.out_norm = T["token_embd"].data_ptr(), T["output"].data_ptr(), T["output_norm"].data_ptr()
+        for k, v in arrs.items():
+            setattr(d, k, C.cast(v, C.POINTER(C.c_void_p) if k.startswith(("w", "attn", "ffn")) else C.POINTER(C.c_int)))
+        d.vocab_full = s.vocab
+        d.vocab_offset = self.tp_rank * (s.vocab // self.tp_world)
+        self.desc = d
+        return d
+
+
+# Per-tensor seeds of synthetic models: a fixed function of the model seed
+# and the tensor's name, so every rank of a TP group (and the host oracle)
+# draws the same full tensors and takes its own slice.
+def tensor_seed(model_seed: int, name: str) -> int:
+    h = 1469598103934665603
+    for ch in name.encode():
+        h = ((h ^ ch) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return (h ^ (model_seed * 0x9E3779B97F4A7C15)) & 0xFFFFFFFFFFFFFFFF
+
+
+def shard_spec(name: str, shape: LlamaShape, rank: int, world: int):
+    """(rows, cols, row0, col0, full_cols) of this rank's slice of `name`.
+    Megatron-style: q/k/v/gate/up/output by rows, o/down by columns."""
+    hd, D, F = shape.head_dim, shape.dim, shape.ffn
+    base = name.split(".")[-1] if name.startswith("blk.") else name
+    full = {"attn_q": (shape.n_heads * hd, D), "attn_k": (shape.n_kv_heads * hd, D),
+            "attn_v": (shape.n_kv_heads * hd, D), "attn_output": (D, shape.n_heads * hd), "ffn_gate": (F, D),
+            "ffn_up": (F, D), "ffn_down": (D, F), "output": (shape.vocab, D), "token_embd": (shape.vocab, D)}[base]
+    rows, cols = full
+    if world == 1 or base == "token_embd":
+        return rows, cols, 0, 0, cols
+    if base in ("attn_output", "ffn_down"):
+        if cols % world:
+            raise ValueError(f"{name}: {cols} columns do not split over {world} ranks")
+        c = cols // world
+        return rows, c, 0, rank * c, cols
+    if rows % world:
+        raise ValueError(f"{name}: {rows} rows do not split over {world} ranks")
+    r = rows // world
+    return r, cols, rank * r, 0, cols
+
+
+def synth_llama(shape: LlamaShape, types: dict, seed: int = 1234, std: float = 0.02, device="cuda",
+                tp_rank: int = 0, tp_world: int = 1, stream: int = 0) -> DeviceModel:
+    """A seeded random llama-shaped model generated and quantized on the
+    device (norm weights 1.0). `types` maps token_embd, output, attn_q,
+    attn_k, attn_v, attn_output, ffn_gate, ffn_up, ffn_down to type ids."""
+    import torch
+    m = DeviceModel(shape=shape, types=dict(types), tp_rank=tp_rank, tp_world=tp_world)
+    sc = synth_scale(std)
+
+    def add(name, base):
+        rows, cols, r0, c0, fc = shard_spec(name, shape, tp_rank, tp_world)
+        t = torch.empty(rows * row_bytes(types[base], cols) + 256, dtype=torch.uint8, device=device)
+        synth(types[base], t.data_ptr(), rows, cols, tensor_seed(seed, name), sc, r0, c0, fc, stream)
+        m.tensors[name] = t
+
+    add("token_embd", "token_embd")
+    add("output", "output")
+    m.tensors["output_norm"] = torch.ones(shape.dim, dtype=torch.float32, device=device)
+    for l in range(shape.n_layers):
+        for base in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
+            add(f"blk.{l}.{base}", base)
+        m.tensors[f"blk.{l}.attn_norm"] = torch.ones(shape.dim, dtype=torch.float32, device=device)
+        m.tensors[f"blk.{l}.ffn_norm"] = torch.ones(shape.dim, dtype=torch.float32, device=device)
+    m.make_desc()
+    return m
+
+
+class Decoder:
+    """vbs_cu_decoder_t: the decode step as one replayable device program."""
+
+    def __init__(self, model: DeviceModel, max_ctx: int, flags: int = 0):
+        self.model = model
+        desc = model.desc or model.make_desc()
+        err = C.create_string_buffer(512)
+        self.h = lib().vbs_cu_decoder_create(C.byref(desc), max_ctx, flags, err, 512)
+        if not self.h:
+            raise VbsError(f"vbs_cu_decoder_create: {err.value.decode()}")
+        self.max_ctx = max_ctx
+        self.vocab = model.shape.vocab
+
+    def forward(self, tokens, logits: bool = True):
+        import numpy as np
+        arr = (C.c_uint32 * len(tokens))(*[int(t) for t in tokens])
+        out = np.empty(self.vocab, dtype=np.float32) if logits else None
+        ptr = out.ctypes.data_as(C.POINTER(C.c_float)) if logits else None
+        check(lib().vbs_cu_decoder_forward(self.h, arr, len(tokens), ptr), "vbs_cu_decoder_forward")
+        return out
+
+    def forward_into(self, tok_arr, n: int, logits_ptr) -> None:
+        check(lib().vbs_cu_decoder_forward(self.h, tok_arr, n, logits_ptr), "vbs_cu_decoder_forward")
+
+    def generate(self, prompt, n_new: int):
+        arr = (C.c_uint32 * len(prompt))(*[int(t) for t in prompt])
+        out = (C.c_uint32 * max(1, n_new))()
+        check(lib().vbs_cu_decoder_generate(self.h, arr, len(prompt), n_new, out), "vbs_cu_decoder_generate")
+        return list(out)[:n_new]
+
+    def reset(self) -> None:
+        lib().vbs_cu_decoder_reset(self.h)
+
+    def set_position(self, pos: int, token: int) -> None:
+        check(lib().vbs_cu_decoder_set_position(self.h, pos, token), "vbs_cu_decoder_set_position")
+
+    @property
+    def position(self) -> int:
+        return int(lib().vbs_cu_decoder_position(self.h))
+
+    def enqueue_steps(self, n: int) -> None:
+        check(lib().vbs_cu_decoder_enqueue_steps(self.h, n), "vbs_cu_decoder_enqueue_steps")
+
+    @property
+    def stream(self) -> int:
+        return int(lib().vbs_cu_decoder_stream(self.h) or 0)
+
+    @property
+    def kernels_per_step(self) -> int:
+        return int(lib().vbs_cu_decoder_kernels_per_step(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            lib().vbs_cu_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------
+# GGUF v3 (the container the reference loads, src/vbs_gguf.c)
+# ---------------------------------------------------------------------------
+_GG_U32, _GG_F32, _GG_STR = 4, 6, 8
+
+
+def write_gguf(path, metadata: dict, tensors: list, alignment: int = 32) -> None:
+    """tensors: [(name, type_id, dims (ne0 = columns first), bytes)].
+    metadata values: int -> u32, float -> f32, str -> string."""
+    def s(x: str) -> bytes:
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    kv = b""
+    for k, v in metadata.items():
+        if isinstance(v, str):
+            kv += s(k) + struct.pack("<I", _GG_STR) + s(v)
+        elif isinstance(v, float):
+            kv += s(k) + struct.pack("<If", _GG_F32, v)
+        else:
+            kv += s(k) + struct.pack("<II", _GG_U32, int(v))
+    info, blobs, off = b"", [], 0
+    for name, typ, dims, data in tensors:
+        if off % alignment:
+            pad = alignment - off % alignment
+            blobs.append(b"\0" * pad)
+            off += pad
+        info += s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        info += struct.pack("<IQ", typ, off)
+        blobs.append(bytes(data))
+        off += len(data)
+    head = struct.pack("<4sIQQ", b"GGUF", 3, len(tensors), len(metadata)) + kv + info
+    start = (len(head) + alignment - 1) // alignment * alignment
+    with open(path, "wb") as f:
+        f.write(head)
+        f.write(b"\0" * (start - len(head)))
+        for b in blobs:
+            f.write(b)
+
+
+def read_gguf(path) -> tuple[dict, dict]:
+    """Minimal GGUF v3 reader: (metadata, {name: (type, dims, bytes)})."""
+    data = Path(path).read_bytes()
+    o = 0
+
+    def rd(fmt):
+        nonlocal o
+        v = struct.unpack_from(fmt, data, o)
+        o += struct.calcsize(fmt)
+        return v
+
+    def rs():
+        (n,) = rd("<Q")
+        nonlocal o
+        v = data[o:o + n].decode()
+        o += n
+        return v
+
+    magic, ver, nt, nkv = rd("<4sIQQ")
+    if magic != b"GGUF" or ver != 3:
+        raise ValueError("not a GGUF v3 file")
+    meta = {}
+    scal = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
+    for _ in range(nkv):
+        k = rs()
+        (t,) = rd("<I")
+        if t == _GG_STR:
+            meta[k] = rs()
+        elif t in scal:
+            (meta[k],) = rd(scal[t])
+        else:
+            raise ValueError(f"unsupported metadata type {t} for {k}")
+    infos = []
+    for _ in range(nt):
+        name = rs()
+        (nd,) = rd("<I")
+        dims = rd("<" + "Q" * nd)
+        typ, rel = rd("<IQ")
+        infos.append((name, typ, dims, rel))
+    align = int(meta.get("general.alignment", 32))
+    start = (o + align - 1) // align * align
+    tens = {}
+    for name, typ, dims, rel in infos:
+        cols, rows = dims[0], 1
+        for d in dims[1:]:
+            rows *= d
+        nbytes = row_bytes(typ, cols) * rows
+        tens[name] = (typ, dims, data[start + rel:start + rel + nbytes])
+    return meta, tens
+
+
+def upload_gguf(path, device="cuda") -> DeviceModel:
+    """Load a llama GGUF onto the device (one copy per tensor, like the
+    reference fabric's copy_to_device, src/vbs_fabric.c:81-94)."""
+    import numpy as np
+    import torch
+    meta, tens = read_gguf(path)
+    a = "llama."
+    nl = int(meta[a + "block_count"])
+    dim = int(meta[a + "embedding_length"])
+    nh = int(meta[a + "attention.head_count"])
+    nkv = int(meta.get(a + "attention.head_count_kv", nh))
+    ffn = int(meta[a + "feed_forward_length"])
+    vocab = tens["token_embd.weight"][1][1]
+    shape = LlamaShape(nl, dim, nh, nkv, ffn, vocab, float(meta.get(a + "attention.layer_norm_rms_epsilon", 1e-5)),
+                       float(meta.get(a + "rope.freq_base", 10000.0)))
+    types = {"token_embd": tens["token_embd.weight"][0],
+             "output": tens.get("output.weight", tens["token_embd.weight"])[0]}
+    for base in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
+        types[base] = tens[f"blk.0.{base}.weight"][0]
+    m = DeviceModel(shape=shape, types=types)
+
+    def put(key, name, as_float=False):
+        typ, dims, b = tens[name]
+        if as_float:
+            arr = np.frombuffer(b, dtype=np.float32).copy() if typ == F32 else None
+            if arr is None:
+                raise ValueError(f"{name}: norm weights must be F32")
+            m.tensors[key] = torch.from_numpy(arr).to(device)
+        else:
+            t = torch.zeros(len(b) + 256, dtype=torch.uint8)
+            t[:len(b)] = torch.frombuffer(bytearray(b), dtype=torch.uint8)
+            m.tensors[key] = t.to(device)
+
+    put("token_embd", "token_embd.weight")
+    put("output", "output.weight" if "output.weight" in tens else "token_embd.weight")
+    put("output_norm", "output_norm.weight", as_float=True)
+    for l in range(nl):
+        for base in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
+            put(f"blk.{l}.{base}", f"blk.{l}.{base}.weight")
+        put(f"blk.{l}.attn_norm", f"blk.{l}.attn_norm.weight", as_float=True)
+        put(f"blk.{l}.ffn_norm", f"blk.{l}.ffn_norm.weight", as_float=True)
+    m.make_desc()
+    return m

@@ -1,0 +1,38 @@
+// backend.h -- state shared between the ops-table implementation
+// (backend.cu) and the decode program (decoder.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace vbs {
+
+struct DevState {
+    int ordinal = -1;
+    int n_sm = 0;
+    uint32_t *err = nullptr;        // device error word (see common.cuh)
+    void *attn_work = nullptr;      // shared split-KV workspace for the ops table / vbs_cu_attention
+    size_t attn_work_bytes = 0;
+};
+
+// Devices usable by this library (sm_100). Index = position in the ops
+// table's device list; ordinal = CUDA device ordinal.
+int backend_device_count();
+DevState *backend_device(size_t index);
+// DevState of the calling thread's current CUDA device (initialising the
+// backend if needed); NULL when that device is not usable.
+DevState *backend_current();
+
+// Sticky error: the first message wins until vbs_cu_clear_error().
+void latch_error(const char *fmt, ...);
+bool has_error();
+// Latch and return false when e != cudaSuccess.
+bool cuda_ok(cudaError_t e, const char *what);
+// Read (and clear) the device error word of `d`; latch when nonzero.
+bool check_device_error(DevState *d, cudaStream_t st);
+
+// Grow the device's shared attention workspace to `bytes` (zeroed).
+void *attn_workspace(DevState *d, size_t bytes);
+
+}  // namespace vbs

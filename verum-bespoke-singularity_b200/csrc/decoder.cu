@@ -1,0 +1,489 @@
+// decoder.cu -- the per-token decode step as one device program.
+//
+// The reference JIT emits forward_token() as ~16 host calls per layer
+// through the bridge (src/vbs_specializer.c:270-349) and reads all logits
+// back after every call (:351-359). Here the same step, in the same op
+// order, is a short chain of fused kernels recorded once into a CUDA graph
+// and replayed per token; the position and the token live in a device
+// control block (ctrl[0] = position, ctrl[1] = token), so consecutive steps
+// need no host work: the argmax at the end of a step writes the next token
+// and advances the position.
+//
+// Fast step, per layer (5 kernels, programmatic dependent launch between
+// them so each kernel's weight stream starts while the previous one ends):
+//   1. RMSNorm(attn_norm) + Q/K/V matvec + RoPE + fp16 KV store
+//   2. split-KV GQA attention
+//   3. o_proj matvec + residual add
+//   4. RMSNorm(ffn_norm) + gate/up matvec + SiLU*up
+//   5. down matvec + residual add
+// then RMSNorm(output_norm) + output matvec, and the argmax.
+//
+// Strict step (VBS_CU_DEC_STRICT): the vbs_cpu arithmetic
+// (src/vbs_cpu.c:572-639) op by op, fp32 KV cache, for token-exact parity.
+//
+// Tensor parallelism: o_proj and down produce partial sums that are
+// all-reduced (NCCL) and added into the residual by the next kernel's
+// prologue; the output rows are sharded and all-gathered before the argmax.
+#include "../../include/vbs_b200.h"
+#include "backend.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "tp.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace vbs;
+
+namespace {
+
+struct Layer {
+    const float *attn_norm, *ffn_norm;
+    const uint8_t *wq, *wk, *wv, *wo, *wgate, *wup, *wdown;
+    int tq, tk, tv, to, tgate, tup, tdown;
+};
+
+}  // namespace
+
+struct vbs_cu_decoder {
+    vbs_cu_model_t m;
+    std::vector<Layer> L;
+    uint32_t flags = 0, max_ctx = 0, kv_dim = 0, q_dim = 0, vocab_full = 0;
+    bool strict = false, use_graph = true, use_pdl = true;
+    int tp_world = 1;
+    DevState *dev = nullptr;
+    cudaStream_t st = nullptr;
+    // activations
+    float *x = nullptr, *x2 = nullptr, *q = nullptr, *att = nullptr, *hid = nullptr, *logits = nullptr,
+          *logits_full = nullptr, *partial = nullptr;
+    float *norm = nullptr, *k = nullptr, *v = nullptr, *gate = nullptr, *up = nullptr, *tmp = nullptr, *scores = nullptr;
+    int8_t *xq = nullptr;
+    float *qd = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    float *kcf = nullptr, *vcf = nullptr;
+    uint32_t *ctrl = nullptr, *hist = nullptr, *tok_dev = nullptr;
+    size_t tok_cap = 0;
+    uint32_t *pinned = nullptr;      // [0..1] ctrl readback
+    float *logits_pinned = nullptr;
+    void *attn_work = nullptr;
+    uint32_t n_splits = 1;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint32_t kernels_per_step = 0;
+    bool resid_in_x2 = false;        // TP ping-pong: where the residual of the next step lives
+};
+
+namespace {
+
+bool dmalloc(void **p, size_t bytes, const char *what) {
+    return cuda_ok(cudaMalloc(p, bytes ? bytes : 16), what);
+}
+
+// Launch one matvec y (+)= W x through the fastest kernel that supports it.
+bool step_matvec(vbs_cu_decoder *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
+                 bool accumulate, const float *norm_w, const float *x_add, float *x_write) {
+    const void *wv[1] = {w};
+    if (mv_fast_supported(type, rows, cols, wv, 1, x, 0)) {
+        MvParams p = {};
+        p.w[0] = p.w[1] = p.w[2] = w;
+        p.seg_end[0] = p.seg_end[1] = p.seg_end[2] = rows;
+        p.rb = row_bytes(type, cols);
+        p.rows = rows;
+        p.cols = cols;
+        p.x = x;
+        p.norm_w = norm_w;
+        p.eps = d->m.eps;
+        p.x_add = x_add;
+        p.x_write = x_write;
+        p.y = y;
+        p.accumulate = accumulate ? 1u : 0u;
+        p.err = d->dev->err;
+        return cuda_ok(mv_fast_launch(type, 0, MV_EPI_STORE, p, d->dev->n_sm, d->st, d->use_pdl, 0), "decode matvec");
+    }
+    // portable path: explicit norm into d->norm when requested
+    const float *xin = x;
+    if (x_add) {
+        if (!cuda_ok(add_launch(x, x_add, x_write, cols, d->st), "decode residual")) return false;
+        xin = x_write;
+    }
+    if (norm_w) {
+        if (!cuda_ok(rmsnorm_launch(xin, norm_w, d->norm, cols, d->m.eps, d->st), "decode norm")) return false;
+        xin = d->norm;
+    }
+    return cuda_ok(mv_generic_launch(type, w, xin, y, rows, cols, 1, cols, rows, accumulate ? 1 : 0, d->dev->n_sm, d->st),
+                   "decode matvec");
+}
+
+bool enqueue_fast_step(vbs_cu_decoder *d) {
+    const vbs_cu_model_t &m = d->m;
+    const uint32_t dim = m.dim, hd = m.head_dim, nq = m.n_heads * hd, nk = d->kv_dim;
+    cudaStream_t st = d->st;
+    const bool tp = d->tp_world > 1;
+    // residual ping-pong (TP): xr is the residual read by this kernel's
+    // prologue, xw where the summed residual is written
+    float *xr = d->x, *xw = d->x2;
+
+    if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->x, dim, st, d->use_pdl),
+                 "decode embed"))
+        return false;
+    const float *pending = nullptr;   // TP: partial sum to add into the residual
+    for (uint32_t l = 0; l < m.n_layers; ++l) {
+        const Layer &ly = d->L[l];
+        // ---- 1. norm + QKV + RoPE + KV store ----
+        const void *wv[3] = {ly.wq, ly.wk, ly.wv};
+        const bool fused = ly.tq == ly.tk && ly.tq == ly.tv && mv_fast_supported(ly.tq, nq + 2 * nk, dim, wv, 3, xr, 0);
+        if (fused) {
+            MvParams p = {};
+            p.w[0] = ly.wq; p.w[1] = ly.wk; p.w[2] = ly.wv;
+            p.seg_end[0] = nq; p.seg_end[1] = nq + nk; p.seg_end[2] = nq + 2 * nk;
+            p.rb = row_bytes(ly.tq, dim);
+            p.rows = nq + 2 * nk;
+            p.cols = dim;
+            p.x = xr;
+            p.norm_w = ly.attn_norm;
+            p.eps = m.eps;
+            p.x_add = pending;
+            p.x_write = pending ? xw : nullptr;
+            p.err = d->dev->err;
+            p.q_out = d->q;
+            p.kc = d->kc; p.vc = d->vc;
+            p.ctrl = d->ctrl;
+            p.layer = l; p.max_ctx = d->max_ctx; p.kv_dim = nk; p.head_dim = hd;
+            p.theta = m.theta;
+            if (!cuda_ok(mv_fast_launch(ly.tq, 0, MV_EPI_QKV, p, d->dev->n_sm, st, d->use_pdl, 0), "decode qkv")) return false;
+        } else {
+            if (!step_matvec(d, ly.tq, ly.wq, xr, d->q, nq, dim, false, ly.attn_norm, pending, pending ? xw : nullptr)) return false;
+            const float *xin = pending ? xw : xr;
+            if (!step_matvec(d, ly.tk, ly.wk, xin, d->k, nk, dim, false, ly.attn_norm, nullptr, nullptr)) return false;
+            if (!step_matvec(d, ly.tv, ly.wv, xin, d->v, nk, dim, false, ly.attn_norm, nullptr, nullptr)) return false;
+            if (!cuda_ok(rope_launch(d->q, 0, d->ctrl, hd, m.n_heads, m.theta, st), "decode rope")) return false;
+            if (!cuda_ok(rope_launch(d->k, 0, d->ctrl, hd, m.n_kv_heads, m.theta, st), "decode rope")) return false;
+            if (!cuda_ok(cache_store_launch(d->k, d->v, d->kc, d->vc, 0, d->ctrl, l, d->max_ctx, nk, st), "decode kv store"))
+                return false;
+        }
+        if (pending) { std::swap(xr, xw); pending = nullptr; }
+        // ---- 2. attention ----
+        AttnParams ap = {};
+        ap.q = d->q; ap.kc = d->kc; ap.vc = d->vc; ap.out = d->att;
+        ap.seq_dev = d->ctrl;
+        ap.layer = l; ap.max_ctx = d->max_ctx;
+        ap.nqh = m.n_heads; ap.nkh = m.n_kv_heads; ap.hd = hd;
+        ap.scale = 1.0f / sqrtf((float)hd);
+        ap.batch = 1;
+        ap.work = d->attn_work;
+        ap.err = d->dev->err;
+        if (!cuda_ok(attn_launch(ap, d->n_splits, st, d->use_pdl), "decode attention")) return false;
+        // ---- 3. o_proj (+ residual, or partial under TP) ----
+        if (tp) {
+            if (!step_matvec(d, ly.to, ly.wo, d->att, d->partial, dim, nq, false, nullptr, nullptr, nullptr)) return false;
+            if (!tp_allreduce_sum(d->partial, dim, st)) return false;
+            pending = d->partial;
+        } else {
+            if (!step_matvec(d, ly.to, ly.wo, d->att, xr, dim, nq, true, nullptr, nullptr, nullptr)) return false;
+        }
+        // ---- 4. norm + gate/up + SiLU ----
+        const void *wg[2] = {ly.wgate, ly.wup};
+        const bool dual = ly.tgate == ly.tup && mv_fast_supported(ly.tgate, m.ffn, dim, wg, 2, xr, 1);
+        if (dual) {
+            MvParams p = {};
+            p.w[0] = p.w[1] = p.w[2] = ly.wgate;
+            p.seg_end[0] = p.seg_end[1] = p.seg_end[2] = m.ffn;
+            p.wb = ly.wup;
+            p.rb = row_bytes(ly.tgate, dim);
+            p.rows = m.ffn;
+            p.cols = dim;
+            p.x = xr;
+            p.norm_w = ly.ffn_norm;
+            p.eps = m.eps;
+            p.x_add = pending;
+            p.x_write = pending ? xw : nullptr;
+            p.y = d->hid;
+            p.err = d->dev->err;
+            if (!cuda_ok(mv_fast_launch(ly.tgate, 1, MV_EPI_SILU, p, d->dev->n_sm, st, d->use_pdl, 0), "decode gate/up")) return false;
+        } else {
+            if (!step_matvec(d, ly.tgate, ly.wgate, xr, d->gate, m.ffn, dim, false, ly.ffn_norm, pending, pending ? xw : nullptr))
+                return false;
+            const float *xin = pending ? xw : xr;
+            if (!step_matvec(d, ly.tup, ly.wup, xin, d->up, m.ffn, dim, false, ly.ffn_norm, nullptr, nullptr)) return false;
+            if (!cuda_ok(silu_mul_launch(d->gate, d->up, d->hid, m.ffn, st), "decode silu")) return false;
+        }
+        if (pending) { std::swap(xr, xw); pending = nullptr; }
+        // ---- 5. down (+ residual, or partial under TP) ----
+        if (tp) {
+            if (!step_matvec(d, ly.tdown, ly.wdown, d->hid, d->partial, dim, m.ffn, false, nullptr, nullptr, nullptr)) return false;
+            if (!tp_allreduce_sum(d->partial, dim, st)) return false;
+            pending = d->partial;
+        } else {
+            if (!step_matvec(d, ly.tdown, ly.wdown, d->hid, xr, dim, m.ffn, true, nullptr, nullptr, nullptr)) return false;
+        }
+    }
+    // ---- final norm + output ----
+    if (!step_matvec(d, m.out_type, static_cast<const uint8_t *>(m.out), xr, d->logits, m.vocab, dim, false, m.out_norm,
+                     pending, pending ? xw : nullptr))
+        return false;
+    if (pending) std::swap(xr, xw);
+    const float *lg = d->logits;
+    if (tp) {
+        if (!tp_allgather(d->logits, d->logits_full, m.vocab, st)) return false;
+        lg = d->logits_full;
+    }
+    // the embedding of the next step writes d->x: the residual must end in d->x
+    (void)xr;
+    return cuda_ok(argmax_launch(lg, d->vocab_full, nullptr, d->ctrl, d->hist, (uint32_t)d->max_ctx + 1, st, d->use_pdl),
+                   "decode argmax");
+}
+
+bool enqueue_strict_step(vbs_cu_decoder *d) {
+    const vbs_cu_model_t &m = d->m;
+    const uint32_t dim = m.dim, hd = m.head_dim, nq = m.n_heads * hd, nk = d->kv_dim;
+    cudaStream_t st = d->st;
+    auto mat = [&](int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols, bool quantized) -> bool {
+        if (type == T_F32) return cuda_ok(strict_matvec_f32_launch(reinterpret_cast<const float *>(w), rows, cols, x, y, 0, st), "strict matvec");
+        if (type != T_Q8_0) { latch_error("strict mode supports Q8_0 and F32 weights only (type %d)", type); return false; }
+        if (!quantized && !cuda_ok(strict_quantize_q8_launch(x, cols, d->xq, d->qd, st), "strict quantize")) return false;
+        return cuda_ok(strict_matvec_q8_0_launch(w, rows, cols, d->xq, d->qd, y, 0, st), "strict matvec");
+    };
+    if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->x, dim, st, false), "strict embed"))
+        return false;
+    for (uint32_t l = 0; l < m.n_layers; ++l) {
+        const Layer &ly = d->L[l];
+        if (!cuda_ok(strict_rmsnorm_launch(d->x, ly.attn_norm, d->norm, dim, m.eps, st), "strict norm")) return false;
+        if (!mat(ly.tq, ly.wq, d->norm, d->q, nq, dim, false)) return false;
+        const bool shared_q8 = ly.tq == T_Q8_0;
+        if (!mat(ly.tk, ly.wk, d->norm, d->k, nk, dim, shared_q8 && ly.tk == T_Q8_0)) return false;
+        if (!mat(ly.tv, ly.wv, d->norm, d->v, nk, dim, shared_q8 && ly.tk == T_Q8_0 && ly.tv == T_Q8_0)) return false;
+        if (!cuda_ok(strict_rope_launch(d->q, m.n_heads, hd, d->ctrl, m.theta, st), "strict rope")) return false;
+        if (!cuda_ok(strict_rope_launch(d->k, m.n_kv_heads, hd, d->ctrl, m.theta, st), "strict rope")) return false;
+        if (!cuda_ok(strict_attention_launch(d->q, d->k, d->v, d->kcf, d->vcf, d->att, d->ctrl, l, d->max_ctx, m.n_heads,
+                                             m.n_kv_heads, hd, d->scores, d->dev->err, st),
+                     "strict attention"))
+            return false;
+        if (!mat(ly.to, ly.wo, d->att, d->tmp, dim, nq, false)) return false;
+        if (!cuda_ok(strict_add_launch(d->x, d->tmp, dim, st), "strict add")) return false;
+        if (!cuda_ok(strict_rmsnorm_launch(d->x, ly.ffn_norm, d->norm, dim, m.eps, st), "strict norm")) return false;
+        if (!mat(ly.tgate, ly.wgate, d->norm, d->gate, m.ffn, dim, false)) return false;
+        if (!mat(ly.tup, ly.wup, d->norm, d->up, m.ffn, dim, ly.tgate == T_Q8_0 && ly.tup == T_Q8_0)) return false;
+        if (!cuda_ok(strict_silu_launch(d->gate, d->up, d->hid, m.ffn, st), "strict silu")) return false;
+        if (!mat(ly.tdown, ly.wdown, d->hid, d->tmp, dim, m.ffn, false)) return false;
+        if (!cuda_ok(strict_add_launch(d->x, d->tmp, dim, st), "strict add")) return false;
+    }
+    if (!cuda_ok(strict_rmsnorm_launch(d->x, m.out_norm, d->norm, dim, m.eps, st), "strict norm")) return false;
+    if (!mat(m.out_type, static_cast<const uint8_t *>(m.out), d->norm, d->logits, m.vocab, dim, false)) return false;
+    return cuda_ok(argmax_launch(d->logits, m.vocab, nullptr, d->ctrl, d->hist, (uint32_t)d->max_ctx + 1, st, false), "strict argmax");
+}
+
+bool enqueue_step_raw(vbs_cu_decoder *d) { return d->strict ? enqueue_strict_step(d) : enqueue_fast_step(d); }
+
+// One step: graph replay when available, else direct launches.
+bool enqueue_step(vbs_cu_decoder *d) {
+    if (d->exec) {
+        note_launches(d->kernels_per_step);
+        return cuda_ok(cudaGraphLaunch(d->exec, d->st), "decode graph launch");
+    }
+    return enqueue_step_raw(d);
+}
+
+bool build_graph(vbs_cu_decoder *d) {
+    const uint64_t before = vbs_cu_kernel_launches();
+    if (!cuda_ok(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal), "graph capture")) return false;
+    const bool ok = enqueue_step_raw(d);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(d->st, &g);
+    if (!ok || !cuda_ok(e, "graph capture")) {
+        if (g) cudaGraphDestroy(g);
+        return false;
+    }
+    d->kernels_per_step = (uint32_t)(vbs_cu_kernel_launches() - before);
+    d->graph = g;
+    return cuda_ok(cudaGraphInstantiate(&d->exec, g, 0), "graph instantiate");
+}
+
+bool sync_and_check(vbs_cu_decoder *d) {
+    if (!cuda_ok(cudaStreamSynchronize(d->st), "decode synchronise")) return false;
+    return check_device_error(d->dev, d->st);
+}
+
+bool put_tokens(vbs_cu_decoder *d, const uint32_t *tokens, size_t n) {
+    if (n > d->tok_cap) {
+        if (d->tok_dev) cudaFree(d->tok_dev);
+        d->tok_dev = nullptr;
+        d->tok_cap = 0;
+        if (!dmalloc(reinterpret_cast<void **>(&d->tok_dev), n * 4, "token buffer")) return false;
+        d->tok_cap = n;
+    }
+    return cuda_ok(cudaMemcpyAsync(d->tok_dev, tokens, n * 4, cudaMemcpyHostToDevice, d->st), "token upload");
+}
+
+}  // namespace
+
+extern "C" {
+
+vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t flags, char *err, size_t cap) {
+    auto fail = [&](const char *msg, vbs_cu_decoder *d) -> vbs_cu_decoder_t * {
+        if (err && cap) snprintf(err, cap, "%s%s%s", msg, has_error() ? ": " : "", has_error() ? vbs_cuda_last_error() : "");
+        if (d) vbs_cu_decoder_destroy(d);
+        return nullptr;
+    };
+    DevState *dev = backend_current();
+    if (!dev) return fail("no usable sm_100 device", nullptr);
+    if (!m || !m->n_layers || !m->dim || !m->n_heads || !m->n_kv_heads || !m->head_dim || m->n_heads % m->n_kv_heads ||
+        !m->ffn || !m->vocab || !max_ctx || m->head_dim % 2 || !m->embd || !m->out || !m->out_norm)
+        return fail("invalid model description", nullptr);
+    vbs_cu_decoder *d = new vbs_cu_decoder();
+    d->m = *m;
+    d->flags = flags;
+    d->strict = (flags & VBS_CU_DEC_STRICT) != 0;
+    d->use_graph = !(flags & VBS_CU_DEC_NO_GRAPH);
+    d->use_pdl = !(flags & VBS_CU_DEC_NO_PDL) && !d->strict;
+    d->max_ctx = max_ctx;
+    d->dev = dev;
+    d->kv_dim = m->n_kv_heads * m->head_dim;
+    d->q_dim = m->n_heads * m->head_dim;
+    d->vocab_full = m->vocab_full ? m->vocab_full : m->vocab;
+    d->tp_world = tp_world();
+    if (d->tp_world > 1 && d->strict) return fail("strict mode runs on one GPU", d);
+    if (d->tp_world == 1 && d->vocab_full != m->vocab) return fail("vocab_full differs from vocab without TP", d);
+    d->L.resize(m->n_layers);
+    for (uint32_t l = 0; l < m->n_layers; ++l) {
+        Layer &y = d->L[l];
+        y.attn_norm = m->attn_norm[l]; y.ffn_norm = m->ffn_norm[l];
+        y.wq = static_cast<const uint8_t *>(m->wq[l]); y.wk = static_cast<const uint8_t *>(m->wk[l]);
+        y.wv = static_cast<const uint8_t *>(m->wv[l]); y.wo = static_cast<const uint8_t *>(m->wo[l]);
+        y.wgate = static_cast<const uint8_t *>(m->wgate[l]); y.wup = static_cast<const uint8_t *>(m->wup[l]);
+        y.wdown = static_cast<const uint8_t *>(m->wdown[l]);
+        y.tq = m->tq[l]; y.tk = m->tk[l]; y.tv = m->tv[l]; y.to = m->to[l];
+        y.tgate = m->tgate[l]; y.tup = m->tup[l]; y.tdown = m->tdown[l];
+    }
+    if (!cuda_ok(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "decoder stream")) return fail("stream", d);
+    const size_t big = std::max<size_t>(std::max<size_t>(m->dim, m->ffn), d->q_dim);
+    bool ok = dmalloc((void **)&d->x, m->dim * 4, "x") && dmalloc((void **)&d->x2, m->dim * 4, "x2") &&
+              dmalloc((void **)&d->q, d->q_dim * 4, "q") && dmalloc((void **)&d->att, d->q_dim * 4, "att") &&
+              dmalloc((void **)&d->hid, m->ffn * 4, "hidden") && dmalloc((void **)&d->logits, m->vocab * 4, "logits") &&
+              dmalloc((void **)&d->norm, big * 4, "norm") && dmalloc((void **)&d->k, d->kv_dim * 4, "k") &&
+              dmalloc((void **)&d->v, d->kv_dim * 4, "v") && dmalloc((void **)&d->gate, m->ffn * 4, "gate") &&
+              dmalloc((void **)&d->up, m->ffn * 4, "up") && dmalloc((void **)&d->tmp, big * 4, "tmp") &&
+              dmalloc((void **)&d->ctrl, 64, "ctrl") && dmalloc((void **)&d->hist, ((size_t)max_ctx + 2) * 4, "history") &&
+              dmalloc((void **)&d->partial, m->dim * 4, "partial");
+    if (ok && d->tp_world > 1) ok = dmalloc((void **)&d->logits_full, (size_t)d->vocab_full * 4, "logits_full");
+    const size_t cache_elems = (size_t)m->n_layers * max_ctx * d->kv_dim;
+    if (ok && d->strict) {
+        ok = dmalloc((void **)&d->kcf, cache_elems * 4, "kv cache") && dmalloc((void **)&d->vcf, cache_elems * 4, "kv cache") &&
+             dmalloc((void **)&d->scores, (size_t)m->n_heads * max_ctx * 4, "scores") &&
+             dmalloc((void **)&d->xq, big, "xq") && dmalloc((void **)&d->qd, (big / 32 + 1) * 4, "qd");
+    } else if (ok) {
+        ok = dmalloc((void **)&d->kc, cache_elems * 2, "kv cache") && dmalloc((void **)&d->vc, cache_elems * 2, "kv cache");
+        if (ok) {
+            d->n_splits = attn_num_splits(max_ctx, m->n_kv_heads, 1, dev->n_sm);
+            const size_t wb = attn_workspace_bytes(m->n_heads, m->n_kv_heads, m->head_dim, 1, d->n_splits);
+            ok = dmalloc(&d->attn_work, wb, "attention workspace") && cuda_ok(cudaMemset(d->attn_work, 0, wb), "workspace");
+        }
+    }
+    if (ok) ok = cuda_ok(cudaMallocHost((void **)&d->pinned, 64), "pinned") &&
+                 cuda_ok(cudaMallocHost((void **)&d->logits_pinned, (size_t)d->vocab_full * 4), "pinned logits");
+    if (!ok) return fail("device allocation failed", d);
+    if (d->kc) {
+        cudaMemsetAsync(d->kc, 0, cache_elems * 2, d->st);
+        cudaMemsetAsync(d->vc, 0, cache_elems * 2, d->st);
+    }
+    cudaMemsetAsync(d->ctrl, 0, 64, d->st);
+    cudaMemsetAsync(d->x, 0, m->dim * 4, d->st);
+    if (d->use_graph) {
+        if (!build_graph(d)) return fail("decode graph build failed", d);
+    } else {
+        // count kernels per step by recording one step's launches without running it
+        d->kernels_per_step = 0;
+    }
+    if (!sync_and_check(d)) return fail("decoder initialisation failed", d);
+    return d;
+}
+
+void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
+    if (!d) return;
+    if (d->st) cudaStreamSynchronize(d->st);
+    if (d->exec) cudaGraphExecDestroy(d->exec);
+    if (d->graph) cudaGraphDestroy(d->graph);
+    void *bufs[] = {d->x, d->x2, d->q, d->att, d->hid, d->logits, d->logits_full, d->partial, d->norm, d->k, d->v,
+                    d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
+                    d->tok_dev, d->attn_work};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    if (d->pinned) cudaFreeHost(d->pinned);
+    if (d->logits_pinned) cudaFreeHost(d->logits_pinned);
+    if (d->st) cudaStreamDestroy(d->st);
+    delete d;
+}
+
+int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n, float *logits_out) {
+    if (!d || (!tokens && n)) { latch_error("decoder_forward: invalid arguments"); return -1; }
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != d->dev->ordinal) cudaSetDevice(d->dev->ordinal);
+    if (n) {
+        if (!put_tokens(d, tokens, n)) return -1;
+        for (size_t i = 0; i < n; ++i) {
+            if (!cuda_ok(cudaMemcpyAsync(d->ctrl + 1, d->tok_dev + i, 4, cudaMemcpyDeviceToDevice, d->st), "token feed")) return -1;
+            if (!enqueue_step(d)) return -1;
+        }
+    }
+    if (logits_out) {
+        const float *src = d->tp_world > 1 ? d->logits_full : d->logits;
+        if (!cuda_ok(cudaMemcpyAsync(d->logits_pinned, src, (size_t)d->vocab_full * 4, cudaMemcpyDeviceToHost, d->st), "logits readback"))
+            return -1;
+    }
+    if (!sync_and_check(d)) return -1;
+    if (logits_out) memcpy(logits_out, d->logits_pinned, (size_t)d->vocab_full * 4);
+    return 0;
+}
+
+void vbs_cu_decoder_reset(vbs_cu_decoder_t *d) {
+    if (!d) return;
+    cudaMemsetAsync(d->ctrl, 0, 4, d->st);
+    cudaStreamSynchronize(d->st);
+}
+
+int vbs_cu_decoder_set_position(vbs_cu_decoder_t *d, uint32_t pos, uint32_t token) {
+    if (!d || pos >= d->max_ctx) { latch_error("decoder_set_position: position out of range"); return -1; }
+    d->pinned[0] = pos;
+    d->pinned[1] = token;
+    if (!cuda_ok(cudaMemcpyAsync(d->ctrl, d->pinned, 8, cudaMemcpyHostToDevice, d->st), "set position")) return -1;
+    return cuda_ok(cudaStreamSynchronize(d->st), "set position") ? 0 : -1;
+}
+
+uint32_t vbs_cu_decoder_position(vbs_cu_decoder_t *d) {
+    if (!d) return 0;
+    if (!cuda_ok(cudaMemcpyAsync(d->pinned, d->ctrl, 8, cudaMemcpyDeviceToHost, d->st), "position")) return 0;
+    cudaStreamSynchronize(d->st);
+    return d->pinned[0];
+}
+
+int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t n_prompt, uint32_t n_new, uint32_t *out) {
+    if (!d || !prompt || !n_prompt || (n_new && !out)) { latch_error("decoder_generate: invalid arguments"); return -1; }
+    if (n_prompt + (n_new ? n_new - 1 : 0) > d->max_ctx) { latch_error("decoder_generate: exceeds context capacity"); return -1; }
+    const uint32_t start = vbs_cu_decoder_position(d);
+    if (vbs_cu_decoder_forward(d, prompt, n_prompt, nullptr)) return -1;
+    for (uint32_t i = 1; i < n_new; ++i)
+        if (!enqueue_step(d)) return -1;
+    if (n_new) {
+        if (!cuda_ok(cudaMemcpyAsync(out, d->hist + start + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, d->st), "tokens"))
+            return -1;
+    }
+    return sync_and_check(d) ? 0 : -1;
+}
+
+int vbs_cu_decoder_enqueue_steps(vbs_cu_decoder_t *d, uint32_t n) {
+    if (!d) return -1;
+    for (uint32_t i = 0; i < n; ++i)
+        if (!enqueue_step(d)) return -1;
+    return 0;
+}
+
+void *vbs_cu_decoder_stream(vbs_cu_decoder_t *d) { return d ? d->st : nullptr; }
+const float *vbs_cu_decoder_logits_device(vbs_cu_decoder_t *d) {
+    return d ? (d->tp_world > 1 ? d->logits_full : d->logits) : nullptr;
+}
+uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d) { return d ? d->kernels_per_step : 0; }
+
+}  // extern "C"

@@ -1,0 +1,119 @@
+// kernels.h -- host-side launch interface between the backend and the
+// kernel translation units. Device pointers only; every launcher returns a
+// cudaError_t and never synchronises.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace vbs {
+
+// ---- matvec ----------------------------------------------------------------
+
+enum MvEpi : int {
+    MV_EPI_STORE = 0,   // y[r] = v, or y[r] += v when accumulate
+    MV_EPI_SILU = 1,    // dual: y[r] = silu(gate_r) * up_r
+    MV_EPI_QKV = 2,     // rows [q | k | v]: RoPE on q/k, k/v stored as fp16 into the KV cache
+};
+
+struct MvParams {
+    const uint8_t *w[3];        // row segments of matrix A (concatenated row space)
+    uint32_t seg_end[3];        // cumulative row ends of the segments
+    const uint8_t *wb;          // dual: matrix B (row r pairs with A's row r)
+    uint64_t rb;                // packed bytes per row
+    uint32_t rows, cols;
+    const float *x;             // input (cols floats)
+    const float *norm_w;        // optional RMSNorm weight applied to x first (NULL: none)
+    float eps;
+    const float *x_add;         // optional: x := x + x_add (before the norm), CTA 0 writes x back
+    float *x_write;             // where CTA 0 stores the summed x (may alias x)
+    float *y;                   // STORE / SILU output
+    uint32_t accumulate;
+    uint32_t nstage;
+    uint32_t *err;
+    // QKV epilogue
+    float *q_out;
+    uint16_t *kc, *vc;          // full caches; layer offset folded in from layer/max_ctx
+    const uint32_t *ctrl;       // ctrl[0] = current position
+    uint32_t layer, max_ctx, kv_dim, head_dim;
+    float theta;
+};
+
+// True when the TMA/mma kernel can serve this shape/alignment.
+bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const *w, int nw,
+                       const void *x, int dual);
+cudaError_t mv_fast_launch(int type, int dual, int epi, const MvParams &p, int n_sm, cudaStream_t st,
+                           bool pdl, int grid_override);
+
+// Portable exact-dequant fp32 kernel (any type, any alignment, batched).
+cudaError_t mv_generic_launch(int type, const uint8_t *w, const float *x, float *y, uint32_t rows,
+                              uint32_t cols, uint32_t batch, uint64_t x_stride, uint64_t y_stride,
+                              int accumulate, int n_sm, cudaStream_t st);
+
+cudaError_t dequant_launch(int type, const uint8_t *w, float *out, uint64_t n_elems, cudaStream_t st);
+
+// ---- primitives (host_math semantics, src/vbs_host_math.h) -----------------
+
+cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, uint32_t token, float *out,
+                         uint32_t dim, cudaStream_t st, bool pdl);
+cudaError_t rmsnorm_launch(const float *in, const float *w, float *out, uint32_t n, float eps, cudaStream_t st);
+// rope/cache store take the position from ctrl[0] when ctrl != NULL.
+cudaError_t rope_launch(float *x, uint32_t pos, const uint32_t *ctrl, uint32_t head_dim, uint32_t n_heads, float theta,
+                        cudaStream_t st);
+cudaError_t silu_mul_launch(const float *g, const float *u, float *out, uint32_t n, cudaStream_t st);
+cudaError_t add_launch(const float *a, const float *b, float *out, uint32_t n, cudaStream_t st);
+cudaError_t cache_store_launch(const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t pos,
+                               const uint32_t *ctrl, uint32_t layer, uint32_t max_ctx, uint32_t kv_dim, cudaStream_t st);
+
+// Split-KV GQA decode attention. seq_len from `seq_dev` (+1) when non-NULL,
+// else `seq_len`. `work` holds the split partials and merge counters:
+// attn_workspace_bytes() bytes, counters zero on first use (self-resetting).
+struct AttnParams {
+    const float *q;
+    const uint16_t *kc, *vc;
+    float *out;
+    uint32_t seq_len;
+    const uint32_t *seq_dev;
+    uint32_t layer, max_ctx, nqh, nkh, hd;
+    float scale;
+    uint32_t batch;
+    uint64_t kv_batch_stride;   // elements between sequences' caches
+    void *work;
+    uint32_t *err;
+};
+size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t batch, uint32_t max_splits);
+uint32_t attn_num_splits(uint32_t seq_len_hint, uint32_t nkh, uint32_t batch, int n_sm);
+cudaError_t attn_launch(const AttnParams &p, uint32_t n_splits, cudaStream_t st, bool pdl);
+
+// argmax over n floats (first maximum wins); writes out_token and, when
+// ctrl != NULL, advances ctrl[0] (position) by one, stores the token in
+// ctrl[1] and in hist[new position] when hist != NULL and it fits.
+cudaError_t argmax_launch(const float *v, uint32_t n, uint32_t *out_token, uint32_t *ctrl, uint32_t *hist,
+                          uint32_t hist_cap, cudaStream_t st, bool pdl);
+
+// ---- strict-parity kernels (vbs_cpu arithmetic) -----------------------------
+cudaError_t strict_quantize_q8_launch(const float *x, uint32_t cols, int8_t *xq, float *qd, cudaStream_t st);
+cudaError_t strict_matvec_q8_0_launch(const uint8_t *w, uint32_t rows, uint32_t cols, const int8_t *xq,
+                                      const float *qd, float *y, int accumulate, cudaStream_t st);
+cudaError_t strict_matvec_f32_launch(const float *w, uint32_t rows, uint32_t cols, const float *x, float *y,
+                                     int accumulate, cudaStream_t st);
+cudaError_t strict_rmsnorm_launch(const float *in, const float *w, float *out, uint32_t n, float eps,
+                                  cudaStream_t st);
+cudaError_t strict_rope_launch(float *x, uint32_t n_heads, uint32_t head_dim, const uint32_t *ctrl,
+                               float theta, cudaStream_t st);
+cudaError_t strict_attention_launch(const float *q, const float *k, const float *v, float *kcache, float *vcache,
+                                    float *out, const uint32_t *ctrl, uint32_t layer, uint32_t context,
+                                    uint32_t nqh, uint32_t nkh, uint32_t hd, float *scores, uint32_t *err,
+                                    cudaStream_t st);
+cudaError_t strict_silu_launch(const float *g, const float *u, float *h, uint32_t n, cudaStream_t st);
+cudaError_t strict_add_launch(float *x, const float *t, uint32_t n, cudaStream_t st);
+
+// ---- synthetic weights -------------------------------------------------------
+cudaError_t synth_launch(int type, uint8_t *dst, uint64_t rows, uint64_t cols, uint64_t row0, uint64_t col0,
+                         uint64_t full_cols, uint64_t seed, float scale, cudaStream_t st);
+
+// Launch bookkeeping (counts kernels for vbs_cu_kernel_launches).
+void note_launches(uint64_t n);
+
+}  // namespace vbs

@@ -1,0 +1,16 @@
+// tp.h -- tensor-parallel collectives used by the decode program.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace vbs {
+
+int tp_world();   // 1 when no TP group has been joined
+int tp_rank();
+// In-place sum of n floats across the group, enqueued on `st`.
+bool tp_allreduce_sum(float *buf, size_t n, cudaStream_t st);
+// full[r * n_local .. +n_local) = rank r's `local`.
+bool tp_allgather(const float *local, float *full, size_t n_local, cudaStream_t st);
+
+}  // namespace vbs
