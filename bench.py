@@ -1,0 +1,426 @@
+"""Decode benchmark: Llama-3-8B-shaped Q4_K model, tokens/s.
+
+A "step" is one decode token of the full model: embedding, 32 layers of
+norm + Q/K/V + RoPE + KV store + split-KV attention + o_proj + norm +
+gate/up + SiLU + down, final norm, the 128256-row output projection and
+the greedy argmax, replayed as one CUDA graph through the C ABI
+(libvbs_b200.so, vbs_cu_decoder_*). Weights are seeded N(0, 0.02) synthesized
+and quantized on the device (Q4_K attention and gate/up, Q6_K down, output
+and embedding; no network, no checkpoint); the KV cache is filled by a real
+prefill of `--ctx` seeded prompt tokens (untimed), then K timed steps decode
+at context ctx..ctx+K. 4.84 GB of weights per token are far larger than the
+126 MB L2, so nothing is flushed between steps.
+
+Prints one JSON line (rank 0). N > 1 runs under torchrun as tensor
+parallelism over NVLink (NCCL all-reduce after o_proj and down_proj).
+`--impl reference` times the reference's CPU decode kernel instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT, ROOT / "tests"):
+    sys.path.insert(0, str(p))
+
+# Algorithmic bytes (weights excluding the embedding table, which decode
+# reads one row of) per token for the 8B shape, and KV bytes per position.
+L8B_WEIGHT_BYTES = 4_841_250_816
+KV_BYTES_PER_POS = 32 * 8 * 128 * 2 * 2     # layers x kv heads x head_dim x (K,V) x fp16
+FFN_GATE_UP_BYTES = 2 * 14336 * 4096 // 256 * 144   # the dominant kernel: two Q4_K [14336 x 4096]
+# weights (elements) one decode step multiplies: 32 x 218,103,808 + 128256 x 4096
+L8B_WEIGHTS = 32 * (2 * 4096 * 4096 + 2 * 1024 * 4096 + 3 * 14336 * 4096) + 128256 * 4096
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", default=None,
+                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode"],
+                    help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
+                         "(a small case for ncu); prints per-launch times")
+    return ap.parse_args()
+
+
+def profile_kernel(args):
+    """Standalone launches of one hot kernel at its Llama-3-8B shape. Four
+    weight sets rotate so no launch finds its weights in L2."""
+    import torch
+    import vbs_b200 as vbs
+    torch.cuda.set_device(0)
+    if not vbs.ops().init():
+        raise SystemExit(vbs.last_error())
+    sc = vbs.synth_scale(0.02)
+    shapes = {"ffn_gate_up": (vbs.Q4_K, 14336, 4096), "down": (vbs.Q6_K, 4096, 14336),
+              "output": (vbs.Q6_K, 128256, 4096), "qkv_like": (vbs.Q4_K, 6144, 4096)}
+    st = torch.cuda.Stream()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    if args.profile == "decode":
+        # the full decode step: a 1-token prompt, then --steps graph replays
+        import models
+        model = vbs.synth_llama(models.shape_of(models.L8B), models.L8B_TYPES, seed=2024)
+        dec = vbs.Decoder(model, 64)
+        dec.forward([1], logits=False)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            dec.enqueue_steps(1)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": "decode", "kernels_per_step": dec.kernels_per_step, "steps": args.steps}))
+        dec.close()
+        return
+    if args.profile == "attention":
+        nqh, nkh, hd, ctx = 32, 8, 128, args.ctx
+        kc = [torch.randn((ctx, nkh * hd), device="cuda").half() for _ in range(4)]
+        vc = [torch.randn((ctx, nkh * hd), device="cuda").half() for _ in range(4)]
+        q = torch.randn(nqh * hd, device="cuda")
+        out = torch.empty(nqh * hd, device="cuda")
+        alg = 2 * ctx * nkh * hd * 2 + 2 * nqh * hd * 4
+
+        def launch(i):
+            vbs.attention(q.data_ptr(), kc[i % 4].data_ptr(), vc[i % 4].data_ptr(), out.data_ptr(), ctx, 0, ctx,
+                          nqh, nkh, hd, 0.0883883, stream=st.cuda_stream)
+    else:
+        t, rows, cols = shapes[args.profile]
+        nmat = 2 if args.profile == "ffn_gate_up" else 1
+        ws = []
+        for i in range(4 * nmat):
+            w = torch.empty(rows * vbs.row_bytes(t, cols), dtype=torch.uint8, device="cuda")
+            vbs.synth(t, w.data_ptr(), rows, cols, 100 + i, sc)
+            ws.append(w)
+        x = torch.randn(cols, device="cuda")
+        nw = torch.ones(cols, device="cuda")
+        y = torch.empty(rows, device="cuda")
+        alg = nmat * rows * vbs.row_bytes(t, cols) + cols * 4 + rows * 4
+
+        def launch(i):
+            if nmat == 2:
+                vbs.ffn_gate_up(t, ws[2 * (i % 4)].data_ptr(), ws[2 * (i % 4) + 1].data_ptr(), x.data_ptr(),
+                                nw.data_ptr(), 1e-5, y.data_ptr(), rows, cols, st.cuda_stream)
+            else:
+                vbs.matvec(t, ws[i % 4].data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, stream=st.cuda_stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(st):
+        for i in range(args.steps):
+            evs[2 * i].record(st)
+            launch(i)
+            evs[2 * i + 1].record(st)
+    torch.cuda.synchronize()
+    us = [evs[2 * i].elapsed_time(evs[2 * i + 1]) * 1e3 for i in range(args.steps)]
+    med = statistics.median(us[1:] if len(us) > 1 else us)
+    print(json.dumps({"profile": args.profile, "launch_us": [round(u, 2) for u in us], "median_us": round(med, 2),
+                      "algorithmic_bytes": alg, "gbs": round(alg / (med * 1e-6) / 1e9, 1)}), flush=True)
+
+
+def peaks():
+    try:
+        j = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx, self.rows, self.proc = gpu_index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's decode kernel on the host cores
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(n_tokens: float, threads: int):
+    """Time the reference CPU path's matvec work for n_tokens decode steps of
+    the 8B shape: vbs_cpu requantizes K-quants to Q8_0 at load
+    (src/vbs_cpu.c:312-346) and runs every projection through the hot-kernel
+    table's matvec_q8_0 (src/hotkernels/vbs_hot_ref_impl.h:49-64), >97% of
+    its per-token time. The kernel (the reference's own code from
+    oracle/_ref when built, else the oracle's bit-identical port) streams a
+    14336 x 4096 Q8_0 matrix in row shards, one shard per thread, as many
+    times as a token's 7.50 G weights require. Returns (tokens/s, kind)."""
+    import ctypes as C
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    R = orc.ref()
+    if R is not None:
+        fn, kind = R.ref_hot_matvec_q8_0, "reference"
+    else:
+        fn, kind = orc.lib().orc_cpu_matvec_q8_0, "port"
+    rows, cols = 14336, 4096
+    rng = np.random.default_rng(0)
+    w = rng.integers(-127, 128, size=(rows, cols // 32, 34), dtype=np.int16).astype(np.int8).view(np.uint8)
+    w[:, :, 0] = 0x00
+    w[:, :, 1] = 0x1C       # fp16 scale 2^-8
+    w = np.ascontiguousarray(w.reshape(-1))
+    xq = rng.integers(-127, 128, size=cols, dtype=np.int8)
+    qd = np.full(cols // 32, 0.01, np.float32)
+    y = np.empty(rows, np.float32)
+    weights_per_token = L8B_WEIGHTS
+    passes = max(1, round(n_tokens * weights_per_token / (rows * cols)))
+    shard = (rows + threads - 1) // threads
+    rb = cols // 32 * 34
+
+    def work(i):
+        r0 = i * shard
+        n = min(shard, rows - r0)
+        if n > 0:
+            fn(C.c_void_p(w.ctypes.data + r0 * rb), n, cols, orc.ptr(xq), orc.ptr(qd),
+               C.c_void_p(y.ctypes.data + r0 * 4))
+
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(work, range(threads)))          # warm-up pass
+        t0 = time.perf_counter()
+        for _ in range(passes):
+            list(ex.map(work, range(threads)))
+        dt = time.perf_counter() - t0
+    tokens = passes * rows * cols / weights_per_token
+    return tokens / dt, kind, passes
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_decode_sample(0.05, threads)
+    tok_s, kind, passes = cpu_decode_sample(max(1, args.steps) * 0.25, threads)
+    line = {
+        "impl": "reference", "metric": "decode tokens/s, Llama-3-8B Q4_K shape", "value": round(tok_s, 4),
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / tok_s, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
+        "config": {"workload": "llama3-8b-shape decode, reference CPU path (vbs_cpu hot kernel, Q8_0 requant)",
+                   "ctx": args.ctx, "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{passes} passes of matvec_q8_0 over a 14336x4096 Q8_0 matrix "
+                                   f"(= {args.steps * 0.25:g} tokens of 8B decode matvec work), row-sharded"},
+        "e2e": {"value": round(tok_s, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    if args.profile:
+        profile_kernel(args)
+        return
+
+    import numpy as np
+    import torch
+    import models
+    import vbs_b200 as vbs
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    if not vbs.ops().init():
+        raise SystemExit(f"backend init failed: {vbs.last_error()}")
+    if world > 1:
+        import ctypes as C
+        idb = (C.c_uint8 * 128)()
+        if rank == 0:
+            vbs.check(vbs.lib().vbs_cu_tp_unique_id(idb), "tp unique id")
+        obj = [bytes(idb)]
+        dist.broadcast_object_list(obj, src=0)
+        idb = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+        vbs.check(vbs.lib().vbs_cu_tp_init(rank, world, idb), "tp init")
+
+    shape = models.shape_of(models.L8B)
+    model = vbs.synth_llama(shape, models.L8B_TYPES, seed=2024, tp_rank=rank, tp_world=world)
+    torch.cuda.synchronize()
+    max_ctx = args.ctx + args.warmup + args.steps + args.e2e_steps + 8
+    dec = vbs.Decoder(model, max_ctx)
+    kps = dec.kernels_per_step
+    prompt = models.splitmix_ints(4096, args.ctx, shape.vocab)
+    t0 = time.perf_counter()
+    dec.forward(prompt, logits=False)                 # prefill, one token per step like the engine
+    prefill_s = time.perf_counter() - t0
+
+    stream = torch.cuda.ExternalStream(dec.stream)
+    dec.enqueue_steps(args.warmup)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = vbs.kernel_launches()
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        dec.enqueue_steps(args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = vbs.kernel_launches() - l0
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_step = ms / args.steps
+    tok_s = 1000.0 / ms_step
+    ctx_mid = args.ctx + args.warmup + args.steps / 2
+
+    # e2e: the reference-facing call (verum_forward's contract): host token
+    # array in pinned memory -> device, one step, logits -> host, per step.
+    tok_pinned = torch.empty(args.e2e_steps, dtype=torch.int32, pin_memory=True)
+    tok_pinned.copy_(torch.tensor(models.splitmix_ints(99, args.e2e_steps, shape.vocab), dtype=torch.int32))
+    logits_host = np.empty(shape.vocab, np.float32)
+    import ctypes as C
+    tp_ptr = C.cast(C.c_void_p(tok_pinned.data_ptr()), C.POINTER(C.c_uint32))
+    lp = logits_host.ctypes.data_as(C.POINTER(C.c_float))
+    dec.forward_into(tp_ptr, 1, lp)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(1, args.e2e_steps):
+        dec.forward_into(C.cast(C.c_void_p(tok_pinned.data_ptr() + 4 * i), C.POINTER(C.c_uint32)), 1, lp)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tok_s = (args.e2e_steps - 1) / e2e_s
+
+    # roofline of the dominant kernel: fused norm + gate/up + SiLU (two Q4_K
+    # [14336 x 4096] per layer, 66 MB), timed live over all 32 layers' weights
+    # (2.1 GB, so no launch finds its weights in L2)
+    peak, peak_kind = peaks()
+    roof = None
+    if world == 1:
+        x = torch.randn(shape.dim, device="cuda")
+        h = torch.empty(shape.ffn, device="cuda")
+        nrm = model.tensors["blk.0.ffn_norm"]
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            for l in range(2):
+                vbs.ffn_gate_up(vbs.Q4_K, model.tensors[f"blk.{l}.ffn_gate"].data_ptr(),
+                                model.tensors[f"blk.{l}.ffn_up"].data_ptr(), x.data_ptr(), nrm.data_ptr(), 1e-5,
+                                h.data_ptr(), shape.ffn, shape.dim, st.cuda_stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for l in range(shape.n_layers):
+                vbs.ffn_gate_up(vbs.Q4_K, model.tensors[f"blk.{l}.ffn_gate"].data_ptr(),
+                                model.tensors[f"blk.{l}.ffn_up"].data_ptr(), x.data_ptr(), nrm.data_ptr(), 1e-5,
+                                h.data_ptr(), shape.ffn, shape.dim, st.cuda_stream)
+            e1.record(st)
+        st.synchronize()
+        k_ms = e0.elapsed_time(e1) / shape.n_layers
+        alg = FFN_GATE_UP_BYTES + shape.dim * 4 + shape.ffn * 4
+        achieved = alg / (k_ms * 1e-3) / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / "ffn_gate_up_q4k_8b.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+        roof = {"bound": "hbm", "kernel": "mv_fast_kernel<Q4_K,dual,SILU> (norm+gate/up+SiLU)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": alg, "launch_us": round(k_ms * 1e3, 2),
+                "frac_of_8tbs": round(achieved / 8000.0, 4)}
+
+    step_bytes = L8B_WEIGHT_BYTES + KV_BYTES_PER_POS * ctx_mid
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, kind, passes = cpu_decode_sample(1.0, threads)
+        cpu = {"value": round(v, 4), "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{passes} passes of the vbs_cpu hot kernel matvec_q8_0 over a 14336x4096 Q8_0 matrix = "
+                         f"1 token of 8B decode matvec work (K-quants are requantized to Q8_0 by the reference CPU "
+                         f"path), row-sharded over {threads} threads"}
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s, Llama-3-8B Q4_K shape", "value": round(tok_s, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-mma/f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantized on device; seeded prompt ids)",
+            "config": {"workload": "llama3-8b-shape decode (32L, dim 4096, 32/8 heads, ffn 14336, vocab 128256; "
+                                   "Q4_K attn+gate/up, Q6_K down/output/embd)",
+                       "ctx": args.ctx, "batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (4.84 GB weights per step)",
+                       "kernels_per_step": kps, "prefill_s": round(prefill_s, 2)},
+            "step_bandwidth": {"algorithmic_bytes": int(step_bytes),
+                               "achieved_gbs": round(step_bytes * tok_s / 1e9, 1),
+                               "frac_of_measured": round(step_bytes * tok_s / 1e9 / peak, 4),
+                               "frac_of_8tbs": round(step_bytes * tok_s / 1e9 / 8000.0, 4)},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": shape.vocab * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if world > 1:
+        vbs.lib().vbs_cu_tp_finalize()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

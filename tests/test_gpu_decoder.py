@@ -1,0 +1,131 @@
+"""The decode program on a B200 through the C ABI.
+
+* Tiny model, strict mode: the 64 greedy tokens of the reference's CPU
+  path (vbs-cpu, golden fixture) exactly.
+* Tiny model, fast mode: logits step by step against the oracle with the
+  engine's semantics (exact dequant, double sums, fp16 KV cache), the path
+  the reference's GPU backends implement; teacher-forced so one near-tie
+  cannot end the comparison.
+* An 8B-width model (two Llama-3-8B layers, Q4_K/Q6_K, vocab cut to 4096)
+  against the same oracle.
+* Graph replay, plain launches and PDL give identical bits; the on-device
+  greedy loop equals the host-driven one.
+"""
+import numpy as np
+import pytest
+
+import models
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny_dev(gpu, vbs, tiny_gguf):
+    return vbs.upload_gguf(tiny_gguf)
+
+
+def test_tiny_strict_greedy_matches_reference(vbs, tiny_dev, tiny_golden, clean_errors):
+    dec = vbs.Decoder(tiny_dev, 128, vbs.DEC_STRICT)
+    toks = dec.generate(tiny_golden["prompt"], 64)
+    assert toks == tiny_golden["generated"]
+    dec.close()
+
+
+def test_tiny_strict_final_logits(vbs, tiny_dev, tiny_golden, clean_errors):
+    dec = vbs.Decoder(tiny_dev, 128, vbs.DEC_STRICT)
+    lg = dec.forward(list(tiny_golden["prompt"]) + list(tiny_golden["generated"][:-1]))
+    want = np.array(tiny_golden["final_logits"], np.float32)
+    # only expf/powf/sinf/cosf differ (CUDA's vs glibc's, <= 2 ulp)
+    assert np.abs(lg - want).max() <= 1e-5 * np.abs(want).max()
+    dec.close()
+
+
+def _teacher_forced(dec, state, tokens, tol):
+    worst = 0.0
+    for t in tokens:
+        got = dec.forward([t])
+        want = state.step(t)
+        err = np.abs(got - want).max() / np.abs(want).max()
+        worst = max(worst, err)
+        assert err <= tol, f"step {t}: rel err {err}"
+    return worst
+
+
+def test_tiny_fast_vs_engine_oracle(vbs, orc, tiny_dev, tiny_gguf, tiny_golden, clean_errors):
+    hm = orc.load_gguf_host(tiny_gguf)
+    st = orc.OrcState(hm, 128, 1)
+    dec = vbs.Decoder(tiny_dev, 128)
+    toks = list(tiny_golden["prompt"]) + list(tiny_golden["generated"][:24])
+    _teacher_forced(dec, st, toks, 1e-3)
+    dec.close()
+
+
+@pytest.fixture(scope="module")
+def l8b_2layer(gpu, vbs):
+    cfg = dict(models.L8B, n_layers=2, vocab=4096)
+    return cfg, vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=99)
+
+
+def test_8b_width_vs_engine_oracle(vbs, orc, l8b_2layer, clean_errors):
+    cfg, dm = l8b_2layer
+    host = {}
+    for name, t in dm.tensors.items():
+        arr = t.cpu().numpy()
+        if name.endswith("norm"):
+            host[name] = (orc.F32, 1, cfg["dim"], arr)
+        else:
+            base = name.split(".")[-1]
+            rows, cols, *_ = models.vbs.shard_spec(name, dm.shape, 0, 1)
+            host[name] = (dm.types[base], rows, cols, arr[:rows * orc.row_bytes(dm.types[base], cols)])
+    hm = orc.HostModel(cfg, host)
+    st = orc.OrcState(hm, 64, 1)
+    dec = vbs.Decoder(dm, 64)
+    _teacher_forced(dec, st, [17, 2044, 5, 4000], 2e-3)
+    dec.close()
+
+
+def test_graph_pdl_plain_identical(vbs, l8b_2layer, clean_errors):
+    _, dm = l8b_2layer
+    toks = [1, 2, 3, 4, 5, 6]
+    outs = []
+    for flags in (0, vbs.DEC_NO_PDL, vbs.DEC_NO_GRAPH, vbs.DEC_NO_GRAPH | vbs.DEC_NO_PDL):
+        dec = vbs.Decoder(dm, 32, flags)
+        outs.append(dec.forward(toks))
+        dec.close()
+    for o in outs[1:]:
+        assert (o.view(np.uint32) == outs[0].view(np.uint32)).all()
+
+
+def test_device_greedy_loop_equals_host_loop(vbs, l8b_2layer, clean_errors):
+    _, dm = l8b_2layer
+    dec = vbs.Decoder(dm, 64)
+    dev_toks = dec.generate([11, 12, 13], 20)
+    dec2 = vbs.Decoder(dm, 64)
+    lg = dec2.forward([11, 12, 13])
+    host_toks = []
+    for i in range(20):
+        t = int(np.argmax(lg))
+        host_toks.append(t)
+        if i + 1 < 20:
+            lg = dec2.forward([t])
+    assert dev_toks == host_toks
+    dec.close()
+    dec2.close()
+
+
+def test_context_capacity_is_enforced(vbs, tiny_dev, clean_errors):
+    dec = vbs.Decoder(tiny_dev, 8)
+    dec.forward([1] * 8, logits=False)
+    with pytest.raises(vbs.VbsError):
+        dec.forward([1])
+    vbs.clear_error()
+    dec.reset()
+    assert dec.forward([1, 2]).shape == (512,)
+    dec.close()
+
+
+def test_out_of_range_token_rejected(vbs, tiny_dev, clean_errors):
+    dec = vbs.Decoder(tiny_dev, 8)
+    with pytest.raises(vbs.VbsError):
+        dec.forward([512])
+    dec.close()

@@ -92,6 +92,7 @@ static bool do_init() {
         s.n_sm = pr.multiProcessorCount;
         if (cudaMalloc(&s.err, 256) != cudaSuccess) continue;
         cudaMemset(s.err, 0, 256);
+        if (mv_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
         vbs_device_t &d = g_devices[g_ndev];
         memset(&d, 0, sizeof(d));
         snprintf(d.name, sizeof(d.name), "%s", pr.name);
@@ -402,7 +403,7 @@ static bool ops_dispatch_primitive(vbs_device_t *dev, void *pipeline, const vbs_
             void *w, *o;
             uint32_t tok, dim;
             ok = n == 4 && arg_ptr(&args[0], &w) && arg_u32(&args[1], &tok) && arg_ptr(&args[2], &o) && arg_u32(&args[3], &dim);
-            if (ok) e = embed_launch(np->type, static_cast<const uint8_t *>(w), nullptr, tok, static_cast<float *>(o), dim, 0, false);
+            if (ok) e = embed_launch(np->type, static_cast<const uint8_t *>(w), nullptr, tok, 0xFFFFFFFFu, static_cast<float *>(o), dim, d->err, 0, false);
             break;
         }
         case VBS_OP_NORMALIZE: {   // B in, B w, B out, S dim, S eps

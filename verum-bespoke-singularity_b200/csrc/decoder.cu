@@ -73,7 +73,7 @@ struct vbs_cu_decoder {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     uint32_t kernels_per_step = 0;
-    bool resid_in_x2 = false;        // TP ping-pong: where the residual of the next step lives
+    uint64_t host_pos = 0;           // host shadow of ctrl[0] (steps enqueued since the last reset)
 };
 
 namespace {
@@ -126,7 +126,7 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
     // prologue, xw where the summed residual is written
     float *xr = d->x, *xw = d->x2;
 
-    if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->x, dim, st, d->use_pdl),
+    if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->vocab_full, d->x, dim, d->dev->err, st, d->use_pdl),
                  "decode embed"))
         return false;
     const float *pending = nullptr;   // TP: partial sum to add into the residual
@@ -246,7 +246,7 @@ bool enqueue_strict_step(vbs_cu_decoder *d) {
         if (!quantized && !cuda_ok(strict_quantize_q8_launch(x, cols, d->xq, d->qd, st), "strict quantize")) return false;
         return cuda_ok(strict_matvec_q8_0_launch(w, rows, cols, d->xq, d->qd, y, 0, st), "strict matvec");
     };
-    if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->x, dim, st, false), "strict embed"))
+    if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->vocab_full, d->x, dim, d->dev->err, st, false), "strict embed"))
         return false;
     for (uint32_t l = 0; l < m.n_layers; ++l) {
         const Layer &ly = d->L[l];
@@ -279,6 +279,11 @@ bool enqueue_step_raw(vbs_cu_decoder *d) { return d->strict ? enqueue_strict_ste
 
 // One step: graph replay when available, else direct launches.
 bool enqueue_step(vbs_cu_decoder *d) {
+    if (d->host_pos >= d->max_ctx) {
+        latch_error("decode step at position %llu exceeds the KV capacity %u", (unsigned long long)d->host_pos, d->max_ctx);
+        return false;
+    }
+    d->host_pos++;
     if (d->exec) {
         note_launches(d->kernels_per_step);
         return cuda_ok(cudaGraphLaunch(d->exec, d->st), "decode graph launch");
@@ -421,6 +426,9 @@ int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n
     int cur = -1;
     cudaGetDevice(&cur);
     if (cur != d->dev->ordinal) cudaSetDevice(d->dev->ordinal);
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] >= d->vocab_full) { latch_error("decoder_forward: token %u >= vocab %u", tokens[i], d->vocab_full); return -1; }
+    if (d->host_pos + n > d->max_ctx) { latch_error("decoder_forward: %zu tokens exceed the KV capacity", n); return -1; }
     if (n) {
         if (!put_tokens(d, tokens, n)) return -1;
         for (size_t i = 0; i < n; ++i) {
@@ -442,6 +450,7 @@ void vbs_cu_decoder_reset(vbs_cu_decoder_t *d) {
     if (!d) return;
     cudaMemsetAsync(d->ctrl, 0, 4, d->st);
     cudaStreamSynchronize(d->st);
+    d->host_pos = 0;
 }
 
 int vbs_cu_decoder_set_position(vbs_cu_decoder_t *d, uint32_t pos, uint32_t token) {
@@ -449,6 +458,7 @@ int vbs_cu_decoder_set_position(vbs_cu_decoder_t *d, uint32_t pos, uint32_t toke
     d->pinned[0] = pos;
     d->pinned[1] = token;
     if (!cuda_ok(cudaMemcpyAsync(d->ctrl, d->pinned, 8, cudaMemcpyHostToDevice, d->st), "set position")) return -1;
+    d->host_pos = pos;
     return cuda_ok(cudaStreamSynchronize(d->st), "set position") ? 0 : -1;
 }
 
@@ -461,8 +471,13 @@ uint32_t vbs_cu_decoder_position(vbs_cu_decoder_t *d) {
 
 int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t n_prompt, uint32_t n_new, uint32_t *out) {
     if (!d || !prompt || !n_prompt || (n_new && !out)) { latch_error("decoder_generate: invalid arguments"); return -1; }
-    if (n_prompt + (n_new ? n_new - 1 : 0) > d->max_ctx) { latch_error("decoder_generate: exceeds context capacity"); return -1; }
-    const uint32_t start = vbs_cu_decoder_position(d);
+    for (size_t i = 0; i < n_prompt; ++i)
+        if (prompt[i] >= d->vocab_full) { latch_error("decoder_generate: token %u >= vocab", prompt[i]); return -1; }
+    if (d->host_pos + n_prompt + (n_new ? n_new - 1 : 0) > d->max_ctx) {
+        latch_error("decoder_generate: exceeds context capacity");
+        return -1;
+    }
+    const uint32_t start = (uint32_t)d->host_pos;
     if (vbs_cu_decoder_forward(d, prompt, n_prompt, nullptr)) return -1;
     for (uint32_t i = 1; i < n_new; ++i)
         if (!enqueue_step(d)) return -1;
@@ -475,6 +490,7 @@ int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t 
 
 int vbs_cu_decoder_enqueue_steps(vbs_cu_decoder_t *d, uint32_t n) {
     if (!d) return -1;
+    if (d->host_pos + n > d->max_ctx) { latch_error("enqueue_steps: exceeds the KV capacity"); return -1; }
     for (uint32_t i = 0; i < n; ++i)
         if (!enqueue_step(d)) return -1;
     return 0;

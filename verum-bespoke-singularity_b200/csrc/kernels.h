@@ -45,6 +45,10 @@ bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const
                        const void *x, int dual);
 cudaError_t mv_fast_launch(int type, int dual, int epi, const MvParams &p, int n_sm, cudaStream_t st,
                            bool pdl, int grid_override);
+// Raise the dynamic shared-memory limit of every fast-kernel instance on the
+// current device (done once per device at initialisation, never during
+// stream capture).
+cudaError_t mv_configure();
 
 // Portable exact-dequant fp32 kernel (any type, any alignment, batched).
 cudaError_t mv_generic_launch(int type, const uint8_t *w, const float *x, float *y, uint32_t rows,
@@ -55,8 +59,10 @@ cudaError_t dequant_launch(int type, const uint8_t *w, float *out, uint64_t n_el
 
 // ---- primitives (host_math semantics, src/vbs_host_math.h) -----------------
 
-cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, uint32_t token, float *out,
-                         uint32_t dim, cudaStream_t st, bool pdl);
+// Token from token_dev when non-NULL; a token >= rows flags DERR_BAD_ARG
+// and writes zeros.
+cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, uint32_t token, uint32_t rows,
+                         float *out, uint32_t dim, uint32_t *err, cudaStream_t st, bool pdl);
 cudaError_t rmsnorm_launch(const float *in, const float *w, float *out, uint32_t n, float eps, cudaStream_t st);
 // rope/cache store take the position from ctrl[0] when ctrl != NULL.
 cudaError_t rope_launch(float *x, uint32_t pos, const uint32_t *ctrl, uint32_t head_dim, uint32_t n_heads, float theta,

@@ -303,6 +303,10 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, boo
         const float other = __shfl_xor_sync(0x0000FFFFu, va, 1);
         if (!valid) return;
         const uint32_t pos = p.ctrl[0];
+        if (pos >= p.max_ctx) {   // position past the KV capacity: report, never write out of bounds
+            dev_flag_error(p.err, DERR_BAD_ARG);
+            return;
+        }
         const uint64_t kvbase = ((uint64_t)p.layer * p.max_ctx + pos) * p.kv_dim;
         if (row >= p.seg_end[1]) {
             p.vc[kvbase + (row - p.seg_end[1])] = f32_to_f16_kv(va);
@@ -524,12 +528,6 @@ static cudaError_t mv_fast_go(const MvParams &p0, int n_sm, cudaStream_t st, boo
     p.nstage = mv_nstage<TYPE>(DUAL);
     const uint32_t smem = mv_smem_bytes<TYPE>(p.cols, DUAL, p.nstage);
     auto kern = mv_fast_kernel<TYPE, DUAL, EPI>;
-    static int configured_smem = 0;   // per instantiation
-    if ((int)smem > configured_smem) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        configured_smem = 227 * 1024;
-    }
     uint32_t grid = grid_override > 0 ? (uint32_t)grid_override
                                       : std::max(1u, std::min((uint32_t)n_sm, (p.rows + 1) / 2));
     cudaLaunchConfig_t cfg = {};
@@ -544,6 +542,20 @@ static cudaError_t mv_fast_go(const MvParams &p0, int n_sm, cudaStream_t st, boo
     cfg.numAttrs = pdl ? 1 : 0;
     note_launches(1);
     return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int TYPE, int DUAL, int EPI> static cudaError_t mv_set_attr() {
+    return cudaFuncSetAttribute(mv_fast_kernel<TYPE, DUAL, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+cudaError_t mv_configure() {
+    const cudaError_t es[] = {
+        mv_set_attr<T_Q4_K, 0, MV_EPI_STORE>(), mv_set_attr<T_Q4_K, 0, MV_EPI_QKV>(), mv_set_attr<T_Q4_K, 1, MV_EPI_SILU>(),
+        mv_set_attr<T_Q6_K, 0, MV_EPI_STORE>(), mv_set_attr<T_Q6_K, 0, MV_EPI_QKV>(), mv_set_attr<T_Q6_K, 1, MV_EPI_SILU>(),
+        mv_set_attr<T_Q8_0, 0, MV_EPI_STORE>(), mv_set_attr<T_Q8_0, 0, MV_EPI_QKV>(), mv_set_attr<T_Q8_0, 1, MV_EPI_SILU>()};
+    for (cudaError_t e : es)
+        if (e != cudaSuccess) return e;
+    return cudaSuccess;
 }
 
 template <int TYPE>

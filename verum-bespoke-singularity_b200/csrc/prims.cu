@@ -14,9 +14,15 @@ namespace vbs {
 // embedding: out[e] = dequant(row token)[e], exact
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(int type, const uint8_t *__restrict__ w, const uint32_t *token_dev, uint32_t token,
-                             float *__restrict__ out, uint32_t dim) {
+                             uint32_t rows, float *__restrict__ out, uint32_t dim, uint32_t *err) {
     pdl_wait();
     const uint32_t tok = token_dev ? *token_dev : token;
+    if (tok >= rows) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(err, DERR_BAD_ARG);
+        for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x) out[e] = 0.0f;
+        pdl_launch_dependents();
+        return;
+    }
     const int E = block_elems(type), BB = block_bytes(type);
     const uint8_t *row = w + (uint64_t)tok * row_bytes(type, dim);
     for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x)
@@ -24,8 +30,8 @@ __global__ void embed_kernel(int type, const uint8_t *__restrict__ w, const uint
     pdl_launch_dependents();
 }
 
-cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, uint32_t token, float *out,
-                         uint32_t dim, cudaStream_t st, bool pdl) {
+cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, uint32_t token, uint32_t rows,
+                         float *out, uint32_t dim, uint32_t *err, cudaStream_t st, bool pdl) {
     if (!block_elems(type) || dim % block_elems(type)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::max(1u, std::min(64u, (dim + 255) / 256)));
@@ -37,7 +43,7 @@ cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, 
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     note_launches(1);
-    return cudaLaunchKernelEx(&cfg, embed_kernel, type, w, token_dev, token, out, dim);
+    return cudaLaunchKernelEx(&cfg, embed_kernel, type, w, token_dev, token, rows, out, dim, err);
 }
 
 // ---------------------------------------------------------------------------
@@ -106,6 +112,7 @@ __global__ void add_kernel(const float *a, const float *b, float *o, uint32_t n)
 }
 __global__ void cache_store_kernel(const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint64_t base_arg,
                                    const uint32_t *ctrl, uint32_t layer, uint32_t max_ctx, uint32_t kv_dim) {
+    if (ctrl && ctrl[0] >= max_ctx) return;   // past the KV capacity (attention reports it)
     const uint64_t base = ctrl ? ((uint64_t)layer * max_ctx + ctrl[0]) * kv_dim : base_arg;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < kv_dim; i += gridDim.x * blockDim.x) {
         kc[base + i] = f32_to_f16_kv(k[i]);
@@ -148,6 +155,8 @@ cudaError_t cache_store_launch(const float *k, const float *v, uint16_t *kc, uin
 // (atomic ticket) merges the splits in split order and resets the ticket.
 // ---------------------------------------------------------------------------
 constexpr int AT_NW = 4;   // warps per CTA
+constexpr size_t ATTN_TICKET_BYTES = 64 * 1024;        // one ticket per (sequence, kv head)
+constexpr uint32_t ATTN_MAX_SLOTS = ATTN_TICKET_BYTES / 4;
 
 template <int HD, int DPL, int GMAX>
 __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, uint32_t n_splits) {
@@ -159,7 +168,11 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
     const uint32_t G = p.nqh / p.nkh;
 
     pdl_wait();
-    const uint32_t seq = p.seq_dev ? (*p.seq_dev + 1u) : p.seq_len;
+    uint32_t seq = p.seq_dev ? (*p.seq_dev + 1u) : p.seq_len;
+    if (seq > p.max_ctx) {   // never read past the cache; report instead
+        if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) dev_flag_error(p.err, DERR_BAD_ARG);
+        seq = p.max_ctx;
+    }
     const uint32_t per = (seq + n_splits - 1) / n_splits;
     const uint32_t t0 = split * per, t1 = min(seq, t0 + per);
 
@@ -254,7 +267,10 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
     }
     __syncthreads();
     // thread layout for the final stages: one thread per (g, d)
-    float *work = reinterpret_cast<float *>(p.work);
+    // workspace: merge tickets first (fixed place, left at zero by every
+    // launch), then the split partials
+    uint32_t *counters = reinterpret_cast<uint32_t *>(p.work);
+    float *work = reinterpret_cast<float *>(static_cast<char *>(p.work) + ATTN_TICKET_BYTES);
     const uint32_t slot = bq * p.nkh + kvh;
     const size_t part_stride = (size_t)GMAX * (2 + HD);
     float *mypart = work + ((size_t)slot * n_splits + split) * part_stride;
@@ -279,7 +295,6 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
     __threadfence();
     __syncthreads();
     __shared__ uint32_t ticket;
-    uint32_t *counters = reinterpret_cast<uint32_t *>(work + (size_t)p.batch * p.nkh * n_splits * part_stride);
     if (threadIdx.x == 0) ticket = atomicAdd(&counters[slot], 1u);
     __syncthreads();
     if (ticket != n_splits - 1) { pdl_launch_dependents(); return; }
@@ -306,7 +321,7 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
 size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t batch, uint32_t max_splits) {
     (void)nqh;
     const size_t gmax = 8;
-    return ((size_t)batch * nkh * max_splits * gmax * (2 + hd)) * sizeof(float) + (size_t)batch * nkh * sizeof(uint32_t) + 256;
+    return ATTN_TICKET_BYTES + ((size_t)batch * nkh * max_splits * gmax * (2 + hd)) * sizeof(float);
 }
 
 uint32_t attn_num_splits(uint32_t seq_len_hint, uint32_t nkh, uint32_t batch, int n_sm) {
@@ -333,6 +348,7 @@ static cudaError_t attn_go(const AttnParams &p, uint32_t n_splits, cudaStream_t 
 
 cudaError_t attn_launch(const AttnParams &p, uint32_t n_splits, cudaStream_t st, bool pdl) {
     if (!p.nkh || !p.nqh || p.nqh % p.nkh || p.nqh / p.nkh > 8 || !p.batch) return cudaErrorInvalidValue;
+    if ((uint64_t)p.batch * p.nkh > ATTN_MAX_SLOTS) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(p.kc) | reinterpret_cast<uintptr_t>(p.vc)) & 15) return cudaErrorInvalidValue;
     const uint32_t G = p.nqh / p.nkh;
     switch (p.hd) {

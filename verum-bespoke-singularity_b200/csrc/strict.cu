@@ -152,6 +152,10 @@ __global__ void strict_attention_kernel(const float *q, const float *k, const fl
                                         float *out, const uint32_t *ctrl, uint32_t layer, uint32_t context, uint32_t nqh,
                                         uint32_t nkh, uint32_t hd, float *scores_all, uint32_t *err) {
     const uint32_t h = blockIdx.x, pos = ctrl[0], kvd = nkh * hd;
+    if (pos >= context) {
+        if (h == 0 && threadIdx.x == 0) dev_flag_error(err, DERR_BAD_ARG);
+        return;
+    }
     const uint32_t groups = nqh / nkh, kh = h / groups;
     float *scores = scores_all + (size_t)h * context;
     const size_t here = ((size_t)layer * context + pos) * kvd + (size_t)kh * hd;
