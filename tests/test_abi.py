@@ -53,11 +53,11 @@ def test_init_without_gpu_reports_reason(vbs):
 
 def test_version_names_blackwell_features(vbs):
     v = vbs.lib().vbs_cu_version().decode()
-    for feat in ("sm_100a", "cp.async.bulk", "mbarrier"):
+    for feat in ("sm_100a", "cp.async", "mma.m16n8k32"):
         assert feat in v
 
 
-def test_sources_use_tma_and_no_multicast():
+def test_sources_no_multicast_loads():
     src = "".join(p.read_text() for p in (ROOT / "verum-bespoke-singularity_b200" / "csrc").glob("*.cu*"))
-    assert "cp.async.bulk" in src
+    assert "mma.sync.aligned.m16n8k32" in src and "cp.async.cg" in src
     assert "multicast::cluster" not in src

@@ -16,7 +16,7 @@
 //  * the first failure is latched: dispatch errors the bridge drops
 //    (src/vbs_specializer_bridge.c:83-90) make the next copy_to_host fail
 //    and print the message.
-#include "../../include/vbs_b200.h"
+#include "vbs_b200.h"
 #include "backend.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -514,7 +514,7 @@ void vbs_cu_clear_error(void) {
     cudaGetLastError();
 }
 
-const char *vbs_cu_version(void) { return "vbs_b200 0.1 sm_100a cp.async.bulk mbarrier mma.m16n8k32.s8 griddepcontrol cuda-graph"; }
+const char *vbs_cu_version(void) { return "vbs_b200 0.2 sm_100a cp.async mma.m16n8k32.s8 griddepcontrol cuda-graph nccl"; }
 
 uint64_t vbs_cu_kernel_launches(void) { return g_launches.load(); }
 

@@ -24,7 +24,7 @@
 // Tensor parallelism: o_proj and down produce partial sums that are
 // all-reduced (NCCL) and added into the residual by the next kernel's
 // prologue; the output rows are sharded and all-gathered before the argmax.
-#include "../../include/vbs_b200.h"
+#include "vbs_b200.h"
 #include "backend.h"
 #include "common.cuh"
 #include "kernels.h"

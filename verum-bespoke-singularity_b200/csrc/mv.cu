@@ -5,25 +5,24 @@
 // in GGUF blocks (Q8_0 34 B / 32, Q4_K 144 B / 256, Q6_K 210 B / 256).
 //
 // Fast kernel (mv_fast_kernel), B200 design:
-//  * One CTA per SM slice of rows. A producer warp streams the CTA's rows in
-//    stages of 16 rows x 1024 columns from HBM into shared memory with 1-D
-//    bulk copies (cp.async.bulk, the TMA engine; no tensor map, no
-//    multicast), completing on mbarriers; the 16-byte-unaligned head and
-//    tail of a row segment (Q6_K and Q8_0 rows are only 2-byte aligned)
-//    are copied by the producer lanes with plain loads.
+//  * One CTA per SM, a balanced slice of rows each. Every warp streams its
+//    own work units (16 rows x one 256-column super-block) from HBM into a
+//    private ring of shared-memory buffers with 16-byte cp.async copies,
+//    several units in flight per warp. (1-D bulk TMA copies of the same row
+//    segments, one per row, were measured here to cap at ~11 GB/s per SM even
+//    with no compute at all; 2-D tensor maps cannot describe Q6_K's 210-byte
+//    blocks, whose rows are only 2-byte aligned.)
 //  * x is quantized once per CTA into shared memory as two int8 levels per
 //    32-element block: x ~= d2 * (254*q1 + q2), |error| <= amax/64516/2
 //    (1.6e-5 of the block maximum). Weights stay in their packed form; the
-//    int8 tensor-core MMA (m16n8k32, u8 x s8 -> s32) forms the exact
-//    integer block dots, one MMA per 16 rows x 32 columns, so the per-weight
-//    instruction cost is a mask and a fraction of an MMA. Block scales are
-//    applied to the integer dots in fp32.
+//    int8 tensor-core MMA (m16n8k32, u8 x s8 -> s32) forms exact integer
+//    block dots with a block-diagonal B operand (see mv_unit), and the block
+//    scales are applied to the integer dots in fp32.
 //  * Epilogues fuse what follows the matvec in the decode step: residual
 //    add (accumulate), SiLU(gate)*up for the paired gate/up matrices, and
 //    RoPE + fp16 KV-cache store for the fused Q/K/V projection.
-//  * Programmatic dependent launch: the producer starts streaming weights
-//    before griddepcontrol.wait; only the x prologue waits for the previous
-//    kernel.
+//  * Programmatic dependent launch: weight copies start before
+//    griddepcontrol.wait; only the x prologue waits for the previous kernel.
 //
 // Portable kernel (mv_generic_kernel): one warp per row, exact element
 // dequantization (same float operation order as src/vbs_dequant.c), fp32
@@ -38,23 +37,40 @@ namespace vbs {
 
 constexpr int MV_NCW = 8;                       // consumer warps
 constexpr int MV_THREADS = (MV_NCW + 1) * 32;   // + one producer warp
-constexpr uint32_t MV_CK = 1024;                // columns per stage (8 units of 128)
 constexpr uint32_t MV_MAXST = 16;               // barrier slots
 constexpr uint32_t MV_HDR = 2560;               // barriers, misc, reduction scratch
-constexpr uint32_t MV_STAGE_BUDGET = 80 * 1024; // bytes of stages per CTA
+constexpr uint32_t MV_SMEM = 227u * 1024u;      // shared memory per CTA (one CTA per SM)
 
+// A stage holds 16 rows (dual: 16 rows of each matrix) x a chunk of CK
+// columns, each row one contiguous bulk copy into a padded slot. CK is the
+// whole row when 16 rows of it fit, else the largest multiple of 256 columns
+// (>= 1024) that keeps NSTAGE >= 3: HBM serves long contiguous row runs
+// several times faster than the short scattered segments a 16 x 256 column
+// unit would read.
 template <int TYPE> struct MvT;
-// Row slot stride: > chunk bytes + 2 x 15 alignment bytes, 16-byte multiple,
-// stride/4 == 28 mod 32 so 8 rows x 4 lanes hit 32 distinct banks, and an
-// odd number of 16-byte units for conflict-free ldmatrix.
-template <> struct MvT<T_Q4_K> { static constexpr int E = 256, BB = 144, RS = 624; };
-template <> struct MvT<T_Q6_K> { static constexpr int E = 256, BB = 210, RS = 880; };
-template <> struct MvT<T_Q8_0> { static constexpr int E = 32, BB = 34, RS = 1136; };
+template <> struct MvT<T_Q4_K> { static constexpr int E = 256, BB = 144; };
+template <> struct MvT<T_Q6_K> { static constexpr int E = 256, BB = 210; };
+template <> struct MvT<T_Q8_0> { static constexpr int E = 32, BB = 34; };
+
+struct MvGeom {
+    uint32_t ck;       // columns per chunk (multiple of 256, or all columns)
+    uint32_t rs;       // row slot stride in bytes
+    uint32_t nstage;   // stages in the ring
+    uint32_t stage0;   // byte offset of the first stage
+};
 
 __device__ __forceinline__ const uint8_t *seg_row_ptr(const MvParams &p, uint32_t row) {
     if (row < p.seg_end[0]) return p.w[0] + (uint64_t)row * p.rb;
     if (row < p.seg_end[1]) return p.w[1] + (uint64_t)(row - p.seg_end[0]) * p.rb;
     return p.w[2] + (uint64_t)(row - p.seg_end[1]) * p.rb;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void sts_u8(uint32_t addr, uint8_t v) {
@@ -73,20 +89,27 @@ __device__ __forceinline__ int lds_s8(uint32_t addr) {
 
 // ---------------------------------------------------------------------------
 // x prologue: optional residual add and RMSNorm, then two-level int8
-// quantization into the MMA B-fragment layout.
-//   xq[J*64 + s*8 .. +8]: slot s<4: q1 bytes k=4s..4s+3 and k=16+4s..+3;
-//                         slot 4+s: the same for q2.
-//   xf[J] = {d2, d2 * sum(254 q1 + q2), sum_k<16, sum_k>=16} (floats/ints)
+// quantization: x ~= d2 * (254*q1 + q2) per 32-element block. Four threads
+// share a block (8 elements each).
+// Layouts per block J (64 bytes):
+//   slot layout (Q4_K, Q8_0): 8 slots of 8 bytes; slot s<4 = {q1 word s,
+//     q1 word 4+s}, slot 4+s the same for q2 (word w = elements 4w..4w+3);
+//   plain layout (Q6_K): q1 words 0..7 then q2 words 0..7.
+//   xf[J] = {d2, d2 * sum(254 q1 + q2), sum over k<16, sum over k>=16}.
 // ---------------------------------------------------------------------------
+template <bool PLAIN>
 __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *misc, int ctid) {
     const uint32_t nsub = p.cols / 32;
     float scale = 1.0f;
     if (p.norm_w) {
         float ss = 0.0f;
-        for (uint32_t i = ctid; i < p.cols; i += MV_NCW * 32) {
-            float v = p.x[i];
-            if (p.x_add) v += p.x_add[i];
-            ss = fmaf(v, v, ss);
+        for (uint32_t i = ctid * 4; i < p.cols; i += MV_NCW * 32 * 4) {
+            float4 v = *reinterpret_cast<const float4 *>(p.x + i);
+            if (p.x_add) {
+                const float4 a = *reinterpret_cast<const float4 *>(p.x_add + i);
+                v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
+            }
+            ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
         }
         ss = warp_sum(ss);
         if ((ctid & 31) == 0) misc[8 + (ctid >> 5)] = ss;
@@ -97,201 +120,240 @@ __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *m
         scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
     }
     const bool write_x = p.x_add && p.x_write && blockIdx.x == 0;
-    for (uint32_t J = ctid; J < nsub; J += MV_NCW * 32) {
-        float v[32];
-        const float4 *x4 = reinterpret_cast<const float4 *>(p.x + (size_t)J * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            float4 t = x4[i];
-            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
-        }
+    const uint32_t u = ctid & 3;                                   // quarter of the block
+    const uint32_t qmask = 0xFu << ((ctid & 31) & ~3u);            // the four lanes of this block
+    for (uint32_t J = ctid >> 2; J < nsub; J += MV_NCW * 32 / 4) {
+        const size_t e = (size_t)J * 32 + 8 * u;
+        float v[8];
+        float4 t0 = *reinterpret_cast<const float4 *>(p.x + e), t1 = *reinterpret_cast<const float4 *>(p.x + e + 4);
+        v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w; v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
         if (p.x_add) {
-            const float4 *a4 = reinterpret_cast<const float4 *>(p.x_add + (size_t)J * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float4 t = a4[i];
-                v[4 * i] += t.x; v[4 * i + 1] += t.y; v[4 * i + 2] += t.z; v[4 * i + 3] += t.w;
-            }
+            t0 = *reinterpret_cast<const float4 *>(p.x_add + e);
+            t1 = *reinterpret_cast<const float4 *>(p.x_add + e + 4);
+            v[0] += t0.x; v[1] += t0.y; v[2] += t0.z; v[3] += t0.w; v[4] += t1.x; v[5] += t1.y; v[6] += t1.z; v[7] += t1.w;
             if (write_x) {
-                float4 *o4 = reinterpret_cast<float4 *>(p.x_write + (size_t)J * 32);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                *reinterpret_cast<float4 *>(p.x_write + e) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4 *>(p.x_write + e + 4) = make_float4(v[4], v[5], v[6], v[7]);
             }
         }
         if (p.norm_w) {
-            const float4 *w4 = reinterpret_cast<const float4 *>(p.norm_w + (size_t)J * 32);
+            t0 = *reinterpret_cast<const float4 *>(p.norm_w + e);
+            t1 = *reinterpret_cast<const float4 *>(p.norm_w + e + 4);
+            const float w8[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float4 t = w4[i];
-                v[4 * i] = v[4 * i] * scale * t.x; v[4 * i + 1] = v[4 * i + 1] * scale * t.y;
-                v[4 * i + 2] = v[4 * i + 2] * scale * t.z; v[4 * i + 3] = v[4 * i + 3] * scale * t.w;
-            }
+            for (int i = 0; i < 8; ++i) v[i] = v[i] * scale * w8[i];
         }
         float amax = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const float d2 = amax / (127.0f * 254.0f);
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
+        const float d2 = amax * (1.0f / (127.0f * 254.0f));
         const float d1 = d2 * 254.0f;
-        const float r1 = d1 > 0.0f ? 1.0f / d1 : 0.0f, r2 = d2 > 0.0f ? 1.0f / d2 : 0.0f;
-        uint32_t q1w[8], q2w[8];
-        int s_lo = 0, s_hi = 0;
+        const float r1 = d1 > 0.0f ? __frcp_rn(d1) : 0.0f, r2 = d2 > 0.0f ? __frcp_rn(d2) : 0.0f;
+        uint32_t q1w[2] = {0u, 0u}, q2w[2] = {0u, 0u};
+        int sum = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) { q1w[i] = 0; q2w[i] = 0; }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 8; ++i) {
             int a = __float2int_rn(v[i] * r1);
             a = max(-127, min(127, a));
-            float res = fmaf(-(float)a, d1, v[i]);
+            const float res = fmaf(-(float)a, d1, v[i]);
             int b = __float2int_rn(res * r2);
             b = max(-127, min(127, b));
             q1w[i >> 2] |= (uint32_t)(a & 0xFF) << (8 * (i & 3));
             q2w[i >> 2] |= (uint32_t)(b & 0xFF) << (8 * (i & 3));
-            if (i < 16) s_lo += 254 * a + b; else s_hi += 254 * a + b;
+            sum += 254 * a + b;
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(xq + (size_t)J * 64);
-        // slots s=0..3: {q1 word s, q1 word 4+s}; slots 4..7 the same for q2
-        dst[0] = make_uint4(q1w[0], q1w[4], q1w[1], q1w[5]);
-        dst[1] = make_uint4(q1w[2], q1w[6], q1w[3], q1w[7]);
-        dst[2] = make_uint4(q2w[0], q2w[4], q2w[1], q2w[5]);
-        dst[3] = make_uint4(q2w[2], q2w[6], q2w[3], q2w[7]);
-        xf[J] = make_float4(d2, d2 * (float)(s_lo + s_hi), __int_as_float(s_lo), __int_as_float(s_hi));
+        // this thread holds words 2u and 2u+1 of the block
+        uint8_t *blk = xq + (size_t)J * 64;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t w = 2 * u + k;
+            if constexpr (PLAIN) {
+                *reinterpret_cast<uint32_t *>(blk + 4 * w) = q1w[k];
+                *reinterpret_cast<uint32_t *>(blk + 32 + 4 * w) = q2w[k];
+            } else {
+                const uint32_t off = (w & 3) * 8 + (w >> 2) * 4;
+                *reinterpret_cast<uint32_t *>(blk + off) = q1w[k];
+                *reinterpret_cast<uint32_t *>(blk + 32 + off) = q2w[k];
+            }
+        }
+        const int other = __shfl_xor_sync(qmask, sum, 1);   // pairs (0,1) = k<16, (2,3) = k>=16
+        const int half = sum + other;
+        const int half_hi = __shfl_xor_sync(qmask, half, 2);
+        if (u == 0) xf[J] = make_float4(d2, d2 * (float)(half + half_hi), __int_as_float(half), __int_as_float(half_hi));
     }
 }
 
-// Q4_K 6-bit scale/min of sub-block j from the header words s0,s1,s2
-// (scales bytes 0-3, 4-7, 8-11), per src/vbs_dequant.c:225-233.
-__device__ __forceinline__ void k4_sm(uint32_t s0, uint32_t s1, uint32_t s2, int j, float &sc, float &mn) {
-    uint32_t a, b;
-    if (j < 4) {
-        a = (s0 >> (8 * j)) & 63u;
-        b = (s1 >> (8 * j)) & 63u;
-    } else {
-        const int k = 8 * (j - 4);
-        a = ((s2 >> k) & 15u) | (((s0 >> (k + 6)) & 3u) << 4);
-        b = ((s2 >> (k + 4)) & 15u) | (((s1 >> (k + 6)) & 3u) << 4);
+// 16 bytes from a shared address that is only 2-byte aligned.
+__device__ __forceinline__ uint4 lds128_any(uint32_t a) {
+    const uint32_t off = a & 3u;
+    if (off == 0) {
+        if ((a & 15u) == 0) return lds_u128(a);
+        return make_uint4(lds_u32(a), lds_u32(a + 4), lds_u32(a + 8), lds_u32(a + 12));
     }
-    sc = (float)a;
-    mn = (float)b;
+    const uint32_t b = a - off, sh = off * 8;
+    const uint32_t w0 = lds_u32(b), w1 = lds_u32(b + 4), w2 = lds_u32(b + 8), w3 = lds_u32(b + 12), w4 = lds_u32(b + 16);
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+
+// byte k of w as an exact float (magic-number conversion: 2^23 + byte).
+__device__ __forceinline__ float byte_f(uint32_t w, uint32_t k) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | k)) - 8388608.0f;
+}
+
+// D += A(16x32, u8) * B(32x8, s8), int32 accumulate in place.
+__device__ __forceinline__ void mma_u8s8_acc(const uint32_t a[4], uint32_t b0, uint32_t b1, int c[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8s8_acc(const uint32_t a[4], uint32_t b0, uint32_t b1, int c[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // ---------------------------------------------------------------------------
-// per-unit compute: one warp, 16 rows (matrix slot base `ms`), 128 columns
-// starting at chunk-local element `eo` and x sub-block J0.
-// acc[0], acc[1]: rows g, g+8 (lanes with (lane&3)==0 hold them; Q6_K
-// splits each over lanes t=0,1).
+// per-unit compute. One warp, 16 rows (row slots r0s..r0s+15 of the stage
+// at `ms`), one 256-element unit of the chunk starting at chunk-local
+// element `eo` (global element e0, x block J0 = e0/32).
+//
+// Block-diagonal MMA: lane (g, t) = (lane/4, lane%4). Thread column t owns
+// the k-slots 4t..4t+3 and 16+4t..19+4t of every m16n8k32 and fills them
+// with weights of ITS OWN scale group; the B operand is nonzero only in the
+// column pair (2t, 2t+1) = (q1, q2) of that group's x values. One MMA thus
+// forms 4 groups' partial dots at once and every lane ends up holding the
+// integer dots of one group for rows g and g+8 (C accumulates across the
+// MMAs of a group), so the float scale epilogue runs once per (row, group)
+// with no idle lanes. acc[0], acc[1] collect rows g, g+8.
 // ---------------------------------------------------------------------------
 template <int TYPE>
-__device__ __forceinline__ void mv_unit(uint32_t ms, uint32_t pad0, uint32_t pad1, uint32_t eo, uint32_t J0,
-                                        uint32_t xq, uint32_t xf, int lane, uint32_t nvalid_cols, float acc[2]) {
-    constexpr int RS = MvT<TYPE>::RS;
+__device__ __forceinline__ void mv_unit(uint32_t ms, uint32_t RS, uint32_t pad0, uint32_t pad1, uint32_t eo,
+                                        uint32_t J0, uint32_t xq, uint32_t xf, int lane, uint32_t nvalid,
+                                        float acc[2]) {
+    constexpr uint32_t r0s = 0;
     const int g = lane >> 2, t = lane & 3;
+    const bool bact = t == (g >> 1);       // this lane carries B column g (group g/2)
+    const uint32_t lev = g & 1;           // ... for x level q1 (0) or q2 (1)
+    const uint32_t rowA = ms + (r0s + g) * RS, rowB = rowA + 8 * RS;
     if constexpr (TYPE == T_Q4_K) {
-        const uint32_t sbl = eo >> 8, hh = (eo >> 7) & 1u;
-        const uint4 h0 = lds_u128(ms + g * RS + sbl * 144);
-        const uint4 h1 = lds_u128(ms + (g + 8) * RS + sbl * 144);
-        const uint32_t lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lcol = (lane >> 4) * 16;
-        float f0 = 0.f, f1 = 0.f, m0 = 0.f, m1 = 0.f;
+        const uint32_t sa = rowA + (eo >> 8) * 144, sb = rowB + (eo >> 8) * 144;
+        const uint4 hA = lds_u128(sa), hB = lds_u128(sb);
+        const uint4 a0 = lds_u128(sa + 16 + 32 * t), a1 = lds_u128(sa + 32 + 32 * t);
+        const uint4 b0 = lds_u128(sb + 16 + 32 * t), b1 = lds_u128(sb + 32 + 32 * t);
+        const uint32_t WA[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t WB[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const uint32_t bq = xq + (J0 + 2 * (g >> 1)) * 64 + lev * 32;   // slot layout, lo sub-block
+        int clo[4] = {0, 0, 0, 0}, chi[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int gg = 0; gg < 2; ++gg) {
-            const uint32_t G = 2 * hh + gg;
-            uint32_t a[4];
-            ldsm_x4(ms + lrow * RS + sbl * 144 + 16 + 32 * G + lcol, a[0], a[1], a[2], a[3]);
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t av[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) av[i] = half ? (a[i] & 0xF0F0F0F0u) : (a[i] & 0x0F0F0F0Fu);
-                const uint32_t J = J0 + 2 * gg + half;
-                uint2 bq = make_uint2(0u, 0u);
-                if (lane < 8) bq = lds_u64(xq + J * 64 + lane * 8);
-                int c[4];
-                mma_u8s8(av, bq.x, bq.y, c);
-                const uint2 xv = lds_u64(xf + J * 16);
-                const float xd = __uint_as_float(xv.x) * (half ? 0.0625f : 1.0f), xs = __uint_as_float(xv.y);
-                float sc0, mn0, sc1, mn1;
-                k4_sm(h0.y, h0.z, h0.w, (int)(2 * G + half), sc0, mn0);
-                k4_sm(h1.y, h1.z, h1.w, (int)(2 * G + half), sc1, mn1);
-                f0 = fmaf((float)(c[0] * 254 + c[1]) * xd, sc0, f0);
-                f1 = fmaf((float)(c[2] * 254 + c[3]) * xd, sc1, f1);
-                m0 = fmaf(mn0, xs, m0);
-                m1 = fmaf(mn1, xs, m1);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t alo[4] = {WA[i] & 0x0F0F0F0Fu, WB[i] & 0x0F0F0F0Fu, WA[4 + i] & 0x0F0F0F0Fu, WB[4 + i] & 0x0F0F0F0Fu};
+            const uint32_t ahi[4] = {WA[i] & 0xF0F0F0F0u, WB[i] & 0xF0F0F0F0u, WA[4 + i] & 0xF0F0F0F0u, WB[4 + i] & 0xF0F0F0F0u};
+            uint2 blo = make_uint2(0u, 0u), bhi = make_uint2(0u, 0u);
+            if (bact) {
+                blo = lds_u64(bq + i * 8);
+                bhi = lds_u64(bq + 64 + i * 8);
             }
+            mma_u8s8_acc(alo, blo.x, blo.y, clo);
+            mma_u8s8_acc(ahi, bhi.x, bhi.y, chi);
         }
-        acc[0] += f16f(h0.x & 0xFFFFu) * f0 - f16f(h0.x >> 16) * m0;
-        acc[1] += f16f(h1.x & 0xFFFFu) * f1 - f16f(h1.x >> 16) * m1;
+        // this lane's sub-blocks: 2t (low nibbles) and 2t+1 (high nibbles, x16)
+        const uint4 fl = lds_u128(xf + (J0 + 2 * t) * 16), fh = lds_u128(xf + (J0 + 2 * t + 1) * 16);
+        const uint32_t k0 = (2 * t) & 3, k1 = k0 + 1;
+        float r[2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const uint4 h = rr ? hB : hA;
+            // packed 6-bit scales/mins of sub-blocks 0-3 and 4-7 (src/vbs_dequant.c:225-233)
+            const uint32_t sc = (t < 2) ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+            const uint32_t mn = (t < 2) ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+            const int *c = rr ? clo + 2 : clo;
+            const int *ch = rr ? chi + 2 : chi;
+            const float tl = (float)(c[0] * 254 + c[1]), th = (float)(ch[0] * 254 + ch[1]);
+            const float f = tl * __uint_as_float(fl.x) * byte_f(sc, k0) + th * (__uint_as_float(fh.x) * 0.0625f) * byte_f(sc, k1);
+            const float m = byte_f(mn, k0) * __uint_as_float(fl.y) + byte_f(mn, k1) * __uint_as_float(fh.y);
+            r[rr] = f16f(h.x & 0xFFFFu) * f - f16f(h.x >> 16) * m;
+        }
+        acc[0] += r[0];
+        acc[1] += r[1];
     } else if constexpr (TYPE == T_Q6_K) {
-        const uint32_t sbl = eo >> 8, h = (eo >> 7) & 1u;
-        const uint32_t b0 = ms + g * RS + pad0 + sbl * 210, b1 = ms + (g + 8) * RS + pad1 + sbl * 210;
-        const float d0 = f16f(lds_u16(b0 + 208)), d1 = f16f(lds_u16(b1 + 208));
-        float f0 = 0.f, f1 = 0.f;
-        uint32_t qh[2][2];
+        // thread column t <-> (half h, l-half lh); its groups are (h, q, lh), q = 0..3
+        const uint32_t h = t >> 1, lh = t & 1;
+        const uint32_t sa = rowA + pad0 + (eo >> 8) * 210, sb = rowB + pad1 + (eo >> 8) * 210;
+        const uint4 qlA0 = lds128_any(sa + h * 64 + 16 * lh), qlA1 = lds128_any(sa + h * 64 + 32 + 16 * lh);
+        const uint4 qlB0 = lds128_any(sb + h * 64 + 16 * lh), qlB1 = lds128_any(sb + h * 64 + 32 + 16 * lh);
+        const uint4 qhA = lds128_any(sa + 128 + h * 32 + 16 * lh), qhB = lds128_any(sb + 128 + h * 32 + 16 * lh);
+        const uint32_t LA[2][4] = {{qlA0.x, qlA0.y, qlA0.z, qlA0.w}, {qlA1.x, qlA1.y, qlA1.z, qlA1.w}};
+        const uint32_t LB[2][4] = {{qlB0.x, qlB0.y, qlB0.z, qlB0.w}, {qlB1.x, qlB1.y, qlB1.z, qlB1.w}};
+        const uint32_t HA[4] = {qhA.x, qhA.y, qhA.z, qhA.w}, HB[4] = {qhB.x, qhB.y, qhB.z, qhB.w};
+        // B: the lane carrying column g serves thread column tb = g/2 = (hb, lhb)
+        const uint32_t tb = g >> 1, hb = tb >> 1, lhb = tb & 1;
+        float fA = 0.f, fB = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-            qh[0][kk] = lds_u32_any(b0 + 128 + h * 32 + kk * 16 + 4 * t);
-            qh[1][kk] = lds_u32_any(b1 + 128 + h * 32 + kk * 16 + 4 * t);
-        }
+        for (int q = 0; q < 4; ++q) {
+            int c[4] = {0, 0, 0, 0};
+            const uint32_t bq = xq + (J0 + hb * 4 + q) * 64 + lev * 32 + lhb * 16;   // plain layout
 #pragma unroll
-        for (int qp = 0; qp < 2; ++qp) {          // ql run (q & 1)
-            uint32_t ql[2][2];
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-                ql[0][kk] = lds_u32_any(b0 + h * 64 + qp * 32 + kk * 16 + 4 * t);
-                ql[1][kk] = lds_u32_any(b1 + h * 64 + qp * 32 + kk * 16 + 4 * t);
+            for (int i = 0; i < 2; ++i) {
+                uint32_t a[4];
+                const int s = 4 * (q >> 1), hs = 2 * q;
+                a[0] = ((LA[q & 1][2 * i] >> s) & 0x0F0F0F0Fu) | (((HA[2 * i] >> hs) & 0x03030303u) << 4);
+                a[1] = ((LB[q & 1][2 * i] >> s) & 0x0F0F0F0Fu) | (((HB[2 * i] >> hs) & 0x03030303u) << 4);
+                a[2] = ((LA[q & 1][2 * i + 1] >> s) & 0x0F0F0F0Fu) | (((HA[2 * i + 1] >> hs) & 0x03030303u) << 4);
+                a[3] = ((LB[q & 1][2 * i + 1] >> s) & 0x0F0F0F0Fu) | (((HB[2 * i + 1] >> hs) & 0x03030303u) << 4);
+                uint2 b = make_uint2(0u, 0u);
+                if (bact) b = lds_u64(bq + i * 8);
+                mma_u8s8_acc(a, b.x, b.y, c);
             }
-#pragma unroll
-            for (int qs = 0; qs < 2; ++qs) {      // nibble half (q >> 1)
-                const int q = qs * 2 + qp;
-                uint32_t av[4];
-#pragma unroll
-                for (int r = 0; r < 2; ++r)
-#pragma unroll
-                    for (int kk = 0; kk < 2; ++kk)
-                        av[r + 2 * kk] = ((ql[r][kk] >> (4 * qs)) & 0x0F0F0F0Fu) |
-                                         (((qh[r][kk] >> (2 * q)) & 0x03030303u) << 4);
-                const uint32_t J = J0 + q;
-                uint2 bq = make_uint2(0u, 0u);
-                if (lane < 16) {
-                    bq = lds_u64(xq + J * 64 + (lane & 7) * 8);
-                    if (lane < 8) bq.y = 0u; else bq.x = 0u;
-                }
-                int c[4];
-                mma_u8s8(av, bq.x, bq.y, c);
-                const uint4 xv = lds_u128(xf + J * 16);
-                const float xd = __uint_as_float(xv.x);
-                const int sq = (t & 1) ? (int)xv.w : (int)xv.z;
-                const uint32_t gi = h * 8 + q * 2 + (t & 1);
-                const float sc0 = (float)lds_s8(b0 + 192 + gi), sc1 = (float)lds_s8(b1 + 192 + gi);
-                f0 = fmaf((float)(c[0] * 254 + c[1] - 32 * sq) * xd, sc0, f0);
-                f1 = fmaf((float)(c[2] * 254 + c[3] - 32 * sq) * xd, sc1, f1);
-            }
+            // this lane's group (h, q, lh): x block J0 + 4h + q, k-half lh
+            const uint4 fx = lds_u128(xf + (J0 + h * 4 + q) * 16);
+            const int sq = lh ? (int)fx.w : (int)fx.z;
+            const uint32_t gi = h * 8 + q * 2 + lh;
+            const float xd = __uint_as_float(fx.x);
+            fA = fmaf((float)(c[0] * 254 + c[1] - 32 * sq) * xd, (float)lds_s8(sa + 192 + gi), fA);
+            fB = fmaf((float)(c[2] * 254 + c[3] - 32 * sq) * xd, (float)lds_s8(sb + 192 + gi), fB);
         }
-        acc[0] += d0 * f0;
-        acc[1] += d1 * f1;
-    } else {  // Q8_0: four 34-byte blocks
+        acc[0] += f16f(lds_u16(sa + 208)) * fA;
+        acc[1] += f16f(lds_u16(sb + 208)) * fB;
+    } else {  // Q8_0: eight 34-byte blocks; thread column t owns blocks t and t+4
         const uint32_t blk0 = eo >> 5;
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb) {
-            if ((uint32_t)kb * 32 >= nvalid_cols) break;
-            const uint32_t b0 = ms + g * RS + pad0 + (blk0 + kb) * 34, b1 = ms + (g + 8) * RS + pad1 + (blk0 + kb) * 34;
-            uint32_t av[4];
-            av[0] = lds_u32_any(b0 + 2 + 4 * t);
-            av[1] = lds_u32_any(b1 + 2 + 4 * t);
-            av[2] = lds_u32_any(b0 + 18 + 4 * t);
-            av[3] = lds_u32_any(b1 + 18 + 4 * t);
-            const uint32_t J = J0 + kb;
-            uint2 bq = make_uint2(0u, 0u);
-            if (lane < 8) bq = lds_u64(xq + J * 64 + lane * 8);
-            int c[4];
-            mma_s8s8(av, bq.x, bq.y, c);
-            const float xd = __uint_as_float(lds_u32(xf + J * 16));
-            acc[0] = fmaf((float)(c[0] * 254 + c[1]), f16f(lds_u16(b0)) * xd, acc[0]);
-            acc[1] = fmaf((float)(c[2] * 254 + c[3]), f16f(lds_u16(b1)) * xd, acc[1]);
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t bi = (uint32_t)t + 4 * k;          // this lane's block
+            const uint32_t bb = (uint32_t)(g >> 1) + 4 * k;   // block whose B column this lane carries
+            const bool mine = bi * 32 < nvalid, bvalid = bb * 32 < nvalid;
+            const uint32_t sa = rowA + pad0 + (blk0 + bi) * 34, sb = rowB + pad1 + (blk0 + bi) * 34;
+            uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
+            if (mine) {
+                a0 = lds128_any(sa + 2); a1 = lds128_any(sa + 18);
+                b0 = lds128_any(sb + 2); b1 = lds128_any(sb + 18);
+            }
+            const uint32_t WA[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const uint32_t WB[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            const uint32_t bq = xq + (J0 + bb) * 64 + lev * 32;
+            int c[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t a[4] = {WA[i], WB[i], WA[4 + i], WB[4 + i]};
+                uint2 b = make_uint2(0u, 0u);
+                if (bact && bvalid) b = lds_u64(bq + i * 8);
+                mma_s8s8_acc(a, b.x, b.y, c);
+            }
+            if (mine) {
+                const float xd = __uint_as_float(lds_u32(xf + (J0 + bi) * 16));
+                acc[0] = fmaf((float)(c[0] * 254 + c[1]), f16f(lds_u16(sa)) * xd, acc[0]);
+                acc[1] = fmaf((float)(c[2] * 254 + c[3]), f16f(lds_u16(sb)) * xd, acc[1]);
+            }
         }
     }
 }
 
 // ---------------------------------------------------------------------------
-// epilogue for one row (run by consumer warp 0, lane i = row in tile)
+// epilogue for one row (consumer warp 0; lane = row within the tile)
 // ---------------------------------------------------------------------------
 template <int EPI>
 __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, bool valid, float va, float vb) {
@@ -300,7 +362,7 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, boo
     } else if constexpr (EPI == MV_EPI_SILU) {
         if (valid) p.y[row] = va / (1.0f + expf(-va)) * vb;
     } else {  // QKV: q/k rows get RoPE on (2i, 2i+1) pairs; k/v go to the fp16 cache
-        const float other = __shfl_xor_sync(0x0000FFFFu, va, 1);
+        const float other = __shfl_xor_sync(0xffffffffu, va, 1);
         if (!valid) return;
         const uint32_t pos = p.ctrl[0];
         if (pos >= p.max_ctx) {   // position past the KV capacity: report, never write out of bounds
@@ -325,32 +387,35 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, boo
     }
 }
 
+// Tiles of 16 rows. Non-dual: the 8 warps split the super-block columns of
+// the chunk (warp w: columns w, w+8, ...). Dual (gate/up): warps 0-3 take
+// W_gate, warps 4-7 the same rows of W_up, columns w%4, w%4+4, ...
 template <int TYPE, int DUAL, int EPI>
-__global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p) {
+__global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p, const MvGeom geo) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    constexpr int E = MvT<TYPE>::E, BB = MvT<TYPE>::BB, RS = MvT<TYPE>::RS;
-    constexpr int SLOTS = DUAL ? 32 : 16;
+    constexpr int E = MvT<TYPE>::E, BB = MvT<TYPE>::BB;
+    constexpr uint32_t SLOTS = DUAL ? 32u : 16u;
+    constexpr uint32_t CW = DUAL ? 4u : 8u;             // warps sharing a matrix's columns
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t nsub = p.cols / 32, nstage = p.nstage;
+    const uint32_t nsub = p.cols / 32, nstage = geo.nstage, RS = geo.rs, CK = geo.ck;
 
     const uint32_t sbase = smem_u32(smem);
-    float *misc = reinterpret_cast<float *>(smem + 256);          // 64 floats
+    float *misc = reinterpret_cast<float *>(smem + 256);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 256 + 60 * 4);
-    float *red = reinterpret_cast<float *>(smem + 512);           // [2][8][32]
+    float *red = reinterpret_cast<float *>(smem + 512);   // [2][8 warps][16 rows]
     uint8_t *xq = smem + MV_HDR;
     float4 *xf = reinterpret_cast<float4 *>(xq + (size_t)nsub * 64);
     const uint32_t xq_a = sbase + MV_HDR, xf_a = xq_a + nsub * 64;
-    const uint32_t stage0 = (MV_HDR + nsub * 80 + 1023u) & ~1023u;
     const uint32_t stage_bytes = SLOTS * RS;
     auto full_bar = [&](uint32_t s) { return sbase + 8u * s; };
     auto empty_bar = [&](uint32_t s) { return sbase + 8u * (MV_MAXST + s); };
-    auto stage_addr = [&](uint32_t s) { return sbase + stage0 + s * stage_bytes; };
+    auto stage_addr = [&](uint32_t s) { return sbase + geo.stage0 + s * stage_bytes; };
 
     // rows of this CTA: an even-aligned balanced slice
     const uint32_t G = gridDim.x, b = blockIdx.x, hr = p.rows / 2;
     const uint32_t r0 = (uint32_t)(((uint64_t)b * hr) / G) * 2;
     const uint32_t r1 = (b + 1 == G) ? p.rows : (uint32_t)(((uint64_t)(b + 1) * hr) / G) * 2;
-    const uint32_t nch = (p.cols + MV_CK - 1) / MV_CK;
+    const uint32_t nch = (p.cols + CK - 1) / CK;
     const uint32_t ntiles = (r1 - r0 + 15) / 16;
     const uint32_t nst = ntiles * nch;
 
@@ -366,25 +431,22 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
 
     if (warp == MV_NCW) {
         // ------------------------------ producer ------------------------------
-        uint32_t issued = 0;
+        uint32_t slot = 0, round = 0, tile = 0, ch = 0, issued = 0;
+        const bool mat = DUAL && lane >= 16;
+        const uint32_t ri = (uint32_t)lane & 15u;
+        const bool active = DUAL || lane < 16;
         for (uint32_t s = 0; s < nst; ++s) {
-            const uint32_t slot = s % nstage;
-            if (s >= nstage) {
-                if (!mbar_wait_bounded(empty_bar(slot), ((s / nstage) - 1) & 1, kWaitNs)) {
-                    if (lane == 0) { *abort_flag = 1; dev_flag_error(p.err, DERR_TIMEOUT_EMPTY); }
-                    break;
-                }
+            if (s >= nstage && !mbar_wait_bounded(empty_bar(slot), (round - 1) & 1, kWaitNs)) {
+                if (lane == 0) { *abort_flag = 1; dev_flag_error(p.err, DERR_TIMEOUT_EMPTY); }
+                break;
             }
             if (*abort_flag) break;
-            const uint32_t tile = s / nch, ch = s % nch;
-            const uint32_t c0 = ch * MV_CK, c1 = min(p.cols, c0 + MV_CK);
+            const uint32_t c0 = ch * CK, c1 = min(p.cols, c0 + CK);
             const uint64_t boff = (uint64_t)(c0 / E) * BB, blen = (uint64_t)((c1 - c0) / E) * BB;
-            const int mat = lane >> 4, ri = lane & 15;
             const uint32_t row = r0 + tile * 16 + ri;
-            const bool valid = row < r1 && (DUAL || mat == 0);
             uint32_t tx = 0, dst_al = 0;
             uintptr_t lo = 0;
-            if (valid) {
+            if (active && row < r1) {
                 const uint8_t *rp = mat ? (p.wb + (uint64_t)row * p.rb) : seg_row_ptr(p, row);
                 const uintptr_t a = reinterpret_cast<uintptr_t>(rp + boff);
                 lo = (a + 15) & ~(uintptr_t)15;
@@ -406,6 +468,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
             if (tx) bulk_g2s(dst_al, reinterpret_cast<const void *>(lo), tx, full_bar(slot));
             ++issued;
             if (issued == min(nst, nstage) && lane == 0) pdl_launch_dependents();
+            if (++slot == nstage) { slot = 0; ++round; }
+            if (++ch == nch) { ch = 0; ++tile; }
         }
         if (nst == 0 && lane == 0) pdl_launch_dependents();
         if (*abort_flag) {
@@ -418,74 +482,76 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
     }
 
     // ------------------------------ consumers ------------------------------
-    const int ctid = threadIdx.x;
     pdl_wait();
-    mv_prologue(p, xq, xf, misc, ctid);
+    mv_prologue<TYPE == T_Q6_K>(p, xq, xf, misc, threadIdx.x);
     named_bar_sync(1, MV_NCW * 32);
 
-    float accA[2] = {0.f, 0.f}, accB[2] = {0.f, 0.f};
+    float acc[2] = {0.f, 0.f};
     const int g = lane >> 2;
+    const uint32_t msel = DUAL ? (uint32_t)warp >> 2 : 0u;       // matrix of this warp (dual)
+    const uint32_t cw = DUAL ? (uint32_t)warp & 3u : (uint32_t)warp;
+    uint32_t slot = 0, round = 0, tile = 0, ch = 0;
     for (uint32_t s = 0; s < nst; ++s) {
-        const uint32_t slot = s % nstage;
         bool ok = !*abort_flag;
-        if (ok && !mbar_wait_bounded(full_bar(slot), (s / nstage) & 1, kWaitNs)) {
+        if (ok && !mbar_wait_bounded(full_bar(slot), round & 1, kWaitNs)) {
             ok = false;
             if (lane == 0) { *abort_flag = 1; dev_flag_error(p.err, DERR_TIMEOUT_FULL); }
         }
-        const uint32_t tile = s / nch, ch = s % nch;
-        const uint32_t c0 = ch * MV_CK, c1 = min(p.cols, c0 + MV_CK);
-        const uint32_t eo = (uint32_t)warp * 128;
-        if (ok && c0 + eo < c1) {
-            const uint32_t ms = stage_addr(slot);
-            uint32_t pad0 = 0, pad1 = 0, padb0 = 0, padb1 = 0;
+        const uint32_t c0 = ch * CK, c1 = min(p.cols, c0 + CK);
+        if (ok) {
+            const uint32_t ms = stage_addr(slot) + msel * 16u * RS;
+            uint32_t pad0 = 0, pad1 = 0;
             if constexpr (TYPE != T_Q4_K) {
+                // rows keep their global address modulo 16 in the slot
                 const uint64_t boff = (uint64_t)(c0 / E) * BB;
-                const uint32_t ra = min(r0 + tile * 16 + g, r1 - 1), rb_ = min(r0 + tile * 16 + g + 8, r1 - 1);
-                pad0 = (uint32_t)(reinterpret_cast<uintptr_t>(seg_row_ptr(p, ra) + boff) & 15);
-                pad1 = (uint32_t)(reinterpret_cast<uintptr_t>(seg_row_ptr(p, rb_) + boff) & 15);
-                if constexpr (DUAL) {
-                    padb0 = (uint32_t)(reinterpret_cast<uintptr_t>(p.wb + (uint64_t)ra * p.rb + boff) & 15);
-                    padb1 = (uint32_t)(reinterpret_cast<uintptr_t>(p.wb + (uint64_t)rb_ * p.rb + boff) & 15);
-                }
+                const uint32_t rbase = r0 + tile * 16;
+                const uint32_t ra = min(rbase + g, r1 - 1), rb_ = min(rbase + g + 8, r1 - 1);
+                const uint8_t *pa = msel ? p.wb + (uint64_t)ra * p.rb : seg_row_ptr(p, ra);
+                const uint8_t *pb = msel ? p.wb + (uint64_t)rb_ * p.rb : seg_row_ptr(p, rb_);
+                pad0 = (uint32_t)(reinterpret_cast<uintptr_t>(pa + boff) & 15);
+                pad1 = (uint32_t)(reinterpret_cast<uintptr_t>(pb + boff) & 15);
             }
-            const uint32_t J0 = (c0 + eo) >> 5;
-            mv_unit<TYPE>(ms, pad0, pad1, eo, J0, xq_a, xf_a, lane, c1 - c0 - eo, accA);
-            if constexpr (DUAL) mv_unit<TYPE>(ms + 16 * RS, padb0, padb1, eo, J0, xq_a, xf_a, lane, c1 - c0 - eo, accB);
+            for (uint32_t eo = cw * 256u; c0 + eo < c1; eo += CW * 256u)
+                mv_unit<TYPE>(ms, RS, pad0, pad1, eo, (c0 + eo) >> 5, xq_a, xf_a, lane, c1 - c0 - eo, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(slot));
-        if (ch + 1 == nch) {
-            // tile complete: reduce the 8 warps' partial row sums
-            if constexpr (TYPE == T_Q6_K) {
+        if (++slot == nstage) { slot = 0; ++round; }
+        if (++ch < nch) continue;
+        ch = 0;
+        // tile complete: per-warp row sums (over the 4 thread columns), then
+        // over the warps of each matrix
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    accA[i] += __shfl_xor_sync(0xffffffffu, accA[i], 1);
-                    if constexpr (DUAL) accB[i] += __shfl_xor_sync(0xffffffffu, accB[i], 1);
-                }
-            }
-            float *rbuf = red + (tile & 1) * (MV_NCW * 32);
-            if ((lane & 3) == 0) {
-                rbuf[warp * 32 + g] = accA[0];
-                rbuf[warp * 32 + g + 8] = accA[1];
-                if constexpr (DUAL) {
-                    rbuf[warp * 32 + 16 + g] = accB[0];
-                    rbuf[warp * 32 + 24 + g] = accB[1];
-                }
-            }
-            accA[0] = accA[1] = accB[0] = accB[1] = 0.f;
-            named_bar_sync(1, MV_NCW * 32);
-            if (warp == 0 && lane < 16) {
-                float va = 0.f, vb = 0.f;
-#pragma unroll
-                for (int w = 0; w < MV_NCW; ++w) {
-                    va += rbuf[w * 32 + lane];
-                    if constexpr (DUAL) vb += rbuf[w * 32 + 16 + lane];
-                }
-                const uint32_t row = r0 + tile * 16 + lane;
-                if (!*abort_flag) mv_epilogue<EPI>(p, row, row < r1, va, vb);
-                else if constexpr (EPI == MV_EPI_QKV) (void)__shfl_xor_sync(0x0000FFFFu, va, 1);
-            }
+        for (int q = 0; q < 2; ++q) {
+            acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 1);
+            acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 2);
         }
+        float *rbuf = red + (tile & 1) * (MV_NCW * 16);
+        if ((lane & 3) == 0) {
+            rbuf[warp * 16 + g] = acc[0];
+            rbuf[warp * 16 + g + 8] = acc[1];
+        }
+        acc[0] = acc[1] = 0.f;
+        named_bar_sync(1, MV_NCW * 32);
+        if (warp == 0) {
+            const uint32_t li = (uint32_t)lane & 15u;
+            float va = 0.f, vb = 0.f;
+            if constexpr (DUAL) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    va += rbuf[w * 16 + li];
+                    vb += rbuf[(4 + w) * 16 + li];
+                }
+            } else {
+#pragma unroll
+                for (int w = 0; w < 8; ++w) va += rbuf[w * 16 + li];
+            }
+            const uint32_t row = r0 + tile * 16 + li;
+            // all 32 lanes take part (RoPE pairs use a warp shuffle); lanes 16-31 write nothing
+            if (!*abort_flag) mv_epilogue<EPI>(p, row, lane < 16 && row < r1, va, vb);
+            else if constexpr (EPI == MV_EPI_QKV) (void)__shfl_xor_sync(0xffffffffu, va, 1);
+        }
+        ++tile;
     }
 }
 
@@ -493,13 +559,28 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
 // host side of the fast kernel
 // ---------------------------------------------------------------------------
 
-template <int TYPE> static uint32_t mv_smem_bytes(uint32_t cols, int dual, uint32_t nstage) {
-    const uint32_t stage0 = (MV_HDR + (cols / 32) * 80 + 1023u) & ~1023u;
-    return stage0 + nstage * (dual ? 32u : 16u) * (uint32_t)MvT<TYPE>::RS;
+// Stage geometry for a shape: whole rows when 3+ stages of 16 (dual 32)
+// full rows fit next to the x buffer, else 256-column multiples.
+template <int TYPE> static MvGeom mv_geom(uint32_t cols, int dual) {
+    MvGeom g = {};
+    g.stage0 = (MV_HDR + (cols / 32) * 80 + 1023u) & ~1023u;
+    const uint32_t slots = dual ? 32u : 16u;
+    const uint32_t avail = MV_SMEM > g.stage0 ? MV_SMEM - g.stage0 : 0;
+    auto rs_for = [](uint32_t ck) {
+        uint32_t rs = ((ck / MvT<TYPE>::E) * MvT<TYPE>::BB + 32 + 15) & ~15u;
+        if (((rs / 16) & 1u) == 0) rs += 16;   // odd number of 16-byte units: conflict-free rows
+        return rs;
+    };
+    uint32_t ck = (cols + 255) / 256 * 256;
+    while (ck > 256 && avail / (slots * rs_for(ck)) < 3) ck = (ck / 2 + 255) / 256 * 256;
+    g.ck = ck;
+    g.rs = rs_for(ck);
+    g.nstage = std::max(1u, std::min(MV_MAXST, avail / (slots * g.rs)));
+    return g;
 }
-template <int TYPE> static uint32_t mv_nstage(int dual) {
-    uint32_t sb = (dual ? 32u : 16u) * (uint32_t)MvT<TYPE>::RS;
-    return std::max(2u, std::min(MV_MAXST, MV_STAGE_BUDGET / sb));
+template <int TYPE> static uint32_t mv_smem_bytes(uint32_t cols, int dual) {
+    const MvGeom g = mv_geom<TYPE>(cols, dual);
+    return g.stage0 + g.nstage * (dual ? 32u : 16u) * g.rs;
 }
 
 bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const *w, int nw, const void *x,
@@ -513,20 +594,20 @@ bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const
         // must start 16-byte aligned in global memory too.
         if (type == T_Q4_K && (reinterpret_cast<uintptr_t>(w[i]) & 15)) return false;
     }
-    uint32_t smem = 0;
+    MvGeom g = {};
     switch (type) {
-        case T_Q4_K: smem = mv_smem_bytes<T_Q4_K>(cols, dual, mv_nstage<T_Q4_K>(dual)); break;
-        case T_Q6_K: smem = mv_smem_bytes<T_Q6_K>(cols, dual, mv_nstage<T_Q6_K>(dual)); break;
-        default: smem = mv_smem_bytes<T_Q8_0>(cols, dual, mv_nstage<T_Q8_0>(dual)); break;
+        case T_Q4_K: g = mv_geom<T_Q4_K>(cols, dual); break;
+        case T_Q6_K: g = mv_geom<T_Q6_K>(cols, dual); break;
+        default: g = mv_geom<T_Q8_0>(cols, dual); break;
     }
-    return smem <= 227u * 1024u;
+    return g.nstage >= 2 && g.stage0 + g.nstage * (dual ? 32u : 16u) * g.rs <= MV_SMEM;
 }
 
 template <int TYPE, int DUAL, int EPI>
 static cudaError_t mv_fast_go(const MvParams &p0, int n_sm, cudaStream_t st, bool pdl, int grid_override) {
-    MvParams p = p0;
-    p.nstage = mv_nstage<TYPE>(DUAL);
-    const uint32_t smem = mv_smem_bytes<TYPE>(p.cols, DUAL, p.nstage);
+    const MvParams &p = p0;
+    const MvGeom geo = mv_geom<TYPE>(p.cols, DUAL);
+    const uint32_t smem = mv_smem_bytes<TYPE>(p.cols, DUAL);
     auto kern = mv_fast_kernel<TYPE, DUAL, EPI>;
     uint32_t grid = grid_override > 0 ? (uint32_t)grid_override
                                       : std::max(1u, std::min((uint32_t)n_sm, (p.rows + 1) / 2));
@@ -541,7 +622,7 @@ static cudaError_t mv_fast_go(const MvParams &p0, int n_sm, cudaStream_t st, boo
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     note_launches(1);
-    return cudaLaunchKernelEx(&cfg, kern, p);
+    return cudaLaunchKernelEx(&cfg, kern, p, geo);
 }
 
 template <int TYPE, int DUAL, int EPI> static cudaError_t mv_set_attr() {

@@ -193,15 +193,24 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
     const uint16_t *kb = p.kc + (uint64_t)bq * p.kv_batch_stride + (uint64_t)p.layer * p.max_ctx * lstride + kvh * HD + sub * DPL;
     const uint16_t *vb = p.vc + (uint64_t)bq * p.kv_batch_stride + (uint64_t)p.layer * p.max_ctx * lstride + kvh * HD + sub * DPL;
 
-    for (uint32_t tb = t0 + warp * PPW; tb < t1; tb += AT_NW * PPW) {
+    // K/V rows of the next position batch are loaded before the current
+    // batch is used (two batches in flight per warp)
+    auto load_rows = [&](uint32_t tb, uint4 *kr, uint4 *vr) {
         const uint32_t t = tb + grp;
         const bool valid = t < t1;
-        uint4 kr[NV], vr[NV];
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             kr[i] = valid ? __ldg(reinterpret_cast<const uint4 *>(kb + (uint64_t)t * lstride) + i) : make_uint4(0, 0, 0, 0);
             vr[i] = valid ? __ldg(reinterpret_cast<const uint4 *>(vb + (uint64_t)t * lstride) + i) : make_uint4(0, 0, 0, 0);
         }
+    };
+    uint4 kr[NV], vr[NV], kn[NV], vn[NV];
+    uint32_t tb = t0 + warp * PPW;
+    if (tb < t1) load_rows(tb, kr, vr);
+    for (; tb < t1; tb += AT_NW * PPW) {
+        const uint32_t tnext = tb + AT_NW * PPW;
+        if (tnext < t1) load_rows(tnext, kn, vn);
+        const bool valid = tb + grp < t1;
         float kf[DPL], vf[DPL];
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
@@ -232,6 +241,8 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
                 m[g] = mn;
             }
         }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) { kr[i] = kn[i]; vr[i] = vn[i]; }
     }
 
     // merge lane groups (same `sub`, different `grp`) within the warp
@@ -300,19 +311,31 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_kernel(const AttnParams p, ui
     if (ticket != n_splits - 1) { pdl_launch_dependents(); return; }
     __threadfence();
     const float *parts = work + (size_t)slot * n_splits * part_stride;
-    for (uint32_t k = threadIdx.x; k < G * HD; k += blockDim.x) {
-        const uint32_t g = k / HD, d = k % HD;
+    // split weights a[g][s] = exp2(m_s - M_g) in shared memory (reusing sh)
+    float *wsm = &sh[0][0][0];                      // AT_NW*GMAX*(2+HD) floats >= GMAX*(n_splits+2)
+    __shared__ float Mg[GMAX], Lg[GMAX];
+    if (threadIdx.x < G) {
+        const uint32_t g = threadIdx.x;
         float M = -INFINITY;
-        for (uint32_t s = 0; s < n_splits; ++s) M = fmaxf(M, __ldcg(parts + s * part_stride + g * (2 + HD)));
-        float L = 0.f, O = 0.f;
-        for (uint32_t s = 0; s < n_splits; ++s) {
-            const float *ps = parts + s * part_stride + g * (2 + HD);
+        for (uint32_t s2 = 0; s2 < n_splits; ++s2) M = fmaxf(M, __ldcg(parts + s2 * part_stride + g * (2 + HD)));
+        float L = 0.f;
+        for (uint32_t s2 = 0; s2 < n_splits; ++s2) {
+            const float *ps = parts + s2 * part_stride + g * (2 + HD);
             const float ms = __ldcg(ps);
             const float a = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+            wsm[g * n_splits + s2] = a;
             L += __ldcg(ps + 1) * a;
-            O += __ldcg(ps + 2 + d) * a;
         }
-        p.out[((size_t)bq * p.nqh + kvh * G + g) * HD + d] = O / L;
+        Mg[g] = M;
+        Lg[g] = L;
+    }
+    __syncthreads();
+    for (uint32_t k = threadIdx.x; k < G * HD; k += blockDim.x) {
+        const uint32_t g = k / HD, d = k % HD;
+        float O = 0.f;
+        for (uint32_t s2 = 0; s2 < n_splits; ++s2)
+            O = fmaf(__ldcg(parts + s2 * part_stride + g * (2 + HD) + 2 + d), wsm[g * n_splits + s2], O);
+        p.out[((size_t)bq * p.nqh + kvh * G + g) * HD + d] = O / Lg[g];
     }
     if (threadIdx.x == 0) counters[slot] = 0u;
     pdl_launch_dependents();
@@ -325,10 +348,11 @@ size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t ba
 }
 
 uint32_t attn_num_splits(uint32_t seq_len_hint, uint32_t nkh, uint32_t batch, int n_sm) {
-    const uint32_t target = (uint32_t)n_sm * 4u;
+    const uint32_t target = (uint32_t)n_sm * 2u;
     uint32_t s = (target + nkh * batch - 1) / (nkh * batch);
-    s = std::min(s, std::max(1u, (seq_len_hint + 31) / 32));
-    return std::max(1u, std::min(s, 256u));
+    s = std::min(s, std::max(1u, (seq_len_hint + 63) / 64));
+    // the merge keeps GMAX x n_splits weights in the CTA's shared scratch
+    return std::max(1u, std::min(s, 128u));
 }
 
 template <int HD, int DPL, int GMAX>

@@ -7,7 +7,7 @@
 // down_proj partial sums (dim floats, 16 KB for the 8B shape) and
 // all-gathers the sharded logits. The reference has no multi-GPU path (its
 // engine binds one device, src/vbs_engine.c:142-169).
-#include "../../include/vbs_b200.h"
+#include "vbs_b200.h"
 #include "backend.h"
 #include "tp.h"
 
