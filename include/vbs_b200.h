@@ -240,8 +240,11 @@ typedef struct {
 
 typedef struct vbs_cu_decoder vbs_cu_decoder_t;
 
-/* Allocates the activations, the KV cache ([layer][max_ctx][kv_dim], fp16;
- * fp32 under STRICT) and the control block on the current device. */
+/* Allocates the activations, the KV cache (fp16 [layer][kv head][max_ctx]
+ * [head_dim]; fp32 [layer][max_ctx][kv_dim] under STRICT) and the control
+ * block on the current device. Synchronizes the device first, so weights
+ * still being written by work on other streams are complete before the
+ * decoder's own stream reads them. */
 VBS_API vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t flags,
                                         char *err, size_t err_cap);
 VBS_API void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d);

@@ -113,6 +113,26 @@ def test_device_greedy_loop_equals_host_loop(vbs, l8b_2layer, clean_errors):
     dec2.close()
 
 
+def test_device_greedy_loop_large_vocab(vbs, gpu, clean_errors):
+    """A vocabulary of 40000 rows spreads the on-device argmax over several
+    CTAs (slice maxima merged by the last CTA); the tokens must still be the
+    host's first-maximum argmax of the returned logits."""
+    cfg = dict(models.L8B, n_layers=1, vocab=40000)
+    dm = vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=7)
+    dec = vbs.Decoder(dm, 32)
+    dev_toks = dec.generate([3, 1, 4], 12)
+    dec2 = vbs.Decoder(dm, 32)
+    lg = dec2.forward([3, 1, 4])
+    host_toks = []
+    for i in range(12):
+        host_toks.append(int(np.argmax(lg)))
+        if i + 1 < 12:
+            lg = dec2.forward([host_toks[-1]])
+    assert dev_toks == host_toks
+    dec.close()
+    dec2.close()
+
+
 def test_context_capacity_is_enforced(vbs, tiny_dev, clean_errors):
     dec = vbs.Decoder(tiny_dev, 8)
     dec.forward([1] * 8, logits=False)

@@ -182,6 +182,41 @@ def test_attention_partial_context(vbs, orc, torch, clean_errors):
     assert np.all(np.abs(out.cpu().numpy() - want) <= 1e-4 + 1e-3 * np.abs(want))
 
 
+@pytest.mark.parametrize("nqh,nkh,hd,seq,mc", [(8, 1, 256, 300, 301), (64, 8, 128, 1000, 1024), (16, 2, 32, 777, 800),
+                                               (4, 4, 64, 50, 64), (8, 8, 128, 1, 16), (32, 8, 128, 17, 40)])
+def test_attention_shapes(vbs, orc, torch, nqh, nkh, hd, seq, mc, clean_errors):
+    """Head dims 32/64/128 (tensor-core kernel) and 256 (SIMT kernel), GQA
+    groups 1, 4 and 8, single-position and ragged contexts."""
+    g = torch.Generator(device="cuda").manual_seed(nqh * hd + seq)
+    layer = 1
+    kc = torch.randn(((layer + 1) * mc * nkh * hd,), generator=g, device="cuda").half()
+    vc = torch.randn(((layer + 1) * mc * nkh * hd,), generator=g, device="cuda").half()
+    q = torch.randn((nqh * hd,), generator=g, device="cuda")
+    out = torch.empty((nqh * hd,), dtype=torch.float32, device="cuda")
+    scale = float(np.float32(1) / np.sqrt(np.float32(hd)))
+    vbs.attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), seq, layer, mc, nqh, nkh, hd, scale)
+    torch.cuda.synchronize()
+    want = orc.attention(q.cpu().numpy(), kc.cpu().numpy().view(np.uint16), vc.cpu().numpy().view(np.uint16), seq,
+                         layer, mc, nqh, nkh, hd, scale)
+    assert np.all(np.abs(out.cpu().numpy() - want) <= 1e-4 + 1e-3 * np.abs(want))
+
+
+def test_attention_peaked_scores(vbs, orc, torch, clean_errors):
+    """Large-magnitude q (scores spanning hundreds of log2 units) exercises
+    the running-maximum rescale."""
+    nqh, nkh, hd, seq = 32, 8, 128, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    kc = torch.randn((seq * nkh * hd,), generator=g, device="cuda").half()
+    vc = torch.randn((seq * nkh * hd,), generator=g, device="cuda").half()
+    q = 12.0 * torch.randn((nqh * hd,), generator=g, device="cuda")
+    out = torch.empty((nqh * hd,), dtype=torch.float32, device="cuda")
+    vbs.attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), seq, 0, seq, nqh, nkh, hd, 0.0883883)
+    torch.cuda.synchronize()
+    want = orc.attention(q.cpu().numpy(), kc.cpu().numpy().view(np.uint16), vc.cpu().numpy().view(np.uint16), seq, 0,
+                         seq, nqh, nkh, hd, 0.0883883)
+    assert np.all(np.abs(out.cpu().numpy() - want) <= 1e-4 + 1e-3 * np.abs(want))
+
+
 def test_kernel_launch_counter_moves(vbs, torch, clean_errors):
     before = vbs.kernel_launches()
     x = torch.zeros(256, device="cuda")

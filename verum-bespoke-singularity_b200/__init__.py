@@ -335,6 +335,7 @@ def synth_llama(shape: LlamaShape, types: dict, seed: int = 1234, std: float = 0
         m.tensors[f"blk.{l}.attn_norm"] = torch.ones(shape.dim, dtype=torch.float32, device=device)
         m.tensors[f"blk.{l}.ffn_norm"] = torch.ones(shape.dim, dtype=torch.float32, device=device)
     m.make_desc()
+    torch.cuda.synchronize(device)   # the weights are complete when this returns
     return m
 
 

@@ -92,7 +92,7 @@ static bool do_init() {
         s.n_sm = pr.multiProcessorCount;
         if (cudaMalloc(&s.err, 256) != cudaSuccess) continue;
         cudaMemset(s.err, 0, 256);
-        if (mv_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
+        if (mv_configure() != cudaSuccess || attn_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
         vbs_device_t &d = g_devices[g_ndev];
         memset(&d, 0, sizeof(d));
         snprintf(d.name, sizeof(d.name), "%s", pr.name);
@@ -432,7 +432,7 @@ static bool ops_dispatch_primitive(vbs_device_t *dev, void *pipeline, const vbs_
             ok = ok && pos < mc;
             if (ok)
                 e = cache_store_launch(static_cast<const float *>(k), static_cast<const float *>(v), static_cast<uint16_t *>(kc),
-                                       static_cast<uint16_t *>(vc), pos, nullptr, layer, mc, kvd, 0);
+                                       static_cast<uint16_t *>(vc), pos, nullptr, layer, mc, kvd, kvd, false, 0);
             break;
         }
         case VBS_OP_ATTENTION: {   // B q, B kc, B vc, B out, S seq_len, S layer, S max_ctx, S nqh, S nkh, S hd, S scale

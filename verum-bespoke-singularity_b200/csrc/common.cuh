@@ -231,6 +231,29 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &a0, uint32_t &a
                  : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr));
 }
 
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr));
+}
+
+// C += A(16x16 f16) * B(16x8 f16), fp32 accumulators.
+__device__ __forceinline__ void mma_f16_acc(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 16-byte global -> shared copy; src_bytes < 16 fills the rest with zeros
+// (0: nothing is read, the destination is zeroed).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes = 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // D = A(16x32, unsigned bytes) * B(32x8, signed bytes), int32, no accumulate-in.
 __device__ __forceinline__ void mma_u8s8(const uint32_t a[4], uint32_t b0, uint32_t b1, int c[4]) {
     asm volatile(

@@ -69,6 +69,7 @@ struct vbs_cu_decoder {
     uint32_t *pinned = nullptr;      // [0..1] ctrl readback
     float *logits_pinned = nullptr;
     void *attn_work = nullptr;
+    void *argmax_work = nullptr;
     uint32_t n_splits = 1;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -152,6 +153,7 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
             p.kc = d->kc; p.vc = d->vc;
             p.ctrl = d->ctrl;
             p.layer = l; p.max_ctx = d->max_ctx; p.kv_dim = nk; p.head_dim = hd;
+            p.kv_head_major = 1;
             p.theta = m.theta;
             if (!cuda_ok(mv_fast_launch(ly.tq, 0, MV_EPI_QKV, p, d->dev->n_sm, st, d->use_pdl, 0), "decode qkv")) return false;
         } else {
@@ -161,7 +163,7 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
             if (!step_matvec(d, ly.tv, ly.wv, xin, d->v, nk, dim, false, ly.attn_norm, nullptr, nullptr)) return false;
             if (!cuda_ok(rope_launch(d->q, 0, d->ctrl, hd, m.n_heads, m.theta, st), "decode rope")) return false;
             if (!cuda_ok(rope_launch(d->k, 0, d->ctrl, hd, m.n_kv_heads, m.theta, st), "decode rope")) return false;
-            if (!cuda_ok(cache_store_launch(d->k, d->v, d->kc, d->vc, 0, d->ctrl, l, d->max_ctx, nk, st), "decode kv store"))
+            if (!cuda_ok(cache_store_launch(d->k, d->v, d->kc, d->vc, 0, d->ctrl, l, d->max_ctx, nk, hd, true, st), "decode kv store"))
                 return false;
         }
         if (pending) { std::swap(xr, xw); pending = nullptr; }
@@ -173,6 +175,7 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
         ap.nqh = m.n_heads; ap.nkh = m.n_kv_heads; ap.hd = hd;
         ap.scale = 1.0f / sqrtf((float)hd);
         ap.batch = 1;
+        ap.head_major = 1;
         ap.work = d->attn_work;
         ap.err = d->dev->err;
         if (!cuda_ok(attn_launch(ap, d->n_splits, st, d->use_pdl), "decode attention")) return false;
@@ -232,7 +235,8 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
     }
     // the embedding of the next step writes d->x: the residual must end in d->x
     (void)xr;
-    return cuda_ok(argmax_launch(lg, d->vocab_full, nullptr, d->ctrl, d->hist, (uint32_t)d->max_ctx + 1, st, d->use_pdl),
+    return cuda_ok(argmax_launch(lg, d->vocab_full, nullptr, d->ctrl, d->hist, (uint32_t)d->max_ctx + 1, d->argmax_work, st,
+                                 d->use_pdl),
                    "decode argmax");
 }
 
@@ -272,7 +276,8 @@ bool enqueue_strict_step(vbs_cu_decoder *d) {
     }
     if (!cuda_ok(strict_rmsnorm_launch(d->x, m.out_norm, d->norm, dim, m.eps, st), "strict norm")) return false;
     if (!mat(m.out_type, static_cast<const uint8_t *>(m.out), d->norm, d->logits, m.vocab, dim, false)) return false;
-    return cuda_ok(argmax_launch(d->logits, m.vocab, nullptr, d->ctrl, d->hist, (uint32_t)d->max_ctx + 1, st, false), "strict argmax");
+    return cuda_ok(argmax_launch(d->logits, m.vocab, nullptr, d->ctrl, d->hist, (uint32_t)d->max_ctx + 1, d->argmax_work, st,
+                                 false), "strict argmax");
 }
 
 bool enqueue_step_raw(vbs_cu_decoder *d) { return d->strict ? enqueue_strict_step(d) : enqueue_fast_step(d); }
@@ -337,6 +342,11 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
     if (!m || !m->n_layers || !m->dim || !m->n_heads || !m->n_kv_heads || !m->head_dim || m->n_heads % m->n_kv_heads ||
         !m->ffn || !m->vocab || !max_ctx || m->head_dim % 2 || !m->embd || !m->out || !m->out_norm)
         return fail("invalid model description", nullptr);
+    // The decoder runs on its own non-blocking stream, which does not order
+    // itself after work on other streams: weights written by kernels or
+    // copies still in flight elsewhere (uploads, on-device synthesis) must be
+    // complete before its first step reads them.
+    if (!cuda_ok(cudaDeviceSynchronize(), "decoder create: pending work")) return fail("device error", nullptr);
     vbs_cu_decoder *d = new vbs_cu_decoder();
     d->m = *m;
     d->flags = flags;
@@ -386,6 +396,8 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
             ok = dmalloc(&d->attn_work, wb, "attention workspace") && cuda_ok(cudaMemset(d->attn_work, 0, wb), "workspace");
         }
     }
+    if (ok) ok = dmalloc(&d->argmax_work, argmax_workspace_bytes(), "argmax workspace") &&
+                 cuda_ok(cudaMemset(d->argmax_work, 0, argmax_workspace_bytes()), "workspace");
     if (ok) ok = cuda_ok(cudaMallocHost((void **)&d->pinned, 64), "pinned") &&
                  cuda_ok(cudaMallocHost((void **)&d->logits_pinned, (size_t)d->vocab_full * 4), "pinned logits");
     if (!ok) return fail("device allocation failed", d);
@@ -412,7 +424,7 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
     if (d->graph) cudaGraphDestroy(d->graph);
     void *bufs[] = {d->x, d->x2, d->q, d->att, d->hid, d->logits, d->logits_full, d->partial, d->norm, d->k, d->v,
                     d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
-                    d->tok_dev, d->attn_work};
+                    d->tok_dev, d->attn_work, d->argmax_work};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->pinned) cudaFreeHost(d->pinned);

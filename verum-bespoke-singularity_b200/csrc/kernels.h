@@ -9,6 +9,19 @@
 
 namespace vbs {
 
+// ---- fp16 KV cache layouts ---------------------------------------------------
+// Position-major (the reference's, src/vbs_host_math.h:150-159):
+//   [layer][position][kv head][head_dim]
+// Head-major (the decoder's own cache): [layer][kv head][position][head_dim],
+// so one KV head's positions are contiguous and a split of the attention
+// streams one run of bytes.
+__host__ __device__ inline uint64_t kv_index(bool head_major, uint32_t layer, uint32_t pos, uint32_t local,
+                                            uint32_t max_ctx, uint32_t kv_dim, uint32_t head_dim) {
+    const uint64_t lbase = (uint64_t)layer * max_ctx * kv_dim;
+    if (!head_major) return lbase + (uint64_t)pos * kv_dim + local;
+    return lbase + ((uint64_t)(local / head_dim) * max_ctx + pos) * head_dim + local % head_dim;
+}
+
 // ---- matvec ----------------------------------------------------------------
 
 enum MvEpi : int {
@@ -37,6 +50,7 @@ struct MvParams {
     uint16_t *kc, *vc;          // full caches; layer offset folded in from layer/max_ctx
     const uint32_t *ctrl;       // ctrl[0] = current position
     uint32_t layer, max_ctx, kv_dim, head_dim;
+    uint32_t kv_head_major;     // cache layout, see KV_HEAD_MAJOR
     float theta;
 };
 
@@ -70,11 +84,14 @@ cudaError_t rope_launch(float *x, uint32_t pos, const uint32_t *ctrl, uint32_t h
 cudaError_t silu_mul_launch(const float *g, const float *u, float *out, uint32_t n, cudaStream_t st);
 cudaError_t add_launch(const float *a, const float *b, float *out, uint32_t n, cudaStream_t st);
 cudaError_t cache_store_launch(const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t pos,
-                               const uint32_t *ctrl, uint32_t layer, uint32_t max_ctx, uint32_t kv_dim, cudaStream_t st);
+                               const uint32_t *ctrl, uint32_t layer, uint32_t max_ctx, uint32_t kv_dim,
+                               uint32_t head_dim, bool head_major, cudaStream_t st);
 
 // Split-KV GQA decode attention. seq_len from `seq_dev` (+1) when non-NULL,
 // else `seq_len`. `work` holds the split partials and merge counters:
 // attn_workspace_bytes() bytes, counters zero on first use (self-resetting).
+// attn_configure() raises the shared-memory limit of the tensor-core kernels
+// on the current device (once per device, outside stream capture).
 struct AttnParams {
     const float *q;
     const uint16_t *kc, *vc;
@@ -85,18 +102,23 @@ struct AttnParams {
     float scale;
     uint32_t batch;
     uint64_t kv_batch_stride;   // elements between sequences' caches
+    uint32_t head_major;        // cache layout (kv_index)
     void *work;
     uint32_t *err;
 };
 size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t batch, uint32_t max_splits);
 uint32_t attn_num_splits(uint32_t seq_len_hint, uint32_t nkh, uint32_t batch, int n_sm);
 cudaError_t attn_launch(const AttnParams &p, uint32_t n_splits, cudaStream_t st, bool pdl);
+cudaError_t attn_configure();
 
 // argmax over n floats (first maximum wins); writes out_token and, when
 // ctrl != NULL, advances ctrl[0] (position) by one, stores the token in
 // ctrl[1] and in hist[new position] when hist != NULL and it fits.
+// `work` (argmax_workspace_bytes(), zeroed once, self-resetting) lets the
+// scan run on several CTAs; NULL runs one CTA.
 cudaError_t argmax_launch(const float *v, uint32_t n, uint32_t *out_token, uint32_t *ctrl, uint32_t *hist,
-                          uint32_t hist_cap, cudaStream_t st, bool pdl);
+                          uint32_t hist_cap, void *work, cudaStream_t st, bool pdl);
+size_t argmax_workspace_bytes();
 
 // ---- strict-parity kernels (vbs_cpu arithmetic) -----------------------------
 cudaError_t strict_quantize_q8_launch(const float *x, uint32_t cols, int8_t *xq, float *qd, cudaStream_t st);

@@ -65,14 +65,6 @@ __device__ __forceinline__ const uint8_t *seg_row_ptr(const MvParams &p, uint32_
     return p.w[2] + (uint64_t)(row - p.seg_end[1]) * p.rb;
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 __device__ __forceinline__ void sts_u8(uint32_t addr, uint8_t v) {
     asm volatile("st.shared.u8 [%0], %1;" ::"r"(addr), "r"((uint32_t)v) : "memory");
 }
@@ -369,9 +361,9 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, boo
             dev_flag_error(p.err, DERR_BAD_ARG);
             return;
         }
-        const uint64_t kvbase = ((uint64_t)p.layer * p.max_ctx + pos) * p.kv_dim;
+        const bool hm = p.kv_head_major != 0;
         if (row >= p.seg_end[1]) {
-            p.vc[kvbase + (row - p.seg_end[1])] = f32_to_f16_kv(va);
+            p.vc[kv_index(hm, p.layer, pos, row - p.seg_end[1], p.max_ctx, p.kv_dim, p.head_dim)] = f32_to_f16_kv(va);
             return;
         }
         const bool is_q = row < p.seg_end[0];
@@ -383,7 +375,7 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, boo
         const float a = (i & 1u) ? other : va, b = (i & 1u) ? va : other;
         const float outv = (i & 1u) ? (a * s + b * c) : (a * c - b * s);
         if (is_q) p.q_out[local] = outv;
-        else p.kc[kvbase + local] = f32_to_f16_kv(outv);
+        else p.kc[kv_index(hm, p.layer, pos, local, p.max_ctx, p.kv_dim, p.head_dim)] = f32_to_f16_kv(outv);
     }
 }
 
