@@ -70,16 +70,20 @@ def profile_kernel(args):
     st = torch.cuda.Stream()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
     if args.profile == "decode":
-        # the full decode step: a 1-token prompt, then --steps graph replays
+        # the full decode step at position --ctx (the cache rows before it
+        # are zeros: same bytes and kernels as a prefilled cache), then
+        # --steps graph replays
         import models
         model = vbs.synth_llama(models.shape_of(models.L8B), models.L8B_TYPES, seed=2024)
-        dec = vbs.Decoder(model, 64)
+        dec = vbs.Decoder(model, args.ctx + args.steps + 8)
         dec.forward([1], logits=False)
+        dec.set_position(args.ctx - 1, 1)
         torch.cuda.synchronize()
         for i in range(args.steps):
             dec.enqueue_steps(1)
         torch.cuda.synchronize()
-        print(json.dumps({"profile": "decode", "kernels_per_step": dec.kernels_per_step, "steps": args.steps}))
+        print(json.dumps({"profile": "decode", "ctx": args.ctx, "kernels_per_step": dec.kernels_per_step,
+                          "steps": args.steps}))
         dec.close()
         return
     if args.profile == "attention":
@@ -375,10 +379,14 @@ def main():
         k_ms = e0.elapsed_time(e1) / shape.n_layers
         alg = FFN_GATE_UP_BYTES + shape.dim * 4 + shape.ffn * 4
         achieved = alg / (k_ms * 1e-3) / 1e9
+        # DRAM bytes of one launch from the committed ncu summary of this
+        # kernel (dram__bytes_read.sum + dram__bytes_write.sum)
         traffic = None
-        tf = ROOT / "profiles" / "ffn_gate_up_q4k_8b.json"
+        tf = ROOT / "profiles" / "mv_fast_kernel_ffn_gate_up_q4k_8b.md"
         if tf.exists():
-            traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+            import re
+            mt = re.search(r"dram_bytes_per_launch:\s*(\d+)", tf.read_text())
+            traffic = int(mt.group(1)) if mt else None
         roof = {"bound": "hbm", "kernel": "mv_fast_kernel<Q4_K,dual,SILU> (norm+gate/up+SiLU)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": alg, "launch_us": round(k_ms * 1e3, 2),

@@ -237,6 +237,7 @@ typedef struct {
 #define VBS_CU_DEC_STRICT   1u   /* vbs_cpu arithmetic (src/vbs_cpu.c:572-639), fp32 KV */
 #define VBS_CU_DEC_NO_GRAPH 2u   /* launch kernel by kernel instead of one CUDA graph */
 #define VBS_CU_DEC_NO_PDL   4u   /* no programmatic dependent launch between kernels */
+#define VBS_CU_DEC_NO_PERSIST 8u /* per-op kernels instead of the persistent one-launch step */
 
 typedef struct vbs_cu_decoder vbs_cu_decoder_t;
 

@@ -66,8 +66,7 @@ def l8b_2layer(gpu, vbs):
     return cfg, vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=99)
 
 
-def test_8b_width_vs_engine_oracle(vbs, orc, l8b_2layer, clean_errors):
-    cfg, dm = l8b_2layer
+def _host_model(orc, cfg, dm):
     host = {}
     for name, t in dm.tensors.items():
         arr = t.cpu().numpy()
@@ -77,23 +76,63 @@ def test_8b_width_vs_engine_oracle(vbs, orc, l8b_2layer, clean_errors):
             base = name.split(".")[-1]
             rows, cols, *_ = models.vbs.shard_spec(name, dm.shape, 0, 1)
             host[name] = (dm.types[base], rows, cols, arr[:rows * orc.row_bytes(dm.types[base], cols)])
-    hm = orc.HostModel(cfg, host)
-    st = orc.OrcState(hm, 64, 1)
-    dec = vbs.Decoder(dm, 64)
+    return orc.HostModel(cfg, host)
+
+
+@pytest.mark.parametrize("path", ["persistent", "per_op"])
+def test_8b_width_vs_engine_oracle(vbs, orc, l8b_2layer, path, clean_errors):
+    """Both fast paths: the one-launch persistent step kernel (default) and
+    the per-op kernels (VBS_CU_DEC_NO_PERSIST)."""
+    cfg, dm = l8b_2layer
+    st = orc.OrcState(_host_model(orc, cfg, dm), 64, 1)
+    dec = vbs.Decoder(dm, 64, 0 if path == "persistent" else vbs.DEC_NO_PERSIST)
+    assert dec.kernels_per_step == (1 if path == "persistent" else 13)
     _teacher_forced(dec, st, [17, 2044, 5, 4000], 2e-3)
     dec.close()
 
 
-def test_graph_pdl_plain_identical(vbs, l8b_2layer, clean_errors):
+@pytest.mark.parametrize("base", [0, 8])
+def test_graph_pdl_plain_identical(vbs, l8b_2layer, base, clean_errors):
+    """Graph replay and direct launches give identical bits, for the
+    persistent step (base 0) and the per-op kernels (base NO_PERSIST)."""
     _, dm = l8b_2layer
     toks = [1, 2, 3, 4, 5, 6]
     outs = []
     for flags in (0, vbs.DEC_NO_PDL, vbs.DEC_NO_GRAPH, vbs.DEC_NO_GRAPH | vbs.DEC_NO_PDL):
-        dec = vbs.Decoder(dm, 32, flags)
+        dec = vbs.Decoder(dm, 32, flags | base)
         outs.append(dec.forward(toks))
         dec.close()
     for o in outs[1:]:
         assert (o.view(np.uint32) == outs[0].view(np.uint32)).all()
+
+
+def test_persistent_matches_per_op_long_context(vbs, l8b_2layer, clean_errors):
+    """300 positions: the persistent kernel's attention runs on several
+    splits per KV head, the new row lands in different stages and warps.
+    Logits at every 50th step agree with the per-op kernels within 1e-3."""
+    _, dm = l8b_2layer
+    toks = models.splitmix_ints(5, 300, 4096)
+    a, b = vbs.Decoder(dm, 512), vbs.Decoder(dm, 512, vbs.DEC_NO_PERSIST)
+    for i in range(0, 300, 50):
+        la, lb = a.forward(toks[i:i + 50]), b.forward(toks[i:i + 50])
+        assert np.abs(la - lb).max() <= 1e-3 * np.abs(lb).max(), i
+    a.close()
+    b.close()
+
+
+HD64 = dict(n_layers=2, dim=1024, n_heads=16, n_kv_heads=4, ffn=2816, vocab=2048, eps=1e-5, theta=10000.0)
+
+
+@pytest.mark.parametrize("wt", ["kquant", "q8_0"])
+def test_head_dim_64_vs_engine_oracle(vbs, orc, gpu, wt, clean_errors):
+    """head_dim 64 and Q8_0 weights through the persistent step kernel."""
+    types = dict(models.L8B_TYPES) if wt == "kquant" else {k: orc.Q8_0 for k in models.L8B_TYPES}
+    dm = vbs.synth_llama(models.shape_of(HD64), types, seed=31)
+    st = orc.OrcState(_host_model(orc, HD64, dm), 64, 1)
+    dec = vbs.Decoder(dm, 64)
+    assert dec.kernels_per_step == 1
+    _teacher_forced(dec, st, [5, 1000, 77, 2047, 3, 3], 2e-3)
+    dec.close()
 
 
 def test_device_greedy_loop_equals_host_loop(vbs, l8b_2layer, clean_errors):

@@ -34,7 +34,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34
 ARG_BUFFER, ARG_SCALAR = 0, 1
 
 MV_ACCUMULATE, MV_PORTABLE = 1, 2
-DEC_STRICT, DEC_NO_GRAPH, DEC_NO_PDL = 1, 2, 4
+DEC_STRICT, DEC_NO_GRAPH, DEC_NO_PDL, DEC_NO_PERSIST = 1, 2, 4, 8
 
 
 class VbsError(RuntimeError):

@@ -108,49 +108,53 @@ __device__ void attn_tail(const AttnParams &p, uint32_t n_splits, float *sh, int
     if (ticket != n_splits - 1) { pdl_launch_dependents(); return; }
     __threadfence();
     const float *parts = work + (size_t)slot * n_splits * part_stride;
-    // split weights w[g][s] = exp2(m_s - M_g), one warp per head
+    // split weights w[g][s] = exp2(m_s - M_g), one warp per head; every
+    // load of a phase is issued before any is used (one L2 round trip each)
     float *wsm = sh;                                  // [ATTN_GS][n_splits]
     float *Lg = sh + ATTN_GS * ATTN_MAX_SPLITS;       // [ATTN_GS]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    static_assert(ATTN_MAX_SPLITS <= 128, "four splits per lane");
     for (uint32_t g = warp; g < G; g += nwarps) {
-        float M = -INFINITY;
-        for (uint32_t s2 = lane; s2 < n_splits; s2 += 32) M = fmaxf(M, __ldcg(parts + s2 * part_stride + g * RS));
-        M = warp_max(M);
-        float L = 0.f;
-        for (uint32_t s2 = lane; s2 < n_splits; s2 += 32) {
+        float ms[4], ls[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t s2 = lane + 32 * k;
             const float *ps = parts + s2 * part_stride + g * RS;
-            const float ms = __ldcg(ps);
-            const float a = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-            wsm[g * n_splits + s2] = a;
-            L += __ldcg(ps + 1) * a;
+            ms[k] = s2 < n_splits ? __ldcg(ps) : -INFINITY;
+            ls[k] = s2 < n_splits ? __ldcg(ps + 1) : 0.f;
+        }
+        const float M = warp_max(fmaxf(fmaxf(ms[0], ms[1]), fmaxf(ms[2], ms[3])));
+        float L = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t s2 = lane + 32 * k;
+            const float a = (ms[k] == -INFINITY) ? 0.f : exp2f(ms[k] - M);
+            if (s2 < n_splits) wsm[g * n_splits + s2] = a;
+            L += ls[k] * a;
         }
         L = warp_sum(L);
         if (lane == 0) Lg[g] = L;
     }
     __syncthreads();
-    // outputs, 4 consecutive dims per thread
+    // outputs, 4 consecutive dims per thread, 16 splits' loads in flight
+    constexpr uint32_t MB = 16;
     for (uint32_t k = threadIdx.x; k < G * HD / 4; k += blockDim.x) {
         const uint32_t g = k / (HD / 4), d = (k % (HD / 4)) * 4;
         const float *src = parts + g * RS + 4 + d;
         const float *wg = wsm + g * n_splits;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        uint32_t s2 = 0;
-        for (; s2 + 4 <= n_splits; s2 += 4) {
-            float4 v[4];
+        for (uint32_t s0 = 0; s0 < n_splits; s0 += MB) {
+            float4 v[MB];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4 *>(src + (s2 + u) * part_stride));
+            for (uint32_t u = 0; u < MB; ++u)
+                v[u] = s0 + u < n_splits ? __ldcg(reinterpret_cast<const float4 *>(src + (s0 + u) * part_stride))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float a = wg[s2 + u];
+            for (uint32_t u = 0; u < MB; ++u) {
+                const float a = s0 + u < n_splits ? wg[s0 + u] : 0.f;
                 acc.x = fmaf(v[u].x, a, acc.x); acc.y = fmaf(v[u].y, a, acc.y);
                 acc.z = fmaf(v[u].z, a, acc.z); acc.w = fmaf(v[u].w, a, acc.w);
             }
-        }
-        for (; s2 < n_splits; ++s2) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(src + s2 * part_stride));
-            const float a = wg[s2];
-            acc.x = fmaf(v.x, a, acc.x); acc.y = fmaf(v.y, a, acc.y);
-            acc.z = fmaf(v.z, a, acc.z); acc.w = fmaf(v.w, a, acc.w);
         }
         const float il = 1.0f / Lg[g];
         *reinterpret_cast<float4 *>(outp + g * HD + d) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);

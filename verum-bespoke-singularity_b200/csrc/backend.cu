@@ -92,7 +92,7 @@ static bool do_init() {
         s.n_sm = pr.multiProcessorCount;
         if (cudaMalloc(&s.err, 256) != cudaSuccess) continue;
         cudaMemset(s.err, 0, 256);
-        if (mv_configure() != cudaSuccess || attn_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
+        if (mv_configure() != cudaSuccess || attn_configure() != cudaSuccess || step_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
         vbs_device_t &d = g_devices[g_ndev];
         memset(&d, 0, sizeof(d));
         snprintf(d.name, sizeof(d.name), "%s", pr.name);

@@ -238,7 +238,7 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &a0, uint3
 
 // C += A(16x16 f16) * B(16x8 f16), fp32 accumulators.
 __device__ __forceinline__ void mma_f16_acc(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));

@@ -70,6 +70,14 @@ struct vbs_cu_decoder {
     float *logits_pinned = nullptr;
     void *attn_work = nullptr;
     void *argmax_work = nullptr;
+    // persistent step kernel (one cooperative launch per token)
+    bool persist = false;
+    StepParams sp = {};
+    StepLayer *step_layers = nullptr;
+    uint8_t *step_packed = nullptr;   // weights repacked into stage units
+    float *step_acc = nullptr;        // accumulation buffers, then the sync words
+    size_t step_acc_bytes = 0;
+    void *step_attn = nullptr;
     uint32_t n_splits = 1;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -82,6 +90,8 @@ namespace {
 bool dmalloc(void **p, size_t bytes, const char *what) {
     return cuda_ok(cudaMalloc(p, bytes ? bytes : 16), what);
 }
+
+bool plan_persistent(vbs_cu_decoder *d);
 
 // Launch one matvec y (+)= W x through the fastest kernel that supports it.
 bool step_matvec(vbs_cu_decoder *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
@@ -118,7 +128,15 @@ bool step_matvec(vbs_cu_decoder *d, int type, const uint8_t *w, const float *x, 
                    "decode matvec");
 }
 
+bool enqueue_persistent_step(vbs_cu_decoder *d) {
+    // every activation is written once per step; only the barrier and ticket words start at zero
+    const size_t sync_bytes = step_sync_words(d->dev->n_sm) * 4;
+    if (!cuda_ok(cudaMemsetAsync(d->sp.sync, 0, sync_bytes, d->st), "step sync words")) return false;
+    return cuda_ok(step_launch(d->sp, d->dev->n_sm, d->st), "decode step kernel");
+}
+
 bool enqueue_fast_step(vbs_cu_decoder *d) {
+    if (d->persist) return enqueue_persistent_step(d);
     const vbs_cu_model_t &m = d->m;
     const uint32_t dim = m.dim, hd = m.head_dim, nq = m.n_heads * hd, nk = d->kv_dim;
     cudaStream_t st = d->st;
@@ -327,6 +345,71 @@ bool put_tokens(vbs_cu_decoder *d, const uint32_t *tokens, size_t n) {
     return cuda_ok(cudaMemcpyAsync(d->tok_dev, tokens, n * 4, cudaMemcpyHostToDevice, d->st), "token upload");
 }
 
+// Chooses the persistent step kernel when the model fits its plan (uniform
+// per-op weight types, head_dim 64/128, one GPU); otherwise the per-op
+// kernels stay in use. Returns false only on an allocation failure.
+bool plan_persistent(vbs_cu_decoder *d) {
+    const vbs_cu_model_t &m = d->m;
+    const Layer &y0 = d->L[0];
+    for (const Layer &y : d->L)
+        if (y.tq != y0.tq || y.tk != y0.tq || y.tv != y0.tq || y.to != y0.to || y.tgate != y0.tgate ||
+            y.tup != y0.tgate || y.tdown != y0.tdown)
+            return true;
+    StepParams &p = d->sp;
+    p = StepParams{};
+    p.n_layers = m.n_layers; p.dim = m.dim; p.nqh = m.n_heads; p.nkh = m.n_kv_heads; p.hd = m.head_dim;
+    p.ffn = m.ffn; p.vocab = m.vocab; p.max_ctx = d->max_ctx;
+    p.eps = m.eps; p.theta = m.theta; p.scale = 1.0f / sqrtf((float)m.head_dim);
+    p.t_embd = m.embd_type; p.t_qkv = y0.tq; p.t_o = y0.to; p.t_gu = y0.tgate; p.t_down = y0.tdown; p.t_out = m.out_type;
+    p.embd = static_cast<const uint8_t *>(m.embd);
+    p.out_norm = m.out_norm;
+    char why[160];
+    if (!step_plan(p, d->dev->n_sm, why, sizeof why)) return true;
+    // repacked weights: per layer QKV | O | GU | DOWN, then the output matrix
+    const size_t bq = step_packed_bytes(p, STEP_QKV), bo = step_packed_bytes(p, STEP_O),
+                 bg = step_packed_bytes(p, STEP_GU), bd = step_packed_bytes(p, STEP_DOWN),
+                 bout = step_packed_bytes(p, STEP_OUT);
+    const size_t per_layer = bq + bo + bg + bd;
+    if (!dmalloc((void **)&d->step_packed, per_layer * m.n_layers + bout, "repacked weights")) return false;
+    std::vector<StepLayer> hl(m.n_layers);
+    for (uint32_t l = 0; l < m.n_layers; ++l) {
+        const Layer &y = d->L[l];
+        uint8_t *base = d->step_packed + per_layer * l;
+        hl[l] = StepLayer{base, base + bq, base + bq + bo, base + bq + bo + bg, y.attn_norm, y.ffn_norm};
+        if (!cuda_ok(step_repack(p, STEP_QKV, y.wq, y.wk, y.wv, base, d->st), "repack") ||
+            !cuda_ok(step_repack(p, STEP_O, y.wo, nullptr, nullptr, base + bq, d->st), "repack") ||
+            !cuda_ok(step_repack(p, STEP_GU, y.wgate, y.wup, nullptr, base + bq + bo, d->st), "repack") ||
+            !cuda_ok(step_repack(p, STEP_DOWN, y.wdown, nullptr, nullptr, base + bq + bo + bg, d->st), "repack"))
+            return false;
+    }
+    uint8_t *pout = d->step_packed + per_layer * m.n_layers;
+    if (!cuda_ok(step_repack(p, STEP_OUT, static_cast<const uint8_t *>(m.out), nullptr, nullptr, pout, d->st), "repack"))
+        return false;
+    p.out = pout;
+    const size_t acc_floats = (size_t)p.n_layers * p.acc_layer;
+    const size_t sync_words = step_sync_words(d->dev->n_sm);
+    d->step_acc_bytes = acc_floats * 4 + sync_words * 4;
+    const size_t aw = step_attn_work_bytes(p);
+    if (!dmalloc((void **)&d->step_layers, hl.size() * sizeof(StepLayer), "step layers") ||
+        !dmalloc((void **)&d->step_acc, d->step_acc_bytes, "step buffers") || !dmalloc(&d->step_attn, aw, "step attention"))
+        return false;
+    if (!cuda_ok(cudaMemcpy(d->step_layers, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice), "step layers") ||
+        !cuda_ok(cudaMemset(d->step_attn, 0, aw), "step attention") ||
+        !cuda_ok(cudaMemset(d->step_acc, 0, d->step_acc_bytes), "step buffers"))
+        return false;
+    p.layers = d->step_layers;
+    p.kc = d->kc; p.vc = d->vc;
+    p.acc = d->step_acc;
+    p.logits = d->logits;
+    p.att = d->att;
+    p.attn_work = d->step_attn;
+    p.sync = reinterpret_cast<uint32_t *>(d->step_acc + acc_floats);
+    p.ctrl = d->ctrl; p.hist = d->hist; p.hist_cap = d->max_ctx + 1;
+    p.err = d->dev->err;
+    d->persist = true;
+    return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -390,6 +473,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
              dmalloc((void **)&d->xq, big, "xq") && dmalloc((void **)&d->qd, (big / 32 + 1) * 4, "qd");
     } else if (ok) {
         ok = dmalloc((void **)&d->kc, cache_elems * 2, "kv cache") && dmalloc((void **)&d->vc, cache_elems * 2, "kv cache");
+        if (ok && !(flags & VBS_CU_DEC_NO_PERSIST) && d->tp_world == 1) ok = plan_persistent(d);
         if (ok) {
             d->n_splits = attn_num_splits(max_ctx, m->n_kv_heads, 1, dev->n_sm);
             const size_t wb = attn_workspace_bytes(m->n_heads, m->n_kv_heads, m->head_dim, 1, d->n_splits);
@@ -407,12 +491,14 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
     }
     cudaMemsetAsync(d->ctrl, 0, 64, d->st);
     cudaMemsetAsync(d->x, 0, m->dim * 4, d->st);
-    if (d->use_graph) {
-        if (!build_graph(d)) return fail("decode graph build failed", d);
-    } else {
-        // count kernels per step by recording one step's launches without running it
-        d->kernels_per_step = 0;
+    if (d->use_graph && !build_graph(d)) {
+        if (!d->persist) return fail("decode graph build failed", d);
+        // a cooperative launch that cannot be captured: launch the step directly
+        cudaGetLastError();
+        vbs_cu_clear_error();
+        d->use_graph = false;
     }
+    if (!d->use_graph) d->kernels_per_step = d->persist ? 1 : 0;
     if (!sync_and_check(d)) return fail("decoder initialisation failed", d);
     return d;
 }
@@ -424,7 +510,7 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
     if (d->graph) cudaGraphDestroy(d->graph);
     void *bufs[] = {d->x, d->x2, d->q, d->att, d->hid, d->logits, d->logits_full, d->partial, d->norm, d->k, d->v,
                     d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
-                    d->tok_dev, d->attn_work, d->argmax_work};
+                    d->tok_dev, d->attn_work, d->argmax_work, d->step_layers, d->step_acc, d->step_attn, d->step_packed};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->pinned) cudaFreeHost(d->pinned);

@@ -120,6 +120,74 @@ cudaError_t argmax_launch(const float *v, uint32_t n, uint32_t *out_token, uint3
                           uint32_t hist_cap, void *work, cudaStream_t st, bool pdl);
 size_t argmax_workspace_bytes();
 
+// ---- persistent decode step (step.cu) -----------------------------------------
+// One cooperative launch per token runs every op of the step; see step.cu.
+
+// Per-layer weights of the step kernel, repacked by step_repack into stage
+// units: unit (tile, chunk) = 16 slot rows x rs bytes, one contiguous run, so
+// the kernel moves a whole stage with one bulk copy.
+struct StepLayer {
+    const uint8_t *qkv, *o, *gu, *down;
+    const float *attn_norm, *ffn_norm;
+};
+
+struct StepMvGeom {
+    uint32_t ck;       // columns per stage chunk
+    uint32_t rs;       // row slot stride in the stage (bytes)
+    uint32_t nch;      // chunks per row
+    uint32_t ntiles;   // 16-row tiles
+};
+
+enum : int { STEP_QKV = 0, STEP_O = 1, STEP_GU = 2, STEP_DOWN = 3, STEP_OUT = 4 };
+
+struct StepParams {
+    uint32_t n_layers, dim, nqh, nkh, hd, ffn, vocab, max_ctx;
+    float eps, theta, scale;
+    int t_embd, t_qkv, t_o, t_gu, t_down, t_out;
+    const uint8_t *embd;        // embedding table, GGUF layout
+    const uint8_t *out;         // output matrix, repacked (step_repack)
+    const float *out_norm;
+    const StepLayer *layers;    // device array [n_layers]
+    uint16_t *kc, *vc;          // fp16 KV cache, head-major, 16-byte chunks swizzled by position (kv_index_swz)
+    float *acc;                 // per layer [q|k|v | o_proj | h | down partials per column chunk]
+    uint64_t acc_layer;         // floats per layer in `acc`
+    float *logits;              // [vocab]
+    float *att;                 // [nqh * hd]
+    void *attn_work;            // split partials
+    uint32_t attn_splits;       // at most this many splits per KV head (nkh * attn_splits <= grid)
+    uint32_t *sync;             // zeroed before each step: grid barrier, abort word, tickets, argmax slots
+    uint32_t *ctrl, *hist;
+    uint32_t hist_cap;
+    uint32_t *err;
+    StepMvGeom geo[5];          // by STEP_* op
+    uint32_t slot_bytes, nslots, x_off, xq_off, xf_off, ring_off;   // shared-memory plan
+};
+
+// Element (pos, i) of one layer's KV block in the step kernel's cache:
+// [kv head][position][head_dim] with the 16-byte chunk index of each row
+// XOR-ed with (position & 7), so 8 consecutive rows read at one logical
+// chunk fall in 8 different bank groups.
+__host__ __device__ inline uint64_t kv_index_swz(uint32_t layer, uint32_t pos, uint32_t local, uint32_t max_ctx,
+                                                uint32_t n_kv, uint32_t head_dim) {
+    const uint32_t h = local / head_dim, d = local % head_dim;
+    const uint32_t c = (d >> 3) ^ (pos & 7u);
+    return (((uint64_t)layer * n_kv + h) * max_ctx + pos) * head_dim + (c << 3) + (d & 7u);
+}
+
+// Fills the geometry/shared-memory plan of `p` for a grid of n_sm CTAs;
+// false (with a reason) when the model shape is outside what the step
+// kernel serves.
+bool step_plan(StepParams &p, int n_sm, char *why, size_t cap);
+size_t step_attn_work_bytes(const StepParams &p);
+// Repacked size of op `op`'s matrix, and the repack from GGUF rows: QKV takes
+// w0/w1/w2 = q/k/v, GU w0/w1 = gate/up, the others w0.
+size_t step_packed_bytes(const StepParams &p, int op);
+cudaError_t step_repack(const StepParams &p, int op, const uint8_t *w0, const uint8_t *w1, const uint8_t *w2,
+                        uint8_t *dst, cudaStream_t st);
+size_t step_sync_words(int n_sm);
+cudaError_t step_configure();
+cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st);
+
 // ---- strict-parity kernels (vbs_cpu arithmetic) -----------------------------
 cudaError_t strict_quantize_q8_launch(const float *x, uint32_t cols, int8_t *xq, float *qd, cudaStream_t st);
 cudaError_t strict_matvec_q8_0_launch(const uint8_t *w, uint32_t rows, uint32_t cols, const int8_t *xq,

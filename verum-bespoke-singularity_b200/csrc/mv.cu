@@ -5,13 +5,16 @@
 // in GGUF blocks (Q8_0 34 B / 32, Q4_K 144 B / 256, Q6_K 210 B / 256).
 //
 // Fast kernel (mv_fast_kernel), B200 design:
-//  * One CTA per SM, a balanced slice of rows each. Every warp streams its
-//    own work units (16 rows x one 256-column super-block) from HBM into a
-//    private ring of shared-memory buffers with 16-byte cp.async copies,
-//    several units in flight per warp. (1-D bulk TMA copies of the same row
-//    segments, one per row, were measured here to cap at ~11 GB/s per SM even
-//    with no compute at all; 2-D tensor maps cannot describe Q6_K's 210-byte
-//    blocks, whose rows are only 2-byte aligned.)
+//  * One CTA per SM, a balanced slice of rows each. A producer warp streams
+//    stages of 16 rows (32 for the paired gate/up matrices) x a column chunk
+//    from HBM into a ring of shared-memory stages with 1-D bulk TMA copies
+//    (cp.async.bulk), one copy per row: whole rows when they fit, so each
+//    copy is kilobytes long (short scattered segments were measured to
+//    stream several times slower). Rows land in padded slots (an odd number
+//    of 16-byte units apart) so the consumers' shared loads are
+//    conflict-free; Q6_K/Q8_0 rows are only 2-byte aligned in GGUF, their
+//    unaligned head and tail bytes are copied by the producer lanes.
+//    Full/empty mbarriers, every wait bounded.
 //  * x is quantized once per CTA into shared memory as two int8 levels per
 //    32-element block: x ~= d2 * (254*q1 + q2), |error| <= amax/64516/2
 //    (1.6e-5 of the block maximum). Weights stay in their packed form; the
@@ -30,6 +33,7 @@
 // not, and batches.
 #include "common.cuh"
 #include "kernels.h"
+#include "mv_core.cuh"
 
 #include <algorithm>
 
@@ -47,11 +51,6 @@ constexpr uint32_t MV_SMEM = 227u * 1024u;      // shared memory per CTA (one CT
 // (>= 1024) that keeps NSTAGE >= 3: HBM serves long contiguous row runs
 // several times faster than the short scattered segments a 16 x 256 column
 // unit would read.
-template <int TYPE> struct MvT;
-template <> struct MvT<T_Q4_K> { static constexpr int E = 256, BB = 144; };
-template <> struct MvT<T_Q6_K> { static constexpr int E = 256, BB = 210; };
-template <> struct MvT<T_Q8_0> { static constexpr int E = 32, BB = 34; };
-
 struct MvGeom {
     uint32_t ck;       // columns per chunk (multiple of 256, or all columns)
     uint32_t rs;       // row slot stride in bytes
@@ -63,20 +62,6 @@ __device__ __forceinline__ const uint8_t *seg_row_ptr(const MvParams &p, uint32_
     if (row < p.seg_end[0]) return p.w[0] + (uint64_t)row * p.rb;
     if (row < p.seg_end[1]) return p.w[1] + (uint64_t)(row - p.seg_end[0]) * p.rb;
     return p.w[2] + (uint64_t)(row - p.seg_end[1]) * p.rb;
-}
-
-__device__ __forceinline__ void sts_u8(uint32_t addr, uint8_t v) {
-    asm volatile("st.shared.u8 [%0], %1;" ::"r"(addr), "r"((uint32_t)v) : "memory");
-}
-__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ int lds_s8(uint32_t addr) {
-    int16_t v;
-    asm volatile("ld.shared.s8 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -135,212 +120,7 @@ __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *m
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = v[i] * scale * w8[i];
         }
-        float amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
-        const float d2 = amax * (1.0f / (127.0f * 254.0f));
-        const float d1 = d2 * 254.0f;
-        const float r1 = d1 > 0.0f ? __frcp_rn(d1) : 0.0f, r2 = d2 > 0.0f ? __frcp_rn(d2) : 0.0f;
-        uint32_t q1w[2] = {0u, 0u}, q2w[2] = {0u, 0u};
-        int sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            int a = __float2int_rn(v[i] * r1);
-            a = max(-127, min(127, a));
-            const float res = fmaf(-(float)a, d1, v[i]);
-            int b = __float2int_rn(res * r2);
-            b = max(-127, min(127, b));
-            q1w[i >> 2] |= (uint32_t)(a & 0xFF) << (8 * (i & 3));
-            q2w[i >> 2] |= (uint32_t)(b & 0xFF) << (8 * (i & 3));
-            sum += 254 * a + b;
-        }
-        // this thread holds words 2u and 2u+1 of the block
-        uint8_t *blk = xq + (size_t)J * 64;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const uint32_t w = 2 * u + k;
-            if constexpr (PLAIN) {
-                *reinterpret_cast<uint32_t *>(blk + 4 * w) = q1w[k];
-                *reinterpret_cast<uint32_t *>(blk + 32 + 4 * w) = q2w[k];
-            } else {
-                const uint32_t off = (w & 3) * 8 + (w >> 2) * 4;
-                *reinterpret_cast<uint32_t *>(blk + off) = q1w[k];
-                *reinterpret_cast<uint32_t *>(blk + 32 + off) = q2w[k];
-            }
-        }
-        const int other = __shfl_xor_sync(qmask, sum, 1);   // pairs (0,1) = k<16, (2,3) = k>=16
-        const int half = sum + other;
-        const int half_hi = __shfl_xor_sync(qmask, half, 2);
-        if (u == 0) xf[J] = make_float4(d2, d2 * (float)(half + half_hi), __int_as_float(half), __int_as_float(half_hi));
-    }
-}
-
-// 16 bytes from a shared address that is only 2-byte aligned.
-__device__ __forceinline__ uint4 lds128_any(uint32_t a) {
-    const uint32_t off = a & 3u;
-    if (off == 0) {
-        if ((a & 15u) == 0) return lds_u128(a);
-        return make_uint4(lds_u32(a), lds_u32(a + 4), lds_u32(a + 8), lds_u32(a + 12));
-    }
-    const uint32_t b = a - off, sh = off * 8;
-    const uint32_t w0 = lds_u32(b), w1 = lds_u32(b + 4), w2 = lds_u32(b + 8), w3 = lds_u32(b + 12), w4 = lds_u32(b + 16);
-    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
-                      __funnelshift_r(w3, w4, sh));
-}
-
-// byte k of w as an exact float (magic-number conversion: 2^23 + byte).
-__device__ __forceinline__ float byte_f(uint32_t w, uint32_t k) {
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | k)) - 8388608.0f;
-}
-
-// D += A(16x32, u8) * B(32x8, s8), int32 accumulate in place.
-__device__ __forceinline__ void mma_u8s8_acc(const uint32_t a[4], uint32_t b0, uint32_t b1, int c[4]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void mma_s8s8_acc(const uint32_t a[4], uint32_t b0, uint32_t b1, int c[4]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// ---------------------------------------------------------------------------
-// per-unit compute. One warp, 16 rows (row slots r0s..r0s+15 of the stage
-// at `ms`), one 256-element unit of the chunk starting at chunk-local
-// element `eo` (global element e0, x block J0 = e0/32).
-//
-// Block-diagonal MMA: lane (g, t) = (lane/4, lane%4). Thread column t owns
-// the k-slots 4t..4t+3 and 16+4t..19+4t of every m16n8k32 and fills them
-// with weights of ITS OWN scale group; the B operand is nonzero only in the
-// column pair (2t, 2t+1) = (q1, q2) of that group's x values. One MMA thus
-// forms 4 groups' partial dots at once and every lane ends up holding the
-// integer dots of one group for rows g and g+8 (C accumulates across the
-// MMAs of a group), so the float scale epilogue runs once per (row, group)
-// with no idle lanes. acc[0], acc[1] collect rows g, g+8.
-// ---------------------------------------------------------------------------
-template <int TYPE>
-__device__ __forceinline__ void mv_unit(uint32_t ms, uint32_t RS, uint32_t pad0, uint32_t pad1, uint32_t eo,
-                                        uint32_t J0, uint32_t xq, uint32_t xf, int lane, uint32_t nvalid,
-                                        float acc[2]) {
-    constexpr uint32_t r0s = 0;
-    const int g = lane >> 2, t = lane & 3;
-    const bool bact = t == (g >> 1);       // this lane carries B column g (group g/2)
-    const uint32_t lev = g & 1;           // ... for x level q1 (0) or q2 (1)
-    const uint32_t rowA = ms + (r0s + g) * RS, rowB = rowA + 8 * RS;
-    if constexpr (TYPE == T_Q4_K) {
-        const uint32_t sa = rowA + (eo >> 8) * 144, sb = rowB + (eo >> 8) * 144;
-        const uint4 hA = lds_u128(sa), hB = lds_u128(sb);
-        const uint4 a0 = lds_u128(sa + 16 + 32 * t), a1 = lds_u128(sa + 32 + 32 * t);
-        const uint4 b0 = lds_u128(sb + 16 + 32 * t), b1 = lds_u128(sb + 32 + 32 * t);
-        const uint32_t WA[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const uint32_t WB[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-        const uint32_t bq = xq + (J0 + 2 * (g >> 1)) * 64 + lev * 32;   // slot layout, lo sub-block
-        int clo[4] = {0, 0, 0, 0}, chi[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t alo[4] = {WA[i] & 0x0F0F0F0Fu, WB[i] & 0x0F0F0F0Fu, WA[4 + i] & 0x0F0F0F0Fu, WB[4 + i] & 0x0F0F0F0Fu};
-            const uint32_t ahi[4] = {WA[i] & 0xF0F0F0F0u, WB[i] & 0xF0F0F0F0u, WA[4 + i] & 0xF0F0F0F0u, WB[4 + i] & 0xF0F0F0F0u};
-            uint2 blo = make_uint2(0u, 0u), bhi = make_uint2(0u, 0u);
-            if (bact) {
-                blo = lds_u64(bq + i * 8);
-                bhi = lds_u64(bq + 64 + i * 8);
-            }
-            mma_u8s8_acc(alo, blo.x, blo.y, clo);
-            mma_u8s8_acc(ahi, bhi.x, bhi.y, chi);
-        }
-        // this lane's sub-blocks: 2t (low nibbles) and 2t+1 (high nibbles, x16)
-        const uint4 fl = lds_u128(xf + (J0 + 2 * t) * 16), fh = lds_u128(xf + (J0 + 2 * t + 1) * 16);
-        const uint32_t k0 = (2 * t) & 3, k1 = k0 + 1;
-        float r[2];
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-            const uint4 h = rr ? hB : hA;
-            // packed 6-bit scales/mins of sub-blocks 0-3 and 4-7 (src/vbs_dequant.c:225-233)
-            const uint32_t sc = (t < 2) ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
-            const uint32_t mn = (t < 2) ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
-            const int *c = rr ? clo + 2 : clo;
-            const int *ch = rr ? chi + 2 : chi;
-            const float tl = (float)(c[0] * 254 + c[1]), th = (float)(ch[0] * 254 + ch[1]);
-            const float f = tl * __uint_as_float(fl.x) * byte_f(sc, k0) + th * (__uint_as_float(fh.x) * 0.0625f) * byte_f(sc, k1);
-            const float m = byte_f(mn, k0) * __uint_as_float(fl.y) + byte_f(mn, k1) * __uint_as_float(fh.y);
-            r[rr] = f16f(h.x & 0xFFFFu) * f - f16f(h.x >> 16) * m;
-        }
-        acc[0] += r[0];
-        acc[1] += r[1];
-    } else if constexpr (TYPE == T_Q6_K) {
-        // thread column t <-> (half h, l-half lh); its groups are (h, q, lh), q = 0..3
-        const uint32_t h = t >> 1, lh = t & 1;
-        const uint32_t sa = rowA + pad0 + (eo >> 8) * 210, sb = rowB + pad1 + (eo >> 8) * 210;
-        const uint4 qlA0 = lds128_any(sa + h * 64 + 16 * lh), qlA1 = lds128_any(sa + h * 64 + 32 + 16 * lh);
-        const uint4 qlB0 = lds128_any(sb + h * 64 + 16 * lh), qlB1 = lds128_any(sb + h * 64 + 32 + 16 * lh);
-        const uint4 qhA = lds128_any(sa + 128 + h * 32 + 16 * lh), qhB = lds128_any(sb + 128 + h * 32 + 16 * lh);
-        const uint32_t LA[2][4] = {{qlA0.x, qlA0.y, qlA0.z, qlA0.w}, {qlA1.x, qlA1.y, qlA1.z, qlA1.w}};
-        const uint32_t LB[2][4] = {{qlB0.x, qlB0.y, qlB0.z, qlB0.w}, {qlB1.x, qlB1.y, qlB1.z, qlB1.w}};
-        const uint32_t HA[4] = {qhA.x, qhA.y, qhA.z, qhA.w}, HB[4] = {qhB.x, qhB.y, qhB.z, qhB.w};
-        // B: the lane carrying column g serves thread column tb = g/2 = (hb, lhb)
-        const uint32_t tb = g >> 1, hb = tb >> 1, lhb = tb & 1;
-        float fA = 0.f, fB = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            int c[4] = {0, 0, 0, 0};
-            const uint32_t bq = xq + (J0 + hb * 4 + q) * 64 + lev * 32 + lhb * 16;   // plain layout
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                uint32_t a[4];
-                const int s = 4 * (q >> 1), hs = 2 * q;
-                a[0] = ((LA[q & 1][2 * i] >> s) & 0x0F0F0F0Fu) | (((HA[2 * i] >> hs) & 0x03030303u) << 4);
-                a[1] = ((LB[q & 1][2 * i] >> s) & 0x0F0F0F0Fu) | (((HB[2 * i] >> hs) & 0x03030303u) << 4);
-                a[2] = ((LA[q & 1][2 * i + 1] >> s) & 0x0F0F0F0Fu) | (((HA[2 * i + 1] >> hs) & 0x03030303u) << 4);
-                a[3] = ((LB[q & 1][2 * i + 1] >> s) & 0x0F0F0F0Fu) | (((HB[2 * i + 1] >> hs) & 0x03030303u) << 4);
-                uint2 b = make_uint2(0u, 0u);
-                if (bact) b = lds_u64(bq + i * 8);
-                mma_u8s8_acc(a, b.x, b.y, c);
-            }
-            // this lane's group (h, q, lh): x block J0 + 4h + q, k-half lh
-            const uint4 fx = lds_u128(xf + (J0 + h * 4 + q) * 16);
-            const int sq = lh ? (int)fx.w : (int)fx.z;
-            const uint32_t gi = h * 8 + q * 2 + lh;
-            const float xd = __uint_as_float(fx.x);
-            fA = fmaf((float)(c[0] * 254 + c[1] - 32 * sq) * xd, (float)lds_s8(sa + 192 + gi), fA);
-            fB = fmaf((float)(c[2] * 254 + c[3] - 32 * sq) * xd, (float)lds_s8(sb + 192 + gi), fB);
-        }
-        acc[0] += f16f(lds_u16(sa + 208)) * fA;
-        acc[1] += f16f(lds_u16(sb + 208)) * fB;
-    } else {  // Q8_0: eight 34-byte blocks; thread column t owns blocks t and t+4
-        const uint32_t blk0 = eo >> 5;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const uint32_t bi = (uint32_t)t + 4 * k;          // this lane's block
-            const uint32_t bb = (uint32_t)(g >> 1) + 4 * k;   // block whose B column this lane carries
-            const bool mine = bi * 32 < nvalid, bvalid = bb * 32 < nvalid;
-            const uint32_t sa = rowA + pad0 + (blk0 + bi) * 34, sb = rowB + pad1 + (blk0 + bi) * 34;
-            uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
-            if (mine) {
-                a0 = lds128_any(sa + 2); a1 = lds128_any(sa + 18);
-                b0 = lds128_any(sb + 2); b1 = lds128_any(sb + 18);
-            }
-            const uint32_t WA[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            const uint32_t WB[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-            const uint32_t bq = xq + (J0 + bb) * 64 + lev * 32;
-            int c[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t a[4] = {WA[i], WB[i], WA[4 + i], WB[4 + i]};
-                uint2 b = make_uint2(0u, 0u);
-                if (bact && bvalid) b = lds_u64(bq + i * 8);
-                mma_s8s8_acc(a, b.x, b.y, c);
-            }
-            if (mine) {
-                const float xd = __uint_as_float(lds_u32(xf + (J0 + bi) * 16));
-                acc[0] = fmaf((float)(c[0] * 254 + c[1]), f16f(lds_u16(sa)) * xd, acc[0]);
-                acc[1] = fmaf((float)(c[2] * 254 + c[3]), f16f(lds_u16(sb)) * xd, acc[1]);
-            }
-        }
+        quant_block8<PLAIN>(v, u, qmask, J, xq, xf);
     }
 }
 
@@ -396,8 +176,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 256 + 60 * 4);
     float *red = reinterpret_cast<float *>(smem + 512);   // [2][8 warps][16 rows]
     uint8_t *xq = smem + MV_HDR;
-    float4 *xf = reinterpret_cast<float4 *>(xq + (size_t)nsub * 64);
-    const uint32_t xq_a = sbase + MV_HDR, xf_a = xq_a + nsub * 64;
+    float4 *xf = reinterpret_cast<float4 *>(xq + (size_t)nsub * XQ_MAX_STRIDE);
+    const uint32_t xq_a = sbase + MV_HDR, xf_a = xq_a + nsub * XQ_MAX_STRIDE;
     const uint32_t stage_bytes = SLOTS * RS;
     auto full_bar = [&](uint32_t s) { return sbase + 8u * s; };
     auto empty_bar = [&](uint32_t s) { return sbase + 8u * (MV_MAXST + s); };
@@ -555,7 +335,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
 // full rows fit next to the x buffer, else 256-column multiples.
 template <int TYPE> static MvGeom mv_geom(uint32_t cols, int dual) {
     MvGeom g = {};
-    g.stage0 = (MV_HDR + (cols / 32) * 80 + 1023u) & ~1023u;
+    g.stage0 = (MV_HDR + (cols / 32) * (XQ_MAX_STRIDE + 16) + 1023u) & ~1023u;
     const uint32_t slots = dual ? 32u : 16u;
     const uint32_t avail = MV_SMEM > g.stage0 ? MV_SMEM - g.stage0 : 0;
     auto rs_for = [](uint32_t ck) {

@@ -1,0 +1,1085 @@
+// step.cu -- the whole decode step as one persistent kernel.
+//
+// The op chain of a token (the reference's forward_token,
+// src/vbs_specializer.c:270-349) is, per layer,
+//   QKV   RMSNorm(attn_norm) + Q/K/V matvec
+//   ATTN  RoPE + fp16 KV store + split-KV GQA attention
+//   O     o_proj matvec
+//   GU    residual add + RMSNorm(ffn_norm) + gate/up matvecs
+//   DOWN  SiLU(gate)*up + down matvec
+// then the residual add + RMSNorm(output_norm) + output matvec, and the
+// greedy argmax. Launched as one kernel per op, every op pays a launch, a
+// prologue and a pipeline fill and drain; on the small per-layer matrices
+// that is as long as streaming their weights. Here one cooperative launch of
+// one CTA per SM runs every op:
+//
+//  * A producer warp per CTA walks the same op list as the consumers and
+//    streams the CTA's share of every op's weights (and of the KV cache
+//    rows older than the current position) into a shared-memory ring with
+//    1-D bulk TMA copies. Weights do not depend on activations, so it runs
+//    ahead across op boundaries: while the consumers wait at a grid barrier
+//    the next op's weights are already landing. The ring's empty/full
+//    mbarriers are the only thing that paces it.
+//  * Eight consumer warps run the ops. Between ops a grid barrier (one
+//    counter in global memory, acquire/release, bounded spin) orders the
+//    activations. Matvec units are (16-row tile x column chunk), split into
+//    equal contiguous ranges per CTA; a row's partial dot products go to a
+//    zeroed fp32 buffer with atomicAdd. The plan guarantees at most two
+//    contributions per row, and fp32 addition is commutative, so the sums
+//    are deterministic.
+//  * What follows a matvec in the reference (residual add, RMSNorm, SiLU,
+//    RoPE) is applied by the NEXT op as it reads the complete sums: every
+//    CTA keeps its own copy of the residual stream x in shared memory and
+//    updates it identically, so no extra pass or barrier is needed.
+//  * Attention units are (KV head, split). The split that holds the current
+//    position applies RoPE to the new key, stores the new K/V row (fp16, the
+//    engine's rounding) into the cache and patches it into its staged copy.
+//    q.K and p.V run on mma.sync m16n8k16 with f16 hi/lo operand splits
+//    (fp32-accurate); the last CTA of a KV head merges the splits.
+//  * The argmax runs on slices per CTA; the last CTA advances the position
+//    and token in the device control block.
+//
+// Every wait is bounded (2 s of %globaltimer). A timeout sets an abort word
+// that every other wait polls, records the error and unwinds the kernel.
+#include "common.cuh"
+#include "kernels.h"
+#include "mv_core.cuh"
+
+#include <algorithm>
+#include <cstdio>
+
+namespace vbs {
+
+constexpr int SK_NCW = 8;                          // consumer warps (warpgroups 0 and 1)
+constexpr int SK_CT = SK_NCW * 32;                 // consumer threads
+constexpr int SK_THREADS = SK_CT + 128;            // + the producer warpgroup (one warp issues)
+// Register split: launched at 168 per thread (384 x 168 = 64512), the
+// producer warpgroup gives back to 40 and the consumers take 232:
+// 256 x 232 + 128 x 40 = 64512, exactly the launch total.
+constexpr uint32_t SK_REG_LAUNCH = 168, SK_REG_CONSUMER = 232, SK_REG_PRODUCER = 40;
+static_assert(SK_CT * SK_REG_CONSUMER + 128 * SK_REG_PRODUCER <= SK_THREADS * SK_REG_LAUNCH, "register split");
+constexpr uint32_t SK_MAXSLOT = 16;
+constexpr uint32_t SK_HDR = 4096;                  // barriers, flags, reduction scratch
+constexpr uint32_t SK_SMEM = 227u * 1024u;
+constexpr uint32_t SK_AP = 64;                     // attention positions per stage
+constexpr uint32_t SK_MAX_SPLITS = 128;
+constexpr int SK_GS = 8;                           // query-head slots per KV head
+constexpr float SK_LAZY = 8.0f;                    // softmax rescale threshold (log2 units)
+// sync words: [0] grid barrier, [1] abort, [2] argmax ticket,
+// [16 + h] attention merge ticket of KV head h, [SK_SLOTS + 2c] argmax slots
+constexpr uint32_t SK_TICKET0 = 16, SK_MAX_KV = 112, SK_SLOTS = SK_TICKET0 + SK_MAX_KV;
+
+enum : int { K_QKV = 0, K_ATTN = 1, K_O = 2, K_GU = 3, K_DOWN = 4, K_OUT = 5, K_ARGMAX = 6 };
+
+__host__ __device__ inline int sk_kind(uint32_t i, uint32_t L, uint32_t &layer) {
+    if (i < 5 * L) { layer = i / 5; return (int)(i % 5); }
+    layer = L - 1;
+    return i == 5 * L ? K_OUT : K_ARGMAX;
+}
+
+// ---------------------------------------------------------------------------
+// op descriptors
+// ---------------------------------------------------------------------------
+struct SkMv {
+    int type;
+    int gu;                 // gate/up: slot rows 0-7 gate, 8-15 up (tiles of 8 rows); writes h
+    int chunk_major;        // units ordered chunk by chunk (a CTA spans one or two column chunks)
+    const uint8_t *packed;  // stage units, (tile, chunk) at (tile * nch + chunk) * 16 * rs
+    uint32_t rows, cols;
+    float *out;             // chunk c's sums at out + c * rows (one writer per element)
+    StepMvGeom g;
+};
+
+// Tile and chunk of this op's unit u.
+__device__ __forceinline__ void sk_unit(const SkMv &d, uint32_t u, uint32_t &tile, uint32_t &ch) {
+    if (d.chunk_major) { ch = u / d.g.ntiles; tile = u % d.g.ntiles; }
+    else { tile = u / d.g.nch; ch = u % d.g.nch; }
+}
+
+__device__ __forceinline__ float *sk_acc(const StepParams &p, uint32_t l) { return p.acc + (uint64_t)l * p.acc_layer; }
+__device__ __forceinline__ uint32_t sk_qkv_rows(const StepParams &p) { return (p.nqh + 2 * p.nkh) * p.hd; }
+// Per-layer activations: [q|k|v sums] [o_proj] [h = SiLU(gate)*up] [down,
+// one plane of dim partial sums per column chunk]
+__device__ __forceinline__ float *sk_acc_o(const StepParams &p, uint32_t l) { return sk_acc(p, l) + sk_qkv_rows(p); }
+__device__ __forceinline__ float *sk_acc_h(const StepParams &p, uint32_t l) { return sk_acc_o(p, l) + p.dim; }
+__device__ __forceinline__ float *sk_acc_down(const StepParams &p, uint32_t l) { return sk_acc_h(p, l) + p.ffn; }
+__device__ __forceinline__ float *sk_logits(const StepParams &p) { return p.logits; }
+
+__device__ __forceinline__ SkMv sk_mv_desc(const StepParams &p, int kind, uint32_t l) {
+    SkMv d = {};
+    const uint32_t qd = p.nqh * p.hd, kvd = p.nkh * p.hd;
+    const StepLayer &L = p.layers[kind == K_OUT ? 0 : l];
+    switch (kind) {
+        case K_QKV:
+            d.type = p.t_qkv; d.packed = L.qkv;
+            d.rows = qd + 2 * kvd; d.cols = p.dim; d.out = sk_acc(p, l); d.g = p.geo[STEP_QKV];
+            break;
+        case K_O:
+            d.type = p.t_o; d.packed = L.o;
+            d.rows = p.dim; d.cols = qd; d.out = sk_acc_o(p, l); d.g = p.geo[STEP_O];
+            break;
+        case K_GU:
+            d.type = p.t_gu; d.gu = 1; d.packed = L.gu;
+            d.rows = p.ffn; d.cols = p.dim; d.out = sk_acc_h(p, l); d.g = p.geo[STEP_GU];
+            break;
+        case K_DOWN:
+            d.type = p.t_down; d.packed = L.down; d.chunk_major = 1;
+            d.rows = p.dim; d.cols = p.ffn; d.out = sk_acc_down(p, l); d.g = p.geo[STEP_DOWN];
+            break;
+        default:   // K_OUT
+            d.type = p.t_out; d.packed = p.out;
+            d.rows = p.vocab; d.cols = p.dim; d.out = sk_logits(p); d.g = p.geo[STEP_OUT];
+            break;
+    }
+    return d;
+}
+
+// Output row held by stage slot r (0..15) of tile `tile`. Gate/up tiles hold
+// 8 rows of each matrix: slot r < 8 is gate row tile*8 + r, slot r >= 8 the
+// up row tile*8 + r - 8.
+__host__ __device__ __forceinline__ uint32_t sk_slot_row(bool gu, uint32_t tile, uint32_t r) {
+    return gu ? tile * 8 + (r & 7u) : tile * 16 + r;
+}
+
+// This CTA's contiguous share [u0, u1) of U units.
+__device__ __forceinline__ void sk_range(uint32_t U, uint32_t &u0, uint32_t &u1) {
+    u0 = (uint32_t)(((uint64_t)blockIdx.x * U) / gridDim.x);
+    u1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * U) / gridDim.x);
+}
+
+struct SkAttn {
+    uint32_t S, h, split, t0, t1, nst;
+    bool has;
+};
+
+// Attention unit of this CTA: KV head h, split `split` of S over [0, seq).
+__device__ __forceinline__ SkAttn sk_attn_unit(const StepParams &p, uint32_t seq) {
+    SkAttn a;
+    a.S = max(1u, min(p.attn_splits, (seq + SK_AP - 1) / SK_AP));
+    const uint32_t c = blockIdx.x;
+    a.has = c < p.nkh * a.S;
+    a.h = a.has ? c / a.S : 0;
+    a.split = a.has ? c % a.S : 0;
+    uint32_t per = (seq + a.S - 1) / a.S;
+    per = (per + SK_AP - 1) / SK_AP * SK_AP;
+    a.t0 = min(seq, a.split * per);
+    a.t1 = min(seq, a.t0 + per);
+    a.nst = a.has ? (a.t1 - a.t0 + SK_AP - 1) / SK_AP : 0;
+    return a;
+}
+
+// ---------------------------------------------------------------------------
+// waits
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// mbarrier phase wait, bounded, giving up early when the grid aborts.
+__device__ __forceinline__ bool sk_wait(uint32_t bar, uint32_t parity, const uint32_t *gabort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0 && (*reinterpret_cast<const volatile uint32_t *>(gabort) || global_ns() - t0 > kWaitNs))
+            return false;
+    }
+}
+
+// Generic-proxy writes to a ring slot (byte copies, zero fill, the patched
+// row) must be ordered before the TMA (async proxy) writes that later reuse
+// the slot.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void sk_abort(const StepParams &p, uint32_t code) {
+    atomicExch(&p.sync[1], 1u);
+    dev_flag_error(p.err, code);
+}
+
+// Grid barrier among the consumer warps of all CTAs: arrive, then wait for
+// `target` arrivals. Returns false, the same value in every consumer thread
+// of the CTA, when this CTA or the grid aborted: thread 0 decides after the
+// first CTA barrier and the second one publishes its decision.
+__device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t target, volatile int *flag,
+                                             volatile int *cta_abort) {
+    named_bar_sync(1, SK_CT);
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(&p.sync[0], 1u);
+        bool ok = *cta_abort == 0;
+        const uint64_t t0 = global_ns();
+        for (uint32_t it = 1; ok && ld_acquire_gpu(&p.sync[0]) < target; ++it) {
+            __nanosleep(32);
+            if ((it & 15u) == 0) {
+                if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
+                if (global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
+            }
+        }
+        __threadfence();
+        *flag = ok ? 1 : 0;
+    }
+    named_bar_sync(1, SK_CT);
+    return *flag != 0;
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory map
+// ---------------------------------------------------------------------------
+struct SkSmem {
+    uint32_t base;                 // shared address of the dynamic buffer
+    uint8_t *ptr;
+    uint32_t ring, slot_bytes, nslots;
+    __device__ uint32_t full(uint32_t s) const { return base + 8u * s; }
+    __device__ uint32_t empty(uint32_t s) const { return base + 8u * (SK_MAXSLOT + s); }
+    __device__ uint32_t slot(uint32_t s) const { return ring + s * slot_bytes; }
+    __device__ volatile int *abort_flag() const { return reinterpret_cast<volatile int *>(ptr + 256); }
+    __device__ volatile int *sync_flag() const { return reinterpret_cast<volatile int *>(ptr + 260); }
+    __device__ uint32_t *scratch_u() const { return reinterpret_cast<uint32_t *>(ptr + 512); }   // 64 words
+    __device__ float *misc() const { return reinterpret_cast<float *>(ptr + 1024); }            // 256 floats
+    __device__ float *red() const { return reinterpret_cast<float *>(ptr + 2048); }             // [2][8][16]
+};
+
+struct SkRing {
+    uint32_t slot = 0, round = 0;
+    __device__ void advance(uint32_t nslots) {
+        if (++slot == nslots) { slot = 0; ++round; }
+    }
+};
+
+// ---------------------------------------------------------------------------
+// producer
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S, uint32_t seq) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t nops = 5 * p.n_layers + 2;
+    SkRing r;
+    uint32_t issued = 0;
+    bool ok = true;
+    auto acquire = [&]() -> bool {
+        if (issued < S.nslots) return true;
+        if (sk_wait(S.empty(r.slot), (r.round - 1) & 1, p.sync + 1)) return true;
+        if (lane == 0) sk_abort(p, DERR_TIMEOUT_EMPTY);
+        return false;
+    };
+    for (uint32_t i = 0; i < nops && ok; ++i) {
+        uint32_t l;
+        const int kind = sk_kind(i, p.n_layers, l);
+        if (kind == K_ARGMAX) continue;
+        if (kind == K_ATTN) {
+            const SkAttn a = sk_attn_unit(p, seq);
+            const uint64_t hb = (((uint64_t)l * p.nkh + a.h) * p.max_ctx) * p.hd;
+            const uint32_t rowb = p.hd * 2;
+            for (uint32_t s = 0; s < a.nst; ++s) {
+                if (!acquire()) { ok = false; break; }
+                const uint32_t t = a.t0 + s * SK_AP, len = min(SK_AP, a.t1 - t), bytes = len * rowb;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(S.full(r.slot), 2 * bytes);
+                    bulk_g2s(S.slot(r.slot), p.kc + hb + (uint64_t)t * p.hd, bytes, S.full(r.slot));
+                    bulk_g2s(S.slot(r.slot) + SK_AP * rowb, p.vc + hb + (uint64_t)t * p.hd, bytes, S.full(r.slot));
+                }
+                __syncwarp();
+                ++issued;
+                r.advance(S.nslots);
+            }
+            continue;
+        }
+        const SkMv d = sk_mv_desc(p, kind, l);
+        const uint32_t bytes = 16u * d.g.rs;
+        uint32_t u0, u1;
+        sk_range(d.g.ntiles * d.g.nch, u0, u1);
+        for (uint32_t u = u0; u < u1; ++u) {
+            if (!acquire()) { ok = false; break; }
+            uint32_t tile, ch;
+            sk_unit(d, u, tile, ch);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(S.full(r.slot), bytes);
+                bulk_g2s(S.slot(r.slot), d.packed + (uint64_t)(tile * d.g.nch + ch) * bytes, bytes, S.full(r.slot));
+            }
+            __syncwarp();
+            ++issued;
+            r.advance(S.nslots);
+        }
+    }
+    if (!ok) {
+        // wait (bounded) for copies still in flight before the CTA may exit
+        const uint32_t first = issued > S.nslots ? issued - S.nslots : 0;
+        for (uint32_t s = first; s < issued; ++s) mbar_wait_bounded(S.full(s % S.nslots), (s / S.nslots) & 1, kWaitNs);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// consumer prologues: the quantized input vector of a matvec op. Thread
+// (quad q = tid/4, quarter u = tid%4) owns elements 8u..8u+7 of the 32-value
+// blocks q, q+64, q+128, ...: the layout quant_block8 consumes, so values stay
+// in registers from the load to the quantizer. All loads of a prologue are
+// issued before the first is used: while the weight stream saturates the
+// memory system every dependent round trip costs microseconds.
+// ---------------------------------------------------------------------------
+constexpr int SK_PB = 2;        // blocks per thread in the norm prologue (dim <= 4096)
+
+__device__ __forceinline__ void ld8_cg(const float *src, float v[8]) {
+    const float4 a = __ldcg(reinterpret_cast<const float4 *>(src)), b = __ldcg(reinterpret_cast<const float4 *>(src + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void ld8_g(const float *src, float v[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(src)), b = __ldg(reinterpret_cast<const float4 *>(src + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void sk_quant(int type, const float v[8], uint32_t u, uint32_t qmask, uint32_t J, uint8_t *xq,
+                                         float4 *xf) {
+    if (type == T_Q6_K) quant_block8<true>(v, u, qmask, J, xq, xf);
+    else quant_block8<false>(v, u, qmask, J, xq, xf);
+}
+
+// Residual update x += add (or x = the embedding row when add is NULL,
+// src/vbs_host_math.h:136-142), RMSNorm (src/vbs_host_math.h:28-36) with
+// weight nw, and, when `quant`, the quantized normalized vector.
+constexpr int SK_MAXPL = 4;      // partial planes summed by the norm prologue
+
+__device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSmem &S, float *x, const float *add,
+                                                 uint32_t nadd, const float *nw, uint32_t token, bool quant, int type,
+                                                 uint8_t *xq, float4 *xf) {
+    const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = p.dim / 32;
+    const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
+    float xv[SK_PB][8], wv[SK_PB][8];
+    // add = nadd planes of dim partial sums, summed in plane order
+#pragma unroll
+    for (int r = 0; r < SK_PB; ++r) {
+        const uint32_t J = q + r * (SK_CT / 4);
+        if (J < nsub) {
+            const uint32_t e = J * 32 + 8 * u;
+            ld8_g(nw + e, wv[r]);
+            if (add) {
+                float pv[SK_MAXPL][8];
+#pragma unroll
+                for (int c = 0; c < SK_MAXPL; ++c)
+                    if ((uint32_t)c < nadd) ld8_cg(add + (uint64_t)c * p.dim + e, pv[c]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) xv[r][k] = pv[0][k];
+#pragma unroll
+                for (int c = 1; c < SK_MAXPL; ++c)
+                    if ((uint32_t)c < nadd)
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) xv[r][k] += pv[c][k];
+            }
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int r = 0; r < SK_PB; ++r) {
+        const uint32_t J = q + r * (SK_CT / 4);
+        if (J >= nsub) continue;
+        const uint32_t e = J * 32 + 8 * u;
+        float4 *xs = reinterpret_cast<float4 *>(x + e);
+        if (add) {
+            const float4 o0 = xs[0], o1 = xs[1];
+            xv[r][0] += o0.x; xv[r][1] += o0.y; xv[r][2] += o0.z; xv[r][3] += o0.w;
+            xv[r][4] += o1.x; xv[r][5] += o1.y; xv[r][6] += o1.z; xv[r][7] += o1.w;
+        } else {
+            const uint32_t E = (uint32_t)block_elems(p.t_embd), BB = (uint32_t)block_bytes(p.t_embd);
+            const uint8_t *row = p.embd + (uint64_t)token * row_bytes(p.t_embd, p.dim);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) xv[r][k] = dq_elem(p.t_embd, row + ((e + k) / E) * BB, (int)((e + k) % E));
+        }
+        xs[0] = make_float4(xv[r][0], xv[r][1], xv[r][2], xv[r][3]);
+        xs[1] = make_float4(xv[r][4], xv[r][5], xv[r][6], xv[r][7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss = fmaf(xv[r][k], xv[r][k], ss);
+    }
+    ss = warp_sum(ss);
+    float *misc = S.misc();
+    if ((ctid & 31u) == 0) misc[ctid >> 5] = ss;
+    named_bar_sync(1, SK_CT);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < SK_NCW; ++w) tot += misc[w];
+    const float scale = 1.0f / sqrtf(tot / (float)p.dim + p.eps);
+    if (!quant) return;
+#pragma unroll
+    for (int r = 0; r < SK_PB; ++r) {
+        const uint32_t J = q + r * (SK_CT / 4);
+        if (J >= nsub) continue;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = xv[r][k] * scale * wv[r][k];
+        sk_quant(type, v, u, qmask, J, xq, xf);
+    }
+}
+
+// Quantizes n values, load8(e, v) yielding elements e..e+7; NB blocks per
+// thread per batch, every load of a batch issued before any is used.
+template <int NB, class F>
+__device__ __forceinline__ void sk_prologue_vec(uint32_t n, int type, F load8, uint8_t *xq, float4 *xf) {
+    const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = n / 32;
+    const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
+    for (uint32_t J0 = q; J0 < nsub; J0 += NB * (SK_CT / 4)) {
+        float v[NB][8];
+#pragma unroll
+        for (int r = 0; r < NB; ++r) {
+            const uint32_t J = J0 + r * (SK_CT / 4);
+            if (J < nsub) load8(J * 32 + 8 * u, v[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < NB; ++r) {
+            const uint32_t J = J0 + r * (SK_CT / 4);
+            if (J < nsub) sk_quant(type, v[r], u, qmask, J, xq, xf);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// matvec consumer: this CTA's units of one op. The 8 warps split each
+// stage's 256-column super-blocks; at the end of the CTA's part of a tile the
+// row sums go out: one atomicAdd per row (at most two CTAs share a row), or
+// for whole gate/up rows SiLU(gate)*up stored directly.
+// ---------------------------------------------------------------------------
+template <int TYPE>
+__device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
+                                              uint32_t xq_a, uint32_t xf_a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    const uint32_t RS = d.g.rs, CK = d.g.ck;
+    volatile int *cta_abort = S.abort_flag();
+    float *red = S.red();
+    uint32_t u0, u1;
+    sk_range(d.g.ntiles * d.g.nch, u0, u1);
+    for (uint32_t u = u0; u < u1; ++u) {
+        uint32_t tile, ch;
+        sk_unit(d, u, tile, ch);
+        // one decision per warp: the MMAs and shuffles below need all 32 lanes
+        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.slot), r.round & 1, p.sync + 1));
+        if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
+        float acc[2] = {0.f, 0.f};
+        if (got) {
+            const uint32_t c0 = ch * CK, c1 = min(d.cols, c0 + CK);
+            // packed rows start 16-byte aligned in the slot: no alignment pads;
+            // two super-blocks per warp interleave their independent MMA chains
+            const uint32_t ms = S.slot(r.slot);
+#pragma unroll 2
+            for (uint32_t eo = (uint32_t)warp * 256u; c0 + eo < c1; eo += SK_NCW * 256u)
+                mv_unit<TYPE, true>(ms, RS, 0u, 0u, eo, (c0 + eo) >> 5, xq_a, xf_a, lane, c1 - c0 - eo, acc);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(S.empty(r.slot));
+        r.advance(S.nslots);
+        // the unit's row sums: over the thread columns, then the warps
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 1);
+            acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 2);
+        }
+        float *rbuf = red + ((u - u0) & 1) * (SK_NCW * 16);
+        if ((lane & 3) == 0) {
+            rbuf[warp * 16 + g] = acc[0];
+            rbuf[warp * 16 + g + 8] = acc[1];
+        }
+        named_bar_sync(1, SK_CT);
+        if (warp == 0) {
+            const uint32_t li = (uint32_t)lane & 15u;
+            float va = 0.f;
+#pragma unroll
+            for (int w = 0; w < SK_NCW; ++w) va += rbuf[w * 16 + li];
+            const float vu = __shfl_sync(0xffffffffu, va, (lane & 7) + 8);   // up sum of the same row
+            const uint32_t row = sk_slot_row(d.gu != 0, tile, li);
+            if (lane < 16 && row < d.rows && !*cta_abort) {
+                // h = SiLU(gate) * up (src/vbs_host_math.h:53-57)
+                if (d.gu) { if (lane < 8) d.out[row] = va / (1.0f + expf(-va)) * vu; }
+                else d.out[(uint64_t)ch * d.rows + row] = va;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void sk_mv_dispatch(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
+                                               uint32_t xq_a, uint32_t xf_a) {
+    if (d.type == T_Q4_K) sk_mv_consume<T_Q4_K>(p, d, S, r, xq_a, xf_a);
+    else if (d.type == T_Q6_K) sk_mv_consume<T_Q6_K>(p, d, S, r, xq_a, xf_a);
+    else sk_mv_consume<T_Q8_0>(p, d, S, r, xq_a, xf_a);
+}
+
+// ---------------------------------------------------------------------------
+// attention consumer
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sk_pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ void sk_split_h2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = sk_pack_h2(a - f.x, b - f.y);
+}
+
+// RoPE of the pair (d, d+1), d even, at position pos (src/vbs_host_math.h:38-51,
+// the same expression as the per-op kernels' Q/K/V epilogue).
+__device__ __forceinline__ float2 sk_rope(float a, float b, uint32_t d, uint32_t pos, uint32_t hd, float theta) {
+    const float ang = (float)pos * powf(theta, -(float)d / (float)hd);
+    float s, c;
+    sincosf(ang, &s, &c);
+    return make_float2(a * c - b * s, a * s + b * c);
+}
+
+template <int HD>
+__device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_t pos, uint32_t seq, const SkSmem &S, SkRing &r,
+                        float *sh) {
+    constexpr int RS = 4 + HD;                 // state row [m, l, pad, pad, o[HD]]
+    constexpr uint32_t ROWB = HD * 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = warp >> 2, wl = warp & 3;  // warp groups take alternate stages
+    volatile int *cta_abort = S.abort_flag();
+    const SkAttn a = sk_attn_unit(p, seq);
+    if (!a.has) return;
+    const uint32_t G = p.nqh / p.nkh;
+    const float *accq = sk_acc(p, l);
+    const uint32_t qdim = p.nqh * HD, kvdim = p.nkh * HD;
+
+    // q as the A operand: a 16 x HD f16 matrix in shared memory, row g =
+    // fp16(q_g), row g+8 = fp16(q_g - fp16(q_g)) (zero for g >= G); RoPE'd
+    // and pre-scaled by scale*log2(e). Read back with ldmatrix per k-step.
+    constexpr uint32_t ASTR = HD * 2 + 16;     // padded row: conflict-free ldmatrix
+    const uint32_t a_base = smem_u32(sh + SK_NCW * G * RS);
+    const int g = lane >> 2, qd = 2 * (lane & 3);
+    {
+        const float qscale = p.scale * 1.4426950408889634f;
+        for (uint32_t k = threadIdx.x; k < SK_GS * (HD / 2); k += SK_CT) {
+            const uint32_t gg = k / (HD / 2), dd = 2 * (k % (HD / 2));
+            float2 v = make_float2(0.f, 0.f);
+            if (gg < G) {
+                const float2 raw = __ldcg(reinterpret_cast<const float2 *>(accq + (a.h * G + gg) * HD + dd));
+                v = sk_rope(raw.x, raw.y, dd, pos, HD, p.theta);
+            }
+            uint32_t hi, lo;
+            sk_split_h2(v.x * qscale, v.y * qscale, hi, lo);
+            asm volatile("st.shared.u32 [%0], %1;" ::"r"(a_base + gg * ASTR + dd * 2), "r"(hi) : "memory");
+            asm volatile("st.shared.u32 [%0], %1;" ::"r"(a_base + (gg + 8) * ASTR + dd * 2), "r"(lo) : "memory");
+        }
+        named_bar_sync(1, SK_CT);
+    }
+    const uint32_t a_lane = a_base + (lane & 15) * ASTR + (lane >> 4) * 16;
+
+    float o[HD / 8][4];
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float mrun = -INFINITY, lrun = 0.f;
+    const uint64_t hb = (((uint64_t)l * p.nkh + a.h) * p.max_ctx) * HD;
+
+    for (uint32_t s = 0; s < a.nst; ++s) {
+        // one decision per warp: the MMAs and shuffles below need all 32 lanes
+        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.slot), r.round & 1, p.sync + 1));
+        if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
+        const uint32_t ts = a.t0 + s * SK_AP, tb = ts + 16 * wl;
+        if (got && (int)(s & 1) == grp && tb < a.t1) {
+            const uint32_t kst = S.slot(r.slot) + 16 * wl * ROWB;
+            const uint32_t vst = S.slot(r.slot) + SK_AP * ROWB + 16 * wl * ROWB;
+            // rows past the end of the unit: zero V (p = 0 must not meet stale bits)
+            if (tb + 16 > a.t1) {
+                const uint32_t nv = a.t1 - tb;
+                for (uint32_t i = lane; i < (16 - nv) * (ROWB / 16); i += 32) {
+                    const uint32_t rr = nv + i / (ROWB / 16), cc = i % (ROWB / 16);
+                    asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(vst + rr * ROWB + cc * 16), "r"(0u) : "memory");
+                }
+            }
+            // the current position: RoPE'd key and value from the Q/K/V sums,
+            // fp16 with the engine's rounding, into the cache and this stage
+            if (pos >= tb && pos < tb + 16 && pos < a.t1) {
+                constexpr int DPL = HD / 32;   // dims per lane (even)
+                const uint32_t d0 = DPL * lane, rr = pos - tb;
+                const float *kr = accq + qdim + a.h * HD, *vr = accq + qdim + kvdim + a.h * HD;
+                uint16_t kh[DPL], vh[DPL];
+#pragma unroll
+                for (int j = 0; j < DPL; j += 2) {
+                    const float2 k2 = __ldcg(reinterpret_cast<const float2 *>(kr + d0 + j));
+                    const float2 v2 = __ldcg(reinterpret_cast<const float2 *>(vr + d0 + j));
+                    const float2 kro = sk_rope(k2.x, k2.y, d0 + j, pos, HD, p.theta);
+                    kh[j] = f32_to_f16_kv(kro.x); kh[j + 1] = f32_to_f16_kv(kro.y);
+                    vh[j] = f32_to_f16_kv(v2.x); vh[j + 1] = f32_to_f16_kv(v2.y);
+                }
+                // swizzled place of dims d0..d0+DPL-1 (inside one 16-byte chunk)
+                const uint32_t off = ((((d0 >> 3) ^ (pos & 7u)) << 3) + (d0 & 7u));
+                uint16_t *kg = p.kc + hb + (uint64_t)pos * HD + off, *vg = p.vc + hb + (uint64_t)pos * HD + off;
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) {
+                    kg[j] = kh[j];
+                    vg[j] = vh[j];
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(kst + rr * ROWB + (off + j) * 2), "h"(kh[j]) : "memory");
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(vst + rr * ROWB + (off + j) * 2), "h"(vh[j]) : "memory");
+                }
+            }
+            __syncwarp();
+            float sc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; kk += 2) {
+                uint32_t qa0[4], qa1[4];
+                ldsm_x4(a_lane + kk * 32, qa0[0], qa0[1], qa0[2], qa0[3]);
+                ldsm_x4(a_lane + kk * 32 + 32, qa1[0], qa1[1], qa1[2], qa1[3]);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const uint32_t rr = 8 * j + (lane & 7), c = 2 * kk + (lane >> 3);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(kst + rr * ROWB + ((c ^ (rr & 7u)) << 4), b0, b1, b2, b3);
+                    mma_f16_acc(sc2[j], qa0, b0, b1);
+                    mma_f16_acc(sc2[j], qa1, b2, b3);
+                }
+            }
+            float sc[4] = {sc2[0][0] + sc2[0][2], sc2[0][1] + sc2[0][3], sc2[1][0] + sc2[1][2], sc2[1][1] + sc2[1][3]};
+            const uint32_t pq = tb + qd;
+            if (pq >= a.t1) sc[0] = -INFINITY;
+            if (pq + 1 >= a.t1) sc[1] = -INFINITY;
+            if (pq + 8 >= a.t1) sc[2] = -INFINITY;
+            if (pq + 9 >= a.t1) sc[3] = -INFINITY;
+            float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            if (mx > mrun + SK_LAZY) {
+                const float rs = exp2f(mrun - mx);
+                lrun *= rs;
+#pragma unroll
+                for (int n = 0; n < HD / 8; ++n) { o[n][0] *= rs; o[n][1] *= rs; o[n][2] *= rs; o[n][3] *= rs; }
+                mrun = mx;
+            }
+            float pe[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pe[e] = exp2f(sc[e] - mrun);
+            lrun += (pe[0] + pe[1]) + (pe[2] + pe[3]);
+            uint32_t pa[4];
+            sk_split_h2(pe[0], pe[1], pa[0], pa[1]);
+            sk_split_h2(pe[2], pe[3], pa[2], pa[3]);
+#pragma unroll
+            for (int n = 0; n < HD / 8; n += 2) {
+                const uint32_t rr = (lane & 7) + 8 * ((lane >> 3) & 1), c = n + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_trans(vst + rr * ROWB + ((c ^ (rr & 7u)) << 4), b0, b1, b2, b3);
+                mma_f16_acc(o[n], pa, b0, b1);
+                mma_f16_acc(o[n + 1], pa, b2, b3);
+            }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(S.empty(r.slot));
+        r.advance(S.nslots);
+    }
+
+    // warp states -> shared memory, merge over the 8 warps
+    lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
+    lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
+    if ((uint32_t)g < G) {
+        float *row = sh + (warp * G + g) * RS;
+        if ((lane & 3) == 0) { row[0] = mrun; row[1] = lrun; }
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+            row[4 + 8 * n + qd] = o[n][0] + o[n][2];
+            row[5 + 8 * n + qd] = o[n][1] + o[n][3];
+        }
+    }
+    named_bar_sync(1, SK_CT);
+    float *work = reinterpret_cast<float *>(p.attn_work);
+    constexpr size_t part_stride = (size_t)SK_GS * RS;
+    float *mypart = work + ((size_t)a.h * SK_MAX_SPLITS + a.split) * part_stride;
+    float *outp = p.att + (size_t)a.h * G * HD;
+    for (uint32_t k = threadIdx.x; k < G * HD; k += SK_CT) {
+        const uint32_t gg = k / HD, d = k % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < SK_NCW; ++w) M = fmaxf(M, sh[(w * G + gg) * RS]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < SK_NCW; ++w) {
+            const float *rw = sh + (w * G + gg) * RS;
+            const float wt = (rw[0] == -INFINITY) ? 0.f : exp2f(rw[0] - M);
+            L += rw[1] * wt;
+            O += rw[4 + d] * wt;
+        }
+        if (a.S == 1) {
+            outp[gg * HD + d] = O / L;
+        } else {
+            if (d == 0) { mypart[gg * RS] = M; mypart[gg * RS + 1] = L; }
+            mypart[gg * RS + 4 + d] = O;
+        }
+    }
+    if (a.S == 1) return;
+    __threadfence();
+    named_bar_sync(1, SK_CT);
+    volatile int *flag = S.sync_flag();
+    if (threadIdx.x == 0) *flag = atomicAdd(&p.sync[SK_TICKET0 + a.h], 1u) == a.S - 1;
+    named_bar_sync(1, SK_CT);
+    if (!*flag) return;
+    __threadfence();
+    // last split of this KV head: merge the splits in split order
+    const float *parts = work + (size_t)a.h * SK_MAX_SPLITS * part_stride;
+    float *wsm = sh;                                    // [SK_GS][S]
+    float *Lg = sh + SK_GS * SK_MAX_SPLITS;             // [SK_GS]
+    for (uint32_t gg = warp; gg < G; gg += SK_NCW) {
+        float ms[4], ls[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t s2 = lane + 32 * k;
+            const float *ps = parts + s2 * part_stride + gg * RS;
+            ms[k] = s2 < a.S ? __ldcg(ps) : -INFINITY;
+            ls[k] = s2 < a.S ? __ldcg(ps + 1) : 0.f;
+        }
+        const float M = warp_max(fmaxf(fmaxf(ms[0], ms[1]), fmaxf(ms[2], ms[3])));
+        float L = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t s2 = lane + 32 * k;
+            const float wt = (ms[k] == -INFINITY) ? 0.f : exp2f(ms[k] - M);
+            if (s2 < a.S) wsm[gg * a.S + s2] = wt;
+            L += ls[k] * wt;
+        }
+        L = warp_sum(L);
+        if (lane == 0) Lg[gg] = L;
+    }
+    named_bar_sync(1, SK_CT);
+    constexpr uint32_t MB = 16;
+    for (uint32_t k = threadIdx.x; k < G * HD / 4; k += SK_CT) {
+        const uint32_t gg = k / (HD / 4), d = (k % (HD / 4)) * 4;
+        const float *src = parts + gg * RS + 4 + d;
+        const float *wg = wsm + gg * a.S;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t s0 = 0; s0 < a.S; s0 += MB) {
+            float4 v[MB];
+#pragma unroll
+            for (uint32_t u = 0; u < MB; ++u)
+                v[u] = s0 + u < a.S ? __ldcg(reinterpret_cast<const float4 *>(src + (s0 + u) * part_stride))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (uint32_t u = 0; u < MB; ++u) {
+                const float wt = s0 + u < a.S ? wg[s0 + u] : 0.f;
+                acc.x = fmaf(v[u].x, wt, acc.x); acc.y = fmaf(v[u].y, wt, acc.y);
+                acc.z = fmaf(v[u].z, wt, acc.z); acc.w = fmaf(v[u].w, wt, acc.w);
+            }
+        }
+        const float il = 1.0f / Lg[gg];
+        *reinterpret_cast<float4 *>(outp + gg * HD + d) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+    }
+    if (threadIdx.x == 0) p.sync[SK_TICKET0 + a.h] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// argmax over the logits (first maximum wins, src/vbs_cpu_main.c:78-80)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void sk_pick(float &best, uint32_t &bi, float ov, uint32_t oi) {
+    if (oi != 0xFFFFFFFFu && (bi == 0xFFFFFFFFu || ov > best || (ov == best && oi < bi))) { best = ov; bi = oi; }
+}
+
+__device__ __forceinline__ void sk_block_argmax(const SkSmem &S, float &best, uint32_t &bi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int o = 16; o; o >>= 1) sk_pick(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    float *mv = S.misc() + 64;
+    uint32_t *mi = S.scratch_u();
+    if (lane == 0) { mv[warp] = best; mi[warp] = bi; }
+    named_bar_sync(1, SK_CT);
+    best = lane < SK_NCW ? mv[lane] : -INFINITY;
+    bi = lane < SK_NCW ? mi[lane] : 0xFFFFFFFFu;
+    for (int o = 16; o; o >>= 1) sk_pick(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    named_bar_sync(1, SK_CT);
+}
+
+__device__ __forceinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uint32_t pos) {
+    const float *lg = sk_logits(p);
+    const uint32_t n = p.vocab, per = (n + gridDim.x - 1) / gridDim.x;
+    const uint32_t lo = min(n, blockIdx.x * per), hi = min(n, lo + per);
+    float best = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += SK_CT) sk_pick(best, bi, __ldcg(lg + i), i);
+    sk_block_argmax(S, best, bi);
+    volatile int *flag = S.sync_flag();
+    if (threadIdx.x == 0) {
+        p.sync[SK_SLOTS + 2 * blockIdx.x] = __float_as_uint(best);
+        p.sync[SK_SLOTS + 2 * blockIdx.x + 1] = bi;
+        __threadfence();
+        *flag = atomicAdd(&p.sync[2], 1u) == gridDim.x - 1;
+    }
+    named_bar_sync(1, SK_CT);
+    if (!*flag) return;
+    __threadfence();
+    best = -INFINITY;
+    bi = 0xFFFFFFFFu;
+    for (uint32_t c = threadIdx.x; c < gridDim.x; c += SK_CT)
+        sk_pick(best, bi, __uint_as_float(__ldcg(&p.sync[SK_SLOTS + 2 * c])), __ldcg(&p.sync[SK_SLOTS + 2 * c + 1]));
+    sk_block_argmax(S, best, bi);
+    if (threadIdx.x == 0) {
+        if (bi == 0xFFFFFFFFu) bi = 0;
+        const uint32_t np = pos + 1u;
+        p.ctrl[1] = bi;
+        p.ctrl[0] = np;
+        if (p.hist && np < p.hist_cap) p.hist[np] = bi;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p) {
+    static_assert(65536 / SK_THREADS / 8 * 8 >= SK_REG_LAUNCH, "launch register count");
+    extern __shared__ __align__(1024) uint8_t smem[];
+    SkSmem S;
+    S.ptr = smem;
+    S.base = smem_u32(smem);
+    S.ring = S.base + p.ring_off;
+    S.slot_bytes = p.slot_bytes;
+    S.nslots = p.nslots;
+    const int warp = threadIdx.x >> 5;
+    // read once: the last CTA rewrites the control block at the end of the step
+    const uint32_t pos = *reinterpret_cast<const volatile uint32_t *>(p.ctrl);
+    const uint32_t token = *reinterpret_cast<const volatile uint32_t *>(p.ctrl + 1);
+    if (pos >= p.max_ctx || token >= p.vocab) {   // the same decision in every CTA: nothing runs, nothing waits
+        if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(p.err, DERR_BAD_ARG);
+        return;
+    }
+    const uint32_t seq = pos + 1;
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < S.nslots; ++i) {
+            mbar_init(S.full(i), 1);
+            mbar_init(S.empty(i), SK_NCW);
+        }
+        *S.abort_flag() = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (warp >= SK_NCW) {   // producer warpgroup
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(SK_REG_PRODUCER));
+        if (warp == SK_NCW) sk_producer(p, S, seq);
+        return;
+    }
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(SK_REG_CONSUMER));
+
+    // ------------------------------ consumers ------------------------------
+    float *x = reinterpret_cast<float *>(smem + p.x_off);
+    uint8_t *xq = smem + p.xq_off;
+    float4 *xf = reinterpret_cast<float4 *>(smem + p.xf_off);
+    const uint32_t xq_a = S.base + p.xq_off, xf_a = S.base + p.xf_off;
+    float *sh = reinterpret_cast<float *>(xq);   // attention states alias the x buffers
+    SkRing r;
+    const uint32_t nops = 5 * p.n_layers + 2;
+    for (uint32_t i = 0; i < nops; ++i) {
+        if (i > 0 && !sk_grid_sync(p, i * gridDim.x, S.sync_flag(), S.abort_flag())) break;
+        uint32_t l;
+        const int kind = sk_kind(i, p.n_layers, l);
+        if (kind == K_ATTN) {
+            if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh);
+            else sk_attn<64>(p, l, pos, seq, S, r, sh);
+            continue;
+        }
+        if (kind == K_ARGMAX) {
+            sk_argmax(p, S, pos);
+            continue;
+        }
+        const SkMv d = sk_mv_desc(p, kind, l);
+        uint32_t u0, u1;
+        sk_range(d.g.ntiles * d.g.nch, u0, u1);
+        const bool work = u1 > u0;
+        uint32_t xq_u = xq_a, xf_u = xf_a;   // shared addresses of x block 0 for mv_unit
+        if (kind == K_QKV || kind == K_GU || kind == K_OUT) {
+            // every CTA keeps x current, whether or not it has units of this op
+            const float *add = kind == K_QKV ? (l ? sk_acc_down(p, l - 1) : nullptr)
+                                             : (kind == K_GU ? sk_acc_o(p, l) : sk_acc_down(p, p.n_layers - 1));
+            const uint32_t nadd = kind == K_GU ? 1u : p.geo[STEP_DOWN].nch;
+            const float *nw = kind == K_QKV ? p.layers[l].attn_norm : (kind == K_GU ? p.layers[l].ffn_norm : p.out_norm);
+            sk_prologue_norm(p, S, x, add, nadd, nw, token, work, d.type, xq, xf);
+        } else if (kind == K_O) {
+            if (work) sk_prologue_vec<2>(d.cols, d.type, [&](uint32_t e, float v[8]) { ld8_cg(p.att + e, v); }, xq, xf);
+        } else if (work) {   // K_DOWN: only the column chunks of this CTA's units
+            const uint32_t c_lo = u0 / d.g.ntiles, c_hi = (u1 - 1) / d.g.ntiles;
+            const uint32_t col0 = c_lo * d.g.ck, col1 = min(d.cols, (c_hi + 1) * d.g.ck);
+            const float *hp = sk_acc_h(p, l) + col0;
+            sk_prologue_vec<2>(col1 - col0, d.type, [&](uint32_t e, float v[8]) { ld8_cg(hp + e, v); }, xq, xf);
+            xq_u = xq_a - (col0 / 32) * (d.type == T_Q6_K ? XQ_PLAIN_STRIDE : XQ_SLOT_STRIDE);   // mv_unit indexes x blocks from column 0
+            xf_u = xf_a - (col0 / 32) * 16;
+        }
+        if (!work) continue;
+        named_bar_sync(1, SK_CT);
+        sk_mv_dispatch(p, d, S, r, xq_u, xf_u);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+// Packed bytes of a row chunk (Q6_K blocks padded to Q6P_BYTES).
+static uint32_t sk_chunk_bytes(int type, uint32_t ck) {
+    return type == T_Q6_K ? ck / 256 * Q6P_BYTES : (uint32_t)row_bytes(type, ck);
+}
+// Row slot stride: Q6_K rows 32 or 96 (mod 128) bytes apart, the others an
+// odd number of 16-byte units: the lane patterns of mv_unit's loads then
+// fall in distinct banks.
+static uint32_t sk_rs(int type, uint32_t ck) {
+    uint32_t rs = (sk_chunk_bytes(type, ck) + 15) & ~15u;
+    if (type == T_Q6_K) {
+        while (rs % 128 != 32 && rs % 128 != 96) rs += 16;
+    } else if (((rs / 16) & 1u) == 0) {
+        rs += 16;
+    }
+    return rs;
+}
+
+size_t step_sync_words(int n_sm) { return SK_SLOTS + 2 * (size_t)n_sm + 16; }
+
+size_t step_attn_work_bytes(const StepParams &p) {
+    return (size_t)p.nkh * SK_MAX_SPLITS * SK_GS * (4 + p.hd) * sizeof(float);
+}
+
+bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
+    auto no = [&](const char *m) {
+        if (why && cap) snprintf(why, cap, "%s", m);
+        return false;
+    };
+    const uint32_t qd = p.nqh * p.hd, kvd = p.nkh * p.hd;
+    if (p.hd != 64 && p.hd != 128) return no("head_dim must be 64 or 128");
+    if (!p.nkh || p.nqh % p.nkh || p.nqh / p.nkh > (uint32_t)SK_GS) return no("query heads per KV head must be 1..8");
+    if (p.nkh > SK_MAX_KV || p.nkh > (uint32_t)n_sm) return no("too many KV heads");
+    const int ts[5] = {p.t_qkv, p.t_o, p.t_gu, p.t_down, p.t_out};
+    const uint32_t cols[5] = {p.dim, qd, p.dim, p.ffn, p.dim};
+    const uint32_t rows[5] = {qd + 2 * kvd, p.dim, p.ffn, p.dim, p.vocab};
+    for (int k = 0; k < 5; ++k) {
+        if (ts[k] != T_Q4_K && ts[k] != T_Q6_K && ts[k] != T_Q8_0) return no("matvec weights must be Q4_K, Q6_K or Q8_0");
+        if (cols[k] % (uint32_t)block_elems(ts[k]) || cols[k] % 32) return no("matrix width not a whole number of blocks");
+    }
+    if (!block_elems(p.t_embd) || p.dim % (uint32_t)block_elems(p.t_embd)) return no("embedding type");
+    if (p.dim % 32 || qd % 32 || p.ffn % 32) return no("widths must be multiples of 32");
+    if (p.dim > (uint32_t)(SK_CT / 4) * 32 * SK_PB) return no("model width above the prologue's register budget");
+    // shared memory: header | x | quantized x (or attention states) | ring.
+    // The down projection quantizes only its CTA's (at most two) column
+    // chunks; the chunk size is fixed first from a provisional ring.
+    const uint32_t G = p.nqh / p.nkh;
+    const uint32_t attn_sh = (uint32_t)(SK_NCW * G * (4 + p.hd) * 4 + 16 * (p.hd * 2 + 16));
+    const uint32_t merge_sh = (uint32_t)(SK_GS * (SK_MAX_SPLITS + 1) * 4);
+    auto plan_smem = [&](uint32_t down_ck) {
+        const uint32_t nb = std::max(std::max(p.dim, qd), std::min(p.ffn, 2 * down_ck)) / 32;
+        p.x_off = SK_HDR;
+        p.xq_off = (p.x_off + p.dim * 4 + 1023) & ~1023u;
+        p.xf_off = p.xq_off + nb * XQ_MAX_STRIDE;
+        const uint32_t region = std::max(nb * (XQ_MAX_STRIDE + 16), std::max(attn_sh, merge_sh));
+        p.ring_off = (p.xq_off + region + 1023) & ~1023u;
+    };
+    plan_smem(4096);
+    if (p.ring_off >= SK_SMEM) return no("model width too large for shared memory");
+    const uint32_t ring = SK_SMEM - p.ring_off;
+    const uint32_t slot_max = (ring / 3) & ~127u;
+    uint32_t slot = 2 * SK_AP * p.hd * 2;   // attention stage
+    for (int k = 0; k < 5; ++k) {
+        const uint32_t SL = 16u, E = (uint32_t)block_elems(ts[k]);
+        uint32_t ck = cols[k];
+        // whole rows when 16 fit a slot, else 4096- or 2048-column chunks
+        // (16 or 8 super-blocks: the 8 consumer warps share them evenly),
+        // else halve in 256-column steps
+        if (SL * sk_rs(ts[k], ck) > slot_max)
+            for (uint32_t c : {4096u, 2048u})
+                if (ck > c && SL * sk_rs(ts[k], c) <= slot_max) { ck = c; break; }
+        while (ck > 256 && SL * sk_rs(ts[k], ck) > slot_max) ck = std::max(256u, (ck / 2 + 255) / 256 * 256);
+        if (ck % E) return no("chunk not a whole number of blocks");
+        StepMvGeom &gg = p.geo[k];
+        gg.ck = ck;
+        gg.rs = sk_rs(ts[k], ck);
+        gg.nch = (cols[k] + ck - 1) / ck;
+        gg.ntiles = (rows[k] + (k == STEP_GU ? 7 : 15)) / (k == STEP_GU ? 8 : 16);   // gate/up: 8 rows of each
+        slot = std::max(slot, SL * gg.rs);
+        if (k != STEP_DOWN && gg.nch != 1) return no("rows of this width do not fit one stage");
+    }
+    {   // down: chunk-major units, every CTA within at most two chunks
+        const StepMvGeom &gd = p.geo[STEP_DOWN];
+        const uint64_t U = (uint64_t)gd.ntiles * gd.nch;
+        if (gd.nch > (uint32_t)SK_MAXPL) return no("too many column chunks in the down projection");
+        if ((U + n_sm - 1) / n_sm > gd.ntiles) return no("down projection units per CTA exceed a chunk");
+        plan_smem(gd.ck);
+        if (SK_SMEM - p.ring_off < ring) return no("shared-memory plan");
+    }
+    p.slot_bytes = (slot + 127) & ~127u;
+    p.nslots = std::min(SK_MAXSLOT, ring / p.slot_bytes);
+    if (p.nslots < 2) return no("shared-memory ring too small");
+    p.attn_splits = std::max(1u, std::min(SK_MAX_SPLITS, (uint32_t)n_sm / p.nkh));
+    p.acc_layer = (uint64_t)(qd + 2 * kvd) + p.dim + p.ffn + (uint64_t)p.geo[STEP_DOWN].nch * p.dim;
+    return true;
+}
+
+// One CTA per stage unit: slot row r of unit (tile, chunk) <- the chunk's
+// bytes of row sk_slot_row(tile, r), zero-padded to rs; rows past the
+// matrix are zeros.
+__global__ void step_repack_kernel(int type, const uint8_t *w0, const uint8_t *w1, const uint8_t *w2, uint32_t seg0,
+                                   uint32_t seg1, int gu, uint32_t rows, uint32_t cols, StepMvGeom g, uint8_t *dst) {
+    const uint32_t unit = blockIdx.x, tile = unit / g.nch, ch = unit % g.nch;
+    const uint32_t E = (uint32_t)block_elems(type), BB = (uint32_t)block_bytes(type);
+    const uint64_t rb = row_bytes(type, cols);
+    const uint32_t c0 = ch * g.ck, c1 = min(cols, c0 + g.ck);
+    const uint64_t boff = (uint64_t)(c0 / E) * BB;
+    const bool q6 = type == T_Q6_K;
+    const uint32_t pb = q6 ? Q6P_BYTES : BB;                 // packed bytes per block
+    const uint32_t blen = (c1 - c0) / E * pb;
+    uint8_t *out = dst + (uint64_t)unit * 16 * g.rs;
+    for (uint32_t i = threadIdx.x; i < 16 * g.rs; i += blockDim.x) {
+        const uint32_t r = i / g.rs, b = i % g.rs;
+        const uint32_t row = sk_slot_row(gu != 0, tile, r);
+        uint8_t v = 0;
+        if (row < rows && b < blen) {
+            const uint8_t *src;
+            if (gu) src = (r >= 8 ? w1 : w0) + (uint64_t)row * rb;
+            else if (row < seg0) src = w0 + (uint64_t)row * rb;
+            else if (row < seg1) src = w1 + (uint64_t)(row - seg0) * rb;
+            else src = w2 + (uint64_t)(row - seg1) * rb;
+            src += boff;
+            if (q6) {   // GGUF Q6_K block (ql 0, qh 128, scales 192, d 208) -> the packed layout
+                const uint32_t blk = b / Q6P_BYTES, o = b % Q6P_BYTES;
+                const uint8_t *sb = src + (uint64_t)blk * 210;
+                if (o < 128) v = sb[o];
+                else if (o < 160) v = sb[128 + (o - 128)];
+                else if (o < 176) v = sb[192 + (o - 160)];
+                else if (o < 178) v = sb[208 + (o - 176)];
+                else if (o >= 192) v = sb[160 + (o - 192)];
+            } else {
+                v = src[b];
+            }
+        }
+        out[i] = v;
+    }
+}
+
+static void sk_op_shape(const StepParams &p, int op, int &type, uint32_t &rows, uint32_t &cols) {
+    const uint32_t qd = p.nqh * p.hd, kvd = p.nkh * p.hd;
+    switch (op) {
+        case STEP_QKV: type = p.t_qkv; rows = qd + 2 * kvd; cols = p.dim; break;
+        case STEP_O: type = p.t_o; rows = p.dim; cols = qd; break;
+        case STEP_GU: type = p.t_gu; rows = p.ffn; cols = p.dim; break;
+        case STEP_DOWN: type = p.t_down; rows = p.dim; cols = p.ffn; break;
+        default: type = p.t_out; rows = p.vocab; cols = p.dim; break;
+    }
+}
+
+size_t step_packed_bytes(const StepParams &p, int op) {
+    const StepMvGeom &g = p.geo[op];
+    return (size_t)g.ntiles * g.nch * 16 * g.rs;
+}
+
+cudaError_t step_repack(const StepParams &p, int op, const uint8_t *w0, const uint8_t *w1, const uint8_t *w2,
+                        uint8_t *dst, cudaStream_t st) {
+    int type;
+    uint32_t rows, cols;
+    sk_op_shape(p, op, type, rows, cols);
+    const uint32_t qd = p.nqh * p.hd, kvd = p.nkh * p.hd;
+    const uint32_t seg0 = op == STEP_QKV ? qd : rows, seg1 = op == STEP_QKV ? qd + kvd : rows;
+    const StepMvGeom &g = p.geo[op];
+    note_launches(1);
+    step_repack_kernel<<<g.ntiles * g.nch, 256, 0, st>>>(type, w0, w1, w2, seg0, seg1, op == STEP_GU, rows, cols, g, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t step_configure() {
+    return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+}
+
+cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_sm);
+    cfg.blockDim = dim3(SK_THREADS);
+    cfg.dynamicSmemBytes = SK_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs co-resident: the grid barrier relies on it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    note_launches(1);
+    return cudaLaunchKernelEx(&cfg, step_kernel, p);
+}
+
+}  // namespace vbs
