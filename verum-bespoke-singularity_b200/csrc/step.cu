@@ -59,7 +59,8 @@ constexpr int SK_THREADS = SK_CT + 128;            // + the producer warpgroup (
 constexpr uint32_t SK_REG_LAUNCH = 168, SK_REG_CONSUMER = 232, SK_REG_PRODUCER = 40;
 static_assert(SK_CT * SK_REG_CONSUMER + 128 * SK_REG_PRODUCER <= SK_THREADS * SK_REG_LAUNCH, "register split");
 constexpr uint32_t SK_MAXSLOT = 16;
-constexpr uint32_t SK_HDR = 4096;                  // barriers, flags, reduction scratch
+constexpr uint32_t SK_HDR = 8192;                  // barriers, flags, reduction buffers
+constexpr uint32_t SK_MAXRING = 7;                 // ring slots (SK_MAXRING + 1 unit reduction buffers)
 constexpr uint32_t SK_SMEM = 227u * 1024u;
 constexpr uint32_t SK_AP = 64;                     // attention positions per stage
 constexpr uint32_t SK_MAX_SPLITS = 128;
@@ -236,9 +237,10 @@ struct SkSmem {
     __device__ uint32_t slot(uint32_t s) const { return ring + s * slot_bytes; }
     __device__ volatile int *abort_flag() const { return reinterpret_cast<volatile int *>(ptr + 256); }
     __device__ volatile int *sync_flag() const { return reinterpret_cast<volatile int *>(ptr + 260); }
+    __device__ int *red_count() const { return reinterpret_cast<int *>(ptr + 320); }            // [SK_MAXRING + 1]
     __device__ uint32_t *scratch_u() const { return reinterpret_cast<uint32_t *>(ptr + 512); }   // 64 words
     __device__ float *misc() const { return reinterpret_cast<float *>(ptr + 1024); }            // 256 floats
-    __device__ float *red() const { return reinterpret_cast<float *>(ptr + 2048); }             // [2][8][16]
+    __device__ float *red() const { return reinterpret_cast<float *>(ptr + 2048); }             // [SK_MAXRING + 1][8][16]
 };
 
 struct SkRing {
@@ -457,26 +459,41 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
             // packed rows start 16-byte aligned in the slot: no alignment pads;
             // two super-blocks per warp interleave their independent MMA chains
             const uint32_t ms = S.slot(r.slot);
-#pragma unroll 2
-            for (uint32_t eo = (uint32_t)warp * 256u; c0 + eo < c1; eo += SK_NCW * 256u)
-                mv_unit<TYPE, true>(ms, RS, 0u, 0u, eo, (c0 + eo) >> 5, xq_a, xf_a, lane, c1 - c0 - eo, acc);
+            // chunks are at most 16 super-blocks (the plan caps them at 4096
+            // columns): at most two per warp, as straight-line code so their
+            // independent load/MMA chains interleave
+            const uint32_t e0 = (uint32_t)warp * 256u, e1 = e0 + SK_NCW * 256u;
+            if (c0 + e0 < c1) mv_unit<TYPE, true>(ms, RS, 0u, 0u, e0, (c0 + e0) >> 5, xq_a, xf_a, lane, c1 - c0 - e0, acc);
+            if (c0 + e1 < c1) mv_unit<TYPE, true>(ms, RS, 0u, 0u, e1, (c0 + e1) >> 5, xq_a, xf_a, lane, c1 - c0 - e1, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(S.empty(r.slot));
         r.advance(S.nslots);
-        // the unit's row sums: over the thread columns, then the warps
+        // the unit's row sums: over the thread columns, then the warps. No
+        // CTA barrier: each warp leaves its partials in the unit's buffer and
+        // the last of the 8 to arrive sums them in warp order and writes the
+        // rows. A warp runs at most nslots units ahead of the slowest (slot
+        // reuse waits for all of them), so nslots + 1 buffers never collide.
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
             acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 1);
             acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 2);
         }
-        float *rbuf = red + ((u - u0) & 1) * (SK_NCW * 16);
+        const uint32_t b = (u - u0) % (S.nslots + 1);
+        float *rbuf = red + b * (SK_NCW * 16);
         if ((lane & 3) == 0) {
             rbuf[warp * 16 + g] = acc[0];
             rbuf[warp * 16 + g + 8] = acc[1];
         }
-        named_bar_sync(1, SK_CT);
-        if (warp == 0) {
+        __syncwarp();
+        int arrived = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            arrived = atomicAdd(S.red_count() + b, 1);
+        }
+        arrived = __shfl_sync(0xffffffffu, arrived, 0);
+        if (arrived == SK_NCW - 1) {
+            __threadfence_block();
             const uint32_t li = (uint32_t)lane & 15u;
             float va = 0.f;
 #pragma unroll
@@ -488,15 +505,20 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
                 if (d.gu) { if (lane < 8) d.out[row] = va / (1.0f + expf(-va)) * vu; }
                 else d.out[(uint64_t)ch * d.rows + row] = va;
             }
+            __syncwarp();
+            if (lane == 0) S.red_count()[b] = 0;
         }
     }
 }
 
+// Types the kernel instance carries code for: a compile-time list (a
+// specialized instance) or all three (TQ4 = TQ6 = TQ8 = true).
+template <bool HAS_Q4, bool HAS_Q6, bool HAS_Q8>
 __device__ __forceinline__ void sk_mv_dispatch(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                                uint32_t xq_a, uint32_t xf_a) {
-    if (d.type == T_Q4_K) sk_mv_consume<T_Q4_K>(p, d, S, r, xq_a, xf_a);
-    else if (d.type == T_Q6_K) sk_mv_consume<T_Q6_K>(p, d, S, r, xq_a, xf_a);
-    else sk_mv_consume<T_Q8_0>(p, d, S, r, xq_a, xf_a);
+    if constexpr (HAS_Q4) if (d.type == T_Q4_K) { sk_mv_consume<T_Q4_K>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q6) if (d.type == T_Q6_K) { sk_mv_consume<T_Q6_K>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q8) if (d.type == T_Q8_0) { sk_mv_consume<T_Q8_0>(p, d, S, r, xq_a, xf_a); return; }
 }
 
 // ---------------------------------------------------------------------------
@@ -811,6 +833,11 @@ __device__ __forceinline__ void sk_argmax(const StepParams &p, const SkSmem &S, 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// Instances: step_kernel<0, true, true, true> serves every planned shape with
+// runtime type and head_dim dispatch; specialized instances carry only the
+// code their model uses (a kernel that runs every op of a step is large, and
+// its instruction fetch is otherwise a bottleneck).
+template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8>
 __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p) {
     static_assert(65536 / SK_THREADS / 8 * 8 >= SK_REG_LAUNCH, "launch register count");
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -835,6 +862,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             mbar_init(S.empty(i), SK_NCW);
         }
         *S.abort_flag() = 0;
+        for (uint32_t i = 0; i <= SK_MAXRING; ++i) S.red_count()[i] = 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -858,7 +886,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
         if (kind == K_ATTN) {
-            if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh);
+            if constexpr (HD != 0) sk_attn<HD>(p, l, pos, seq, S, r, sh);
+            else if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh);
             else sk_attn<64>(p, l, pos, seq, S, r, sh);
             continue;
         }
@@ -890,7 +919,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         }
         if (!work) continue;
         named_bar_sync(1, SK_CT);
-        sk_mv_dispatch(p, d, S, r, xq_u, xf_u);
+        sk_mv_dispatch<HAS_Q4, HAS_Q6, HAS_Q8>(p, d, S, r, xq_u, xf_u);
     }
 }
 
@@ -976,6 +1005,7 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
         gg.ntiles = (rows[k] + (k == STEP_GU ? 7 : 15)) / (k == STEP_GU ? 8 : 16);   // gate/up: 8 rows of each
         slot = std::max(slot, SL * gg.rs);
         if (k != STEP_DOWN && gg.nch != 1) return no("rows of this width do not fit one stage");
+        if (gg.ck > 4096) return no("stage chunks above 4096 columns");
     }
     {   // down: chunk-major units, every CTA within at most two chunks
         const StepMvGeom &gd = p.geo[STEP_DOWN];
@@ -986,7 +1016,7 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
         if (SK_SMEM - p.ring_off < ring) return no("shared-memory plan");
     }
     p.slot_bytes = (slot + 127) & ~127u;
-    p.nslots = std::min(SK_MAXSLOT, ring / p.slot_bytes);
+    p.nslots = std::min(SK_MAXRING, ring / p.slot_bytes);
     if (p.nslots < 2) return no("shared-memory ring too small");
     p.attn_splits = std::max(1u, std::min(SK_MAX_SPLITS, (uint32_t)n_sm / p.nkh));
     p.acc_layer = (uint64_t)(qd + 2 * kvd) + p.dim + p.ffn + (uint64_t)p.geo[STEP_DOWN].nch * p.dim;
@@ -1063,8 +1093,23 @@ cudaError_t step_repack(const StepParams &p, int op, const uint8_t *w0, const ui
     return cudaGetLastError();
 }
 
+// The Llama-3-8B mix: Q4_K attention and gate/up, Q6_K down and output, head_dim 128.
+static bool sk_is_8b_mix(const StepParams &p) {
+    return p.hd == 128 && p.t_qkv == T_Q4_K && p.t_o == T_Q4_K && p.t_gu == T_Q4_K && p.t_down == T_Q6_K &&
+           p.t_out == T_Q6_K;
+}
+static bool sk_is_q4k_only(const StepParams &p) {
+    return p.hd == 128 && p.t_qkv == T_Q4_K && p.t_o == T_Q4_K && p.t_gu == T_Q4_K && p.t_down == T_Q4_K &&
+           p.t_out == T_Q4_K;
+}
+
 cudaError_t step_configure() {
-    return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<0, true, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(step_kernel<128, true, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(step_kernel<128, true, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+    return e;
 }
 
 cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st) {
@@ -1079,7 +1124,9 @@ cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     note_launches(1);
-    return cudaLaunchKernelEx(&cfg, step_kernel, p);
+    if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false>, p);
+    if (sk_is_q4k_only(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, false, false>, p);
+    return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true>, p);
 }
 
 }  // namespace vbs
