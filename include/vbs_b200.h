@@ -204,6 +204,33 @@ VBS_API int vbs_cu_attention(const float *q, const uint16_t *kc, const uint16_t 
                      uint32_t n_kv_heads, uint32_t head_dim, float scale, uint32_t batch,
                      uint64_t kv_batch_stride, void *stream);
 
+/* vbs_cu_attention without any device allocation. No reference counterpart:
+ * an addition of this library for callers that cannot allocate device memory
+ * on the call path, e.g. code running under a fixed device-memory budget, or
+ * code where a cudaMalloc (which can fail, and can synchronize the device) is
+ * not acceptable in the middle of a decode loop. vbs_cu_attention grows a
+ * workspace on demand; this entry point uses a fixed scratch of 2 MiB per
+ * device in the library's static device memory instead.
+ *  - Limit: the split partials must fit the scratch. The number of splits is
+ *    lowered until they do; a call whose single-split need (about 64 KiB +
+ *    batch * n_kv_heads * 4 KiB at head_dim 128) is above 2 MiB fails with an
+ *    error naming the size.
+ *  - Setup: the first call on a device initialises the backend for that
+ *    device if needed and looks up the scratch address (cudaGetSymbolAddress
+ *    with that device current); make that first call before any stream
+ *    capture. Later calls allocate nothing.
+ *  - State: the scratch's merge counters are zero when the library loads and
+ *    every call leaves them at zero again; nothing else needs an initial
+ *    value.
+ *  - Concurrency: all calls on a device share the one scratch. Calls that
+ *    can overlap in time (different streams, or different host threads)
+ *    race on it and must be serialized by the caller.
+ * Arguments, layout and results as vbs_cu_attention. */
+VBS_API int vbs_cu_attention_static(const float *q, const uint16_t *kc, const uint16_t *vc, float *out,
+                                    uint32_t seq_len, uint32_t layer, uint32_t max_ctx, uint32_t n_q_heads,
+                                    uint32_t n_kv_heads, uint32_t head_dim, float scale, uint32_t batch,
+                                    uint64_t kv_batch_stride, void *stream);
+
 /* Seeded synthetic weights: the [rows x cols] tile at (row0, col0) of a
  * tensor with full_cols columns, element (r, c) drawn from the Irwin-Hall
  * (n = 4) normal approximation of stream `seed` at index r*full_cols + c,

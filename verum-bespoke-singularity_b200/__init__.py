@@ -142,6 +142,7 @@ def lib() -> C.CDLL:
         "vbs_cu_matvec": (i32, [i32, vp, vp, vp, u32, u32, u32, u32, vp]),
         "vbs_cu_ffn_gate_up": (i32, [i32, vp, vp, vp, vp, f32, vp, u32, u32, vp]),
         "vbs_cu_attention": (i32, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, f32, u32, u64, vp]),
+        "vbs_cu_attention_static": (i32, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, f32, u32, u64, vp]),
         "vbs_cu_synth": (i32, [i32, vp, u64, u64, u64, u64, u64, u64, f32, vp]),
         "vbs_cu_decoder_create": (vp, [C.POINTER(ModelDesc), u32, u32, C.c_char_p, sz]),
         "vbs_cu_decoder_destroy": (None, [vp]),
@@ -207,6 +208,14 @@ def ffn_gate_up(type_id, wg_ptr, wu_ptr, x_ptr, norm_ptr, eps, h_ptr, rows, cols
 def attention(q, kc, vc, out, seq_len, layer, max_ctx, nqh, nkh, hd, scale, batch=1, kv_batch_stride=0, stream=0):
     check(lib().vbs_cu_attention(q, kc, vc, out, seq_len, layer, max_ctx, nqh, nkh, hd, scale, batch,
                                  kv_batch_stride, stream or None), "vbs_cu_attention")
+
+
+def attention_static(q, kc, vc, out, seq_len, layer, max_ctx, nqh, nkh, hd, scale, batch=1, kv_batch_stride=0,
+                     stream=0):
+    """vbs_cu_attention_static: the same op with a fixed per-device scratch
+    and no device allocation (see include/vbs_b200.h for its limit)."""
+    check(lib().vbs_cu_attention_static(q, kc, vc, out, seq_len, layer, max_ctx, nqh, nkh, hd, scale, batch,
+                                        kv_batch_stride, stream or None), "vbs_cu_attention_static")
 
 
 def synth(type_id, dst_ptr, rows, cols, seed, scale, row0=0, col0=0, full_cols=None, stream=0) -> None:

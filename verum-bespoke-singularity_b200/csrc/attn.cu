@@ -451,6 +451,20 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_simt_kernel(const AttnParams 
 }
 
 // ---------------------------------------------------------------------------
+// Fixed scratch of the no-allocation entry point (vbs_cu_attention_static):
+// one per device, in the module's static device memory. Zero at module load;
+// every launch leaves its merge tickets at zero again, and the split partials
+// need no initial value.
+// ---------------------------------------------------------------------------
+constexpr size_t ATTN_STATIC_BYTES = 2u << 20;
+static __device__ __align__(256) unsigned char g_attn_static[ATTN_STATIC_BYTES];
+
+size_t attn_static_bytes() { return ATTN_STATIC_BYTES; }
+
+// Device address of the fixed scratch on the current device.
+cudaError_t attn_static_address(void **ptr) { return cudaGetSymbolAddress(ptr, g_attn_static); }
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t batch, uint32_t max_splits) {

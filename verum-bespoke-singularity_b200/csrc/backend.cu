@@ -594,6 +594,40 @@ int vbs_cu_attention(const float *q, const uint16_t *kc, const uint16_t *vc, flo
     return cuda_ok(attn_launch(ap, ns, static_cast<cudaStream_t>(stream), false), "attention") ? 0 : -1;
 }
 
+
+int vbs_cu_attention_static(const float *q, const uint16_t *kc, const uint16_t *vc, float *out, uint32_t seq_len,
+                            uint32_t layer, uint32_t max_ctx, uint32_t nqh, uint32_t nkh, uint32_t hd, float scale,
+                            uint32_t batch, uint64_t kv_batch_stride, void *stream) {
+    DevState *d = backend_current();
+    if (!d) { latch_error("vbs_cu_attention_static: no usable device"); return -1; }
+    if (!q || !kc || !vc || !out || !seq_len || seq_len > max_ctx || !batch || !nkh) {
+        latch_error("vbs_cu_attention_static: invalid arguments");
+        return -1;
+    }
+    if (!d->attn_static) {   // first call on this device: look the scratch up (its device is current here)
+        void *ptr = nullptr;
+        if (!cuda_ok(attn_static_address(&ptr), "vbs_cu_attention_static: scratch address")) return -1;
+        d->attn_static = ptr;
+    }
+    // as many splits as the fixed scratch holds, never more than the allocating entry point uses
+    uint32_t ns = attn_num_splits(seq_len, nkh, batch, d->n_sm);
+    while (ns > 1 && attn_workspace_bytes(nqh, nkh, hd, batch, ns) > attn_static_bytes()) --ns;
+    const size_t need = attn_workspace_bytes(nqh, nkh, hd, batch, ns);
+    if (need > attn_static_bytes()) {
+        latch_error("vbs_cu_attention_static: batch %u x %u KV heads x head_dim %u needs %zu bytes of scratch, above the "
+                    "fixed %zu; use vbs_cu_attention",
+                    batch, nkh, hd, need, attn_static_bytes());
+        return -1;
+    }
+    AttnParams ap = {};
+    ap.q = q; ap.kc = kc; ap.vc = vc; ap.out = out;
+    ap.seq_len = seq_len; ap.layer = layer; ap.max_ctx = max_ctx;
+    ap.nqh = nqh; ap.nkh = nkh; ap.hd = hd; ap.scale = scale;
+    ap.batch = batch; ap.kv_batch_stride = kv_batch_stride; ap.err = d->err;
+    ap.work = d->attn_static;
+    return cuda_ok(attn_launch(ap, ns, static_cast<cudaStream_t>(stream), false), "attention (static scratch)") ? 0 : -1;
+}
+
 int vbs_cu_synth(int type, void *dst, uint64_t rows, uint64_t cols, uint64_t row0, uint64_t col0, uint64_t full_cols,
                  uint64_t seed, float scale, void *stream) {
     DevState *d = backend_current();

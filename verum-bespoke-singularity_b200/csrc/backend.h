@@ -14,6 +14,7 @@ struct DevState {
     uint32_t *err = nullptr;        // device error word (see common.cuh)
     void *attn_work = nullptr;      // shared split-KV workspace for the ops table / vbs_cu_attention
     size_t attn_work_bytes = 0;
+    void *attn_static = nullptr;    // address of the fixed scratch of vbs_cu_attention_static
 };
 
 // Devices usable by this library (sm_100). Index = position in the ops

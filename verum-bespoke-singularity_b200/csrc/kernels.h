@@ -110,6 +110,10 @@ size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t ba
 uint32_t attn_num_splits(uint32_t seq_len_hint, uint32_t nkh, uint32_t batch, int n_sm);
 cudaError_t attn_launch(const AttnParams &p, uint32_t n_splits, cudaStream_t st, bool pdl);
 cudaError_t attn_configure();
+// The fixed per-device scratch of vbs_cu_attention_static: its size, and its
+// address on the current device.
+size_t attn_static_bytes();
+cudaError_t attn_static_address(void **ptr);
 
 // argmax over n floats (first maximum wins); writes out_token and, when
 // ctrl != NULL, advances ctrl[0] (position) by one, stores the token in
