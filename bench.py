@@ -53,6 +53,10 @@ def parse():
                     choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
+    ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
+    ap.add_argument("--vocab", type=int, default=128256, help="--profile decode: vocabulary rows")
+    ap.add_argument("--per-op", action="store_true",
+                    help="--profile decode: the per-op kernels (one launch per op) instead of the one-launch step")
     return ap.parse_args()
 
 
@@ -72,18 +76,20 @@ def profile_kernel(args):
     if args.profile == "decode":
         # the full decode step at position --ctx (the cache rows before it
         # are zeros: same bytes and kernels as a prefilled cache), then
-        # --steps graph replays
+        # --steps graph replays; --layers/--vocab cut the model for a small
+        # ncu case
         import models
-        model = vbs.synth_llama(models.shape_of(models.L8B), models.L8B_TYPES, seed=2024)
-        dec = vbs.Decoder(model, args.ctx + args.steps + 8)
+        cfg = dict(models.L8B, n_layers=args.layers, vocab=args.vocab)
+        model = vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=2024)
+        dec = vbs.Decoder(model, args.ctx + args.steps + 8, vbs.DEC_NO_PERSIST if args.per_op else 0)
         dec.forward([1], logits=False)
         dec.set_position(args.ctx - 1, 1)
         torch.cuda.synchronize()
         for i in range(args.steps):
             dec.enqueue_steps(1)
         torch.cuda.synchronize()
-        print(json.dumps({"profile": "decode", "ctx": args.ctx, "kernels_per_step": dec.kernels_per_step,
-                          "steps": args.steps}))
+        print(json.dumps({"profile": "decode", "ctx": args.ctx, "layers": args.layers, "vocab": args.vocab,
+                          "kernels_per_step": dec.kernels_per_step, "steps": args.steps}))
         dec.close()
         return
     if args.profile == "attention":
@@ -353,12 +359,34 @@ def main():
         e2e_s = float(t.item())
     e2e_tok_s = (args.e2e_steps - 1) / e2e_s
 
-    # roofline of the dominant kernel: fused norm + gate/up + SiLU (two Q4_K
-    # [14336 x 4096] per layer, 66 MB), timed live over all 32 layers' weights
-    # (2.1 GB, so no launch finds its weights in L2)
+    # roofline of the dominant kernel. One GPU: the persistent step kernel
+    # is the whole step (one launch per token, timed above on its stream);
+    # its algorithmic bytes are the step's weights + KV. Otherwise (the
+    # per-op kernels under TP): fused norm + gate/up + SiLU, two Q4_K
+    # [14336 x 4096] per layer (66 MB), timed live over all 32 layers'
+    # weights (2.1 GB, so no launch finds its weights in L2).
     peak, peak_kind = peaks()
     roof = None
-    if world == 1:
+    step_bytes = L8B_WEIGHT_BYTES + KV_BYTES_PER_POS * ctx_mid
+
+    def committed_traffic(name):
+        # DRAM bytes of one launch (dram__bytes_read.sum + dram__bytes_write.sum)
+        # from the committed ncu summary of that kernel
+        tf = ROOT / "profiles" / name
+        if tf.exists():
+            import re
+            mt = re.search(r"dram_bytes_per_launch:\s*(\d+)", tf.read_text())
+            return int(mt.group(1)) if mt else None
+        return None
+
+    if world == 1 and kps == 1:
+        achieved = step_bytes / (ms_step * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "step_kernel (persistent decode step: every op of a token, one launch)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_kind": peak_kind, "traffic": committed_traffic("step_kernel_decode_l8b_ctx4096.md"),
+                "algorithmic_bytes": int(step_bytes), "launch_us": round(ms_step * 1e3, 2),
+                "frac_of_8tbs": round(achieved / 8000.0, 4)}
+    elif world == 1:
         x = torch.randn(shape.dim, device="cuda")
         h = torch.empty(shape.ffn, device="cuda")
         nrm = model.tensors["blk.0.ffn_norm"]
@@ -379,20 +407,12 @@ def main():
         k_ms = e0.elapsed_time(e1) / shape.n_layers
         alg = FFN_GATE_UP_BYTES + shape.dim * 4 + shape.ffn * 4
         achieved = alg / (k_ms * 1e-3) / 1e9
-        # DRAM bytes of one launch from the committed ncu summary of this
-        # kernel (dram__bytes_read.sum + dram__bytes_write.sum)
-        traffic = None
-        tf = ROOT / "profiles" / "mv_fast_kernel_ffn_gate_up_q4k_8b.md"
-        if tf.exists():
-            import re
-            mt = re.search(r"dram_bytes_per_launch:\s*(\d+)", tf.read_text())
-            traffic = int(mt.group(1)) if mt else None
+        traffic = committed_traffic("mv_fast_kernel_ffn_gate_up_q4k_8b.md")
         roof = {"bound": "hbm", "kernel": "mv_fast_kernel<Q4_K,dual,SILU> (norm+gate/up+SiLU)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": alg, "launch_us": round(k_ms * 1e3, 2),
                 "frac_of_8tbs": round(achieved / 8000.0, 4)}
 
-    step_bytes = L8B_WEIGHT_BYTES + KV_BYTES_PER_POS * ctx_mid
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
