@@ -144,15 +144,39 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """SM clocks and clock-event (throttle) reasons during the timed region.
+
+    NVML is polled every 5 ms from a thread (read-only queries); only the
+    samples taken between mark() and stop() count. Without NVML it falls
+    back to `nvidia-smi -lms 100`."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    # nvmlClocksEventReason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index: int):
-        self.idx, self.rows, self.proc = gpu_index, [], None
+        self.idx, self.rows, self.proc, self.nvml = gpu_index, [], None, None
+        self.t0 = self.t1 = None
+        self.stop_evt = threading.Event()
 
     def __enter__(self):
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            h = None
+            try:   # the CUDA device's own GPU: NVML indices ignore CUDA_VISIBLE_DEVICES
+                import torch
+                h = N.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(self.idx).uuid))
+            except Exception:
+                h = N.nvmlDeviceGetHandleByIndex(self.idx)
+            self.nvml = (N, h)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -163,13 +187,34 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def mark(self):
+        self.t0 = time.monotonic()
+
+    def stop(self):
+        self.t1 = time.monotonic()
+
+    def _poll(self):
+        N, h = self.nvml
+        get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            N.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_evt.is_set():
+            try:
+                t = time.monotonic()
+                self.rows.append((t, float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)), int(get_reasons(h))))
+            except Exception:
+                pass
+            time.sleep(0.005)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
-                self.rows.append(parts)
+                self.rows.append((time.monotonic(), parts))
 
     def __exit__(self, *a):
+        self.stop_evt.set()
+        if self.nvml:
+            self.t.join(1)
         if self.proc:
             self.proc.terminate()
             try:
@@ -177,15 +222,28 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
+    def _window(self):
+        t0 = self.t0 if self.t0 is not None else -1e30
+        t1 = self.t1 if self.t1 is not None else 1e30
+        inside = [r for r in self.rows if t0 <= r[0] <= t1]
+        return inside or self.rows[-1:]
+
     def summary(self):
-        if not self.rows:
+        rows = self._window() if self.rows else []
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        if self.nvml:
+            sm = [r[1] for r in rows]
+            reasons = sorted({k for r in rows for k, b in self.BITS.items() if r[2] & b})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(self.max_mhz), "reasons": reasons,
+                    "samples": len(rows), "source": "nvml 5 ms"}
+        rows = [r[1] for r in rows]
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi 100 ms"}
 
 
 # ---------------------------------------------------------------------------
@@ -323,10 +381,12 @@ def main():
     with ClockSampler(local) as clk:
         time.sleep(0.3)
         torch.cuda.synchronize()
+        clk.mark()
         ev0.record(stream)
         dec.enqueue_steps(args.steps)
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.stop()
     launches = vbs.kernel_launches() - l0
     ms = ev0.elapsed_time(ev1)
     if dist:

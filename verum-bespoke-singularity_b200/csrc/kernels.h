@@ -164,7 +164,7 @@ struct StepParams {
     uint32_t hist_cap;
     uint32_t *err;
     StepMvGeom geo[5];          // by STEP_* op
-    uint32_t slot_bytes, nslots, x_off, xq_off, xf_off, ring_off;   // shared-memory plan
+    uint32_t ring_bytes, stage_max, x_off, xq_off, xf_off, ring_off;   // shared-memory plan (byte ring)
 };
 
 // Element (pos, i) of one layer's KV block in the step kernel's cache:

@@ -255,19 +255,33 @@ __device__ __forceinline__ void quant_block8(const float v[8], uint32_t u, uint3
     amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
     const float d2 = amax * (1.0f / (127.0f * 254.0f));
     const float d1 = d2 * 254.0f;
-    const float r1 = d1 > 0.0f ? __frcp_rn(d1) : 0.0f, r2 = d2 > 0.0f ? __frcp_rn(d2) : 0.0f;
-    uint32_t q1w[2] = {0u, 0u}, q2w[2] = {0u, 0u};
+    float r1 = 0.0f, r2 = 0.0f;
+    if (d2 > 0.0f) {   // approximate reciprocals: only the rounding of x changes, the scales d1, d2 are exact
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r2) : "f"(d2));
+    }
+    // Round to nearest even by adding 1.5 * 2^23: the float's low mantissa
+    // bits are then the integer (two's complement in the low byte), and
+    // t - 1.5 * 2^23 is that integer as an exact float. |q| <= 127 by the
+    // choice of d1, d2; the clamps guard the approximate reciprocals.
+    constexpr float kMagic = 12582912.0f;
+    constexpr int kMagicBits = 0x4B400000;
+    uint32_t t1[8], t2[8];
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        int a = __float2int_rn(v[i] * r1);
-        a = max(-127, min(127, a));
-        const float res = fmaf(-(float)a, d1, v[i]);
-        int b = __float2int_rn(res * r2);
-        b = max(-127, min(127, b));
-        q1w[i >> 2] |= (uint32_t)(a & 0xFF) << (8 * (i & 3));
-        q2w[i >> 2] |= (uint32_t)(b & 0xFF) << (8 * (i & 3));
-        sum += 254 * a + b;
+        const float a = fminf(fmaxf(v[i] * r1, -127.0f), 127.0f) + kMagic;
+        const float res = fmaf(-(a - kMagic), d1, v[i]);
+        const float b = fminf(fmaxf(res * r2, -127.0f), 127.0f) + kMagic;
+        t1[i] = __float_as_uint(a);
+        t2[i] = __float_as_uint(b);
+        sum += 254 * (__float_as_int(a) - kMagicBits) + (__float_as_int(b) - kMagicBits);
+    }
+    uint32_t q1w[2], q2w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {   // low bytes of four words -> one word
+        q1w[k] = __byte_perm(__byte_perm(t1[4 * k], t1[4 * k + 1], 0x0040u), __byte_perm(t1[4 * k + 2], t1[4 * k + 3], 0x0040u), 0x5410u);
+        q2w[k] = __byte_perm(__byte_perm(t2[4 * k], t2[4 * k + 1], 0x0040u), __byte_perm(t2[4 * k + 2], t2[4 * k + 3], 0x0040u), 0x5410u);
     }
     // this thread holds words 2u and 2u+1 of the block
     uint8_t *blk = xq + (size_t)J * xq_stride<PLAIN>();

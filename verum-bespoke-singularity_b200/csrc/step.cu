@@ -5,8 +5,8 @@
 //   QKV   RMSNorm(attn_norm) + Q/K/V matvec
 //   ATTN  RoPE + fp16 KV store + split-KV GQA attention
 //   O     o_proj matvec
-//   GU    residual add + RMSNorm(ffn_norm) + gate/up matvecs
-//   DOWN  SiLU(gate)*up + down matvec
+//   GU    residual add + RMSNorm(ffn_norm) + gate/up matvecs + SiLU(gate)*up
+//   DOWN  down matvec
 // then the residual add + RMSNorm(output_norm) + output matvec, and the
 // greedy argmax. Launched as one kernel per op, every op pays a launch, a
 // prologue and a pipeline fill and drain; on the small per-layer matrices
@@ -23,10 +23,12 @@
 //  * Eight consumer warps run the ops. Between ops a grid barrier (one
 //    counter in global memory, acquire/release, bounded spin) orders the
 //    activations. Matvec units are (16-row tile x column chunk), split into
-//    equal contiguous ranges per CTA; a row's partial dot products go to a
-//    zeroed fp32 buffer with atomicAdd. The plan guarantees at most two
-//    contributions per row, and fp32 addition is commutative, so the sums
-//    are deterministic.
+//    equal contiguous ranges per CTA. Each unit's row sums are stored
+//    (plain stores, one writer per element) into its chunk's plane of
+//    partial sums; the reader adds the planes in chunk order, so the sums
+//    are deterministic and nothing needs clearing between steps. Only the
+//    down projection is split into column chunks; every other matvec has
+//    one chunk.
 //  * What follows a matvec in the reference (residual add, RMSNorm, SiLU,
 //    RoPE) is applied by the NEXT op as it reads the complete sums: every
 //    CTA keeps its own copy of the residual stream x in shared memory and
@@ -58,9 +60,10 @@ constexpr int SK_THREADS = SK_CT + 128;            // + the producer warpgroup (
 // 256 x 232 + 128 x 40 = 64512, exactly the launch total.
 constexpr uint32_t SK_REG_LAUNCH = 168, SK_REG_CONSUMER = 232, SK_REG_PRODUCER = 40;
 static_assert(SK_CT * SK_REG_CONSUMER + 128 * SK_REG_PRODUCER <= SK_THREADS * SK_REG_LAUNCH, "register split");
-constexpr uint32_t SK_MAXSLOT = 16;
-constexpr uint32_t SK_HDR = 8192;                  // barriers, flags, reduction buffers
-constexpr uint32_t SK_MAXRING = 7;                 // ring slots (SK_MAXRING + 1 unit reduction buffers)
+constexpr uint32_t SK_NB = 8;                      // stages in flight at most (full/empty barrier pairs)
+constexpr uint32_t SK_NU = 8;                      // matvec units per row-sum batch
+constexpr uint32_t SK_RED = 2048;                  // row-sum batches: [2][SK_NU][8 warps][16 rows] floats
+constexpr uint32_t SK_HDR = SK_RED + 2 * SK_NU * 8 * 16 * 4;   // barriers, flags, row-sum batches
 constexpr uint32_t SK_SMEM = 227u * 1024u;
 constexpr uint32_t SK_AP = 64;                     // attention positions per stage
 constexpr uint32_t SK_MAX_SPLITS = 128;
@@ -231,40 +234,74 @@ __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t targe
 struct SkSmem {
     uint32_t base;                 // shared address of the dynamic buffer
     uint8_t *ptr;
-    uint32_t ring, slot_bytes, nslots;
-    __device__ uint32_t full(uint32_t s) const { return base + 8u * s; }
-    __device__ uint32_t empty(uint32_t s) const { return base + 8u * (SK_MAXSLOT + s); }
-    __device__ uint32_t slot(uint32_t s) const { return ring + s * slot_bytes; }
+    uint32_t ring, ring_bytes;     // the stage ring: shared address and size
+    __device__ uint32_t full(uint32_t i) const { return base + 8u * (i % SK_NB); }            // of stage i
+    __device__ uint32_t empty(uint32_t i) const { return base + 8u * (SK_NB + i % SK_NB); }
     __device__ volatile int *abort_flag() const { return reinterpret_cast<volatile int *>(ptr + 256); }
     __device__ volatile int *sync_flag() const { return reinterpret_cast<volatile int *>(ptr + 260); }
-    __device__ int *red_count() const { return reinterpret_cast<int *>(ptr + 320); }            // [SK_MAXRING + 1]
     __device__ uint32_t *scratch_u() const { return reinterpret_cast<uint32_t *>(ptr + 512); }   // 64 words
     __device__ float *misc() const { return reinterpret_cast<float *>(ptr + 1024); }            // 256 floats
-    __device__ float *red() const { return reinterpret_cast<float *>(ptr + 2048); }             // [SK_MAXRING + 1][8][16]
+    __device__ float *red() const { return reinterpret_cast<float *>(ptr + SK_RED); }          // [2][SK_NU][8][16]
 };
+static_assert(16 * SK_NB <= 256 && SK_HDR % 1024 == 0, "shared-memory header");
 
+// Position in the stage sequence, walked identically by the producer and the
+// consumers. Stages take their own size from a ring of bytes (a stage never
+// straddles the end: it starts over at 0), so small stages (attention,
+// Q4_K) keep more bytes in flight than the largest stage would allow in
+// fixed slots. Stage i uses barrier pair i % SK_NB; the phase parity of its
+// use is (i / SK_NB) & 1.
 struct SkRing {
-    uint32_t slot = 0, round = 0;
-    __device__ void advance(uint32_t nslots) {
-        if (++slot == nslots) { slot = 0; ++round; }
+    uint32_t idx = 0, off = 0;
+    __device__ __forceinline__ uint32_t place(uint32_t bytes, uint32_t ring_bytes) {
+        if (off + bytes > ring_bytes) off = 0;
+        return off;
     }
+    __device__ __forceinline__ uint32_t parity() const { return (idx / SK_NB) & 1u; }
+    __device__ __forceinline__ void advance(uint32_t bytes) { off += bytes; ++idx; }
 };
 
 // ---------------------------------------------------------------------------
 // producer
 // ---------------------------------------------------------------------------
+// Before stage r.idx of `bytes` may be issued, every older stage that held
+// any of its bytes, and the stage SK_NB back that used its barrier pair, must
+// be released by the consumers. Lane j of the producer warp tracks the
+// in-flight stage with index = j (mod SK_NB): its byte range and whether it
+// is still held. Stages are released in order, so the producer waits on the
+// oldest one until the new range is free.
+struct SkInflight {
+    uint32_t s = 0, e = 0, tail = 0;   // lane's stage [s, e); oldest stage not seen released
+    bool held = false;
+};
+
+__device__ __forceinline__ bool sk_reserve(const StepParams &p, const SkSmem &S, SkRing &r, SkInflight &f,
+                                           uint32_t bytes, int lane) {
+    const uint32_t o = r.place(bytes, S.ring_bytes);
+    for (;;) {
+        const bool clash = f.held && f.s < o + bytes && o < f.e;
+        if (!__any_sync(0xffffffffu, clash) && r.idx - f.tail < SK_NB) return true;
+        if (!sk_wait(S.empty(f.tail), (f.tail / SK_NB) & 1u, p.sync + 1)) {
+            if (lane == 0) sk_abort(p, DERR_TIMEOUT_EMPTY);
+            return false;
+        }
+        if ((uint32_t)lane == f.tail % SK_NB) f.held = false;
+        ++f.tail;
+    }
+}
+
+__device__ __forceinline__ void sk_issued(SkRing &r, SkInflight &f, uint32_t bytes, int lane) {
+    if ((uint32_t)lane == r.idx % SK_NB) { f.s = r.off; f.e = r.off + bytes; f.held = true; }
+    __syncwarp();
+    r.advance(bytes);
+}
+
 __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S, uint32_t seq) {
     const int lane = threadIdx.x & 31;
     const uint32_t nops = 5 * p.n_layers + 2;
     SkRing r;
-    uint32_t issued = 0;
+    SkInflight f;
     bool ok = true;
-    auto acquire = [&]() -> bool {
-        if (issued < S.nslots) return true;
-        if (sk_wait(S.empty(r.slot), (r.round - 1) & 1, p.sync + 1)) return true;
-        if (lane == 0) sk_abort(p, DERR_TIMEOUT_EMPTY);
-        return false;
-    };
     for (uint32_t i = 0; i < nops && ok; ++i) {
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
@@ -272,18 +309,17 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
         if (kind == K_ATTN) {
             const SkAttn a = sk_attn_unit(p, seq);
             const uint64_t hb = (((uint64_t)l * p.nkh + a.h) * p.max_ctx) * p.hd;
-            const uint32_t rowb = p.hd * 2;
+            const uint32_t rowb = p.hd * 2, sb = 2 * SK_AP * rowb;   // K rows, then V rows at SK_AP * rowb
             for (uint32_t s = 0; s < a.nst; ++s) {
-                if (!acquire()) { ok = false; break; }
+                if (!sk_reserve(p, S, r, f, sb, lane)) { ok = false; break; }
                 const uint32_t t = a.t0 + s * SK_AP, len = min(SK_AP, a.t1 - t), bytes = len * rowb;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(S.full(r.slot), 2 * bytes);
-                    bulk_g2s(S.slot(r.slot), p.kc + hb + (uint64_t)t * p.hd, bytes, S.full(r.slot));
-                    bulk_g2s(S.slot(r.slot) + SK_AP * rowb, p.vc + hb + (uint64_t)t * p.hd, bytes, S.full(r.slot));
+                    const uint32_t dst = S.ring + r.off;
+                    mbar_arrive_expect_tx(S.full(r.idx), 2 * bytes);
+                    bulk_g2s(dst, p.kc + hb + (uint64_t)t * p.hd, bytes, S.full(r.idx));
+                    bulk_g2s(dst + SK_AP * rowb, p.vc + hb + (uint64_t)t * p.hd, bytes, S.full(r.idx));
                 }
-                __syncwarp();
-                ++issued;
-                r.advance(S.nslots);
+                sk_issued(r, f, sb, lane);
             }
             continue;
         }
@@ -292,22 +328,19 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
         uint32_t u0, u1;
         sk_range(d.g.ntiles * d.g.nch, u0, u1);
         for (uint32_t u = u0; u < u1; ++u) {
-            if (!acquire()) { ok = false; break; }
+            if (!sk_reserve(p, S, r, f, bytes, lane)) { ok = false; break; }
             uint32_t tile, ch;
             sk_unit(d, u, tile, ch);
             if (lane == 0) {
-                mbar_arrive_expect_tx(S.full(r.slot), bytes);
-                bulk_g2s(S.slot(r.slot), d.packed + (uint64_t)(tile * d.g.nch + ch) * bytes, bytes, S.full(r.slot));
+                mbar_arrive_expect_tx(S.full(r.idx), bytes);
+                bulk_g2s(S.ring + r.off, d.packed + (uint64_t)(tile * d.g.nch + ch) * bytes, bytes, S.full(r.idx));
             }
-            __syncwarp();
-            ++issued;
-            r.advance(S.nslots);
+            sk_issued(r, f, bytes, lane);
         }
     }
     if (!ok) {
         // wait (bounded) for copies still in flight before the CTA may exit
-        const uint32_t first = issued > S.nslots ? issued - S.nslots : 0;
-        for (uint32_t s = first; s < issued; ++s) mbar_wait_bounded(S.full(s % S.nslots), (s / S.nslots) & 1, kWaitNs);
+        for (uint32_t s = f.tail; s < r.idx; ++s) mbar_wait_bounded(S.full(s), (s / SK_NB) & 1u, kWaitNs);
     }
 }
 
@@ -434,15 +467,15 @@ __device__ __forceinline__ void sk_prologue_vec(uint32_t n, int type, F load8, u
 
 // ---------------------------------------------------------------------------
 // matvec consumer: this CTA's units of one op. The 8 warps split each
-// stage's 256-column super-blocks; at the end of the CTA's part of a tile the
-// row sums go out: one atomicAdd per row (at most two CTAs share a row), or
-// for whole gate/up rows SiLU(gate)*up stored directly.
+// stage's 256-column super-blocks; the unit's row sums go out with plain
+// stores into its column chunk's plane, or for gate/up rows as
+// SiLU(gate)*up.
 // ---------------------------------------------------------------------------
 template <int TYPE>
 __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                               uint32_t xq_a, uint32_t xf_a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
-    const uint32_t RS = d.g.rs, CK = d.g.ck;
+    const uint32_t RS = d.g.rs, CK = d.g.ck, SB = 16u * RS;
     volatile int *cta_abort = S.abort_flag();
     float *red = S.red();
     uint32_t u0, u1;
@@ -451,14 +484,13 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
         uint32_t tile, ch;
         sk_unit(d, u, tile, ch);
         // one decision per warp: the MMAs and shuffles below need all 32 lanes
-        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.slot), r.round & 1, p.sync + 1));
+        const uint32_t ms = S.ring + r.place(SB, S.ring_bytes);
+        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
         if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
         float acc[2] = {0.f, 0.f};
         if (got) {
             const uint32_t c0 = ch * CK, c1 = min(d.cols, c0 + CK);
-            // packed rows start 16-byte aligned in the slot: no alignment pads;
-            // two super-blocks per warp interleave their independent MMA chains
-            const uint32_t ms = S.slot(r.slot);
+            // packed rows start 16-byte aligned in the stage: no alignment pads
             // chunks are at most 16 super-blocks (the plan caps them at 4096
             // columns): at most two per warp, as straight-line code so their
             // independent load/MMA chains interleave
@@ -467,46 +499,47 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
             if (c0 + e1 < c1) mv_unit<TYPE, true>(ms, RS, 0u, 0u, e1, (c0 + e1) >> 5, xq_a, xf_a, lane, c1 - c0 - e1, acc);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(S.empty(r.slot));
-        r.advance(S.nslots);
-        // the unit's row sums: over the thread columns, then the warps. No
-        // CTA barrier: each warp leaves its partials in the unit's buffer and
-        // the last of the 8 to arrive sums them in warp order and writes the
-        // rows. A warp runs at most nslots units ahead of the slowest (slot
-        // reuse waits for all of them), so nslots + 1 buffers never collide.
+        if (lane == 0) mbar_arrive(S.empty(r.idx));
+        r.advance(SB);
+        // the unit's row sums: over the thread columns here, then over the
+        // warps for a batch of SK_NU units at once: each warp leaves its 16
+        // partials in the batch buffer, and after one consumer barrier the
+        // threads sum the batch's rows in warp order and write them. Batches
+        // alternate between two buffers, so the next batch's partials never
+        // meet a buffer still being read (its writers passed that barrier).
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
             acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 1);
             acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 2);
         }
-        const uint32_t b = (u - u0) % (S.nslots + 1);
-        float *rbuf = red + b * (SK_NCW * 16);
+        const uint32_t k = u - u0, slot = k % SK_NU;
+        float *batch = red + ((k / SK_NU) & 1u) * (SK_NU * SK_NCW * 16);
         if ((lane & 3) == 0) {
-            rbuf[warp * 16 + g] = acc[0];
-            rbuf[warp * 16 + g + 8] = acc[1];
+            batch[(slot * SK_NCW + warp) * 16 + g] = acc[0];
+            batch[(slot * SK_NCW + warp) * 16 + g + 8] = acc[1];
         }
-        __syncwarp();
-        int arrived = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            arrived = atomicAdd(S.red_count() + b, 1);
-        }
-        arrived = __shfl_sync(0xffffffffu, arrived, 0);
-        if (arrived == SK_NCW - 1) {
-            __threadfence_block();
-            const uint32_t li = (uint32_t)lane & 15u;
-            float va = 0.f;
+        if (slot == SK_NU - 1 || u + 1 == u1) {
+            named_bar_sync(1, SK_CT);
+            const uint32_t n = slot + 1, j = threadIdx.x >> 4, rr = threadIdx.x & 15u;
+            if (j < n && !*cta_abort) {
+                uint32_t tile, ch;
+                sk_unit(d, u - slot + j, tile, ch);
+                const float *b = batch + j * SK_NCW * 16;
+                float va = 0.f;
 #pragma unroll
-            for (int w = 0; w < SK_NCW; ++w) va += rbuf[w * 16 + li];
-            const float vu = __shfl_sync(0xffffffffu, va, (lane & 7) + 8);   // up sum of the same row
-            const uint32_t row = sk_slot_row(d.gu != 0, tile, li);
-            if (lane < 16 && row < d.rows && !*cta_abort) {
-                // h = SiLU(gate) * up (src/vbs_host_math.h:53-57)
-                if (d.gu) { if (lane < 8) d.out[row] = va / (1.0f + expf(-va)) * vu; }
-                else d.out[(uint64_t)ch * d.rows + row] = va;
+                for (int w = 0; w < SK_NCW; ++w) va += b[w * 16 + rr];
+                const uint32_t row = sk_slot_row(d.gu != 0, tile, rr);
+                if (d.gu) {   // h = SiLU(gate) * up (src/vbs_host_math.h:53-57): slot rr < 8 gate, rr + 8 up
+                    if (rr < 8 && row < d.rows) {
+                        float vu = 0.f;
+#pragma unroll
+                        for (int w = 0; w < SK_NCW; ++w) vu += b[w * 16 + rr + 8];
+                        d.out[row] = va / (1.0f + expf(-va)) * vu;
+                    }
+                } else if (row < d.rows) {
+                    d.out[(uint64_t)ch * d.rows + row] = va;
+                }
             }
-            __syncwarp();
-            if (lane == 0) S.red_count()[b] = 0;
         }
     }
 }
@@ -590,12 +623,13 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
 
     for (uint32_t s = 0; s < a.nst; ++s) {
         // one decision per warp: the MMAs and shuffles below need all 32 lanes
-        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.slot), r.round & 1, p.sync + 1));
+        const uint32_t stg = S.ring + r.place(2 * SK_AP * ROWB, S.ring_bytes);
+        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
         if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
         const uint32_t ts = a.t0 + s * SK_AP, tb = ts + 16 * wl;
         if (got && (int)(s & 1) == grp && tb < a.t1) {
-            const uint32_t kst = S.slot(r.slot) + 16 * wl * ROWB;
-            const uint32_t vst = S.slot(r.slot) + SK_AP * ROWB + 16 * wl * ROWB;
+            const uint32_t kst = stg + 16 * wl * ROWB;
+            const uint32_t vst = stg + SK_AP * ROWB + 16 * wl * ROWB;
             // rows past the end of the unit: zero V (p = 0 must not meet stale bits)
             if (tb + 16 > a.t1) {
                 const uint32_t nv = a.t1 - tb;
@@ -680,8 +714,8 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(S.empty(r.slot));
-        r.advance(S.nslots);
+        if (lane == 0) mbar_arrive(S.empty(r.idx));
+        r.advance(2 * SK_AP * ROWB);
     }
 
     // warp states -> shared memory, merge over the 8 warps
@@ -845,8 +879,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     S.ptr = smem;
     S.base = smem_u32(smem);
     S.ring = S.base + p.ring_off;
-    S.slot_bytes = p.slot_bytes;
-    S.nslots = p.nslots;
+    S.ring_bytes = p.ring_bytes;
     const int warp = threadIdx.x >> 5;
     // read once: the last CTA rewrites the control block at the end of the step
     const uint32_t pos = *reinterpret_cast<const volatile uint32_t *>(p.ctrl);
@@ -857,12 +890,11 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     }
     const uint32_t seq = pos + 1;
     if (threadIdx.x == 0) {
-        for (uint32_t i = 0; i < S.nslots; ++i) {
+        for (uint32_t i = 0; i < SK_NB; ++i) {
             mbar_init(S.full(i), 1);
             mbar_init(S.empty(i), SK_NCW);
         }
         *S.abort_flag() = 0;
-        for (uint32_t i = 0; i <= SK_MAXRING; ++i) S.red_count()[i] = 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -1015,9 +1047,9 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
         plan_smem(gd.ck);
         if (SK_SMEM - p.ring_off < ring) return no("shared-memory plan");
     }
-    p.slot_bytes = (slot + 127) & ~127u;
-    p.nslots = std::min(SK_MAXRING, ring / p.slot_bytes);
-    if (p.nslots < 2) return no("shared-memory ring too small");
+    p.stage_max = slot;
+    p.ring_bytes = ring & ~127u;
+    if (p.ring_bytes < 2 * slot) return no("shared-memory ring too small");
     p.attn_splits = std::max(1u, std::min(SK_MAX_SPLITS, (uint32_t)n_sm / p.nkh));
     p.acc_layer = (uint64_t)(qd + 2 * kvd) + p.dim + p.ffn + (uint64_t)p.geo[STEP_DOWN].nch * p.dim;
     return true;
