@@ -363,10 +363,26 @@ __device__ __forceinline__ void ld8_g(const float *src, float v[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-__device__ __forceinline__ void sk_quant(int type, const float v[8], uint32_t u, uint32_t qmask, uint32_t J, uint8_t *xq,
-                                         float4 *xf) {
+// The prologues run once per op: their code is cold in the instruction
+// cache every time, so it is kept to one out-of-line copy per routine
+// instead of being inlined at every call site and unrolled iteration.
+__device__ __noinline__ void sk_quant(int type, float v0, float v1, float v2, float v3, float v4, float v5, float v6,
+                                      float v7, uint32_t u, uint32_t qmask, uint32_t J, uint8_t *xq, float4 *xf) {
+    const float v[8] = {v0, v1, v2, v3, v4, v5, v6, v7};
     if (type == T_Q6_K) quant_block8<true>(v, u, qmask, J, xq, xf);
     else quant_block8<false>(v, u, qmask, J, xq, xf);
+}
+__device__ __forceinline__ void sk_quant(int type, const float v[8], uint32_t u, uint32_t qmask, uint32_t J, uint8_t *xq,
+                                         float4 *xf) {
+    sk_quant(type, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], u, qmask, J, xq, xf);
+}
+
+// Elements e..e+7 of the embedding row of `token` (src/vbs_host_math.h:136-142).
+__device__ __noinline__ void sk_embed8(const StepParams &p, uint32_t token, uint32_t e, float *out) {
+    const uint32_t E = (uint32_t)block_elems(p.t_embd), BB = (uint32_t)block_bytes(p.t_embd);
+    const uint8_t *row = p.embd + (uint64_t)token * row_bytes(p.t_embd, p.dim);
+#pragma unroll 1
+    for (int k = 0; k < 8; ++k) out[k] = dq_elem(p.t_embd, row + ((e + k) / E) * BB, (int)((e + k) % E));
 }
 
 // Residual update x += add (or x = the embedding row when add is NULL,
@@ -414,10 +430,10 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
             xv[r][0] += o0.x; xv[r][1] += o0.y; xv[r][2] += o0.z; xv[r][3] += o0.w;
             xv[r][4] += o1.x; xv[r][5] += o1.y; xv[r][6] += o1.z; xv[r][7] += o1.w;
         } else {
-            const uint32_t E = (uint32_t)block_elems(p.t_embd), BB = (uint32_t)block_bytes(p.t_embd);
-            const uint8_t *row = p.embd + (uint64_t)token * row_bytes(p.t_embd, p.dim);
+            float ev[8];
+            sk_embed8(p, token, e, ev);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) xv[r][k] = dq_elem(p.t_embd, row + ((e + k) / E) * BB, (int)((e + k) % E));
+            for (int k = 0; k < 8; ++k) xv[r][k] = ev[k];
         }
         xs[0] = make_float4(xv[r][0], xv[r][1], xv[r][2], xv[r][3]);
         xs[1] = make_float4(xv[r][4], xv[r][5], xv[r][6], xv[r][7]);
