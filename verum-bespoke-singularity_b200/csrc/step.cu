@@ -460,10 +460,11 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
     }
 }
 
-// Quantizes n values, load8(e, v) yielding elements e..e+7; NB blocks per
-// thread per batch, every load of a batch issued before any is used.
-template <int NB, class F>
-__device__ __forceinline__ void sk_prologue_vec(uint32_t n, int type, F load8, uint8_t *xq, float4 *xf) {
+// Quantizes the n values at src (fp32, global memory, written earlier in
+// the step): NB blocks per thread per batch, every load of a batch issued
+// before any is used.
+template <int NB>
+__device__ __noinline__ void sk_prologue_vec(uint32_t n, int type, const float *src, uint8_t *xq, float4 *xf) {
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = n / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
     for (uint32_t J0 = q; J0 < nsub; J0 += NB * (SK_CT / 4)) {
@@ -471,7 +472,7 @@ __device__ __forceinline__ void sk_prologue_vec(uint32_t n, int type, F load8, u
 #pragma unroll
         for (int r = 0; r < NB; ++r) {
             const uint32_t J = J0 + r * (SK_CT / 4);
-            if (J < nsub) load8(J * 32 + 8 * u, v[r]);
+            if (J < nsub) ld8_cg(src + J * 32 + 8 * u, v[r]);
         }
 #pragma unroll
         for (int r = 0; r < NB; ++r) {
@@ -591,6 +592,52 @@ __device__ __forceinline__ float2 sk_rope(float a, float b, uint32_t d, uint32_t
     float s, c;
     sincosf(ang, &s, &c);
     return make_float2(a * c - b * s, a * s + b * c);
+}
+
+// The last split of a KV head merges the S partial states [m, l, pad, pad,
+// o[HD]] of each query head in split order: every thread two outputs, all
+// loads of a batch of splits in flight at once (a single round trip for
+// S <= SK_MB), batches combined with the usual rescale.
+constexpr uint32_t SK_MB = 20;
+template <int HD>
+__device__ __noinline__ void sk_attn_merge(const StepParams &p, const SkAttn &a, uint32_t G, const float *parts, float *outp) {
+    constexpr uint32_t RS = 4 + HD;
+    constexpr size_t part_stride = (size_t)SK_GS * RS;
+    for (uint32_t e = 2 * threadIdx.x; e < G * HD; e += 2 * SK_CT) {
+        const uint32_t gg = e / HD, d = e % HD;
+        const float *src = parts + gg * RS;
+        float M = -INFINITY, L = 0.f, O0 = 0.f, O1 = 0.f;
+        for (uint32_t s0 = 0; s0 < a.S; s0 += SK_MB) {
+            float ms[SK_MB], ls[SK_MB];
+            float2 os[SK_MB];
+#pragma unroll
+            for (uint32_t u = 0; u < SK_MB; ++u) {
+                const bool in = s0 + u < a.S;
+                const float *ps = src + (size_t)(s0 + u) * part_stride;
+                ms[u] = in ? __ldcg(ps) : -INFINITY;
+                ls[u] = in ? __ldcg(ps + 1) : 0.f;
+                os[u] = in ? __ldcg(reinterpret_cast<const float2 *>(ps + 4 + d)) : make_float2(0.f, 0.f);
+            }
+            float Mb = M;
+#pragma unroll
+            for (uint32_t u = 0; u < SK_MB; ++u) Mb = fmaxf(Mb, ms[u]);
+            if (Mb == -INFINITY) continue;
+            const float rs = (M == -INFINITY) ? 0.f : exp2f(M - Mb);
+            L *= rs;
+            O0 *= rs;
+            O1 *= rs;
+#pragma unroll
+            for (uint32_t u = 0; u < SK_MB; ++u) {
+                const float wt = (ms[u] == -INFINITY) ? 0.f : exp2f(ms[u] - Mb);
+                L = fmaf(ls[u], wt, L);
+                O0 = fmaf(os[u].x, wt, O0);
+                O1 = fmaf(os[u].y, wt, O1);
+            }
+            M = Mb;
+        }
+        const float il = 1.0f / L;
+        *reinterpret_cast<float2 *>(outp + e) = make_float2(O0 * il, O1 * il);
+    }
 }
 
 template <int HD>
@@ -747,25 +794,36 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
         }
     }
     named_bar_sync(1, SK_CT);
+    // per query head: the maximum over the warps, each warp's weight, the sum
+    float *wts = S.misc();   // [SK_NCW][SK_GS] weights, [SK_GS] maxima, [SK_GS] sums
+    if (threadIdx.x < G) {
+        const uint32_t gg = threadIdx.x;
+        float M = -INFINITY, L = 0.f;
+        for (int w = 0; w < SK_NCW; ++w) M = fmaxf(M, sh[(w * G + gg) * RS]);
+        for (int w = 0; w < SK_NCW; ++w) {
+            const float m = sh[(w * G + gg) * RS];
+            const float wt = (m == -INFINITY) ? 0.f : exp2f(m - M);
+            wts[w * SK_GS + gg] = wt;
+            L += sh[(w * G + gg) * RS + 1] * wt;
+        }
+        wts[SK_NCW * SK_GS + gg] = M;
+        wts[SK_NCW * SK_GS + SK_GS + gg] = L;
+    }
+    named_bar_sync(1, SK_CT);
     float *work = reinterpret_cast<float *>(p.attn_work);
     constexpr size_t part_stride = (size_t)SK_GS * RS;
     float *mypart = work + ((size_t)a.h * SK_MAX_SPLITS + a.split) * part_stride;
     float *outp = p.att + (size_t)a.h * G * HD;
     for (uint32_t k = threadIdx.x; k < G * HD; k += SK_CT) {
         const uint32_t gg = k / HD, d = k % HD;
-        float M = -INFINITY;
-        for (int w = 0; w < SK_NCW; ++w) M = fmaxf(M, sh[(w * G + gg) * RS]);
-        float L = 0.f, O = 0.f;
-        for (int w = 0; w < SK_NCW; ++w) {
-            const float *rw = sh + (w * G + gg) * RS;
-            const float wt = (rw[0] == -INFINITY) ? 0.f : exp2f(rw[0] - M);
-            L += rw[1] * wt;
-            O += rw[4 + d] * wt;
-        }
+        float O = 0.f;
+#pragma unroll
+        for (int w = 0; w < SK_NCW; ++w) O += sh[(w * G + gg) * RS + 4 + d] * wts[w * SK_GS + gg];
+        const float L = wts[SK_NCW * SK_GS + SK_GS + gg];
         if (a.S == 1) {
             outp[gg * HD + d] = O / L;
         } else {
-            if (d == 0) { mypart[gg * RS] = M; mypart[gg * RS + 1] = L; }
+            if (d == 0) { mypart[gg * RS] = wts[SK_NCW * SK_GS + gg]; mypart[gg * RS + 1] = L; }
             mypart[gg * RS + 4 + d] = O;
         }
     }
@@ -777,54 +835,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
     named_bar_sync(1, SK_CT);
     if (!*flag) return;
     __threadfence();
-    // last split of this KV head: merge the splits in split order
-    const float *parts = work + (size_t)a.h * SK_MAX_SPLITS * part_stride;
-    float *wsm = sh;                                    // [SK_GS][S]
-    float *Lg = sh + SK_GS * SK_MAX_SPLITS;             // [SK_GS]
-    for (uint32_t gg = warp; gg < G; gg += SK_NCW) {
-        float ms[4], ls[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t s2 = lane + 32 * k;
-            const float *ps = parts + s2 * part_stride + gg * RS;
-            ms[k] = s2 < a.S ? __ldcg(ps) : -INFINITY;
-            ls[k] = s2 < a.S ? __ldcg(ps + 1) : 0.f;
-        }
-        const float M = warp_max(fmaxf(fmaxf(ms[0], ms[1]), fmaxf(ms[2], ms[3])));
-        float L = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t s2 = lane + 32 * k;
-            const float wt = (ms[k] == -INFINITY) ? 0.f : exp2f(ms[k] - M);
-            if (s2 < a.S) wsm[gg * a.S + s2] = wt;
-            L += ls[k] * wt;
-        }
-        L = warp_sum(L);
-        if (lane == 0) Lg[gg] = L;
-    }
-    named_bar_sync(1, SK_CT);
-    constexpr uint32_t MB = 16;
-    for (uint32_t k = threadIdx.x; k < G * HD / 4; k += SK_CT) {
-        const uint32_t gg = k / (HD / 4), d = (k % (HD / 4)) * 4;
-        const float *src = parts + gg * RS + 4 + d;
-        const float *wg = wsm + gg * a.S;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t s0 = 0; s0 < a.S; s0 += MB) {
-            float4 v[MB];
-#pragma unroll
-            for (uint32_t u = 0; u < MB; ++u)
-                v[u] = s0 + u < a.S ? __ldcg(reinterpret_cast<const float4 *>(src + (s0 + u) * part_stride))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (uint32_t u = 0; u < MB; ++u) {
-                const float wt = s0 + u < a.S ? wg[s0 + u] : 0.f;
-                acc.x = fmaf(v[u].x, wt, acc.x); acc.y = fmaf(v[u].y, wt, acc.y);
-                acc.z = fmaf(v[u].z, wt, acc.z); acc.w = fmaf(v[u].w, wt, acc.w);
-            }
-        }
-        const float il = 1.0f / Lg[gg];
-        *reinterpret_cast<float4 *>(outp + gg * HD + d) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
-    }
+    sk_attn_merge<HD>(p, a, G, work + (size_t)a.h * SK_MAX_SPLITS * part_stride, outp);
     if (threadIdx.x == 0) p.sync[SK_TICKET0 + a.h] = 0u;
 }
 
@@ -848,7 +859,7 @@ __device__ __forceinline__ void sk_block_argmax(const SkSmem &S, float &best, ui
     named_bar_sync(1, SK_CT);
 }
 
-__device__ __forceinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uint32_t pos) {
+__device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uint32_t pos) {
     const float *lg = sk_logits(p);
     const uint32_t n = p.vocab, per = (n + gridDim.x - 1) / gridDim.x;
     const uint32_t lo = min(n, blockIdx.x * per), hi = min(n, lo + per);
@@ -956,12 +967,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             const float *nw = kind == K_QKV ? p.layers[l].attn_norm : (kind == K_GU ? p.layers[l].ffn_norm : p.out_norm);
             sk_prologue_norm(p, S, x, add, nadd, nw, token, work, d.type, xq, xf);
         } else if (kind == K_O) {
-            if (work) sk_prologue_vec<2>(d.cols, d.type, [&](uint32_t e, float v[8]) { ld8_cg(p.att + e, v); }, xq, xf);
+            if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
         } else if (work) {   // K_DOWN: only the column chunks of this CTA's units
             const uint32_t c_lo = u0 / d.g.ntiles, c_hi = (u1 - 1) / d.g.ntiles;
             const uint32_t col0 = c_lo * d.g.ck, col1 = min(d.cols, (c_hi + 1) * d.g.ck);
             const float *hp = sk_acc_h(p, l) + col0;
-            sk_prologue_vec<2>(col1 - col0, d.type, [&](uint32_t e, float v[8]) { ld8_cg(hp + e, v); }, xq, xf);
+            sk_prologue_vec<2>(col1 - col0, d.type, hp, xq, xf);
             xq_u = xq_a - (col0 / 32) * (d.type == T_Q6_K ? XQ_PLAIN_STRIDE : XQ_SLOT_STRIDE);   // mv_unit indexes x blocks from column 0
             xf_u = xf_a - (col0 / 32) * 16;
         }
