@@ -351,10 +351,12 @@ bool put_tokens(vbs_cu_decoder *d, const uint32_t *tokens, size_t n) {
 bool plan_persistent(vbs_cu_decoder *d) {
     const vbs_cu_model_t &m = d->m;
     const Layer &y0 = d->L[0];
+    auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     for (const Layer &y : d->L)
         if (y.tq != y0.tq || y.tk != y0.tq || y.tv != y0.tq || y.to != y0.to || y.tgate != y0.tgate ||
-            y.tup != y0.tgate || y.tdown != y0.tdown)
-            return true;
+            y.tup != y0.tgate || y.tdown != y0.tdown || !a16(y.attn_norm) || !a16(y.ffn_norm))
+            return true;   // norm weights are bulk-copied: 16-byte aligned
+    if (!a16(m.out_norm)) return true;
     StepParams &p = d->sp;
     p = StepParams{};
     p.n_layers = m.n_layers; p.dim = m.dim; p.nqh = m.n_heads; p.nkh = m.n_kv_heads; p.hd = m.head_dim;

@@ -323,6 +323,16 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
             }
             continue;
         }
+        if (kind == K_QKV || kind == K_GU || kind == K_OUT) {   // the norm weight, for every CTA
+            const float *nw = kind == K_QKV ? p.layers[l].attn_norm : (kind == K_GU ? p.layers[l].ffn_norm : p.out_norm);
+            const uint32_t nb = p.dim * 4;
+            if (!sk_reserve(p, S, r, f, nb, lane)) { ok = false; break; }
+            if (lane == 0) {
+                mbar_arrive_expect_tx(S.full(r.idx), nb);
+                bulk_g2s(S.ring + r.off, nw, nb, S.full(r.idx));
+            }
+            sk_issued(r, f, nb, lane);
+        }
         const SkMv d = sk_mv_desc(p, kind, l);
         const uint32_t bytes = 16u * d.g.rs;
         uint32_t u0, u1;
@@ -387,22 +397,23 @@ __device__ __noinline__ void sk_embed8(const StepParams &p, uint32_t token, uint
 
 // Residual update x += add (or x = the embedding row when add is NULL,
 // src/vbs_host_math.h:136-142), RMSNorm (src/vbs_host_math.h:28-36) with
-// weight nw, and, when `quant`, the quantized normalized vector.
+// the norm weight, and, when `quant`, the quantized normalized vector. The
+// norm weight arrives as a ring stage of dim floats (the producer issues it
+// ahead of the op's weight stages), so it is never a load on this path.
 constexpr int SK_MAXPL = 4;      // partial planes summed by the norm prologue
 
-__device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSmem &S, float *x, const float *add,
-                                                 uint32_t nadd, const float *nw, uint32_t token, bool quant, int type,
+__device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSmem &S, SkRing &r, float *x,
+                                                 const float *add, uint32_t nadd, uint32_t token, bool quant, int type,
                                                  uint8_t *xq, float4 *xf) {
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = p.dim / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
-    float xv[SK_PB][8], wv[SK_PB][8];
+    float xv[SK_PB][8];
     // add = nadd planes of dim partial sums, summed in plane order
 #pragma unroll
     for (int r = 0; r < SK_PB; ++r) {
         const uint32_t J = q + r * (SK_CT / 4);
         if (J < nsub) {
             const uint32_t e = J * 32 + 8 * u;
-            ld8_g(nw + e, wv[r]);
             if (add) {
                 float pv[SK_MAXPL][8];
 #pragma unroll
@@ -448,16 +459,30 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
 #pragma unroll
     for (int w = 0; w < SK_NCW; ++w) tot += misc[w];
     const float scale = 1.0f / sqrtf(tot / (float)p.dim + p.eps);
-    if (!quant) return;
+    // the norm weight stage (long landed by now); released after use
+    const int lane = (int)(ctid & 31u);
+    volatile int *cta_abort = S.abort_flag();
+    const uint32_t nb = p.dim * 4, ws = S.ring + r.place(nb, S.ring_bytes);
+    const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
+    if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
+    if (quant && got) {
 #pragma unroll
-    for (int r = 0; r < SK_PB; ++r) {
-        const uint32_t J = q + r * (SK_CT / 4);
-        if (J >= nsub) continue;
-        float v[8];
+        for (int r2 = 0; r2 < SK_PB; ++r2) {
+            const uint32_t J = q + r2 * (SK_CT / 4);
+            if (J >= nsub) continue;
+            const uint32_t e = J * 32 + 8 * u;
+            const uint4 w0 = lds_u128(ws + e * 4), w1 = lds_u128(ws + e * 4 + 16);
+            const float wv[8] = {__uint_as_float(w0.x), __uint_as_float(w0.y), __uint_as_float(w0.z), __uint_as_float(w0.w),
+                                 __uint_as_float(w1.x), __uint_as_float(w1.y), __uint_as_float(w1.z), __uint_as_float(w1.w)};
+            float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = xv[r][k] * scale * wv[r][k];
-        sk_quant(type, v, u, qmask, J, xq, xf);
+            for (int k = 0; k < 8; ++k) v[k] = xv[r2][k] * scale * wv[k];
+            sk_quant(type, v, u, qmask, J, xq, xf);
+        }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(S.empty(r.idx));
+    r.advance(nb);
 }
 
 // Quantizes the n values at src (fp32, global memory, written earlier in
@@ -964,8 +989,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             const float *add = kind == K_QKV ? (l ? sk_acc_down(p, l - 1) : nullptr)
                                              : (kind == K_GU ? sk_acc_o(p, l) : sk_acc_down(p, p.n_layers - 1));
             const uint32_t nadd = kind == K_GU ? 1u : p.geo[STEP_DOWN].nch;
-            const float *nw = kind == K_QKV ? p.layers[l].attn_norm : (kind == K_GU ? p.layers[l].ffn_norm : p.out_norm);
-            sk_prologue_norm(p, S, x, add, nadd, nw, token, work, d.type, xq, xf);
+            sk_prologue_norm(p, S, r, x, add, nadd, token, work, d.type, xq, xf);
         } else if (kind == K_O) {
             if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
         } else if (work) {   // K_DOWN: only the column chunks of this CTA's units
@@ -1074,6 +1098,7 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
         plan_smem(gd.ck);
         if (SK_SMEM - p.ring_off < ring) return no("shared-memory plan");
     }
+    slot = std::max(slot, p.dim * 4);   // the norm weight stage
     p.stage_max = slot;
     p.ring_bytes = ring & ~127u;
     if (p.ring_bytes < 2 * slot) return no("shared-memory ring too small");
