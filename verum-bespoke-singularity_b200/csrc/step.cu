@@ -682,22 +682,45 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
     // q as the A operand: a 16 x HD f16 matrix in shared memory, row g =
     // fp16(q_g), row g+8 = fp16(q_g - fp16(q_g)) (zero for g >= G); RoPE'd
     // and pre-scaled by scale*log2(e). Read back with ldmatrix per k-step.
+    // The split that holds the current position also forms the new cache
+    // row here: RoPE'd key and value, fp16 with the engine's rounding, into
+    // the cache and into kvn (plain order) for the stage patch below. One
+    // loop, so RoPE's code exists once.
     constexpr uint32_t ASTR = HD * 2 + 16;     // padded row: conflict-free ldmatrix
     const uint32_t a_base = smem_u32(sh + SK_NCW * G * RS);
+    const uint32_t kvn = a_base + 16 * ASTR;   // new K row [HD] f16, then the V row
     const int g = lane >> 2, qd = 2 * (lane & 3);
+    const uint64_t hb = (((uint64_t)l * p.nkh + a.h) * p.max_ctx) * HD;
+    const bool has_pos = pos >= a.t0 && pos < a.t1;
     {
         const float qscale = p.scale * 1.4426950408889634f;
-        for (uint32_t k = threadIdx.x; k < SK_GS * (HD / 2); k += SK_CT) {
-            const uint32_t gg = k / (HD / 2), dd = 2 * (k % (HD / 2));
+        constexpr uint32_t NQ = SK_GS * (HD / 2);
+        const uint32_t n_items = NQ + (has_pos ? HD / 2 : 0u);
+        for (uint32_t k = threadIdx.x; k < n_items; k += SK_CT) {
+            const bool isq = k < NQ;
+            const uint32_t gg = isq ? k / (HD / 2) : 0u, dd = 2 * ((isq ? k : k - NQ) % (HD / 2));
+            const float *src = isq ? accq + (a.h * G + gg) * HD + dd : accq + qdim + a.h * HD + dd;
             float2 v = make_float2(0.f, 0.f);
-            if (gg < G) {
-                const float2 raw = __ldcg(reinterpret_cast<const float2 *>(accq + (a.h * G + gg) * HD + dd));
+            if (!isq || gg < G) {
+                const float2 raw = __ldcg(reinterpret_cast<const float2 *>(src));
                 v = sk_rope(raw.x, raw.y, dd, pos, HD, p.theta);
             }
-            uint32_t hi, lo;
-            sk_split_h2(v.x * qscale, v.y * qscale, hi, lo);
-            asm volatile("st.shared.u32 [%0], %1;" ::"r"(a_base + gg * ASTR + dd * 2), "r"(hi) : "memory");
-            asm volatile("st.shared.u32 [%0], %1;" ::"r"(a_base + (gg + 8) * ASTR + dd * 2), "r"(lo) : "memory");
+            if (isq) {
+                uint32_t hi, lo;
+                sk_split_h2(v.x * qscale, v.y * qscale, hi, lo);
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(a_base + gg * ASTR + dd * 2), "r"(hi) : "memory");
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(a_base + (gg + 8) * ASTR + dd * 2), "r"(lo) : "memory");
+            } else {
+                const float2 vr = __ldcg(reinterpret_cast<const float2 *>(src + kvdim));
+                const uint32_t kh = (uint32_t)f32_to_f16_kv(v.x) | ((uint32_t)f32_to_f16_kv(v.y) << 16);
+                const uint32_t vh = (uint32_t)f32_to_f16_kv(vr.x) | ((uint32_t)f32_to_f16_kv(vr.y) << 16);
+                // swizzled place of dims dd, dd+1 (inside one 16-byte chunk)
+                const uint32_t off = (((dd >> 3) ^ (pos & 7u)) << 3) + (dd & 7u);
+                *reinterpret_cast<uint32_t *>(p.kc + hb + (uint64_t)pos * HD + off) = kh;
+                *reinterpret_cast<uint32_t *>(p.vc + hb + (uint64_t)pos * HD + off) = vh;
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(kvn + dd * 2), "r"(kh) : "memory");
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(kvn + HD * 2 + dd * 2), "r"(vh) : "memory");
+            }
         }
         named_bar_sync(1, SK_CT);
     }
@@ -707,7 +730,6 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
 #pragma unroll
     for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float mrun = -INFINITY, lrun = 0.f;
-    const uint64_t hb = (((uint64_t)l * p.nkh + a.h) * p.max_ctx) * HD;
 
     for (uint32_t s = 0; s < a.nst; ++s) {
         // one decision per warp: the MMAs and shuffles below need all 32 lanes
@@ -726,30 +748,16 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
                     asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(vst + rr * ROWB + cc * 16), "r"(0u) : "memory");
                 }
             }
-            // the current position: RoPE'd key and value from the Q/K/V sums,
-            // fp16 with the engine's rounding, into the cache and this stage
+            // the current position: the new row (formed above) into this stage,
+            // 16-byte chunks swizzled by the position as in the cache
             if (pos >= tb && pos < tb + 16 && pos < a.t1) {
-                constexpr int DPL = HD / 32;   // dims per lane (even)
-                const uint32_t d0 = DPL * lane, rr = pos - tb;
-                const float *kr = accq + qdim + a.h * HD, *vr = accq + qdim + kvdim + a.h * HD;
-                uint16_t kh[DPL], vh[DPL];
-#pragma unroll
-                for (int j = 0; j < DPL; j += 2) {
-                    const float2 k2 = __ldcg(reinterpret_cast<const float2 *>(kr + d0 + j));
-                    const float2 v2 = __ldcg(reinterpret_cast<const float2 *>(vr + d0 + j));
-                    const float2 kro = sk_rope(k2.x, k2.y, d0 + j, pos, HD, p.theta);
-                    kh[j] = f32_to_f16_kv(kro.x); kh[j + 1] = f32_to_f16_kv(kro.y);
-                    vh[j] = f32_to_f16_kv(v2.x); vh[j + 1] = f32_to_f16_kv(v2.y);
-                }
-                // swizzled place of dims d0..d0+DPL-1 (inside one 16-byte chunk)
-                const uint32_t off = ((((d0 >> 3) ^ (pos & 7u)) << 3) + (d0 & 7u));
-                uint16_t *kg = p.kc + hb + (uint64_t)pos * HD + off, *vg = p.vc + hb + (uint64_t)pos * HD + off;
-#pragma unroll
-                for (int j = 0; j < DPL; ++j) {
-                    kg[j] = kh[j];
-                    vg[j] = vh[j];
-                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(kst + rr * ROWB + (off + j) * 2), "h"(kh[j]) : "memory");
-                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(vst + rr * ROWB + (off + j) * 2), "h"(vh[j]) : "memory");
+                constexpr uint32_t NC = HD / 8;   // 16-byte chunks per row
+                if ((uint32_t)lane < 2 * NC) {
+                    const uint32_t isv = (uint32_t)lane >= NC, c = (uint32_t)lane % NC, rr = pos - tb;
+                    const uint4 val = lds_u128(kvn + isv * HD * 2 + c * 16);
+                    const uint32_t dst = (isv ? vst : kst) + rr * ROWB + ((c ^ (pos & 7u)) << 4);
+                    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(val.x), "r"(val.y), "r"(val.z),
+                                 "r"(val.w) : "memory");
                 }
             }
             __syncwarp();
@@ -1055,7 +1063,7 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
     // The down projection quantizes only its CTA's (at most two) column
     // chunks; the chunk size is fixed first from a provisional ring.
     const uint32_t G = p.nqh / p.nkh;
-    const uint32_t attn_sh = (uint32_t)(SK_NCW * G * (4 + p.hd) * 4 + 16 * (p.hd * 2 + 16));
+    const uint32_t attn_sh = (uint32_t)(SK_NCW * G * (4 + p.hd) * 4 + 16 * (p.hd * 2 + 16) + 4 * p.hd);
     const uint32_t merge_sh = (uint32_t)(SK_GS * (SK_MAX_SPLITS + 1) * 4);
     auto plan_smem = [&](uint32_t down_ck) {
         const uint32_t nb = std::max(std::max(p.dim, qd), std::min(p.ffn, 2 * down_ck)) / 32;
