@@ -130,6 +130,10 @@ def lib() -> C.CDLL:
         return _LIB
     if not LIB_PATH.exists():
         raise VbsError(f"{LIB_PATH} is not built; run build() (make -C {PKG_DIR})")
+    # torch first: the library's libnccl.so.2 then resolves to the NCCL that
+    # torch already loaded. Loaded the other way round, the older system NCCL
+    # takes the soname and torch's CUDA library fails to import.
+    import torch  # noqa: F401
     L = C.CDLL(str(LIB_PATH))
     vp, u32, u64, i32, f32, sz = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_size_t
     sig = {
