@@ -490,6 +490,7 @@ def main():
             "config": {"workload": "llama3-8b-shape decode (32L, dim 4096, 32/8 heads, ffn 14336, vocab 128256; "
                                    "Q4_K attn+gate/up, Q6_K down/output/embd)",
                        "ctx": args.ctx, "batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
+                       "tp_sum": dec.tp_mode if world > 1 else None,
                        "l2": "inputs larger than L2 (4.84 GB weights per step)",
                        "kernels_per_step": kps, "prefill_s": round(prefill_s, 2)},
             "step_bandwidth": {"algorithmic_bytes": int(step_bytes),

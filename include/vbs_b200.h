@@ -265,6 +265,7 @@ typedef struct {
 #define VBS_CU_DEC_NO_GRAPH 2u   /* launch kernel by kernel instead of one CUDA graph */
 #define VBS_CU_DEC_NO_PDL   4u   /* no programmatic dependent launch between kernels */
 #define VBS_CU_DEC_NO_PERSIST 8u /* per-op kernels instead of the persistent one-launch step */
+#define VBS_CU_DEC_TP_NCCL 16u   /* tensor parallelism: per-layer sums with ncclAllReduce instead of peer memory */
 
 typedef struct vbs_cu_decoder vbs_cu_decoder_t;
 
@@ -303,6 +304,11 @@ VBS_API void *vbs_cu_decoder_stream(vbs_cu_decoder_t *d);
 VBS_API const float *vbs_cu_decoder_logits_device(vbs_cu_decoder_t *d);
 /* Kernels one decode step launches. */
 VBS_API uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d);
+/* How the decoder sums the per-layer tensor-parallel partials: 0 one GPU,
+ * 1 ncclAllReduce, 2 peer memory (the o_proj/down epilogue stores into every
+ * rank's receive slots over NVLink; the next kernel waits for the ranks'
+ * flags and sums the slots in rank order). */
+VBS_API uint32_t vbs_cu_decoder_tp_mode(vbs_cu_decoder_t *d);
 
 /* ---- tensor parallelism (no reference counterpart: the engine binds one
  * device, src/vbs_engine.c:142-169) ---- */

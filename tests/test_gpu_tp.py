@@ -2,9 +2,12 @@
 its Megatron shard of the same seeded two-layer 8B-width model
 (`synth_llama(tp_rank, tp_world)`), the ranks join one NCCL communicator
 (unique id broadcast over gloo), and the TP decoder's logits (o_proj/down
-all-reduced, output rows all-gathered) are compared step by step with a
-single-GPU decoder on the unsharded model. Skipped with fewer GPUs than
-ranks: two ranks never share one GPU."""
+partials summed across ranks, output rows all-gathered) are compared step by
+step with a single-GPU decoder on the unsharded model. Both ways of summing
+are covered: peer memory (the default: the matvec epilogue stores into every
+rank's slots over NVLink, the next kernel waits for the flags) and NCCL's
+all-reduce (VBS_CU_DEC_TP_NCCL, the reference collective). Skipped with fewer
+GPUs than ranks: two ranks never share one GPU."""
 import os
 import queue
 import socket
@@ -28,7 +31,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, flags):
     import sys
     import datetime
     from pathlib import Path
@@ -54,11 +57,12 @@ def _rank(rank, world, port, q):
         vbs.check(vbs.lib().vbs_cu_tp_init(rank, world, idb), "tp init")
         cfg = dict(mdl.L8B, n_layers=2, vocab=4096)
         model = vbs.synth_llama(mdl.shape_of(cfg), mdl.L8B_TYPES, seed=99, tp_rank=rank, tp_world=world)
-        dec = vbs.Decoder(model, 64)
+        dec = vbs.Decoder(model, 64, flags)
         out = [dec.forward([t]).copy() for t in TOKENS]
+        dec.reset()
         toks = dec.generate([11, 12, 13], 8)
         if rank == 0:
-            q.put(("ok", out, toks, dec.kernels_per_step))
+            q.put(("ok", out, toks, (dec.kernels_per_step, dec.tp_mode)))
         dist.barrier()
     except Exception as e:  # reported to the parent; the other ranks fail their next collective
         q.put(("error", f"rank {rank}: {e!r}", None, None))
@@ -69,15 +73,17 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["peer-memory", "nccl"])
 @pytest.mark.parametrize("world", [2])
-def test_tp_decoder_matches_single_gpu(vbs, gpu, world):
+def test_tp_decoder_matches_single_gpu(vbs, gpu, world, mode):
     import torch
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    flags = vbs.DEC_TP_NCCL if mode == "nccl" else 0
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, flags)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -102,4 +108,5 @@ def test_tp_decoder_matches_single_gpu(vbs, gpu, world):
     ref2 = vbs.Decoder(ref_model, 64)
     assert toks == ref2.generate([11, 12, 13], 8)
     ref2.close()
-    assert kps > 1   # tensor parallelism runs the per-op kernels
+    assert kps[0] > 1          # tensor parallelism runs the per-op kernels
+    assert kps[1] == mode

@@ -35,6 +35,7 @@ ARG_BUFFER, ARG_SCALAR = 0, 1
 
 MV_ACCUMULATE, MV_PORTABLE = 1, 2
 DEC_STRICT, DEC_NO_GRAPH, DEC_NO_PDL, DEC_NO_PERSIST = 1, 2, 4, 8
+DEC_TP_NCCL = 16   # tensor parallelism: NCCL all-reduce for the per-layer sums (the reference collective)
 
 
 class VbsError(RuntimeError):
@@ -159,6 +160,7 @@ def lib() -> C.CDLL:
         "vbs_cu_decoder_stream": (vp, [vp]),
         "vbs_cu_decoder_logits_device": (vp, [vp]),
         "vbs_cu_decoder_kernels_per_step": (u32, [vp]),
+        "vbs_cu_decoder_tp_mode": (u32, [vp]),
         "vbs_cu_tp_unique_id": (i32, [vp]),
         "vbs_cu_tp_init": (i32, [i32, i32, vp]),
         "vbs_cu_tp_finalize": (i32, []),
@@ -402,6 +404,11 @@ class Decoder:
     @property
     def kernels_per_step(self) -> int:
         return int(lib().vbs_cu_decoder_kernels_per_step(self.h))
+
+    @property
+    def tp_mode(self) -> str:
+        """"single", "nccl" or "peer-memory": how the per-layer TP sums run."""
+        return ("single", "nccl", "peer-memory")[int(lib().vbs_cu_decoder_tp_mode(self.h))]
 
     def close(self) -> None:
         if self.h:

@@ -54,6 +54,7 @@ struct vbs_cu_decoder {
     uint32_t flags = 0, max_ctx = 0, kv_dim = 0, q_dim = 0, vocab_full = 0;
     bool strict = false, use_graph = true, use_pdl = true;
     int tp_world = 1;
+    bool tp_p2p = false;   // per-layer sums over peer memory (else NCCL all-reduce)
     DevState *dev = nullptr;
     cudaStream_t st = nullptr;
     // activations
@@ -95,7 +96,8 @@ bool plan_persistent(vbs_cu_decoder *d);
 
 // Launch one matvec y (+)= W x through the fastest kernel that supports it.
 bool step_matvec(vbs_cu_decoder *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
-                 bool accumulate, const float *norm_w, const float *x_add, float *x_write) {
+                 bool accumulate, const float *norm_w, const float *x_add, float *x_write, bool tp_write = false,
+                 bool tp_read = false) {
     const void *wv[1] = {w};
     if (mv_fast_supported(type, rows, cols, wv, 1, x, 0)) {
         MvParams p = {};
@@ -112,7 +114,14 @@ bool step_matvec(vbs_cu_decoder *d, int type, const uint8_t *w, const float *x, 
         p.y = y;
         p.accumulate = accumulate ? 1u : 0u;
         p.err = d->dev->err;
+        p.tp = (tp_write || tp_read) ? tp_comm() : nullptr;
+        p.tp_write = tp_write;
+        p.tp_read = tp_read;
         return cuda_ok(mv_fast_launch(type, 0, MV_EPI_STORE, p, d->dev->n_sm, d->st, d->use_pdl, 0), "decode matvec");
+    }
+    if (tp_write || tp_read) {
+        latch_error("decode matvec: peer-memory exchange needs the fast kernel");
+        return false;
     }
     // portable path: explicit norm into d->norm when requested
     const float *xin = x;
@@ -148,7 +157,8 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
     if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->ctrl + 1, 0, d->vocab_full, d->x, dim, d->dev->err, st, d->use_pdl),
                  "decode embed"))
         return false;
-    const float *pending = nullptr;   // TP: partial sum to add into the residual
+    const float *pending = nullptr;   // TP over NCCL: partial sum to add into the residual
+    bool pending_tp = false;          // TP over peer memory: the exchange to add into the residual
     for (uint32_t l = 0; l < m.n_layers; ++l) {
         const Layer &ly = d->L[l];
         // ---- 1. norm + QKV + RoPE + KV store ----
@@ -165,7 +175,9 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
             p.norm_w = ly.attn_norm;
             p.eps = m.eps;
             p.x_add = pending;
-            p.x_write = pending ? xw : nullptr;
+            p.x_write = (pending || pending_tp) ? xw : nullptr;
+            p.tp = pending_tp ? tp_comm() : nullptr;
+            p.tp_read = pending_tp;
             p.err = d->dev->err;
             p.q_out = d->q;
             p.kc = d->kc; p.vc = d->vc;
@@ -175,8 +187,10 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
             p.theta = m.theta;
             if (!cuda_ok(mv_fast_launch(ly.tq, 0, MV_EPI_QKV, p, d->dev->n_sm, st, d->use_pdl, 0), "decode qkv")) return false;
         } else {
-            if (!step_matvec(d, ly.tq, ly.wq, xr, d->q, nq, dim, false, ly.attn_norm, pending, pending ? xw : nullptr)) return false;
-            const float *xin = pending ? xw : xr;
+            if (!step_matvec(d, ly.tq, ly.wq, xr, d->q, nq, dim, false, ly.attn_norm, pending,
+                             (pending || pending_tp) ? xw : nullptr, false, pending_tp))
+                return false;
+            const float *xin = (pending || pending_tp) ? xw : xr;
             if (!step_matvec(d, ly.tk, ly.wk, xin, d->k, nk, dim, false, ly.attn_norm, nullptr, nullptr)) return false;
             if (!step_matvec(d, ly.tv, ly.wv, xin, d->v, nk, dim, false, ly.attn_norm, nullptr, nullptr)) return false;
             if (!cuda_ok(rope_launch(d->q, 0, d->ctrl, hd, m.n_heads, m.theta, st), "decode rope")) return false;
@@ -184,7 +198,7 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
             if (!cuda_ok(cache_store_launch(d->k, d->v, d->kc, d->vc, 0, d->ctrl, l, d->max_ctx, nk, hd, true, st), "decode kv store"))
                 return false;
         }
-        if (pending) { std::swap(xr, xw); pending = nullptr; }
+        if (pending || pending_tp) { std::swap(xr, xw); pending = nullptr; pending_tp = false; }
         // ---- 2. attention ----
         AttnParams ap = {};
         ap.q = d->q; ap.kc = d->kc; ap.vc = d->vc; ap.out = d->att;
@@ -198,7 +212,10 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
         ap.err = d->dev->err;
         if (!cuda_ok(attn_launch(ap, d->n_splits, st, d->use_pdl), "decode attention")) return false;
         // ---- 3. o_proj (+ residual, or partial under TP) ----
-        if (tp) {
+        if (tp && d->tp_p2p) {
+            if (!step_matvec(d, ly.to, ly.wo, d->att, d->partial, dim, nq, false, nullptr, nullptr, nullptr, true)) return false;
+            pending_tp = true;
+        } else if (tp) {
             if (!step_matvec(d, ly.to, ly.wo, d->att, d->partial, dim, nq, false, nullptr, nullptr, nullptr)) return false;
             if (!tp_allreduce_sum(d->partial, dim, st)) return false;
             pending = d->partial;
@@ -220,20 +237,27 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
             p.norm_w = ly.ffn_norm;
             p.eps = m.eps;
             p.x_add = pending;
-            p.x_write = pending ? xw : nullptr;
+            p.x_write = (pending || pending_tp) ? xw : nullptr;
+            p.tp = pending_tp ? tp_comm() : nullptr;
+            p.tp_read = pending_tp;
             p.y = d->hid;
             p.err = d->dev->err;
             if (!cuda_ok(mv_fast_launch(ly.tgate, 1, MV_EPI_SILU, p, d->dev->n_sm, st, d->use_pdl, 0), "decode gate/up")) return false;
         } else {
-            if (!step_matvec(d, ly.tgate, ly.wgate, xr, d->gate, m.ffn, dim, false, ly.ffn_norm, pending, pending ? xw : nullptr))
+            if (!step_matvec(d, ly.tgate, ly.wgate, xr, d->gate, m.ffn, dim, false, ly.ffn_norm, pending,
+                             (pending || pending_tp) ? xw : nullptr, false, pending_tp))
                 return false;
-            const float *xin = pending ? xw : xr;
+            const float *xin = (pending || pending_tp) ? xw : xr;
             if (!step_matvec(d, ly.tup, ly.wup, xin, d->up, m.ffn, dim, false, ly.ffn_norm, nullptr, nullptr)) return false;
             if (!cuda_ok(silu_mul_launch(d->gate, d->up, d->hid, m.ffn, st), "decode silu")) return false;
         }
-        if (pending) { std::swap(xr, xw); pending = nullptr; }
+        if (pending || pending_tp) { std::swap(xr, xw); pending = nullptr; pending_tp = false; }
         // ---- 5. down (+ residual, or partial under TP) ----
-        if (tp) {
+        if (tp && d->tp_p2p) {
+            if (!step_matvec(d, ly.tdown, ly.wdown, d->hid, d->partial, dim, m.ffn, false, nullptr, nullptr, nullptr, true))
+                return false;
+            pending_tp = true;
+        } else if (tp) {
             if (!step_matvec(d, ly.tdown, ly.wdown, d->hid, d->partial, dim, m.ffn, false, nullptr, nullptr, nullptr)) return false;
             if (!tp_allreduce_sum(d->partial, dim, st)) return false;
             pending = d->partial;
@@ -243,9 +267,9 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
     }
     // ---- final norm + output ----
     if (!step_matvec(d, m.out_type, static_cast<const uint8_t *>(m.out), xr, d->logits, m.vocab, dim, false, m.out_norm,
-                     pending, pending ? xw : nullptr))
+                     pending, (pending || pending_tp) ? xw : nullptr, false, pending_tp))
         return false;
-    if (pending) std::swap(xr, xw);
+    if (pending || pending_tp) std::swap(xr, xw);
     const float *lg = d->logits;
     if (tp) {
         if (!tp_allgather(d->logits, d->logits_full, m.vocab, st)) return false;
@@ -445,6 +469,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
     d->vocab_full = m->vocab_full ? m->vocab_full : m->vocab;
     d->tp_world = tp_world();
     if (d->tp_world > 1 && d->strict) return fail("strict mode runs on one GPU", d);
+    d->tp_p2p = d->tp_world > 1 && tp_comm() && !(flags & VBS_CU_DEC_TP_NCCL) && m->dim <= TP_DIM_MAX;
     if (d->tp_world == 1 && d->vocab_full != m->vocab) return fail("vocab_full differs from vocab without TP", d);
     d->L.resize(m->n_layers);
     for (uint32_t l = 0; l < m->n_layers; ++l) {
@@ -456,6 +481,21 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
         y.wdown = static_cast<const uint8_t *>(m->wdown[l]);
         y.tq = m->tq[l]; y.tk = m->tk[l]; y.tv = m->tv[l]; y.to = m->to[l];
         y.tgate = m->tgate[l]; y.tup = m->tup[l]; y.tdown = m->tdown[l];
+    }
+    // the peer-memory exchange lives in the fast kernel's epilogue/prologue:
+    // every writer (o_proj, down) and reader (q or fused QKV, gate or fused
+    // gate/up, output) must be a fast-kernel launch
+    for (const Layer &y : d->L) {
+        if (!d->tp_p2p) break;
+        const void *wo[1] = {y.wo}, *wd[1] = {y.wdown}, *wq[1] = {y.wq}, *wg[1] = {y.wgate};
+        d->tp_p2p = mv_fast_supported(y.to, m->dim, d->q_dim, wo, 1, nullptr, 0) &&
+                    mv_fast_supported(y.tdown, m->dim, m->ffn, wd, 1, nullptr, 0) &&
+                    mv_fast_supported(y.tq, d->q_dim, m->dim, wq, 1, nullptr, 0) &&
+                    mv_fast_supported(y.tgate, m->ffn, m->dim, wg, 1, nullptr, 0);
+    }
+    {
+        const void *wout[1] = {m->out};
+        if (d->tp_p2p) d->tp_p2p = mv_fast_supported(m->out_type, m->vocab, m->dim, wout, 1, nullptr, 0);
     }
     if (!cuda_ok(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "decoder stream")) return fail("stream", d);
     const size_t big = std::max<size_t>(std::max<size_t>(m->dim, m->ffn), d->q_dim);
@@ -601,5 +641,6 @@ const float *vbs_cu_decoder_logits_device(vbs_cu_decoder_t *d) {
     return d ? (d->tp_world > 1 ? d->logits_full : d->logits) : nullptr;
 }
 uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d) { return d ? d->kernels_per_step : 0; }
+uint32_t vbs_cu_decoder_tp_mode(vbs_cu_decoder_t *d) { return !d || d->tp_world == 1 ? 0u : (d->tp_p2p ? 2u : 1u); }
 
 }  // extern "C"

@@ -30,6 +30,24 @@ enum MvEpi : int {
     MV_EPI_QKV = 2,     // rows [q | k | v]: RoPE on q/k, k/v stored as fp16 into the KV cache
 };
 
+// Tensor-parallel exchange region of this rank (device memory), set up by
+// vbs_cu_tp_init. Rank r's receive region holds two alternating slot sets
+// of world x dim_max floats (set k % 2 for the k-th exchange) and one flag
+// per sender. A writer stores its partial rows into slot set [k % 2][its
+// rank] of every peer's region, fences at system scope, and the last of its
+// CTAs publishes k + 1 into flag [its rank] of every peer. A reader waits
+// until every flag of its own region reached its own counter, then sums the
+// slots in rank order.
+constexpr int TP_MAX_WORLD = 8;
+constexpr uint32_t TP_DIM_MAX = 16384;
+struct TpComm {
+    float *slots[TP_MAX_WORLD];      // region of rank q (own region at [rank])
+    uint32_t *flags[TP_MAX_WORLD];   // flag words of rank q's region, [world]
+    uint32_t *seq;                   // this rank: exchanges completed
+    uint32_t *ticket;                // this rank: CTAs finished in the current writer kernel
+    uint32_t world, rank;
+};
+
 struct MvParams {
     const uint8_t *w[3];        // row segments of matrix A (concatenated row space)
     uint32_t seg_end[3];        // cumulative row ends of the segments
@@ -52,6 +70,10 @@ struct MvParams {
     uint32_t layer, max_ctx, kv_dim, head_dim;
     uint32_t kv_head_major;     // cache layout, see KV_HEAD_MAJOR
     float theta;
+    // tensor parallelism over peer memory (NULL: none)
+    const TpComm *tp;
+    uint32_t tp_write;          // epilogue: rows go to every peer's slot set, then the flags
+    uint32_t tp_read;           // prologue: x_add := the rank-ordered sum of the own slot set
 };
 
 // True when the TMA/mma kernel can serve this shape/alignment.

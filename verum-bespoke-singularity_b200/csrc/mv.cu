@@ -74,16 +74,61 @@ __device__ __forceinline__ const uint8_t *seg_row_ptr(const MvParams &p, uint32_
 //   plain layout (Q6_K): q1 words 0..7 then q2 words 0..7.
 //   xf[J] = {d2, d2 * sum(254 q1 + q2), sum over k<16, sum over k>=16}.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// Tensor parallelism, reader side: wait (bounded) until every rank published
+// the exchange this rank's counter names, then x_add is the rank-ordered sum
+// of that exchange's slots. The slots were written over NVLink into this
+// GPU's memory: read through L2 (ld.cg), never from a stale L1 line.
+struct TpRead {
+    const float *slots = nullptr;   // slot set of the exchange, sender 0
+    uint32_t world = 0;
+};
+__device__ __forceinline__ bool tp_read_begin(const MvParams &p, int ctid, TpRead &t, float *misc) {
+    const TpComm &c = *p.tp;
+    const uint32_t k = *reinterpret_cast<const volatile uint32_t *>(c.seq);
+    t.world = c.world;
+    t.slots = c.slots[c.rank] + (size_t)((k - 1u) & 1u) * c.world * TP_DIM_MAX;
+    volatile int *ok_s = reinterpret_cast<volatile int *>(misc + 40);   // free word of the misc scratch
+    if (ctid == 0) {
+        bool ok = true;
+        const uint64_t t0 = global_ns();
+        for (uint32_t q = 0; q < c.world && ok; ++q)
+            while ((int)(ld_acquire_sys(c.flags[c.rank] + q) - k) < 0)
+                if (global_ns() - t0 > kWaitNs) { ok = false; dev_flag_error(p.err, DERR_TIMEOUT_PEER); break; }
+        *ok_s = ok;
+    }
+    named_bar_sync(1, MV_NCW * 32);
+    return *ok_s != 0;
+}
+__device__ __forceinline__ float4 tp_add4(const TpRead &t, size_t i) {
+    float4 a = __ldcg(reinterpret_cast<const float4 *>(t.slots + i));
+    for (uint32_t q = 1; q < t.world; ++q) {
+        const float4 b = __ldcg(reinterpret_cast<const float4 *>(t.slots + (size_t)q * TP_DIM_MAX + i));
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    return a;
+}
+
 template <bool PLAIN>
 __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *misc, int ctid) {
     const uint32_t nsub = p.cols / 32;
     float scale = 1.0f;
+    TpRead tpr;
+    const bool tp = p.tp_read != 0;
+    if (tp && !tp_read_begin(p, ctid, tpr, misc)) return;   // error latched; the step's results are not used
+    const bool has_add = tp || p.x_add;
+    auto add4 = [&](size_t i) { return tp ? tp_add4(tpr, i) : *reinterpret_cast<const float4 *>(p.x_add + i); };
     if (p.norm_w) {
         float ss = 0.0f;
         for (uint32_t i = ctid * 4; i < p.cols; i += MV_NCW * 32 * 4) {
             float4 v = *reinterpret_cast<const float4 *>(p.x + i);
-            if (p.x_add) {
-                const float4 a = *reinterpret_cast<const float4 *>(p.x_add + i);
+            if (has_add) {
+                const float4 a = add4(i);
                 v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
             }
             ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
@@ -96,7 +141,7 @@ __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *m
         for (int w = 0; w < MV_NCW; ++w) tot += misc[8 + w];
         scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
     }
-    const bool write_x = p.x_add && p.x_write && blockIdx.x == 0;
+    const bool write_x = has_add && p.x_write && blockIdx.x == 0;
     const uint32_t u = ctid & 3;                                   // quarter of the block
     const uint32_t qmask = 0xFu << ((ctid & 31) & ~3u);            // the four lanes of this block
     for (uint32_t J = ctid >> 2; J < nsub; J += MV_NCW * 32 / 4) {
@@ -104,9 +149,9 @@ __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *m
         float v[8];
         float4 t0 = *reinterpret_cast<const float4 *>(p.x + e), t1 = *reinterpret_cast<const float4 *>(p.x + e + 4);
         v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w; v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
-        if (p.x_add) {
-            t0 = *reinterpret_cast<const float4 *>(p.x_add + e);
-            t1 = *reinterpret_cast<const float4 *>(p.x_add + e + 4);
+        if (has_add) {
+            t0 = add4(e);
+            t1 = add4(e + 4);
             v[0] += t0.x; v[1] += t0.y; v[2] += t0.z; v[3] += t0.w; v[4] += t1.x; v[5] += t1.y; v[6] += t1.z; v[7] += t1.w;
             if (write_x) {
                 *reinterpret_cast<float4 *>(p.x_write + e) = make_float4(v[0], v[1], v[2], v[3]);
@@ -128,9 +173,16 @@ __device__ void mv_prologue(const MvParams &p, uint8_t *xq, float4 *xf, float *m
 // epilogue for one row (consumer warp 0; lane = row within the tile)
 // ---------------------------------------------------------------------------
 template <int EPI>
-__device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, bool valid, float va, float vb) {
+__device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t row, bool valid, float va, float vb,
+                                            uint32_t tp_k) {
     if constexpr (EPI == MV_EPI_STORE) {
-        if (valid) p.y[row] = p.accumulate ? p.y[row] + va : va;
+        if (valid && p.tp_write) {   // this rank's partial row into slot [k % 2][rank] of every region
+            const TpComm &c = *p.tp;
+            const size_t off = ((size_t)(tp_k & 1u) * c.world + c.rank) * TP_DIM_MAX + row;
+            for (uint32_t q = 0; q < c.world; ++q) c.slots[q][off] = va;
+        } else if (valid) {
+            p.y[row] = p.accumulate ? p.y[row] + va : va;
+        }
     } else if constexpr (EPI == MV_EPI_SILU) {
         if (valid) p.y[row] = va / (1.0f + expf(-va)) * vb;
     } else {  // QKV: q/k rows get RoPE on (2i, 2i+1) pairs; k/v go to the fp16 cache
@@ -255,6 +307,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
 
     // ------------------------------ consumers ------------------------------
     pdl_wait();
+    const uint32_t tp_k = (EPI == MV_EPI_STORE && p.tp_write) ? *reinterpret_cast<const volatile uint32_t *>(p.tp->seq) : 0u;
     mv_prologue<TYPE == T_Q6_K>(p, xq, xf, misc, threadIdx.x);
     named_bar_sync(1, MV_NCW * 32);
 
@@ -320,10 +373,31 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_fast_kernel(const MvParams p
             }
             const uint32_t row = r0 + tile * 16 + li;
             // all 32 lanes take part (RoPE pairs use a warp shuffle); lanes 16-31 write nothing
-            if (!*abort_flag) mv_epilogue<EPI>(p, row, lane < 16 && row < r1, va, vb);
+            if (!*abort_flag) mv_epilogue<EPI>(p, row, lane < 16 && row < r1, va, vb, tp_k);
             else if constexpr (EPI == MV_EPI_QKV) (void)__shfl_xor_sync(0xffffffffu, va, 1);
         }
         ++tile;
+    }
+    if constexpr (EPI == MV_EPI_STORE) {
+        if (p.tp_write) {
+            // Tensor parallelism, writer side: once every CTA's rows are out
+            // (system-scope fence, then a ticket), the last CTA publishes
+            // exchange k + 1 into this rank's flag in every region and
+            // advances the counter. The next writer kernel starts after this
+            // one completes, so the ticket is back at zero by then.
+            named_bar_sync(1, MV_NCW * 32);
+            if (threadIdx.x == 0) {
+                const TpComm &c = *p.tp;
+                __threadfence_system();
+                if (atomicAdd(c.ticket, 1u) == gridDim.x - 1) {
+                    *c.ticket = 0u;
+                    __threadfence_system();
+                    for (uint32_t q = 0; q < c.world; ++q)
+                        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(c.flags[q] + c.rank), "r"(tp_k + 1u) : "memory");
+                    *reinterpret_cast<volatile uint32_t *>(c.seq) = tp_k + 1u;
+                }
+            }
+        }
     }
 }
 

@@ -1,23 +1,97 @@
-// tp.cu -- tensor parallelism over NVLink / NVSwitch with NCCL.
+// tp.cu -- tensor parallelism over NVLink / NVSwitch.
 //
 // One process per GPU. Rank 0 creates an NCCL unique id
 // (vbs_cu_tp_unique_id), the host side broadcasts it (the tests and
 // bench.py use torch.distributed's store), every rank joins with
-// vbs_cu_tp_init. The decode program then all-reduces the o_proj and
-// down_proj partial sums (dim floats, 16 KB for the 8B shape) and
-// all-gathers the sharded logits. The reference has no multi-GPU path (its
-// engine binds one device, src/vbs_engine.c:142-169).
+// vbs_cu_tp_init. The decode program then sums the o_proj and down_proj
+// partials (dim floats, 16 KB for the 8B shape) across the ranks twice per
+// layer and all-gathers the sharded logits. The reference has no multi-GPU
+// path (its engine binds one device, src/vbs_engine.c:142-169).
+//
+// The per-layer sums do not go through NCCL: the writing matvec stores its
+// rows straight into every peer's receive region over NVLink (CUDA IPC
+// mappings of each rank's region, exchanged here with one NCCL all-gather
+// of the handles) and publishes a flag; the next kernel's prologue waits
+// for the flags and sums the slots (TpComm, kernels.h). NCCL's all-reduce
+// stays available as the reference collective (VBS_CU_DEC_TP_NCCL).
 #include "vbs_b200.h"
 #include "backend.h"
+#include "kernels.h"
 #include "tp.h"
 
 #include <nccl.h>
 #include <cstring>
+#include <vector>
 
 namespace vbs {
 
 static ncclComm_t g_comm = nullptr;
 static int g_world = 1, g_rank = 0;
+
+// the peer-memory exchange
+static void *g_region = nullptr;              // this rank's receive region
+static void *g_peer_base[TP_MAX_WORLD] = {};  // IPC mappings of the peers' regions
+static TpComm *g_comm_dev = nullptr;          // device copy of the TpComm
+constexpr size_t TP_SLOT_BYTES_PER_RANK = 2ull * TP_DIM_MAX * 4;   // two slot sets of one sender
+
+static size_t region_bytes(int world) { return TP_SLOT_BYTES_PER_RANK * world + 1024; }
+static size_t flags_offset(int world) { return TP_SLOT_BYTES_PER_RANK * world; }
+
+const TpComm *tp_comm() { return g_comm_dev; }
+
+static void p2p_teardown() {
+    for (int q = 0; q < TP_MAX_WORLD; ++q)
+        if (g_peer_base[q]) { cudaIpcCloseMemHandle(g_peer_base[q]); g_peer_base[q] = nullptr; }
+    if (g_comm_dev) { cudaFree(g_comm_dev); g_comm_dev = nullptr; }
+    if (g_region) { cudaFree(g_region); g_region = nullptr; }
+}
+
+// Every rank: allocate and clear the region, all-gather the IPC handles,
+// map the peers' regions. Returns false (with the error latched) when the
+// mapping is impossible; the decoders then use NCCL for the sums.
+static bool p2p_setup(int rank, int world) {
+    const size_t bytes = region_bytes(world);
+    if (!cuda_ok(cudaMalloc(&g_region, bytes), "tp region") || !cuda_ok(cudaMemset(g_region, 0, bytes), "tp region"))
+        return false;
+    cudaIpcMemHandle_t mine;
+    if (!cuda_ok(cudaIpcGetMemHandle(&mine, g_region), "tp ipc handle")) return false;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t *dh = nullptr;
+    if (!cuda_ok(cudaMalloc(&dh, 64 * (world + 1)), "tp handles")) return false;
+    std::vector<uint8_t> all(64 * world);
+    bool ok = cuda_ok(cudaMemcpy(dh + 64 * world, &mine, 64, cudaMemcpyHostToDevice), "tp handles");
+    if (ok) {
+        const ncclResult_t r = ncclAllGather(dh + 64 * world, dh, 64, ncclUint8, g_comm, 0);
+        if (r != ncclSuccess) { latch_error("ncclAllGather (handles): %s", ncclGetErrorString(r)); ok = false; }
+    }
+    ok = ok && cuda_ok(cudaStreamSynchronize(0), "tp handles") &&
+         cuda_ok(cudaMemcpy(all.data(), dh, 64 * world, cudaMemcpyDeviceToHost), "tp handles");
+    cudaFree(dh);
+    if (!ok) return false;
+    TpComm c = {};
+    c.world = (uint32_t)world;
+    c.rank = (uint32_t)rank;
+    for (int q = 0; q < world; ++q) {
+        uint8_t *base = nullptr;
+        if (q == rank) {
+            base = static_cast<uint8_t *>(g_region);
+        } else {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, all.data() + 64 * q, 64);
+            void *pp = nullptr;
+            if (!cuda_ok(cudaIpcOpenMemHandle(&pp, h, cudaIpcMemLazyEnablePeerAccess), "tp ipc open")) return false;
+            g_peer_base[q] = pp;
+            base = static_cast<uint8_t *>(pp);
+        }
+        c.slots[q] = reinterpret_cast<float *>(base);
+        c.flags[q] = reinterpret_cast<uint32_t *>(base + flags_offset(world));
+    }
+    uint8_t *own = static_cast<uint8_t *>(g_region) + flags_offset(world);
+    c.seq = reinterpret_cast<uint32_t *>(own + 512);
+    c.ticket = reinterpret_cast<uint32_t *>(own + 768);
+    return cuda_ok(cudaMalloc(&g_comm_dev, sizeof(TpComm)), "tp comm") &&
+           cuda_ok(cudaMemcpy(g_comm_dev, &c, sizeof(TpComm), cudaMemcpyHostToDevice), "tp comm");
+}
 
 int tp_world() { return g_comm ? g_world : 1; }
 int tp_rank() { return g_comm ? g_rank : 0; }
@@ -63,11 +137,19 @@ int vbs_cu_tp_init(int rank, int world, const void *id128) {
     if (r != ncclSuccess) { g_comm = nullptr; latch_error("ncclCommInitRank: %s", ncclGetErrorString(r)); return -1; }
     g_world = world;
     g_rank = rank;
+    if (world > TP_MAX_WORLD || !p2p_setup(rank, world)) {
+        // no peer-memory exchange: the decoders sum with NCCL instead
+        p2p_teardown();
+        cudaGetLastError();
+        vbs_cu_clear_error();
+    }
     return 0;
 }
 
 int vbs_cu_tp_finalize(void) {
     if (!g_comm) return 0;
+    cudaDeviceSynchronize();
+    p2p_teardown();
     ncclResult_t r = ncclCommDestroy(g_comm);
     g_comm = nullptr;
     g_world = 1;

@@ -12,5 +12,8 @@ int tp_rank();
 bool tp_allreduce_sum(float *buf, size_t n, cudaStream_t st);
 // full[r * n_local .. +n_local) = rank r's `local`.
 bool tp_allgather(const float *local, float *full, size_t n_local, cudaStream_t st);
+// The peer-memory exchange region (device pointer), or NULL when the group
+// has none (one rank, or peers not mappable).
+const struct TpComm *tp_comm();
 
 }  // namespace vbs
