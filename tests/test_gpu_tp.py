@@ -73,7 +73,7 @@ def _rank(rank, world, port, q, flags):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["peer-memory", "nccl"])
+@pytest.mark.parametrize("mode", ["persistent", "peer-memory", "nccl"])
 @pytest.mark.parametrize("world", [2])
 def test_tp_decoder_matches_single_gpu(vbs, gpu, world, mode):
     import torch
@@ -82,7 +82,9 @@ def test_tp_decoder_matches_single_gpu(vbs, gpu, world, mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    flags = vbs.DEC_TP_NCCL if mode == "nccl" else 0
+    # persistent: the one-launch step kernel with its exchanges over peer
+    # memory; peer-memory / nccl: the per-op kernels with either sum
+    flags = {"persistent": 0, "peer-memory": vbs.DEC_NO_PERSIST, "nccl": vbs.DEC_NO_PERSIST | vbs.DEC_TP_NCCL}[mode]
     procs = [ctx.Process(target=_rank, args=(r, world, port, q, flags)) for r in range(world)]
     for p in procs:
         p.start()
@@ -108,5 +110,6 @@ def test_tp_decoder_matches_single_gpu(vbs, gpu, world, mode):
     ref2 = vbs.Decoder(ref_model, 64)
     assert toks == ref2.generate([11, 12, 13], 8)
     ref2.close()
-    assert kps[0] > 1          # tensor parallelism runs the per-op kernels
-    assert kps[1] == mode
+    kernels, tp_mode = kps
+    assert tp_mode == ("peer-memory" if mode == "persistent" else mode)
+    assert (kernels == 1) == (mode == "persistent")   # one launch per step, or the per-op kernels

@@ -389,6 +389,13 @@ bool plan_persistent(vbs_cu_decoder *d) {
     p.t_embd = m.embd_type; p.t_qkv = y0.tq; p.t_o = y0.to; p.t_gu = y0.tgate; p.t_down = y0.tdown; p.t_out = m.out_type;
     p.embd = static_cast<const uint8_t *>(m.embd);
     p.out_norm = m.out_norm;
+    if (d->tp_world > 1) {   // the step's exchanges go over peer memory; the logits gather into the region
+        if (!d->tp_p2p || !tp_own_logits() || d->vocab_full > TP_VOCAB_MAX || m.dim > TP_DIM_MAX) return true;
+        p.tp = tp_comm();
+        p.tp_world = (uint32_t)d->tp_world;
+        p.tp_rank = (uint32_t)tp_rank();
+        p.vocab_full = d->vocab_full;
+    }
     char why[160];
     if (!step_plan(p, d->dev->n_sm, why, sizeof why)) return true;
     // repacked weights: per layer QKV | O | GU | DOWN, then the output matrix
@@ -515,7 +522,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
              dmalloc((void **)&d->xq, big, "xq") && dmalloc((void **)&d->qd, (big / 32 + 1) * 4, "qd");
     } else if (ok) {
         ok = dmalloc((void **)&d->kc, cache_elems * 2, "kv cache") && dmalloc((void **)&d->vc, cache_elems * 2, "kv cache");
-        if (ok && !(flags & VBS_CU_DEC_NO_PERSIST) && d->tp_world == 1) ok = plan_persistent(d);
+        if (ok && !(flags & VBS_CU_DEC_NO_PERSIST) && (d->tp_world == 1 || d->tp_p2p)) ok = plan_persistent(d);
         if (ok) {
             d->n_splits = attn_num_splits(max_ctx, m->n_kv_heads, 1, dev->n_sm);
             const size_t wb = attn_workspace_bytes(m->n_heads, m->n_kv_heads, m->head_dim, 1, d->n_splits);
@@ -577,7 +584,7 @@ int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n
         }
     }
     if (logits_out) {
-        const float *src = d->tp_world > 1 ? d->logits_full : d->logits;
+        const float *src = d->tp_world > 1 ? (d->persist ? tp_own_logits() : d->logits_full) : d->logits;
         if (!cuda_ok(cudaMemcpyAsync(d->logits_pinned, src, (size_t)d->vocab_full * 4, cudaMemcpyDeviceToHost, d->st), "logits readback"))
             return -1;
     }
@@ -638,7 +645,7 @@ int vbs_cu_decoder_enqueue_steps(vbs_cu_decoder_t *d, uint32_t n) {
 
 void *vbs_cu_decoder_stream(vbs_cu_decoder_t *d) { return d ? d->st : nullptr; }
 const float *vbs_cu_decoder_logits_device(vbs_cu_decoder_t *d) {
-    return d ? (d->tp_world > 1 ? d->logits_full : d->logits) : nullptr;
+    return d ? (d->tp_world > 1 ? (d->persist ? tp_own_logits() : d->logits_full) : d->logits) : nullptr;
 }
 uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d) { return d ? d->kernels_per_step : 0; }
 uint32_t vbs_cu_decoder_tp_mode(vbs_cu_decoder_t *d) { return !d || d->tp_world == 1 ? 0u : (d->tp_p2p ? 2u : 1u); }

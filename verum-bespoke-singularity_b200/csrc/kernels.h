@@ -40,8 +40,10 @@ enum MvEpi : int {
 // slots in rank order.
 constexpr int TP_MAX_WORLD = 8;
 constexpr uint32_t TP_DIM_MAX = 16384;
+constexpr uint32_t TP_VOCAB_MAX = 262144;
 struct TpComm {
     float *slots[TP_MAX_WORLD];      // region of rank q (own region at [rank])
+    float *logits[TP_MAX_WORLD];     // rank q's full-logits area (the step kernel gathers the vocab shards there)
     uint32_t *flags[TP_MAX_WORLD];   // flag words of rank q's region, [world]
     uint32_t *seq;                   // this rank: exchanges completed
     uint32_t *ticket;                // this rank: CTAs finished in the current writer kernel
@@ -187,6 +189,12 @@ struct StepParams {
     uint32_t *err;
     StepMvGeom geo[5];          // by STEP_* op
     uint32_t ring_bytes, stage_max, x_off, xq_off, xf_off, ring_off;   // shared-memory plan (byte ring)
+    // tensor parallelism (tp NULL: one GPU). This rank's shard: nqh, nkh,
+    // ffn and vocab above are per rank; o_proj/down partials and the logits
+    // are exchanged over peer memory (TpComm), 2 exchanges per layer and 1
+    // for the logits per step.
+    const TpComm *tp;
+    uint32_t tp_world, tp_rank, vocab_full;
 };
 
 // Element (pos, i) of one layer's KV block in the step kernel's cache:

@@ -92,6 +92,8 @@ struct SkMv {
     uint32_t rows, cols;
     float *out;             // chunk c's sums at out + c * rows (one writer per element)
     StepMvGeom g;
+    int tpw;                // tensor parallelism: 0 local, 1 o/down partial planes to every rank, 2 logits shard to every rank
+    uint32_t tp_k;          // exchange index (its slot set is tp_k % 2)
 };
 
 // Tile and chunk of this op's unit u.
@@ -207,10 +209,12 @@ __device__ __forceinline__ void sk_abort(const StepParams &p, uint32_t code) {
 // of the CTA, when this CTA or the grid aborted: thread 0 decides after the
 // first CTA barrier and the second one publishes its decision.
 __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t target, volatile int *flag,
-                                             volatile int *cta_abort) {
+                                             volatile int *cta_abort, bool sys_fence = false) {
     named_bar_sync(1, SK_CT);
     if (threadIdx.x == 0) {
-        __threadfence();
+        // system scope after an op that stored into peers' memory
+        if (sys_fence) __threadfence_system();
+        else __threadfence();
         atomicAdd(&p.sync[0], 1u);
         bool ok = *cta_abort == 0;
         const uint64_t t0 = global_ns();
@@ -222,6 +226,51 @@ __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t targe
             }
         }
         __threadfence();
+        *flag = ok ? 1 : 0;
+    }
+    named_bar_sync(1, SK_CT);
+    return *flag != 0;
+}
+
+// ---------------------------------------------------------------------------
+// tensor parallelism over peer memory (TpComm): per step, exchange 2l is
+// layer l's o_proj partials, 2l + 1 its down partials, 2L the logits. The
+// writers store into every rank's region in their row flush; after the next
+// grid barrier (system-scope fences) CTA 0 publishes k + 1 into this rank's
+// flag in every region; readers wait until all flags of their own region
+// reached k + 1.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sk_tp_index(const StepParams &p, uint32_t base, int kind, uint32_t l) {
+    return base + (kind == K_OUT ? 2u * p.n_layers : 2u * l + (kind == K_DOWN ? 1u : 0u));
+}
+
+__device__ __noinline__ void sk_tp_publish(const StepParams &p, uint32_t value) {
+    const TpComm &c = *p.tp;
+    for (uint32_t q = 0; q < c.world; ++q)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(c.flags[q] + c.rank), "r"(value) : "memory");
+}
+
+__device__ __forceinline__ uint32_t sk_ld_acquire_sys(const uint32_t *a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// All consumer threads: wait (thread 0 polls, bounded) until every rank
+// published exchange k. False, in every thread, on timeout or abort.
+__device__ __noinline__ bool sk_tp_wait(const StepParams &p, uint32_t k, volatile int *flag, volatile int *cta_abort) {
+    if (threadIdx.x == 0) {
+        const TpComm &c = *p.tp;
+        bool ok = *cta_abort == 0;
+        const uint64_t t0 = global_ns();
+        for (uint32_t q = 0; q < c.world && ok; ++q)
+            for (uint32_t it = 1; (int)(sk_ld_acquire_sys(c.flags[c.rank] + q) - (k + 1u)) < 0; ++it) {
+                if ((it & 15u) == 0) {
+                    if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
+                    if (global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
+                }
+            }
+        if (!ok) *cta_abort = 1;
         *flag = ok ? 1 : 0;
     }
     named_bar_sync(1, SK_CT);
@@ -415,17 +464,20 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
         if (J < nsub) {
             const uint32_t e = J * 32 + 8 * u;
             if (add) {
-                float pv[SK_MAXPL][8];
+                // planes in order, SK_MAXPL loads in flight at a time
+                for (uint32_t c0 = 0; c0 < nadd; c0 += SK_MAXPL) {
+                    float pv[SK_MAXPL][8];
 #pragma unroll
-                for (int c = 0; c < SK_MAXPL; ++c)
-                    if ((uint32_t)c < nadd) ld8_cg(add + (uint64_t)c * p.dim + e, pv[c]);
+                    for (int c = 0; c < SK_MAXPL; ++c)
+                        if (c0 + c < nadd) ld8_cg(add + (uint64_t)(c0 + c) * p.dim + e, pv[c]);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) xv[r][k] = pv[0][k];
+                    for (int k = 0; k < 8; ++k) xv[r][k] = c0 ? xv[r][k] + pv[0][k] : pv[0][k];
 #pragma unroll
-                for (int c = 1; c < SK_MAXPL; ++c)
-                    if ((uint32_t)c < nadd)
+                    for (int c = 1; c < SK_MAXPL; ++c)
+                        if (c0 + c < nadd)
 #pragma unroll
-                        for (int k = 0; k < 8; ++k) xv[r][k] += pv[c][k];
+                            for (int k = 0; k < 8; ++k) xv[r][k] += pv[c][k];
+                }
             }
         }
     }
@@ -513,7 +565,7 @@ __device__ __noinline__ void sk_prologue_vec(uint32_t n, int type, const float *
 // stores into its column chunk's plane, or for gate/up rows as
 // SiLU(gate)*up.
 // ---------------------------------------------------------------------------
-template <int TYPE>
+template <int TYPE, bool TPX>
 __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                               uint32_t xq_a, uint32_t xf_a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
@@ -578,6 +630,16 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
                         for (int w = 0; w < SK_NCW; ++w) vu += b[w * 16 + rr + 8];
                         d.out[row] = va / (1.0f + expf(-va)) * vu;
                     }
+                } else if (TPX && row < d.rows && d.tpw) {   // this rank's partial into every rank's region
+                    const TpComm &c = *p.tp;
+                    if (d.tpw == 1) {
+                        const size_t off = (size_t)(d.tp_k & 1u) * c.world * TP_DIM_MAX +
+                                           ((size_t)c.rank * d.g.nch + ch) * d.rows + row;
+                        for (uint32_t q = 0; q < c.world; ++q) c.slots[q][off] = va;
+                    } else {
+                        const size_t off = (size_t)c.rank * d.rows + row;
+                        for (uint32_t q = 0; q < c.world; ++q) c.logits[q][off] = va;
+                    }
                 } else if (row < d.rows) {
                     d.out[(uint64_t)ch * d.rows + row] = va;
                 }
@@ -588,12 +650,12 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
 
 // Types the kernel instance carries code for: a compile-time list (a
 // specialized instance) or all three (TQ4 = TQ6 = TQ8 = true).
-template <bool HAS_Q4, bool HAS_Q6, bool HAS_Q8>
+template <bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX>
 __device__ __forceinline__ void sk_mv_dispatch(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                                uint32_t xq_a, uint32_t xf_a) {
-    if constexpr (HAS_Q4) if (d.type == T_Q4_K) { sk_mv_consume<T_Q4_K>(p, d, S, r, xq_a, xf_a); return; }
-    if constexpr (HAS_Q6) if (d.type == T_Q6_K) { sk_mv_consume<T_Q6_K>(p, d, S, r, xq_a, xf_a); return; }
-    if constexpr (HAS_Q8) if (d.type == T_Q8_0) { sk_mv_consume<T_Q8_0>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q4) if (d.type == T_Q4_K) { sk_mv_consume<T_Q4_K, TPX>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q6) if (d.type == T_Q6_K) { sk_mv_consume<T_Q6_K, TPX>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q8) if (d.type == T_Q8_0) { sk_mv_consume<T_Q8_0, TPX>(p, d, S, r, xq_a, xf_a); return; }
 }
 
 // ---------------------------------------------------------------------------
@@ -892,9 +954,10 @@ __device__ __forceinline__ void sk_block_argmax(const SkSmem &S, float &best, ui
     named_bar_sync(1, SK_CT);
 }
 
-__device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uint32_t pos) {
-    const float *lg = sk_logits(p);
-    const uint32_t n = p.vocab, per = (n + gridDim.x - 1) / gridDim.x;
+__device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uint32_t pos, uint32_t tp_base) {
+    // under TP every rank holds the full gathered logits and picks the same token
+    const float *lg = p.tp ? p.tp->logits[p.tp->rank] : sk_logits(p);
+    const uint32_t n = p.tp ? p.vocab_full : p.vocab, per = (n + gridDim.x - 1) / gridDim.x;
     const uint32_t lo = min(n, blockIdx.x * per), hi = min(n, lo + per);
     float best = -INFINITY;
     uint32_t bi = 0xFFFFFFFFu;
@@ -920,6 +983,7 @@ __device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uin
         const uint32_t np = pos + 1u;
         p.ctrl[1] = bi;
         p.ctrl[0] = np;
+        if (p.tp) *reinterpret_cast<volatile uint32_t *>(p.tp->seq) = tp_base + 2u * p.n_layers + 1u;
         if (p.hist && np < p.hist_cap) p.hist[np] = bi;
     }
 }
@@ -927,11 +991,12 @@ __device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uin
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// Instances: step_kernel<0, true, true, true> serves every planned shape with
-// runtime type and head_dim dispatch; specialized instances carry only the
-// code their model uses (a kernel that runs every op of a step is large, and
-// its instruction fetch is otherwise a bottleneck).
-template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8>
+// Instances: step_kernel<0, true, true, true, *> serves every planned shape
+// with runtime type and head_dim dispatch; specialized instances carry only
+// the code their model uses (a kernel that runs every op of a step is large,
+// and its instruction fetch is otherwise a bottleneck). TPX instances add
+// the tensor-parallel exchanges; the one-GPU instances carry none of it.
+template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX>
 __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p) {
     static_assert(65536 / SK_THREADS / 8 * 8 >= SK_REG_LAUNCH, "launch register count");
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -944,7 +1009,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     // read once: the last CTA rewrites the control block at the end of the step
     const uint32_t pos = *reinterpret_cast<const volatile uint32_t *>(p.ctrl);
     const uint32_t token = *reinterpret_cast<const volatile uint32_t *>(p.ctrl + 1);
-    if (pos >= p.max_ctx || token >= p.vocab) {   // the same decision in every CTA: nothing runs, nothing waits
+    if (pos >= p.max_ctx || token >= (p.tp ? p.vocab_full : p.vocab)) {   // the same decision in every CTA: nothing runs, nothing waits
         if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(p.err, DERR_BAD_ARG);
         return;
     }
@@ -973,8 +1038,16 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     float *sh = reinterpret_cast<float *>(xq);   // attention states alias the x buffers
     SkRing r;
     const uint32_t nops = 5 * p.n_layers + 2;
+    // tensor parallelism: exchanges completed before this step
+    const uint32_t tp_base = (TPX && p.tp) ? *reinterpret_cast<const volatile uint32_t *>(p.tp->seq) : 0u;
     for (uint32_t i = 0; i < nops; ++i) {
-        if (i > 0 && !sk_grid_sync(p, i * gridDim.x, S.sync_flag(), S.abort_flag())) break;
+        if (i > 0) {
+            uint32_t lp;
+            const int pk = sk_kind(i - 1, p.n_layers, lp);
+            const bool wrote_peers = TPX && p.tp && (pk == K_O || pk == K_DOWN || pk == K_OUT);
+            if (!sk_grid_sync(p, i * gridDim.x, S.sync_flag(), S.abort_flag(), wrote_peers)) break;
+            if (wrote_peers && blockIdx.x == 0 && threadIdx.x == 0) sk_tp_publish(p, sk_tp_index(p, tp_base, pk, lp) + 1u);
+        }
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
         if (kind == K_ATTN) {
@@ -984,10 +1057,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             continue;
         }
         if (kind == K_ARGMAX) {
-            sk_argmax(p, S, pos);
+            if (TPX && p.tp && !sk_tp_wait(p, sk_tp_index(p, tp_base, K_OUT, 0), S.sync_flag(), S.abort_flag())) break;
+            sk_argmax(p, S, pos, tp_base);
             continue;
         }
-        const SkMv d = sk_mv_desc(p, kind, l);
+        SkMv d = sk_mv_desc(p, kind, l);
+        if (TPX && p.tp && (kind == K_O || kind == K_DOWN || kind == K_OUT)) {
+            d.tpw = kind == K_OUT ? 2 : 1;
+            d.tp_k = sk_tp_index(p, tp_base, kind, l);
+        }
         uint32_t u0, u1;
         sk_range(d.g.ntiles * d.g.nch, u0, u1);
         const bool work = u1 > u0;
@@ -996,7 +1074,14 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             // every CTA keeps x current, whether or not it has units of this op
             const float *add = kind == K_QKV ? (l ? sk_acc_down(p, l - 1) : nullptr)
                                              : (kind == K_GU ? sk_acc_o(p, l) : sk_acc_down(p, p.n_layers - 1));
-            const uint32_t nadd = kind == K_GU ? 1u : p.geo[STEP_DOWN].nch;
+            uint32_t nadd = kind == K_GU ? 1u : p.geo[STEP_DOWN].nch;
+            if (TPX && p.tp && add) {   // the exchanged partials: every rank's planes, in rank order
+                const int src = kind == K_GU ? K_O : K_DOWN;
+                const uint32_t k = sk_tp_index(p, tp_base, src, kind == K_QKV ? l - 1 : (kind == K_GU ? l : p.n_layers - 1));
+                if (!sk_tp_wait(p, k, S.sync_flag(), S.abort_flag())) break;
+                add = p.tp->slots[p.tp->rank] + (size_t)(k & 1u) * p.tp->world * TP_DIM_MAX;
+                nadd *= p.tp->world;
+            }
             sk_prologue_norm(p, S, r, x, add, nadd, token, work, d.type, xq, xf);
         } else if (kind == K_O) {
             if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
@@ -1010,7 +1095,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         }
         if (!work) continue;
         named_bar_sync(1, SK_CT);
-        sk_mv_dispatch<HAS_Q4, HAS_Q6, HAS_Q8>(p, d, S, r, xq_u, xf_u);
+        sk_mv_dispatch<HAS_Q4, HAS_Q6, HAS_Q8, TPX>(p, d, S, r, xq_u, xf_u);
     }
 }
 
@@ -1102,6 +1187,7 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
         const StepMvGeom &gd = p.geo[STEP_DOWN];
         const uint64_t U = (uint64_t)gd.ntiles * gd.nch;
         if (gd.nch > (uint32_t)SK_MAXPL) return no("too many column chunks in the down projection");
+        if (p.tp && (uint64_t)gd.nch * p.dim > TP_DIM_MAX) return no("down partial planes exceed the exchange slots");
         if ((U + n_sm - 1) / n_sm > gd.ntiles) return no("down projection units per CTA exceed a chunk");
         plan_smem(gd.ck);
         if (SK_SMEM - p.ring_off < ring) return no("shared-memory plan");
@@ -1195,13 +1281,17 @@ static bool sk_is_q4k_only(const StepParams &p) {
            p.t_out == T_Q4_K;
 }
 
+template <int HD, bool A, bool B, bool C, bool T> static cudaError_t sk_attr() {
+    return cudaFuncSetAttribute(step_kernel<HD, A, B, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+}
+
 cudaError_t step_configure() {
-    cudaError_t e = cudaFuncSetAttribute(step_kernel<0, true, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(step_kernel<128, true, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(step_kernel<128, true, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
-    return e;
+    const cudaError_t es[] = {sk_attr<0, true, true, true, false>(), sk_attr<128, true, true, false, false>(),
+                              sk_attr<128, true, false, false, false>(), sk_attr<0, true, true, true, true>(),
+                              sk_attr<128, true, true, false, true>()};
+    for (cudaError_t e : es)
+        if (e != cudaSuccess) return e;
+    return cudaSuccess;
 }
 
 cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st) {
@@ -1216,9 +1306,14 @@ cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     note_launches(1);
-    if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false>, p);
-    if (sk_is_q4k_only(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, false, false>, p);
-    return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true>, p);
+    // tensor-parallel instances carry the exchange code; the one-GPU ones do not
+    if (p.tp) {
+        if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false, true>, p);
+        return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, true>, p);
+    }
+    if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false, false>, p);
+    if (sk_is_q4k_only(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, false, false, false>, p);
+    return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, false>, p);
 }
 
 }  // namespace vbs

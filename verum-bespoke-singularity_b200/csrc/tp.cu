@@ -34,10 +34,15 @@ static void *g_peer_base[TP_MAX_WORLD] = {};  // IPC mappings of the peers' regi
 static TpComm *g_comm_dev = nullptr;          // device copy of the TpComm
 constexpr size_t TP_SLOT_BYTES_PER_RANK = 2ull * TP_DIM_MAX * 4;   // two slot sets of one sender
 
-static size_t region_bytes(int world) { return TP_SLOT_BYTES_PER_RANK * world + 1024; }
-static size_t flags_offset(int world) { return TP_SLOT_BYTES_PER_RANK * world; }
+// region: [slot sets 2 x world x TP_DIM_MAX][logits TP_VOCAB_MAX][flags | seq | ticket]
+static size_t logits_offset(int world) { return TP_SLOT_BYTES_PER_RANK * world; }
+static size_t flags_offset(int world) { return logits_offset(world) + (size_t)TP_VOCAB_MAX * 4; }
+static size_t region_bytes(int world) { return flags_offset(world) + 1024; }
 
 const TpComm *tp_comm() { return g_comm_dev; }
+float *tp_own_logits() {
+    return g_comm_dev ? reinterpret_cast<float *>(static_cast<uint8_t *>(g_region) + logits_offset(g_world)) : nullptr;
+}
 
 static void p2p_teardown() {
     for (int q = 0; q < TP_MAX_WORLD; ++q)
@@ -84,6 +89,7 @@ static bool p2p_setup(int rank, int world) {
             base = static_cast<uint8_t *>(pp);
         }
         c.slots[q] = reinterpret_cast<float *>(base);
+        c.logits[q] = reinterpret_cast<float *>(base + logits_offset(world));
         c.flags[q] = reinterpret_cast<uint32_t *>(base + flags_offset(world));
     }
     uint8_t *own = static_cast<uint8_t *>(g_region) + flags_offset(world);

@@ -15,5 +15,8 @@ bool tp_allgather(const float *local, float *full, size_t n_local, cudaStream_t 
 // The peer-memory exchange region (device pointer), or NULL when the group
 // has none (one rank, or peers not mappable).
 const struct TpComm *tp_comm();
+// This rank's full-logits area in its exchange region (the step kernel
+// gathers the vocab shards there), or NULL.
+float *tp_own_logits();
 
 }  // namespace vbs
