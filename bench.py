@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default=None,
-                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode"],
+                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
     ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
@@ -73,6 +73,42 @@ def profile_kernel(args):
               "output": (vbs.Q6_K, 128256, 4096), "qkv_like": (vbs.Q4_K, 6144, 4096)}
     st = torch.cuda.Stream()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    if args.profile == "sweep":
+        # the BASELINE matvec sweep through vbs_cu_matvec: 4 shapes x {Q4_K,
+        # Q6_K} x batch {1, 8}; weight sets rotate so no launch hits L2
+        # (sets x bytes > 126 MB), one line per point
+        peak, _ = peaks()
+        for t in (vbs.Q4_K, vbs.Q6_K):
+            for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+                rb = vbs.row_bytes(t, cols)
+                nset = max(2, min(8, -(-300_000_000 // (rows * rb))))
+                ws = []
+                for i in range(nset):
+                    w = torch.empty(rows * rb, dtype=torch.uint8, device="cuda")
+                    vbs.synth(t, w.data_ptr(), rows, cols, 300 + i, sc)
+                    ws.append(w)
+                for b in (1, 8):
+                    x = torch.randn((b, cols), device="cuda")
+                    y = torch.empty((b, rows), device="cuda")
+                    n = max(4, min(args.steps, 24))
+                    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n)]
+                    torch.cuda.synchronize()
+                    with torch.cuda.stream(st):
+                        for i in range(n):
+                            ev[2 * i].record(st)
+                            vbs.matvec(t, ws[i % nset].data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, batch=b,
+                                       stream=st.cuda_stream)
+                            ev[2 * i + 1].record(st)
+                    torch.cuda.synchronize()
+                    us = sorted(ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1e3 for i in range(1, n))
+                    med = us[len(us) // 2]
+                    alg = rows * rb + b * cols * 4 + b * rows * 4
+                    print(json.dumps({"profile": "sweep", "type": vbs.TYPE_NAMES[t], "rows": rows, "cols": cols, "batch": b,
+                                      "median_us": round(med, 2), "algorithmic_bytes": alg,
+                                      "gbs": round(alg / (med * 1e-6) / 1e9, 1),
+                                      "frac_of_measured": round(alg / (med * 1e-6) / 1e9 / peak, 3)}), flush=True)
+                del ws
+        return
     if args.profile == "decode":
         # the full decode step at position --ctx (the cache rows before it
         # are zeros: same bytes and kernels as a prefilled cache), then

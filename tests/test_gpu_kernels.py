@@ -97,6 +97,45 @@ def test_matvec_batch8(vbs, orc, torch, t, clean_errors):
         assert rel_ok(y[b].cpu().numpy(), orc.linear_tile(wh, t, x[b], rows, cols))
 
 
+@pytest.mark.parametrize("t,rows,cols,B", [(12, 14336, 4096, 8), (14, 4096, 14336, 8), (12, 4096, 14336, 3),
+                                           (14, 301, 3328, 5), (12, 19, 512, 2), (14, 1000, 7936, 8),
+                                           (12, 33, 4352, 7)])
+def test_matvec_batched_tensor_cores(vbs, orc, torch, t, rows, cols, B, clean_errors):
+    """The batched kernel (mvb.cu): every batch row against the oracle, for
+    ragged batches (sequences beyond B padded), partial 16-row tiles, Q6_K
+    rows that are only 2-byte aligned, and rows split into column chunks
+    (wider than 4096, summed in chunk order)."""
+    rb = orc.row_bytes(t, cols)
+    w = torch.empty(rows * rb, dtype=torch.uint8, device="cuda")
+    vbs.synth(t, w.data_ptr(), rows, cols, 77 + rows + cols + B, orc.synth_scale(0.02))
+    x = np.random.default_rng(rows + B).standard_normal((B, cols)).astype(np.float32)
+    y = torch.full((B, rows), float("nan"), dtype=torch.float32, device="cuda")
+    xd = dev(torch, x)
+    vbs.matvec(t, w.data_ptr(), xd.data_ptr(), y.data_ptr(), rows, cols, batch=B)
+    torch.cuda.synchronize()
+    wh = w.cpu().numpy()
+    yh = y.cpu().numpy()
+    for b in range(B):
+        assert rel_ok(yh[b], orc.linear_tile(wh, t, x[b], rows, cols)), b
+
+
+def test_matvec_batched_accumulate(vbs, orc, torch, clean_errors):
+    """VBS_CU_MV_ACCUMULATE on the batched path, one chunk and several."""
+    for rows, cols in ((64, 4096), (64, 8192)):
+        t, B = 12, 4
+        rb = orc.row_bytes(t, cols)
+        w = torch.empty(rows * rb, dtype=torch.uint8, device="cuda")
+        vbs.synth(t, w.data_ptr(), rows, cols, 9, orc.synth_scale(0.02))
+        x = np.random.default_rng(1).standard_normal((B, cols)).astype(np.float32)
+        y0 = np.random.default_rng(2).standard_normal((B, rows)).astype(np.float32)
+        y = dev(torch, y0.copy())
+        vbs.matvec(t, w.data_ptr(), dev(torch, x).data_ptr(), y.data_ptr(), rows, cols, batch=B, flags=vbs.MV_ACCUMULATE)
+        torch.cuda.synchronize()
+        wh = w.cpu().numpy()
+        for b in range(B):
+            assert rel_ok(y[b].cpu().numpy(), y0[b] + orc.linear_tile(wh, t, x[b], rows, cols)), (rows, cols, b)
+
+
 @pytest.mark.parametrize("t,rows,cols", [(8, 1, 32), (8, 17, 96), (8, 100, 4128), (14, 3, 256), (14, 33, 768),
                                          (14, 250, 1792), (12, 1, 256), (12, 19, 512), (12, 301, 3328),
                                          (0, 7, 688), (1, 9, 200), (2, 13, 64), (3, 13, 64)])

@@ -92,7 +92,8 @@ static bool do_init() {
         s.n_sm = pr.multiProcessorCount;
         if (cudaMalloc(&s.err, 256) != cudaSuccess) continue;
         cudaMemset(s.err, 0, 256);
-        if (mv_configure() != cudaSuccess || attn_configure() != cudaSuccess || step_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
+        if (mv_configure() != cudaSuccess || mvb_configure() != cudaSuccess || attn_configure() != cudaSuccess ||
+            step_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
         vbs_device_t &d = g_devices[g_ndev];
         memset(&d, 0, sizeof(d));
         snprintf(d.name, sizeof(d.name), "%s", pr.name);
@@ -159,6 +160,19 @@ void *attn_workspace(DevState *d, size_t bytes) {
     return d->attn_work;
 }
 
+void *mvb_workspace(DevState *d, size_t bytes) {
+    if (d->mvb_work_bytes >= bytes) return d->mvb_work;
+    if (d->mvb_work) {
+        cudaDeviceSynchronize();
+        cudaFree(d->mvb_work);
+        d->mvb_work = nullptr;
+        d->mvb_work_bytes = 0;
+    }
+    if (!cuda_ok(cudaMalloc(&d->mvb_work, bytes), "batched matvec workspace")) return nullptr;
+    d->mvb_work_bytes = bytes;
+    return d->mvb_work;
+}
+
 // ---------------------------------------------------------------------------
 // pipelines
 // ---------------------------------------------------------------------------
@@ -192,6 +206,27 @@ static int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, f
         p.accumulate = (flags & VBS_CU_MV_ACCUMULATE) ? 1u : 0u;
         p.err = d->err;
         return cuda_ok(mv_fast_launch(type, 0, MV_EPI_STORE, p, d->n_sm, st, false, 0), "matvec launch") ? 0 : -1;
+    }
+    if (batch > 1 && !(flags & VBS_CU_MV_PORTABLE) && mvb_supported(type, rows, cols, batch, w, x)) {
+        // batched decode on the tensor cores (mvb.cu)
+        MvbParams p = {};
+        p.w = w;
+        p.rb = row_bytes(type, cols);
+        p.rows = rows;
+        p.cols = cols;
+        p.batch = batch;
+        p.x = x;
+        p.x_stride = cols;
+        p.y = y;
+        p.y_stride = rows;
+        p.accumulate = (flags & VBS_CU_MV_ACCUMULATE) ? 1u : 0u;
+        p.err = d->err;
+        float *work = nullptr;
+        if (const size_t wb = mvb_workspace_bytes(type, rows, cols, batch)) {
+            work = static_cast<float *>(mvb_workspace(d, wb));
+            if (!work) return -1;
+        }
+        return cuda_ok(mvb_launch(type, p, work, d->n_sm, st), "batched matvec launch") ? 0 : -1;
     }
     return cuda_ok(mv_generic_launch(type, w, x, y, rows, cols, batch, cols, rows, (flags & VBS_CU_MV_ACCUMULATE) ? 1 : 0,
                                      d->n_sm, st),

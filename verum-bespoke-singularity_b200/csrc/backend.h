@@ -15,6 +15,8 @@ struct DevState {
     void *attn_work = nullptr;      // shared split-KV workspace for the ops table / vbs_cu_attention
     size_t attn_work_bytes = 0;
     void *attn_static = nullptr;    // address of the fixed scratch of vbs_cu_attention_static
+    void *mvb_work = nullptr;       // chunk planes of the batched matvec
+    size_t mvb_work_bytes = 0;
 };
 
 // Devices usable by this library (sm_100). Index = position in the ops
@@ -35,5 +37,7 @@ bool check_device_error(DevState *d, cudaStream_t st);
 
 // Grow the device's shared attention workspace to `bytes` (zeroed).
 void *attn_workspace(DevState *d, size_t bytes);
+// Grow the device's batched-matvec plane workspace to `bytes`.
+void *mvb_workspace(DevState *d, size_t bytes);
 
 }  // namespace vbs

@@ -78,6 +78,25 @@ struct MvParams {
     uint32_t tp_read;           // prologue: x_add := the rank-ordered sum of the own slot set
 };
 
+// ---- batched matvec (mvb.cu): Y[b] = W X[b] for b < batch <= 8 ----
+struct MvbParams {
+    const uint8_t *w;
+    uint64_t rb;                // packed bytes per row
+    uint32_t rows, cols, batch;
+    const float *x;             // [batch][x_stride]
+    uint64_t x_stride;
+    float *y;                   // [batch][y_stride]
+    uint64_t y_stride;
+    float *y_plane;             // set by the launcher: per-chunk partial planes when rows span several chunks
+    uint32_t accumulate;
+    uint32_t *err;
+};
+bool mvb_supported(int type, uint32_t rows, uint32_t cols, uint32_t batch, const void *w, const void *x);
+// Device workspace the launch needs (0: none).
+size_t mvb_workspace_bytes(int type, uint32_t rows, uint32_t cols, uint32_t batch);
+cudaError_t mvb_configure();
+cudaError_t mvb_launch(int type, const MvbParams &p, float *work, int n_sm, cudaStream_t st);
+
 // True when the TMA/mma kernel can serve this shape/alignment.
 bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const *w, int nw,
                        const void *x, int dual);
