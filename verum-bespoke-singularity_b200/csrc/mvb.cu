@@ -12,13 +12,16 @@
 //    sequences are zero), and for Q4_K the per-group sums of those fp16
 //    values (the min term).
 //  * mma.sync m16n8k16 f16 x f16 -> fp32, one MMA column per sequence. The A
-//    operand holds the raw quants (Q4_K nibbles 0..15, Q6_K q - 32), exact in
-//    fp16; the k-slots of an MMA are permuted so that each lane's four
-//    weights are four consecutive bytes and its x values one contiguous load
-//    (the dot product does not care about the order of its terms). One MMA
-//    pair covers one Q4_K sub-block (32) and one MMA one Q6_K scale group
-//    (16), so the group's integer-valued dot gets its scale in fp32:
-//    Q4_K y += d*sc * dot - dmin*m * sum(x), Q6_K y += d*sc * dot.
+//    operand holds the raw quants, exact in fp16: Q4_K 1024 + nibble (the
+//    bits 0x6400 | n, formed by one mask; the bias goes out with the group's
+//    x sum, which the min term needs anyway), Q6_K q - 32. The k-slots of an
+//    MMA are permuted so that each lane's four weights are four consecutive
+//    bytes and its x values one contiguous load (the dot product does not
+//    care about the order of its terms); x is stored with each group of 4 in
+//    the order (0, 2, 1, 3), so a mask of the weight word yields the pairs
+//    directly. One MMA pair covers one Q4_K sub-block (32) and one MMA one
+//    Q6_K scale group (16), so the group's dot gets its scale in fp32:
+//    Q4_K y += d*sc * dot - (dmin*m + 1024*d*sc) * sum(x), Q6_K y += d*sc * dot.
 //  * x in fp16 rounds each element by at most 2^-11 relative: the result is
 //    within ~2.5e-4 of the exact dot (the batch-1 kernel's two-level int8
 //    x is tighter; 1e-3 is the bar).
@@ -32,28 +35,34 @@
 
 namespace vbs {
 
-constexpr int MB_NCW = 8;                        // consumer warps
+constexpr int MB_NCW = 16;                       // consumer warps: one 256-column super-block each at 4096 columns
 constexpr int MB_THREADS = (MB_NCW + 1) * 32;    // + one producer warp
 constexpr uint32_t MB_B = 8;                     // sequences per MMA (the n dimension)
 constexpr uint32_t MB_CK = 4096;                 // max columns per chunk
 constexpr uint32_t MB_MAXST = 16;
 constexpr uint32_t MB_SMEM = 227u * 1024u;
-// shared memory: barriers [0, 256) | abort 256 | red [8 warps][16 rows][8 seqs] fp32 at 1024 |
+// shared memory: barriers [0, 256) | abort 256 | red [MB_NCW warps][16 rows][8 seqs] fp32 at 1024 |
 // x fp16 [8][ck] | group sums [8][ck/16] fp32 | ring
 constexpr uint32_t MB_RED = 1024, MB_X = MB_RED + MB_NCW * 16 * MB_B * 4;
 
 struct MbGeom {
     uint32_t ck, rs, nstage, stage0, nch, xs_off;
+    uint32_t xstride;   // bytes per sequence's fp16 x row
 };
 
 template <int TYPE> __host__ __device__ constexpr uint32_t mb_group() { return TYPE == T_Q6_K ? 16u : 32u; }
+// x row padding: the 8 lanes sharing a column offset read 8 sequences' rows;
+// a row pad of 16 words (Q4_K: 16-byte loads by quarter warps) or 8 words
+// (Q6_K: 8-byte loads by half warps) puts them in distinct banks
+template <int TYPE> __host__ __device__ constexpr uint32_t mb_xpad() { return TYPE == T_Q6_K ? 32u : 64u; }
 
 template <int TYPE> static MbGeom mb_geom(uint32_t cols) {
     MbGeom g = {};
     g.nch = (cols + MB_CK - 1) / MB_CK;
     g.ck = (cols + g.nch - 1) / g.nch;
     g.ck = (g.ck + 255) / 256 * 256;
-    g.xs_off = MB_X + MB_B * g.ck * 2;
+    g.xstride = g.ck * 2 + mb_xpad<TYPE>();
+    g.xs_off = MB_X + MB_B * g.xstride;
     g.stage0 = (g.xs_off + MB_B * (g.ck / mb_group<TYPE>()) * 4 + 1023u) & ~1023u;
     uint32_t rs = ((g.ck / 256) * (uint32_t)MvT<TYPE>::BB + 32 + 15) & ~15u;
     if (((rs / 16) & 1u) == 0) rs += 16;
@@ -63,28 +72,20 @@ template <int TYPE> static MbGeom mb_geom(uint32_t cols) {
     return g;
 }
 
-// four consecutive bytes -> two f16x2 pairs (bytes 0,1 and 2,3) of their low
-// or high nibbles, as exact small integers: 1024 + n is an exact fp16 (the
-// bits 0x6400 | n), minus 1024
-__device__ __forceinline__ void mb_pairs(uint32_t w, int hi_nib, uint32_t &p01, uint32_t &p23) {
-    const uint32_t s01 = __byte_perm(w, 0u, 0x4140u), s23 = __byte_perm(w, 0u, 0x4342u);
-    const uint32_t m = 0x000F000Fu;
-    const uint32_t a = (hi_nib ? ((s01 >> 4) & m) : (s01 & m)) | 0x64006400u;
-    const uint32_t b = (hi_nib ? ((s23 >> 4) & m) : (s23 & m)) | 0x64006400u;
-    const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
-    const __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), k1024);
-    const __half2 hb = __hsub2(*reinterpret_cast<const __half2 *>(&b), k1024);
-    p01 = *reinterpret_cast<const uint32_t *>(&ha);
-    p23 = *reinterpret_cast<const uint32_t *>(&hb);
+// weights w0..w3 in the bytes of one word -> f16x2 pairs (w0, w2) and (w1, w3)
+// of the nibbles at bit `sh` (0 low, 4 high), as 1024 + n (exact)
+__device__ __forceinline__ void mb_nib_pairs(uint32_t w, int sh, uint32_t &p02, uint32_t &p13) {
+    p02 = ((w >> sh) & 0x000F000Fu) | 0x64006400u;
+    p13 = ((w >> (sh + 8)) & 0x000F000Fu) | 0x64006400u;
 }
-__device__ __forceinline__ void mb_pairs6(uint32_t q6, uint32_t &p01, uint32_t &p23) {   // bytes 0..63 -> q - 32
-    const uint32_t s01 = __byte_perm(q6, 0u, 0x4140u), s23 = __byte_perm(q6, 0u, 0x4342u);
+// 6-bit values v0..v3 in the bytes of one word -> f16x2 (v0-32, v2-32), (v1-32, v3-32)
+__device__ __forceinline__ void mb_q6_pairs(uint32_t v, uint32_t &p02, uint32_t &p13) {
     const __half2 k1056 = __floats2half2_rn(1056.f, 1056.f);
-    const uint32_t a = s01 | 0x64006400u, b = s23 | 0x64006400u;
+    const uint32_t a = (v & 0x00FF00FFu) | 0x64006400u, b = ((v >> 8) & 0x00FF00FFu) | 0x64006400u;
     const __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), k1056);
     const __half2 hb = __hsub2(*reinterpret_cast<const __half2 *>(&b), k1056);
-    p01 = *reinterpret_cast<const uint32_t *>(&ha);
-    p23 = *reinterpret_cast<const uint32_t *>(&hb);
+    p02 = *reinterpret_cast<const uint32_t *>(&ha);
+    p13 = *reinterpret_cast<const uint32_t *>(&hb);
 }
 
 // One warp, 16 rows (stage rows g, g+8 at rowA/rowB, pads pa/pb), one
@@ -92,9 +93,9 @@ __device__ __forceinline__ void mb_pairs6(uint32_t q6, uint32_t &p01, uint32_t &
 // acc: rows g, g+8 x sequences 2t, 2t+1.
 template <int TYPE>
 __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t pa, uint32_t pb, uint32_t e, uint32_t xh,
-                                        uint32_t ck, const float *xs, int lane, float acc[4]) {
+                                        uint32_t ck, uint32_t xstride, const float *xs, int lane, float acc[4]) {
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t xrow = xh + (uint32_t)g * ck * 2;   // this lane's B column is sequence g
+    const uint32_t xrow = xh + (uint32_t)g * xstride;   // this lane's B column is sequence g
     if constexpr (TYPE == T_Q4_K) {
         const uint32_t sa = rowA + (e >> 8) * 144, sb = rowB + (e >> 8) * 144;
         const uint4 hA = lds_u128(sa), hB = lds_u128(sb);
@@ -110,7 +111,7 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
                 dsc[rr][s] = d * byte_f(s < 4 ? sc0 : sc1, s & 3);
-                dmm[rr][s] = dmin * byte_f(s < 4 ? mn0 : mn1, s & 3);
+                dmm[rr][s] = dmin * byte_f(s < 4 ? mn0 : mn1, s & 3) + 1024.0f * dsc[rr][s];   // min term + the 1024 bias
             }
         }
 #pragma unroll
@@ -124,8 +125,8 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {   // weights 8t+4hf .. +3
                     uint32_t a[4];
-                    mb_pairs(hf ? wA.y : wA.x, hi, a[0], a[2]);
-                    mb_pairs(hf ? wB.y : wB.x, hi, a[1], a[3]);
+                    mb_nib_pairs(hf ? wA.y : wA.x, 4 * hi, a[0], a[2]);
+                    mb_nib_pairs(hf ? wB.y : wB.x, 4 * hi, a[1], a[3]);
                     mma_f16_acc(c, a, hf ? xv.z : xv.x, hf ? xv.w : xv.y);
                 }
                 const uint32_t grp = (e >> 5) + s;
@@ -153,8 +154,8 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
                     const uint32_t vA = ((lA >> sh) & 0x0F0F0F0Fu) | (((qhA >> (2 * q)) & 0x03030303u) << 4);
                     const uint32_t vB = ((lB >> sh) & 0x0F0F0F0Fu) | (((qhB >> (2 * q)) & 0x03030303u) << 4);
                     uint32_t a[4];
-                    mb_pairs6(vA, a[0], a[2]);
-                    mb_pairs6(vB, a[1], a[3]);
+                    mb_q6_pairs(vA, a[0], a[2]);
+                    mb_q6_pairs(vB, a[1], a[3]);
                     const uint2 xv = lds_u64(xrow + (e + 128 * h + 32 * q + o) * 2);
                     float c[4] = {0.f, 0.f, 0.f, 0.f};
                     mma_f16_acc(c, a, xv.x, xv.y);
@@ -249,16 +250,14 @@ __global__ void __launch_bounds__(MB_THREADS, 1) mvb_kernel(const MvbParams p, c
     // ------------------------------ consumers ------------------------------
     // x chunk as fp16 [8][ck] (sequences >= batch and columns >= ncol zero),
     // then the per-group sums of those fp16 values
-    for (uint32_t i = threadIdx.x; i < MB_B * geo.ck / 2; i += MB_NCW * 32) {
-        const uint32_t b = i / (geo.ck / 2), c = 2 * (i % (geo.ck / 2));
-        float v0 = 0.f, v1 = 0.f;
-        if (b < p.batch && c < ncol) {
-            const float2 v = *reinterpret_cast<const float2 *>(p.x + (uint64_t)b * p.x_stride + c0 + c);
-            v0 = v.x;
-            v1 = v.y;
-        }
-        const __half2 h = __floats2half2_rn(v0, v1);
-        asm volatile("st.shared.u32 [%0], %1;" ::"r"(xh + (b * geo.ck + c) * 2), "r"(*reinterpret_cast<const uint32_t *>(&h)) : "memory");
+    // stored with each group of 4 in the order (0, 2, 1, 3): the MMA k-slot order
+    for (uint32_t i = threadIdx.x; i < MB_B * geo.ck / 4; i += MB_NCW * 32) {
+        const uint32_t b = i / (geo.ck / 4), c = 4 * (i % (geo.ck / 4));
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (b < p.batch && c < ncol) v = *reinterpret_cast<const float4 *>(p.x + (uint64_t)b * p.x_stride + c0 + c);
+        const __half2 h02 = __floats2half2_rn(v.x, v.z), h13 = __floats2half2_rn(v.y, v.w);
+        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(xh + b * geo.xstride + c * 2),
+                     "r"(*reinterpret_cast<const uint32_t *>(&h02)), "r"(*reinterpret_cast<const uint32_t *>(&h13)) : "memory");
     }
     named_bar_sync(1, MB_NCW * 32);
     if constexpr (TYPE == T_Q4_K) {
@@ -267,7 +266,7 @@ __global__ void __launch_bounds__(MB_THREADS, 1) mvb_kernel(const MvbParams p, c
             const uint32_t b = i / ng, gg = i % ng;
             float s = 0.f;
             for (int k = 0; k < 32; k += 2) {
-                const uint32_t w = lds_u32(xh + (b * geo.ck + gg * 32 + k) * 2);
+                const uint32_t w = lds_u32(xh + b * geo.xstride + (gg * 32 + k) * 2);
                 const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
                 s += f.x + f.y;
             }
@@ -294,7 +293,7 @@ __global__ void __launch_bounds__(MB_THREADS, 1) mvb_kernel(const MvbParams p, c
                 pb = (uint32_t)(reinterpret_cast<uintptr_t>(p.w + (uint64_t)rb * p.rb + boff) & 15);
             }
             for (uint32_t e = (uint32_t)warp * 256u; e < ncol; e += MB_NCW * 256u)
-                mb_unit<TYPE>(rowA, rowB, pa, pb, e, xh, geo.ck, xs, lane, acc);
+                mb_unit<TYPE>(rowA, rowB, pa, pb, e, xh, geo.ck, geo.xstride, xs, lane, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(slot));
@@ -337,7 +336,7 @@ __global__ void mvb_reduce_kernel(const float *planes, uint32_t nch, uint32_t ba
 bool mvb_supported(int type, uint32_t rows, uint32_t cols, uint32_t batch, const void *w, const void *x) {
     if (type != T_Q4_K && type != T_Q6_K) return false;
     if (!rows || batch < 1 || batch > MB_B || cols % 256) return false;
-    if (reinterpret_cast<uintptr_t>(x) & 7) return false;
+    if (reinterpret_cast<uintptr_t>(x) & 15) return false;   // float4 loads of x
     // Q4_K rows (144-byte blocks) must start 16-byte aligned for the 16-byte header loads
     if (type == T_Q4_K && (reinterpret_cast<uintptr_t>(w) & 15)) return false;
     const MbGeom g = type == T_Q4_K ? mb_geom<T_Q4_K>(cols) : mb_geom<T_Q6_K>(cols);
