@@ -64,8 +64,16 @@ template <int TYPE> static MbGeom mb_geom(uint32_t cols) {
     g.xstride = g.ck * 2 + mb_xpad<TYPE>();
     g.xs_off = MB_X + MB_B * g.xstride;
     g.stage0 = (g.xs_off + MB_B * (g.ck / mb_group<TYPE>()) * 4 + 1023u) & ~1023u;
+    // stage row stride: Q4_K rows are read as 8-byte words by half warps
+    // (rows g = 0..3, lanes t): a stride of 32 mod 128 bytes puts the four
+    // rows in distinct banks. Q6_K (4-byte words, whole warps): an odd
+    // number of 16-byte units does.
     uint32_t rs = ((g.ck / 256) * (uint32_t)MvT<TYPE>::BB + 32 + 15) & ~15u;
-    if (((rs / 16) & 1u) == 0) rs += 16;
+    if (TYPE == T_Q4_K) {
+        while (rs % 128 != 32) rs += 16;
+    } else if (((rs / 16) & 1u) == 0) {
+        rs += 16;
+    }
     g.rs = rs;
     const uint32_t avail = MB_SMEM > g.stage0 ? MB_SMEM - g.stage0 : 0;
     g.nstage = std::min(MB_MAXST, avail / (16 * rs));
@@ -129,8 +137,9 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
                     mb_nib_pairs(hf ? wB.y : wB.x, 4 * hi, a[1], a[3]);
                     mma_f16_acc(c, a, hf ? xv.z : xv.x, hf ? xv.w : xv.y);
                 }
-                const uint32_t grp = (e >> 5) + s;
-                const float x0 = xs[(2 * t) * (ck / 32) + grp], x1 = xs[(2 * t + 1) * (ck / 32) + grp];
+                const uint32_t grp = (e >> 5) + s;   // group sums [group][8 sequences]
+                const float2 xg = *reinterpret_cast<const float2 *>(xs + grp * MB_B + 2 * t);
+                const float x0 = xg.x, x1 = xg.y;
                 acc[0] += dsc[0][s] * c[0] - dmm[0][s] * x0;
                 acc[1] += dsc[0][s] * c[1] - dmm[0][s] * x1;
                 acc[2] += dsc[1][s] * c[2] - dmm[1][s] * x0;
@@ -263,7 +272,7 @@ __global__ void __launch_bounds__(MB_THREADS, 1) mvb_kernel(const MvbParams p, c
     if constexpr (TYPE == T_Q4_K) {
         const uint32_t ng = geo.ck / 32;
         for (uint32_t i = threadIdx.x; i < MB_B * ng; i += MB_NCW * 32) {
-            const uint32_t b = i / ng, gg = i % ng;
+            const uint32_t gg = i / MB_B, b = i % MB_B;   // stored [group][sequence]
             float s = 0.f;
             for (int k = 0; k < 32; k += 2) {
                 const uint32_t w = lds_u32(xh + b * geo.xstride + (gg * 32 + k) * 2);
