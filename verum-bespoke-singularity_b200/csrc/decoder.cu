@@ -478,6 +478,9 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
     if (d->tp_world > 1 && d->strict) return fail("strict mode runs on one GPU", d);
     d->tp_p2p = d->tp_world > 1 && tp_comm() && !(flags & VBS_CU_DEC_TP_NCCL) && m->dim <= TP_DIM_MAX;
     if (d->tp_world == 1 && d->vocab_full != m->vocab) return fail("vocab_full differs from vocab without TP", d);
+    if (d->tp_world > 1 && (d->vocab_full != (uint32_t)d->tp_world * m->vocab ||
+                            m->vocab_offset != (uint32_t)tp_rank() * m->vocab))   // the logits gather in rank order
+        return fail("tensor parallelism: the output rows must split evenly, rank r owning rows r * vocab onward", d);
     d->L.resize(m->n_layers);
     for (uint32_t l = 0; l < m->n_layers; ++l) {
         Layer &y = d->L[l];

@@ -43,8 +43,13 @@ constexpr uint32_t TP_DIM_MAX = 16384;
 constexpr uint32_t TP_VOCAB_MAX = 262144;
 struct TpComm {
     float *slots[TP_MAX_WORLD];      // region of rank q (own region at [rank])
-    float *logits[TP_MAX_WORLD];     // rank q's full-logits area (the step kernel gathers the vocab shards there)
+    float *logits[TP_MAX_WORLD];     // rank q's full-logits area (the step kernel's argmax leaves the gathered logits there)
     uint32_t *flags[TP_MAX_WORLD];   // flag words of rank q's region, [world]
+    // The step kernel's exchanges carry their own flag: one 64-bit word per
+    // value, (exchange index + 1) << 32 | float bits, stored and loaded
+    // whole, so a reader checks each word itself (no fence, no flag store).
+    uint64_t *ll[TP_MAX_WORLD];        // rank q's word slots: 2 sets x world x TP_DIM_MAX
+    uint64_t *ll_logits[TP_MAX_WORLD]; // rank q's gathered logits words, TP_VOCAB_MAX
     uint32_t *seq;                   // this rank: exchanges completed
     uint32_t *ticket;                // this rank: CTAs finished in the current writer kernel
     uint32_t world, rank;

@@ -209,12 +209,10 @@ __device__ __forceinline__ void sk_abort(const StepParams &p, uint32_t code) {
 // of the CTA, when this CTA or the grid aborted: thread 0 decides after the
 // first CTA barrier and the second one publishes its decision.
 __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t target, volatile int *flag,
-                                             volatile int *cta_abort, bool sys_fence = false) {
+                                             volatile int *cta_abort) {
     named_bar_sync(1, SK_CT);
     if (threadIdx.x == 0) {
-        // system scope after an op that stored into peers' memory
-        if (sys_fence) __threadfence_system();
-        else __threadfence();
+        __threadfence();
         atomicAdd(&p.sync[0], 1u);
         bool ok = *cta_abort == 0;
         const uint64_t t0 = global_ns();
@@ -234,47 +232,62 @@ __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t targe
 
 // ---------------------------------------------------------------------------
 // tensor parallelism over peer memory (TpComm): per step, exchange 2l is
-// layer l's o_proj partials, 2l + 1 its down partials, 2L the logits. The
-// writers store into every rank's region in their row flush; after the next
-// grid barrier (system-scope fences) CTA 0 publishes k + 1 into this rank's
-// flag in every region; readers wait until all flags of their own region
-// reached k + 1.
+// layer l's o_proj partials, 2l + 1 its down partials, 2L the logits. Every
+// value travels as one 64-bit word, (k + 1) << 32 | float bits, which the
+// writers store into every rank's region in their row flush (st.relaxed.sys:
+// single-copy atomic). A reader loads its own region's words until each
+// carries k + 1, so it needs no fence, flag or grid barrier on either side:
+// a word with k + 1 is the value. Exchange k uses slot set k % 2; a writer
+// reaches exchange k + 2 only after reading k + 1 from every rank, and every
+// rank wrote k + 1 behind a grid barrier that followed its reads of k.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t sk_tp_index(const StepParams &p, uint32_t base, int kind, uint32_t l) {
     return base + (kind == K_OUT ? 2u * p.n_layers : 2u * l + (kind == K_DOWN ? 1u : 0u));
 }
 
-__device__ __noinline__ void sk_tp_publish(const StepParams &p, uint32_t value) {
-    const TpComm &c = *p.tp;
-    for (uint32_t q = 0; q < c.world; ++q)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(c.flags[q] + c.rank), "r"(value) : "memory");
+__device__ __forceinline__ void st_word_sys(uint64_t *a, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t sk_ld_acquire_sys(const uint32_t *a) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-    return v;
+__device__ __forceinline__ void ld_words_sys(const uint64_t *a, uint64_t &x, uint64_t &y) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(a));
 }
 
-// All consumer threads: wait (thread 0 polls, bounded) until every rank
-// published exchange k. False, in every thread, on timeout or abort.
-__device__ __noinline__ bool sk_tp_wait(const StepParams &p, uint32_t k, volatile int *flag, volatile int *cta_abort) {
-    if (threadIdx.x == 0) {
-        const TpComm &c = *p.tp;
-        bool ok = *cta_abort == 0;
-        const uint64_t t0 = global_ns();
-        for (uint32_t q = 0; q < c.world && ok; ++q)
-            for (uint32_t it = 1; (int)(sk_ld_acquire_sys(c.flags[c.rank] + q) - (k + 1u)) < 0; ++it) {
-                if ((it & 15u) == 0) {
-                    if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
-                    if (global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
-                }
+// A word load that has not seen k + 1 yet: true (give up) once the grid
+// aborted or the wait passed its limit, recording a peer timeout.
+__device__ __noinline__ bool sk_word_give_up(const StepParams &p, uint64_t t0, volatile int *cta_abort) {
+    if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { *cta_abort = 1; return true; }
+    if (global_ns() - t0 <= kWaitNs) return false;
+    *cta_abort = 1;
+    sk_abort(p, DERR_TIMEOUT_PEER);
+    return true;
+}
+
+// v[c][0..7] = the 8 values at a + c * stride (words, 16-byte aligned) for
+// planes c < n, once every word carries `want`; all planes' loads are in
+// flight together. Garbage (and the abort set) when the wait gives up.
+template <int NP>
+__device__ __forceinline__ void sk_ld8_words(const StepParams &p, const uint64_t *a, uint64_t stride, uint32_t n,
+                                             uint32_t want, float (&v)[NP][8], volatile int *cta_abort) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        bool ok = true;
+#pragma unroll
+        for (int c = 0; c < NP; ++c) {
+            if ((uint32_t)c >= n) continue;
+            uint64_t w[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ld_words_sys(a + c * stride + 2 * k, w[2 * k], w[2 * k + 1]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                ok &= (uint32_t)(w[k] >> 32) == want;
+                v[c][k] = __uint_as_float((uint32_t)w[k]);
             }
-        if (!ok) *cta_abort = 1;
-        *flag = ok ? 1 : 0;
+        }
+        if (ok) break;
+        if (it == 0) t0 = global_ns();
+        else if ((it & 15u) == 0 && sk_word_give_up(p, t0, cta_abort)) break;
     }
-    named_bar_sync(1, SK_CT);
-    return *flag != 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -451,9 +464,12 @@ __device__ __noinline__ void sk_embed8(const StepParams &p, uint32_t token, uint
 // ahead of the op's weight stages), so it is never a load on this path.
 constexpr int SK_MAXPL = 4;      // partial planes summed by the norm prologue
 
+// WORDS (instances with tensor parallelism): when `want` is not 0 the planes
+// are exchange words carrying it.
+template <bool WORDS>
 __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSmem &S, SkRing &r, float *x,
-                                                 const float *add, uint32_t nadd, uint32_t token, bool quant, int type,
-                                                 uint8_t *xq, float4 *xf) {
+                                                 const void *add, uint32_t nadd, uint32_t want, uint32_t token,
+                                                 bool quant, int type, uint8_t *xq, float4 *xf) {
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = p.dim / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
     float xv[SK_PB][8];
@@ -467,9 +483,14 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
                 // planes in order, SK_MAXPL loads in flight at a time
                 for (uint32_t c0 = 0; c0 < nadd; c0 += SK_MAXPL) {
                     float pv[SK_MAXPL][8];
+                    if (WORDS && want) {
+                        sk_ld8_words<SK_MAXPL>(p, static_cast<const uint64_t *>(add) + (uint64_t)c0 * p.dim + e, p.dim,
+                                               nadd - c0, want, pv, S.abort_flag());
+                    } else {
 #pragma unroll
-                    for (int c = 0; c < SK_MAXPL; ++c)
-                        if (c0 + c < nadd) ld8_cg(add + (uint64_t)(c0 + c) * p.dim + e, pv[c]);
+                        for (int c = 0; c < SK_MAXPL; ++c)
+                            if (c0 + c < nadd) ld8_cg(static_cast<const float *>(add) + (uint64_t)(c0 + c) * p.dim + e, pv[c]);
+                    }
 #pragma unroll
                     for (int k = 0; k < 8; ++k) xv[r][k] = c0 ? xv[r][k] + pv[0][k] : pv[0][k];
 #pragma unroll
@@ -632,13 +653,14 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
                     }
                 } else if (TPX && row < d.rows && d.tpw) {   // this rank's partial into every rank's region
                     const TpComm &c = *p.tp;
+                    const uint64_t word = (uint64_t)(d.tp_k + 1u) << 32 | __float_as_uint(va);
                     if (d.tpw == 1) {
                         const size_t off = (size_t)(d.tp_k & 1u) * c.world * TP_DIM_MAX +
                                            ((size_t)c.rank * d.g.nch + ch) * d.rows + row;
-                        for (uint32_t q = 0; q < c.world; ++q) c.slots[q][off] = va;
+                        for (uint32_t q = 0; q < c.world; ++q) st_word_sys(c.ll[q] + off, word);
                     } else {
                         const size_t off = (size_t)c.rank * d.rows + row;
-                        for (uint32_t q = 0; q < c.world; ++q) c.logits[q][off] = va;
+                        for (uint32_t q = 0; q < c.world; ++q) st_word_sys(c.ll_logits[q] + off, word);
                     }
                 } else if (row < d.rows) {
                     d.out[(uint64_t)ch * d.rows + row] = va;
@@ -955,14 +977,35 @@ __device__ __forceinline__ void sk_block_argmax(const SkSmem &S, float &best, ui
 }
 
 __device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uint32_t pos, uint32_t tp_base) {
-    // under TP every rank holds the full gathered logits and picks the same token
-    const float *lg = p.tp ? p.tp->logits[p.tp->rank] : sk_logits(p);
+    // under TP every rank gathers the full logits (exchange words) and picks
+    // the same token; the values also go to the plain logits area for readback
     const uint32_t n = p.tp ? p.vocab_full : p.vocab, per = (n + gridDim.x - 1) / gridDim.x;
     const uint32_t lo = min(n, blockIdx.x * per), hi = min(n, lo + per);
     float best = -INFINITY;
     uint32_t bi = 0xFFFFFFFFu;
-    for (uint32_t i = lo + threadIdx.x; i < hi; i += SK_CT) sk_pick(best, bi, __ldcg(lg + i), i);
+    if (p.tp) {
+        const TpComm &c = *p.tp;
+        const uint32_t want = tp_base + 2u * p.n_layers + 1u;
+        const uint64_t *lw = c.ll_logits[c.rank];
+        volatile int *cta_abort = S.abort_flag();
+        for (uint32_t i = lo + threadIdx.x; i < hi; i += SK_CT) {
+            uint64_t w = 0, t0 = 0;
+            for (uint32_t it = 0;; ++it) {
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(lw + i));
+                if ((uint32_t)(w >> 32) == want) break;
+                if (it == 0) t0 = global_ns();
+                else if ((it & 15u) == 0 && sk_word_give_up(p, t0, cta_abort)) break;
+            }
+            const float v = __uint_as_float((uint32_t)w);
+            c.logits[c.rank][i] = v;
+            sk_pick(best, bi, v, i);
+        }
+    } else {
+        const float *lg = sk_logits(p);
+        for (uint32_t i = lo + threadIdx.x; i < hi; i += SK_CT) sk_pick(best, bi, __ldcg(lg + i), i);
+    }
     sk_block_argmax(S, best, bi);
+    if (*S.abort_flag()) return;   // a word never came: no token, the error is recorded
     volatile int *flag = S.sync_flag();
     if (threadIdx.x == 0) {
         p.sync[SK_SLOTS + 2 * blockIdx.x] = __float_as_uint(best);
@@ -1040,13 +1083,18 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     const uint32_t nops = 5 * p.n_layers + 2;
     // tensor parallelism: exchanges completed before this step
     const uint32_t tp_base = (TPX && p.tp) ? *reinterpret_cast<const volatile uint32_t *>(p.tp->seq) : 0u;
+    uint32_t nsync = 0;   // grid barriers taken (TPX instances skip some)
     for (uint32_t i = 0; i < nops; ++i) {
         if (i > 0) {
             uint32_t lp;
             const int pk = sk_kind(i - 1, p.n_layers, lp);
-            const bool wrote_peers = TPX && p.tp && (pk == K_O || pk == K_DOWN || pk == K_OUT);
-            if (!sk_grid_sync(p, i * gridDim.x, S.sync_flag(), S.abort_flag(), wrote_peers)) break;
-            if (wrote_peers && blockIdx.x == 0 && threadIdx.x == 0) sk_tp_publish(p, sk_tp_index(p, tp_base, pk, lp) + 1u);
+            if (TPX && p.tp && (pk == K_O || pk == K_DOWN)) {
+                // the next op only reads exchange words, which it checks one
+                // by one; an abort is taken at the next grid barrier
+                named_bar_sync(1, SK_CT);
+            } else if (!sk_grid_sync(p, (TPX ? ++nsync : i) * gridDim.x, S.sync_flag(), S.abort_flag())) {
+                break;
+            }
         }
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
@@ -1057,7 +1105,6 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             continue;
         }
         if (kind == K_ARGMAX) {
-            if (TPX && p.tp && !sk_tp_wait(p, sk_tp_index(p, tp_base, K_OUT, 0), S.sync_flag(), S.abort_flag())) break;
             sk_argmax(p, S, pos, tp_base);
             continue;
         }
@@ -1074,15 +1121,16 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             // every CTA keeps x current, whether or not it has units of this op
             const float *add = kind == K_QKV ? (l ? sk_acc_down(p, l - 1) : nullptr)
                                              : (kind == K_GU ? sk_acc_o(p, l) : sk_acc_down(p, p.n_layers - 1));
-            uint32_t nadd = kind == K_GU ? 1u : p.geo[STEP_DOWN].nch;
+            uint32_t nadd = kind == K_GU ? 1u : p.geo[STEP_DOWN].nch, want = 0;
+            const void *planes = add;
             if (TPX && p.tp && add) {   // the exchanged partials: every rank's planes, in rank order
                 const int src = kind == K_GU ? K_O : K_DOWN;
                 const uint32_t k = sk_tp_index(p, tp_base, src, kind == K_QKV ? l - 1 : (kind == K_GU ? l : p.n_layers - 1));
-                if (!sk_tp_wait(p, k, S.sync_flag(), S.abort_flag())) break;
-                add = p.tp->slots[p.tp->rank] + (size_t)(k & 1u) * p.tp->world * TP_DIM_MAX;
+                planes = p.tp->ll[p.tp->rank] + (size_t)(k & 1u) * p.tp->world * TP_DIM_MAX;
                 nadd *= p.tp->world;
+                want = k + 1u;
             }
-            sk_prologue_norm(p, S, r, x, add, nadd, token, work, d.type, xq, xf);
+            sk_prologue_norm<TPX>(p, S, r, x, planes, nadd, want, token, work, d.type, xq, xf);
         } else if (kind == K_O) {
             if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
         } else if (work) {   // K_DOWN: only the column chunks of this CTA's units

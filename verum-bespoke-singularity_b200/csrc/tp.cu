@@ -11,9 +11,12 @@
 // The per-layer sums do not go through NCCL: the writing matvec stores its
 // rows straight into every peer's receive region over NVLink (CUDA IPC
 // mappings of each rank's region, exchanged here with one NCCL all-gather
-// of the handles) and publishes a flag; the next kernel's prologue waits
-// for the flags and sums the slots (TpComm, kernels.h). NCCL's all-reduce
-// stays available as the reference collective (VBS_CU_DEC_TP_NCCL).
+// of the handles). The per-op kernels then publish a flag, which the next
+// kernel's prologue waits for before it sums the slots; the persistent step
+// kernel stores each value with its exchange index in one 64-bit word,
+// which the reader checks word by word (TpComm, kernels.h). NCCL's
+// all-reduce stays available as the reference collective
+// (VBS_CU_DEC_TP_NCCL).
 #include "vbs_b200.h"
 #include "backend.h"
 #include "kernels.h"
@@ -35,9 +38,12 @@ static TpComm *g_comm_dev = nullptr;          // device copy of the TpComm
 constexpr size_t TP_SLOT_BYTES_PER_RANK = 2ull * TP_DIM_MAX * 4;   // two slot sets of one sender
 
 // region: [slot sets 2 x world x TP_DIM_MAX][logits TP_VOCAB_MAX][flags | seq | ticket]
+//         [word slot sets 2 x world x TP_DIM_MAX][logits words TP_VOCAB_MAX]
 static size_t logits_offset(int world) { return TP_SLOT_BYTES_PER_RANK * world; }
 static size_t flags_offset(int world) { return logits_offset(world) + (size_t)TP_VOCAB_MAX * 4; }
-static size_t region_bytes(int world) { return flags_offset(world) + 1024; }
+static size_t ll_offset(int world) { return flags_offset(world) + 1024; }
+static size_t ll_logits_offset(int world) { return ll_offset(world) + 2 * TP_SLOT_BYTES_PER_RANK * world; }
+static size_t region_bytes(int world) { return ll_logits_offset(world) + (size_t)TP_VOCAB_MAX * 8; }
 
 const TpComm *tp_comm() { return g_comm_dev; }
 float *tp_own_logits() {
@@ -91,6 +97,8 @@ static bool p2p_setup(int rank, int world) {
         c.slots[q] = reinterpret_cast<float *>(base);
         c.logits[q] = reinterpret_cast<float *>(base + logits_offset(world));
         c.flags[q] = reinterpret_cast<uint32_t *>(base + flags_offset(world));
+        c.ll[q] = reinterpret_cast<uint64_t *>(base + ll_offset(world));
+        c.ll_logits[q] = reinterpret_cast<uint64_t *>(base + ll_logits_offset(world));
     }
     uint8_t *own = static_cast<uint8_t *>(g_region) + flags_offset(world);
     c.seq = reinterpret_cast<uint32_t *>(own + 512);
