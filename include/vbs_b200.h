@@ -266,6 +266,9 @@ typedef struct {
 #define VBS_CU_DEC_NO_PDL   4u   /* no programmatic dependent launch between kernels */
 #define VBS_CU_DEC_NO_PERSIST 8u /* per-op kernels instead of the persistent one-launch step */
 #define VBS_CU_DEC_TP_NCCL 16u   /* tensor parallelism: per-layer sums with ncclAllReduce instead of peer memory */
+#define VBS_CU_DEC_WORDS 32u     /* one GPU: run the step kernel's tensor-parallel instance (exchange words in place of
+                                    the grid barriers after o_proj and down) over a local area. Same results; slower
+                                    on one GPU (every thread polls its words), there to test that instance. */
 
 typedef struct vbs_cu_decoder vbs_cu_decoder_t;
 

@@ -120,6 +120,27 @@ def test_persistent_matches_per_op_long_context(vbs, l8b_2layer, clean_errors):
     b.close()
 
 
+def test_tp_instance_on_one_gpu_identical(vbs, l8b_2layer, clean_errors):
+    """The step kernel's tensor-parallel instance (DEC_WORDS: exchange words
+    over a local area, no grid barrier after o_proj and down, logits
+    gathered as words) gives the plain instance's bits at every step. The
+    word tags come from a counter that reset() leaves alone, so the second
+    pass over the same positions must not accept the first pass's words."""
+    _, dm = l8b_2layer
+    toks = models.splitmix_ints(9, 120, 4096)
+    a, b = vbs.Decoder(dm, 256, vbs.DEC_WORDS), vbs.Decoder(dm, 256)
+    assert a.kernels_per_step == 1 and a.tp_mode == "single"
+    for rep in range(2):
+        for i in range(0, 120, 40):
+            la, lb = a.forward(toks[i:i + 40]), b.forward(toks[i:i + 40])
+            assert (la.view(np.uint32) == lb.view(np.uint32)).all(), (rep, i)
+        a.reset()
+        b.reset()
+    assert a.generate([11, 12, 13], 24) == b.generate([11, 12, 13], 24)
+    a.close()
+    b.close()
+
+
 HD64 = dict(n_layers=2, dim=1024, n_heads=16, n_kv_heads=4, ffn=2816, vocab=2048, eps=1e-5, theta=10000.0)
 
 

@@ -36,6 +36,7 @@ ARG_BUFFER, ARG_SCALAR = 0, 1
 MV_ACCUMULATE, MV_PORTABLE = 1, 2
 DEC_STRICT, DEC_NO_GRAPH, DEC_NO_PDL, DEC_NO_PERSIST = 1, 2, 4, 8
 DEC_TP_NCCL = 16   # tensor parallelism: NCCL all-reduce for the per-layer sums (the reference collective)
+DEC_WORDS = 32     # one GPU: the step kernel's tensor-parallel instance over a local word area (for testing it)
 
 
 class VbsError(RuntimeError):

@@ -79,6 +79,8 @@ struct vbs_cu_decoder {
     float *step_acc = nullptr;        // accumulation buffers, then the sync words
     size_t step_acc_bytes = 0;
     void *step_attn = nullptr;
+    void *words_mem = nullptr;        // one GPU, VBS_CU_DEC_WORDS: the local exchange-word area
+    TpComm *words_comm = nullptr;
     uint32_t n_splits = 1;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -395,9 +397,21 @@ bool plan_persistent(vbs_cu_decoder *d) {
         p.tp_world = (uint32_t)d->tp_world;
         p.tp_rank = (uint32_t)tp_rank();
         p.vocab_full = d->vocab_full;
+    } else if ((d->flags & VBS_CU_DEC_WORDS) && m.dim <= TP_DIM_MAX && m.vocab <= TP_VOCAB_MAX) {
+        // one GPU on request: the tensor-parallel instance (exchange words,
+        // no grid barrier after o_proj and down) over a local area
+        if (!tp_local_area(d->logits, &d->words_mem, &d->words_comm)) return false;
+        p.tp = d->words_comm;
+        p.tp_world = 1;
+        p.tp_rank = 0;
+        p.vocab_full = m.vocab;
     }
     char why[160];
-    if (!step_plan(p, d->dev->n_sm, why, sizeof why)) return true;
+    if (!step_plan(p, d->dev->n_sm, why, sizeof why)) {
+        if (d->tp_world > 1 || !p.tp) return true;
+        p.tp = nullptr;   // the plain one-GPU instance
+        if (!step_plan(p, d->dev->n_sm, why, sizeof why)) return true;
+    }
     // repacked weights: per layer QKV | O | GU | DOWN, then the output matrix
     const size_t bq = step_packed_bytes(p, STEP_QKV), bo = step_packed_bytes(p, STEP_O),
                  bg = step_packed_bytes(p, STEP_GU), bd = step_packed_bytes(p, STEP_DOWN),
@@ -562,7 +576,8 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
     if (d->graph) cudaGraphDestroy(d->graph);
     void *bufs[] = {d->x, d->x2, d->q, d->att, d->hid, d->logits, d->logits_full, d->partial, d->norm, d->k, d->v,
                     d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
-                    d->tok_dev, d->attn_work, d->argmax_work, d->step_layers, d->step_acc, d->step_attn, d->step_packed};
+                    d->tok_dev, d->attn_work, d->argmax_work, d->step_layers, d->step_acc, d->step_attn, d->step_packed,
+                    d->words_mem, d->words_comm};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->pinned) cudaFreeHost(d->pinned);

@@ -107,6 +107,25 @@ static bool p2p_setup(int rank, int world) {
            cuda_ok(cudaMemcpy(g_comm_dev, &c, sizeof(TpComm), cudaMemcpyHostToDevice), "tp comm");
 }
 
+bool tp_local_area(float *logits, void **mem, TpComm **comm) {
+    *mem = nullptr;
+    *comm = nullptr;
+    const size_t words = 2ull * TP_DIM_MAX * 8, lw = (size_t)TP_VOCAB_MAX * 8;
+    uint8_t *base = nullptr;
+    if (!cuda_ok(cudaMalloc((void **)&base, words + lw + 128), "word area")) return false;
+    *mem = base;
+    if (!cuda_ok(cudaMemset(base, 0, words + lw + 128), "word area")) return false;
+    TpComm c = {};
+    c.world = 1;
+    c.rank = 0;
+    c.ll[0] = reinterpret_cast<uint64_t *>(base);
+    c.ll_logits[0] = reinterpret_cast<uint64_t *>(base + words);
+    c.logits[0] = logits;
+    c.seq = reinterpret_cast<uint32_t *>(base + words + lw);
+    return cuda_ok(cudaMalloc((void **)comm, sizeof(TpComm)), "word area") &&
+           cuda_ok(cudaMemcpy(*comm, &c, sizeof(TpComm), cudaMemcpyHostToDevice), "word area");
+}
+
 int tp_world() { return g_comm ? g_world : 1; }
 int tp_rank() { return g_comm ? g_rank : 0; }
 

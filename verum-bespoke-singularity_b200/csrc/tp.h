@@ -18,5 +18,10 @@ const struct TpComm *tp_comm();
 // This rank's full-logits area in its exchange region (the step kernel
 // gathers the vocab shards there), or NULL.
 float *tp_own_logits();
+// A one-GPU exchange area for the step kernel's word instances: word slots,
+// logits words and the exchange counter in this device's memory; the
+// argmax leaves the plain logits in `logits`. The caller frees *mem and
+// *comm with cudaFree (also after a false return).
+bool tp_local_area(float *logits, void **mem, struct TpComm **comm);
 
 }  // namespace vbs
