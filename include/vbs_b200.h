@@ -240,6 +240,21 @@ VBS_API int vbs_cu_attention_static(const float *q, const uint16_t *kc, const ui
 VBS_API int vbs_cu_synth(int type, void *dst, uint64_t rows, uint64_t cols, uint64_t row0, uint64_t col0,
                  uint64_t full_cols, uint64_t seed, float scale, void *stream);
 
+/* Copies byte ranges of a file into device memory: range i, the bytes
+ * [offsets[i], offsets[i] + sizes[i]) of the file at `path`, lands at the
+ * device pointer dst[i] (on the current device). Replaces the reference
+ * loader's host mirror plus one synchronous copy_to_device per tensor
+ * (src/vbs_fabric.c:81-94, src/vbs_backend_cuda.c:148). n_threads reader
+ * threads (0: 4, at most 32) pread chunks of chunk_bytes (0: 16 MiB;
+ * clamped to 1 MiB..1 GiB) into two pinned staging buffers each and copy
+ * them with cudaMemcpyAsync on their own streams, so reads and copies
+ * overlap. Returns 0 once every byte has landed (all its streams
+ * synchronized); -1, with the error latched, for a range outside the file,
+ * a missing destination, a short read or a CUDA error. Device work the
+ * caller queued before the call (e.g. clearing dst) must be complete. */
+VBS_API int vbs_cu_upload_file(const char *path, size_t n, const uint64_t *offsets, const uint64_t *sizes,
+                               void *const *dst, uint32_t n_threads, uint64_t chunk_bytes);
+
 /* ---- decode program (the JIT forward pass, src/vbs_specializer.c:231-372) ---- */
 
 /* A llama-style model resident on the device. Per-layer fields are host

@@ -150,6 +150,7 @@ def lib() -> C.CDLL:
         "vbs_cu_attention": (i32, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, f32, u32, u64, vp]),
         "vbs_cu_attention_static": (i32, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, f32, u32, u64, vp]),
         "vbs_cu_synth": (i32, [i32, vp, u64, u64, u64, u64, u64, u64, f32, vp]),
+        "vbs_cu_upload_file": (i32, [C.c_char_p, sz, vp, vp, vp, u32, u64]),
         "vbs_cu_decoder_create": (vp, [C.POINTER(ModelDesc), u32, u32, C.c_char_p, sz]),
         "vbs_cu_decoder_destroy": (None, [vp]),
         "vbs_cu_decoder_forward": (i32, [vp, C.POINTER(u32), sz, C.POINTER(f32)]),
@@ -426,24 +427,32 @@ class Decoder:
 # ---------------------------------------------------------------------------
 # GGUF v3 (the container the reference loads, src/vbs_gguf.c)
 # ---------------------------------------------------------------------------
-_GG_U32, _GG_F32, _GG_STR = 4, 6, 8
+_GG_U32, _GG_F32, _GG_STR, _GG_ARR = 4, 6, 8, 9
 
 
 def write_gguf(path, metadata: dict, tensors: list, alignment: int = 32) -> None:
     """tensors: [(name, type_id, dims (ne0 = columns first), bytes)].
-    metadata values: int -> u32, float -> f32, str -> string."""
+    metadata values: int -> u32, float -> f32, str -> string, and a list of
+    one of those -> array (the tokenizer tables of real model files)."""
     def s(x: str) -> bytes:
         b = x.encode()
         return struct.pack("<Q", len(b)) + b
 
+    def typed(v) -> tuple[int, bytes]:
+        if isinstance(v, str):
+            return _GG_STR, s(v)
+        if isinstance(v, float):
+            return _GG_F32, struct.pack("<f", v)
+        return _GG_U32, struct.pack("<I", int(v))
+
     kv = b""
     for k, v in metadata.items():
-        if isinstance(v, str):
-            kv += s(k) + struct.pack("<I", _GG_STR) + s(v)
-        elif isinstance(v, float):
-            kv += s(k) + struct.pack("<If", _GG_F32, v)
+        if isinstance(v, (list, tuple)):
+            et = typed(v[0])[0] if v else _GG_U32
+            kv += s(k) + struct.pack("<IIQ", _GG_ARR, et, len(v)) + b"".join(typed(e)[1] for e in v)
         else:
-            kv += s(k) + struct.pack("<II", _GG_U32, int(v))
+            t, b = typed(v)
+            kv += s(k) + struct.pack("<I", t) + b
     info, blobs, off = b"", [], 0
     for name, typ, dims, data in tensors:
         if off % alignment:
@@ -463,89 +472,141 @@ def write_gguf(path, metadata: dict, tensors: list, alignment: int = 32) -> None
             f.write(b)
 
 
-def read_gguf(path) -> tuple[dict, dict]:
-    """Minimal GGUF v3 reader: (metadata, {name: (type, dims, bytes)})."""
-    data = Path(path).read_bytes()
-    o = 0
+_GG_SCALAR = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
 
-    def rd(fmt):
-        nonlocal o
-        v = struct.unpack_from(fmt, data, o)
-        o += struct.calcsize(fmt)
-        return v
 
-    def rs():
-        (n,) = rd("<Q")
-        nonlocal o
-        v = data[o:o + n].decode()
-        o += n
-        return v
+@dataclass
+class GgufTensor:
+    type: int
+    dims: tuple            # ne0 (columns) first
+    offset: int            # absolute file offset of the data
+    nbytes: int | None     # None for a type this library has no block size for
 
-    magic, ver, nt, nkv = rd("<4sIQQ")
-    if magic != b"GGUF" or ver != 3:
-        raise ValueError("not a GGUF v3 file")
-    meta = {}
-    scal = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
-    for _ in range(nkv):
-        k = rs()
-        (t,) = rd("<I")
-        if t == _GG_STR:
-            meta[k] = rs()
-        elif t in scal:
-            (meta[k],) = rd(scal[t])
-        else:
-            raise ValueError(f"unsupported metadata type {t} for {k}")
-    infos = []
-    for _ in range(nt):
-        name = rs()
-        (nd,) = rd("<I")
-        dims = rd("<" + "Q" * nd)
-        typ, rel = rd("<IQ")
-        infos.append((name, typ, dims, rel))
+
+def gguf_layout(path) -> tuple[dict, dict]:
+    """GGUF v3 header (src/vbs_gguf.c): (metadata, {name: GgufTensor}),
+    reading only the header, never the tensor data. Metadata arrays (the
+    tokenizer's, in real model files) are read into lists."""
+    with open(path, "rb") as f:
+        def rd(fmt):
+            n = struct.calcsize(fmt)
+            b = f.read(n)
+            if len(b) != n:
+                raise ValueError(f"{path}: GGUF header ends early")
+            return struct.unpack(fmt, b)
+
+        def rs():
+            (n,) = rd("<Q")
+            b = f.read(n)
+            if len(b) != n:
+                raise ValueError(f"{path}: GGUF header ends early")
+            return b.decode("utf-8", errors="replace")
+
+        def value(t):
+            if t == _GG_STR:
+                return rs()
+            if t in _GG_SCALAR:
+                return rd(_GG_SCALAR[t])[0]
+            if t == _GG_ARR:
+                et, n = rd("<IQ")
+                if et in _GG_SCALAR:   # one read for a scalar array
+                    fmt = _GG_SCALAR[et]
+                    return list(rd("<" + fmt[1:] * n)) if n else []
+                return [value(et) for _ in range(n)]
+            raise ValueError(f"unsupported GGUF metadata type {t}")
+
+        magic, ver, nt, nkv = rd("<4sIQQ")
+        if magic != b"GGUF" or ver != 3:
+            raise ValueError("not a GGUF v3 file")
+        meta = {}
+        for _ in range(nkv):
+            k = rs()
+            (t,) = rd("<I")
+            meta[k] = value(t)
+        infos = []
+        for _ in range(nt):
+            name = rs()
+            (nd,) = rd("<I")
+            dims = rd("<" + "Q" * nd)
+            typ, rel = rd("<IQ")
+            infos.append((name, typ, dims, rel))
+        o = f.tell()
     align = int(meta.get("general.alignment", 32))
     start = (o + align - 1) // align * align
     tens = {}
     for name, typ, dims, rel in infos:
-        cols, rows = dims[0], 1
+        rows = 1
         for d in dims[1:]:
             rows *= d
-        nbytes = row_bytes(typ, cols) * rows
-        tens[name] = (typ, dims, data[start + rel:start + rel + nbytes])
+        nbytes = row_bytes(typ, dims[0]) * rows if typ in BLOCK else None
+        tens[name] = GgufTensor(typ, tuple(dims), start + rel, nbytes)
     return meta, tens
 
 
-def upload_gguf(path, device="cuda") -> DeviceModel:
-    """Load a llama GGUF onto the device (one copy per tensor, like the
-    reference fabric's copy_to_device, src/vbs_fabric.c:81-94)."""
-    import numpy as np
+def read_gguf(path) -> tuple[dict, dict]:
+    """Minimal GGUF v3 reader: (metadata, {name: (type, dims, bytes)})."""
+    meta, lay = gguf_layout(path)
+    tens = {}
+    with open(path, "rb") as f:
+        for name, t in lay.items():
+            if t.nbytes is None:
+                raise ValueError(f"{name}: tensor type {t.type} is not supported")
+            f.seek(t.offset)
+            b = f.read(t.nbytes)
+            if len(b) != t.nbytes:
+                raise ValueError(f"{name}: file ends inside the tensor")
+            tens[name] = (t.type, t.dims, b)
+    return meta, tens
+
+
+def upload_file(path, ranges, n_threads: int = 0, chunk_bytes: int = 0) -> None:
+    """ranges: [(file offset, bytes, device pointer)]; one native call
+    (vbs_cu_upload_file: reader threads, pinned staging, async copies)."""
+    n = len(ranges)
+    offs = (C.c_uint64 * max(n, 1))(*[r[0] for r in ranges])
+    sizes = (C.c_uint64 * max(n, 1))(*[r[1] for r in ranges])
+    dsts = (C.c_void_p * max(n, 1))(*[r[2] for r in ranges])
+    check(lib().vbs_cu_upload_file(str(path).encode(), n, offs, sizes, dsts, n_threads, chunk_bytes),
+          "vbs_cu_upload_file")
+
+
+def upload_gguf(path, device="cuda", n_threads: int = 0) -> DeviceModel:
+    """Load a llama GGUF onto the device straight from the file: the header
+    gives every tensor's offset, device buffers are allocated (matrices with
+    256 zero bytes of tail padding), then one vbs_cu_upload_file call moves
+    all tensors through pinned staging buffers. Replaces the reference's
+    host mirror plus one synchronous copy_to_device per tensor
+    (src/vbs_fabric.c:81-94)."""
     import torch
-    meta, tens = read_gguf(path)
+    meta, tens = gguf_layout(path)
     a = "llama."
     nl = int(meta[a + "block_count"])
     dim = int(meta[a + "embedding_length"])
     nh = int(meta[a + "attention.head_count"])
     nkv = int(meta.get(a + "attention.head_count_kv", nh))
     ffn = int(meta[a + "feed_forward_length"])
-    vocab = tens["token_embd.weight"][1][1]
+    vocab = tens["token_embd.weight"].dims[1]
     shape = LlamaShape(nl, dim, nh, nkv, ffn, vocab, float(meta.get(a + "attention.layer_norm_rms_epsilon", 1e-5)),
                        float(meta.get(a + "rope.freq_base", 10000.0)))
-    types = {"token_embd": tens["token_embd.weight"][0],
-             "output": tens.get("output.weight", tens["token_embd.weight"])[0]}
+    types = {"token_embd": tens["token_embd.weight"].type,
+             "output": tens.get("output.weight", tens["token_embd.weight"]).type}
     for base in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
-        types[base] = tens[f"blk.0.{base}.weight"][0]
+        types[base] = tens[f"blk.0.{base}.weight"].type
     m = DeviceModel(shape=shape, types=types)
+    ranges = []
 
     def put(key, name, as_float=False):
-        typ, dims, b = tens[name]
+        t = tens[name]
+        if t.nbytes is None:
+            raise ValueError(f"{name}: tensor type {t.type} is not supported")
         if as_float:
-            arr = np.frombuffer(b, dtype=np.float32).copy() if typ == F32 else None
-            if arr is None:
+            if t.type != F32:
                 raise ValueError(f"{name}: norm weights must be F32")
-            m.tensors[key] = torch.from_numpy(arr).to(device)
+            buf = torch.empty(t.nbytes // 4, dtype=torch.float32, device=device)
         else:
-            t = torch.zeros(len(b) + 256, dtype=torch.uint8)
-            t[:len(b)] = torch.frombuffer(bytearray(b), dtype=torch.uint8)
-            m.tensors[key] = t.to(device)
+            buf = torch.zeros(t.nbytes + 256, dtype=torch.uint8, device=device)
+        m.tensors[key] = buf
+        ranges.append((t.offset, t.nbytes, buf.data_ptr()))
 
     put("token_embd", "token_embd.weight")
     put("output", "output.weight" if "output.weight" in tens else "token_embd.weight")
@@ -555,5 +616,7 @@ def upload_gguf(path, device="cuda") -> DeviceModel:
             put(f"blk.{l}.{base}", f"blk.{l}.{base}.weight")
         put(f"blk.{l}.attn_norm", f"blk.{l}.attn_norm.weight", as_float=True)
         put(f"blk.{l}.ffn_norm", f"blk.{l}.ffn_norm.weight", as_float=True)
+    torch.cuda.synchronize()   # the buffers' clears come before the copies
+    upload_file(path, ranges, n_threads)
     m.make_desc()
     return m
