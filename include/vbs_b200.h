@@ -300,6 +300,15 @@ VBS_API void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d);
  * token at consecutive positions, then the logits of the last step are
  * copied to logits_out (host, vocab floats; NULL skips the readback). */
 VBS_API int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n_tokens, float *logits_out);
+/* Prompt tokens as context: their KV rows are computed and stored at
+ * positions position()..position()+n-1, up to 8 tokens sharing one pass over
+ * the weights (batched matvec, causal split-KV attention), no logits. The
+ * next vbs_cu_decoder_forward / generate continues at position()+n; feed
+ * the prompt's last token through it to get its logits. The reference feeds
+ * prompts one token at a time through forward_token (src/main.c:901-904);
+ * the stored rows agree with that to the kernels' rounding. One GPU, not in
+ * strict mode. 0, or -1 with the error latched. */
+VBS_API int vbs_cu_decoder_prefill(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n_tokens);
 
 /* Mirrors verum_reset_cache (src/vbs_specializer.c:370): position 0. */
 VBS_API void vbs_cu_decoder_reset(vbs_cu_decoder_t *d);

@@ -154,6 +154,7 @@ def lib() -> C.CDLL:
         "vbs_cu_decoder_create": (vp, [C.POINTER(ModelDesc), u32, u32, C.c_char_p, sz]),
         "vbs_cu_decoder_destroy": (None, [vp]),
         "vbs_cu_decoder_forward": (i32, [vp, C.POINTER(u32), sz, C.POINTER(f32)]),
+        "vbs_cu_decoder_prefill": (i32, [vp, C.POINTER(u32), sz]),
         "vbs_cu_decoder_reset": (None, [vp]),
         "vbs_cu_decoder_generate": (i32, [vp, C.POINTER(u32), sz, u32, C.POINTER(u32)]),
         "vbs_cu_decoder_enqueue_steps": (i32, [vp, u32]),
@@ -376,6 +377,19 @@ class Decoder:
         ptr = out.ctypes.data_as(C.POINTER(C.c_float)) if logits else None
         check(lib().vbs_cu_decoder_forward(self.h, arr, len(tokens), ptr), "vbs_cu_decoder_forward")
         return out
+
+    def prefill(self, tokens) -> None:
+        """The tokens as context (KV rows only, chunks of 8 through the
+        batched kernels); the next forward continues after them."""
+        arr = (C.c_uint32 * max(len(tokens), 1))(*tokens)
+        check(lib().vbs_cu_decoder_prefill(self.h, arr, len(tokens)), "vbs_cu_decoder_prefill")
+
+    def forward_prompt(self, tokens):
+        """Logits after the whole prompt: prefill all but the last token,
+        then one step for the last."""
+        if len(tokens) > 1:
+            self.prefill(tokens[:-1])
+        return self.forward(tokens[-1:])
 
     def forward_into(self, tok_arr, n: int, logits_ptr) -> None:
         check(lib().vbs_cu_decoder_forward(self.h, tok_arr, n, logits_ptr), "vbs_cu_decoder_forward")

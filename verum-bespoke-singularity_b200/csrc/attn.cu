@@ -56,8 +56,8 @@ __device__ __forceinline__ KvSlice attn_slice(const AttnParams &p, uint32_t bq, 
     return KvSlice{p.kc + off, p.vc + off, p.head_major ? (uint64_t)p.hd : kv_dim};
 }
 
-__device__ __forceinline__ uint32_t attn_seq(const AttnParams &p) {
-    uint32_t seq = p.seq_dev ? (*p.seq_dev + 1u) : p.seq_len;
+__device__ __forceinline__ uint32_t attn_seq(const AttnParams &p, uint32_t bq) {
+    uint32_t seq = (p.seq_dev ? (*p.seq_dev + 1u) : p.seq_len) + bq * p.seq_step;
     if (seq > p.max_ctx) {   // never read past the cache; report instead
         if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) dev_flag_error(p.err, DERR_BAD_ARG);
         seq = p.max_ctx;
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(AttnMma<HD>::NW * 32) attn_mma_kernel(const At
     const KvSlice kv = attn_slice(p, bq, kvh);
 
     pdl_wait();
-    const uint32_t seq = attn_seq(p);
+    const uint32_t seq = attn_seq(p, bq);
     uint32_t per = (seq + n_splits - 1) / n_splits;
     per = (per + 15) & ~15u;
     const uint32_t t0 = min(seq, split * per), t1 = min(seq, t0 + per);
@@ -215,7 +215,9 @@ __global__ void __launch_bounds__(AttnMma<HD>::NW * 32) attn_mma_kernel(const At
             const int isv = i / (C::SP * C::CPR), r = (i / C::CPR) % C::SP, ch = i % C::CPR;
             const uint32_t t = pb + r;
             const bool ok = t < t1;
-            const uint16_t *src = (isv ? kv.v : kv.k) + (uint64_t)(ok ? t : t0) * kv.ps + ch * 8;
+            const uint32_t tr = ok ? t : t0;
+            const uint32_t cs = p.swz ? (ch ^ (tr & 7u)) : (uint32_t)ch;   // the row's 16-byte chunk in memory
+            const uint16_t *src = (isv ? kv.v : kv.k) + (uint64_t)tr * kv.ps + cs * 8;
             cp_async16(slot + (isv * C::SP + r) * C::RSB + ch * 16, src, ok ? 16u : 0u);
         }
     };
@@ -343,7 +345,7 @@ __global__ void __launch_bounds__(AT_NW * 32) attn_simt_kernel(const AttnParams 
     const KvSlice kv = attn_slice(p, bq, kvh);
 
     pdl_wait();
-    const uint32_t seq = attn_seq(p);
+    const uint32_t seq = attn_seq(p, bq);
     const uint32_t per = (seq + n_splits - 1) / n_splits;
     const uint32_t t0 = min(seq, split * per), t1 = min(seq, t0 + per);
 
@@ -527,6 +529,7 @@ cudaError_t attn_launch(const AttnParams &p, uint32_t n_splits, cudaStream_t st,
          reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.out)) & 15)
         return cudaErrorInvalidValue;
     if (p.kv_batch_stride % 8) return cudaErrorInvalidValue;   // keeps every sequence's rows 16-byte aligned
+    if (p.swz && (!p.head_major || (p.hd != 64 && p.hd != 128))) return cudaErrorInvalidValue;   // 8+ chunks per row
     const uint32_t G = p.nqh / p.nkh;
     switch (p.hd) {
         case 32: return attn_mma_go<32>(p, n_splits, st, pdl);

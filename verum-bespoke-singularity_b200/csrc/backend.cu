@@ -187,8 +187,8 @@ static bool type_supported(int t) {
     return t == T_F32 || t == T_F16 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K;
 }
 
-static int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
-                      uint32_t batch, uint32_t flags, cudaStream_t st) {
+int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
+               uint32_t batch, uint32_t flags, cudaStream_t st) {
     if (!type_supported(type) || !w || !x || !y || !rows || !cols || !batch || cols % (uint32_t)block_elems(type)) {
         latch_error("matvec: invalid arguments (type %d, %ux%u, batch %u)", type, rows, cols, batch);
         return -1;

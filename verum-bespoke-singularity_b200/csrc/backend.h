@@ -39,5 +39,10 @@ bool check_device_error(DevState *d, cudaStream_t st);
 void *attn_workspace(DevState *d, size_t bytes);
 // Grow the device's batched-matvec plane workspace to `bytes`.
 void *mvb_workspace(DevState *d, size_t bytes);
+// y[b] (+)= W x[b] for b < batch on `st`, through the kernel the shape and
+// type allow (fast, batched tensor-core or portable); flags VBS_CU_MV_*.
+// 0, or -1 with the error latched.
+int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
+               uint32_t batch, uint32_t flags, cudaStream_t st);
 
 }  // namespace vbs

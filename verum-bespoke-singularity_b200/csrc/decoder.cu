@@ -82,6 +82,11 @@ struct vbs_cu_decoder {
     void *words_mem = nullptr;        // one GPU, VBS_CU_DEC_WORDS: the local exchange-word area
     TpComm *words_comm = nullptr;
     uint32_t n_splits = 1;
+    // prompt chunks (vbs_cu_decoder_prefill), allocated on first use
+    float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_att = nullptr,
+          *pf_g = nullptr, *pf_u = nullptr, *pf_h = nullptr;
+    void *pf_attn_work = nullptr;
+    uint32_t pf_splits = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     uint32_t kernels_per_step = 0;
@@ -457,6 +462,73 @@ bool plan_persistent(vbs_cu_decoder *d) {
     return true;
 }
 
+// ---------------------------------------------------------------------------
+// prompt chunks: up to PF_CHUNK tokens share one pass over the weights
+// ---------------------------------------------------------------------------
+constexpr uint32_t PF_CHUNK = 8;   // the batched matvec's largest batch
+
+bool prefill_buffers(vbs_cu_decoder *d) {
+    if (d->pf_x) return true;
+    const vbs_cu_model_t &m = d->m;
+    const size_t B = PF_CHUNK;
+    // the most splits any chunk takes (fewer for larger batches)
+    d->pf_splits = attn_num_splits(d->max_ctx, m.n_kv_heads, 1, d->dev->n_sm);
+    const size_t aw = attn_workspace_bytes(m.n_heads, m.n_kv_heads, m.head_dim, PF_CHUNK, d->pf_splits);
+    return dmalloc((void **)&d->pf_x, B * m.dim * 4, "prefill rows") && dmalloc((void **)&d->pf_xn, B * m.dim * 4, "prefill rows") &&
+           dmalloc((void **)&d->pf_q, B * d->q_dim * 4, "prefill rows") && dmalloc((void **)&d->pf_att, B * d->q_dim * 4, "prefill rows") &&
+           dmalloc((void **)&d->pf_k, B * d->kv_dim * 4, "prefill rows") && dmalloc((void **)&d->pf_v, B * d->kv_dim * 4, "prefill rows") &&
+           dmalloc((void **)&d->pf_g, B * m.ffn * 4, "prefill rows") && dmalloc((void **)&d->pf_u, B * m.ffn * 4, "prefill rows") &&
+           dmalloc((void **)&d->pf_h, B * m.ffn * 4, "prefill rows") && dmalloc(&d->pf_attn_work, aw, "prefill attention") &&
+           cuda_ok(cudaMemset(d->pf_attn_work, 0, aw), "prefill attention");
+}
+
+// One chunk of B tokens (token ids at tok, positions p0..p0+B-1) through
+// every layer: the KV rows land in the cache, the hidden rows are dropped.
+bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t p0) {
+    const vbs_cu_model_t &m = d->m;
+    cudaStream_t st = d->st;
+    const uint32_t dim = m.dim, nq = d->q_dim, nk = d->kv_dim, ffn = m.ffn, hd = m.head_dim;
+    const int layout = d->persist ? 2 : 1;   // the cache layout of the decoder's steps
+    DevState *dev = d->dev;
+    for (uint32_t b = 0; b < B; ++b)
+        if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), tok + b, 0, d->vocab_full,
+                                  d->pf_x + (size_t)b * dim, dim, dev->err, st, false),
+                     "prefill embed"))
+            return false;
+    for (uint32_t l = 0; l < m.n_layers; ++l) {
+        const Layer &y = d->L[l];
+        if (!cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.attn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm") ||
+            matvec_any(dev, y.tq, y.wq, d->pf_xn, d->pf_q, nq, dim, B, 0, st) ||
+            matvec_any(dev, y.tk, y.wk, d->pf_xn, d->pf_k, nk, dim, B, 0, st) ||
+            matvec_any(dev, y.tv, y.wv, d->pf_xn, d->pf_v, nk, dim, B, 0, st) ||
+            !cuda_ok(pf_rope_store_launch(d->pf_q, d->pf_k, d->pf_v, d->kc, d->vc, B, p0, l, d->max_ctx, m.n_heads,
+                                          m.n_kv_heads, hd, m.theta, layout, st),
+                     "prefill rope/kv store"))
+            return false;
+        // row b attends positions 0..p0+b: seq_len p0 + 1, one more per row
+        AttnParams ap = {};
+        ap.q = d->pf_q; ap.kc = d->kc; ap.vc = d->vc; ap.out = d->pf_att;
+        ap.seq_len = p0 + 1; ap.seq_step = 1;
+        ap.layer = l; ap.max_ctx = d->max_ctx;
+        ap.nqh = m.n_heads; ap.nkh = m.n_kv_heads; ap.hd = hd;
+        ap.scale = 1.0f / sqrtf((float)hd);
+        ap.batch = B; ap.kv_batch_stride = 0;
+        ap.head_major = 1; ap.swz = layout == 2 ? 1u : 0u;
+        ap.work = d->pf_attn_work;
+        ap.err = dev->err;
+        const uint32_t ns = std::min(d->pf_splits, attn_num_splits(p0 + B, m.n_kv_heads, B, dev->n_sm));
+        if (!cuda_ok(attn_launch(ap, ns, st, false), "prefill attention") ||
+            matvec_any(dev, y.to, y.wo, d->pf_att, d->pf_x, dim, nq, B, VBS_CU_MV_ACCUMULATE, st) ||
+            !cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.ffn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm") ||
+            matvec_any(dev, y.tgate, y.wgate, d->pf_xn, d->pf_g, ffn, dim, B, 0, st) ||
+            matvec_any(dev, y.tup, y.wup, d->pf_xn, d->pf_u, ffn, dim, B, 0, st) ||
+            !cuda_ok(silu_mul_launch(d->pf_g, d->pf_u, d->pf_h, B * ffn, st), "prefill silu") ||
+            matvec_any(dev, y.tdown, y.wdown, d->pf_h, d->pf_x, dim, ffn, B, VBS_CU_MV_ACCUMULATE, st))
+            return false;
+    }
+    return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -577,7 +649,8 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
     void *bufs[] = {d->x, d->x2, d->q, d->att, d->hid, d->logits, d->logits_full, d->partial, d->norm, d->k, d->v,
                     d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
                     d->tok_dev, d->attn_work, d->argmax_work, d->step_layers, d->step_acc, d->step_attn, d->step_packed,
-                    d->words_mem, d->words_comm};
+                    d->words_mem, d->words_comm, d->pf_x, d->pf_xn, d->pf_q, d->pf_k, d->pf_v, d->pf_att,
+                    d->pf_g, d->pf_u, d->pf_h, d->pf_attn_work};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->pinned) cudaFreeHost(d->pinned);
@@ -609,6 +682,27 @@ int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n
     if (!sync_and_check(d)) return -1;
     if (logits_out) memcpy(logits_out, d->logits_pinned, (size_t)d->vocab_full * 4);
     return 0;
+}
+
+int vbs_cu_decoder_prefill(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n) {
+    if (!d || (!tokens && n)) { latch_error("decoder_prefill: invalid arguments"); return -1; }
+    if (d->strict) { latch_error("decoder_prefill: strict mode feeds prompts token by token (vbs_cpu arithmetic)"); return -1; }
+    if (d->tp_world > 1) { latch_error("decoder_prefill: tensor parallelism feeds prompts token by token"); return -1; }
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != d->dev->ordinal) cudaSetDevice(d->dev->ordinal);
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] >= d->vocab_full) { latch_error("decoder_prefill: token %u >= vocab %u", tokens[i], d->vocab_full); return -1; }
+    if (d->host_pos + n > d->max_ctx) { latch_error("decoder_prefill: %zu tokens exceed the KV capacity", n); return -1; }
+    if (!n) return 0;
+    if (!prefill_buffers(d) || !put_tokens(d, tokens, n)) return -1;
+    for (size_t c0 = 0; c0 < n; c0 += PF_CHUNK)
+        if (!prefill_chunk(d, d->tok_dev + c0, (uint32_t)std::min<size_t>(PF_CHUNK, n - c0), (uint32_t)(d->host_pos + c0)))
+            return -1;
+    d->host_pos += n;
+    d->pinned[0] = (uint32_t)d->host_pos;   // the next step's position; its token comes with that step
+    if (!cuda_ok(cudaMemcpyAsync(d->ctrl, d->pinned, 4, cudaMemcpyHostToDevice, d->st), "prefill position")) return -1;
+    return sync_and_check(d) ? 0 : -1;
 }
 
 void vbs_cu_decoder_reset(vbs_cu_decoder_t *d) {

@@ -134,6 +134,13 @@ cudaError_t add_launch(const float *a, const float *b, float *out, uint32_t n, c
 cudaError_t cache_store_launch(const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t pos,
                                const uint32_t *ctrl, uint32_t layer, uint32_t max_ctx, uint32_t kv_dim,
                                uint32_t head_dim, bool head_major, cudaStream_t st);
+// prompt chunks (prefill.cu): `rows` rows at positions p0.., cache layout
+// 0 engine order, 1 head-major, 2 head-major swizzled (kv_index_swz)
+cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, uint32_t rows, uint32_t n, float eps,
+                                   cudaStream_t st);
+cudaError_t pf_rope_store_launch(float *q, const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t rows,
+                                 uint32_t p0, uint32_t layer, uint32_t max_ctx, uint32_t nqh, uint32_t nkh, uint32_t hd,
+                                 float theta, int layout, cudaStream_t st);
 
 // Split-KV GQA decode attention. seq_len from `seq_dev` (+1) when non-NULL,
 // else `seq_len`. `work` holds the split partials and merge counters:
@@ -151,6 +158,8 @@ struct AttnParams {
     uint32_t batch;
     uint64_t kv_batch_stride;   // elements between sequences' caches
     uint32_t head_major;        // cache layout (kv_index)
+    uint32_t swz;               // head-major rows with the step kernel's chunk swizzle (kv_index_swz); hd 64/128
+    uint32_t seq_step;          // sequence b attends seq_len + b * seq_step positions (causal prompt chunks)
     void *work;
     uint32_t *err;
 };

@@ -1,0 +1,98 @@
+// prefill.cu -- the per-chunk kernels of the batched prompt pass.
+//
+// The reference feeds a prompt one token at a time through forward_token
+// (src/main.c:901-904), so every prompt token streams all weights once.
+// The decoder's prefill instead takes the prompt in chunks of up to 8
+// tokens: the matrices run through the batched matvec (one weight pass per
+// chunk), attention is the split-KV kernel with a causal step per query,
+// and the two kernels here do the row-wise rest: RMSNorm of each chunk row
+// and RoPE plus the fp16 KV store at the rows' positions.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace vbs {
+
+// RMSNorm of `rows` rows of n floats, one CTA per row, with the arithmetic
+// of rmsnorm_kernel (src/vbs_host_math.h:28-36: sum of squares in double).
+__global__ void __launch_bounds__(256) pf_rmsnorm_rows_kernel(const float *__restrict__ in, const float *__restrict__ w,
+                                                              float *__restrict__ out, uint32_t n, float eps) {
+    __shared__ double part[8];
+    const float *x = in + (size_t)blockIdx.x * n;
+    float *y = out + (size_t)blockIdx.x * n;
+    double ss = 0.0;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += (double)x[i] * (double)x[i];
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int k = 0; k < 8; ++k) tot += part[k];
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tot / (double)n), eps)));
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
+}
+
+cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, uint32_t rows, uint32_t n, float eps,
+                                   cudaStream_t st) {
+    if (!rows || !n) return cudaSuccess;
+    note_launches(1);
+    pf_rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(in, w, out, n, eps);
+    return cudaGetLastError();
+}
+
+// Chunk row b sits at position p0 + b: RoPE on its query heads in place and
+// on its key heads (adjacent pairs, src/vbs_host_math.h:38-51, the rounding
+// of rope_kernel), then its key and value rows go into the cache as fp16
+// with the engine's rounding (src/vbs_host_math.h:150-159) in `layout`:
+// 0 engine order, 1 head-major, 2 head-major with the step kernel's chunk
+// swizzle. One CTA per row.
+__global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const float *k, const float *v, uint16_t *kc,
+                                                            uint16_t *vc, uint32_t p0, uint32_t layer, uint32_t max_ctx,
+                                                            uint32_t nqh, uint32_t nkh, uint32_t hd, float theta,
+                                                            int layout) {
+    const uint32_t b = blockIdx.x, pos = p0 + b, half = hd / 2, kv_dim = nkh * hd;
+    float *qb = q + (size_t)b * nqh * hd;
+    const float *kb = k + (size_t)b * kv_dim, *vb = v + (size_t)b * kv_dim;
+    auto rope = [&](float a, float c2, uint32_t i, float &o0, float &o1) {
+        const float ang = __fmul_rn((float)pos, powf(theta, __fdiv_rn(-(float)i, (float)hd)));
+        const float c = cosf(ang), s = sinf(ang);
+        o0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(c2, s));
+        o1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(c2, c));
+    };
+    for (uint32_t t = threadIdx.x; t < (nqh + nkh) * half; t += blockDim.x) {
+        const bool isq = t < nqh * half;
+        const uint32_t u = isq ? t : t - nqh * half, h = u / half, i = 2 * (u % half);
+        if (isq) {
+            float *p = qb + (size_t)h * hd + i;
+            float o0, o1;
+            rope(p[0], p[1], i, o0, o1);
+            p[0] = o0;
+            p[1] = o1;
+            continue;
+        }
+        if (pos >= max_ctx) continue;   // the host checks capacity; never write past the cache
+        const uint32_t local = h * hd + i;
+        float k0, k1;
+        rope(kb[local], kb[local + 1], i, k0, k1);
+        // dims i, i+1 (i even) are adjacent in every layout: same 16-byte chunk
+        const uint64_t at = layout == 2 ? kv_index_swz(layer, pos, local, max_ctx, nkh, hd)
+                                        : kv_index(layout == 1, layer, pos, local, max_ctx, kv_dim, hd);
+        kc[at] = f32_to_f16_kv(k0);
+        kc[at + 1] = f32_to_f16_kv(k1);
+        vc[at] = f32_to_f16_kv(vb[local]);
+        vc[at + 1] = f32_to_f16_kv(vb[local + 1]);
+    }
+}
+
+cudaError_t pf_rope_store_launch(float *q, const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t rows,
+                                 uint32_t p0, uint32_t layer, uint32_t max_ctx, uint32_t nqh, uint32_t nkh, uint32_t hd,
+                                 float theta, int layout, cudaStream_t st) {
+    if (!rows) return cudaSuccess;
+    if (!hd || hd % 2 || p0 + rows > max_ctx || layout < 0 || layout > 2 || (layout == 2 && hd != 64 && hd != 128))
+        return cudaErrorInvalidValue;
+    note_launches(1);
+    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, k, v, kc, vc, p0, layer, max_ctx, nqh, nkh, hd, theta, layout);
+    return cudaGetLastError();
+}
+
+}  // namespace vbs
