@@ -403,8 +403,23 @@ def main():
     dec = vbs.Decoder(model, max_ctx)
     kps = dec.kernels_per_step
     prompt = models.splitmix_ints(4096, args.ctx, shape.vocab)
+    # the context: one GPU takes the batched prefill (chunks of 8 tokens per
+    # pass over the weights), tensor parallelism one token per step like
+    # the engine; either way the timed steps below start at position ctx
+    prefill_mode = "token-by-token"
+    torch.cuda.synchronize()
     t0 = time.perf_counter()
-    dec.forward(prompt, logits=False)                 # prefill, one token per step like the engine
+    if world == 1:
+        try:
+            dec.prefill(prompt)
+            prefill_mode = "batched"
+        except vbs.VbsError as e:
+            print(f"batched prefill failed ({e}); feeding the prompt token by token", file=sys.stderr)
+            vbs.clear_error()
+            dec.reset()
+    if prefill_mode != "batched":
+        dec.forward(prompt, logits=False)
+    torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
 
     stream = torch.cuda.ExternalStream(dec.stream)
@@ -482,6 +497,15 @@ def main():
                 "peak_kind": peak_kind, "traffic": committed_traffic("step_kernel_decode_l8b_ctx4096.md"),
                 "algorithmic_bytes": int(step_bytes), "launch_us": round(ms_step * 1e3, 2),
                 "frac_of_8tbs": round(achieved / 8000.0, 4)}
+    elif kps == 1:
+        # tensor parallelism: each rank's step kernel streams its shard, 1/world
+        # of the weights and of the KV rows (norm weights aside)
+        achieved = step_bytes / world / (ms_step * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "step_kernel, tensor-parallel instance (per rank: its weight and KV shard)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes": int(step_bytes / world),
+                "launch_us": round(ms_step * 1e3, 2), "frac_of_8tbs": round(achieved / 8000.0, 4),
+                "per": "rank (the slowest rank's time)"}
     elif world == 1:
         x = torch.randn(shape.dim, device="cuda")
         h = torch.empty(shape.ffn, device="cuda")
@@ -510,7 +534,7 @@ def main():
                 "frac_of_8tbs": round(achieved / 8000.0, 4)}
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         v, kind, passes = cpu_decode_sample(1.0, threads)
         cpu = {"value": round(v, 4), "unit": "tokens/s", "cores": threads, "kind": kind,
@@ -528,7 +552,8 @@ def main():
                        "ctx": args.ctx, "batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
                        "tp_sum": dec.tp_mode if world > 1 else None,
                        "l2": "inputs larger than L2 (4.84 GB weights per step)",
-                       "kernels_per_step": kps, "prefill_s": round(prefill_s, 2)},
+                       "kernels_per_step": kps, "prefill_s": round(prefill_s, 2), "prefill": prefill_mode,
+                       "prefill_tok_s": round(args.ctx / prefill_s, 1)},
             "step_bandwidth": {"algorithmic_bytes": int(step_bytes),
                                "achieved_gbs": round(step_bytes * tok_s / 1e9, 1),
                                "frac_of_measured": round(step_bytes * tok_s / 1e9 / peak, 4),
