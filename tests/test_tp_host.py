@@ -1,4 +1,4 @@
-"""Host-side tensor-parallel logic on CPU with gloo, world_size 2: each rank
+"""Host-side tensor-parallel logic on CPU with gloo, world_size 2 and 4: each rank
 takes its Megatron shard (q/k/v/gate/up/output by rows, o/down by columns,
 shard_spec) of seeded tensors, computes its partial with the oracle, and the
 all-reduced / gathered result equals the unsharded computation."""
@@ -56,11 +56,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp_shards_match_full_gloo():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_shards_match_full_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -83,3 +84,15 @@ def test_shard_spec_covers_tensor():
                 assert all(s[1] % 256 == 0 for s in specs)
             else:
                 assert sum(s[0] for s in specs) == full_rows
+
+
+def test_output_rows_split_evenly_in_rank_order():
+    """The decoder gathers the logits in rank order and requires rank r to
+    own rows r * vocab .. (r + 1) * vocab - 1 with vocab = vocab_full / world:
+    the shards and the model description the package builds satisfy it."""
+    import vbs_b200 as vbs
+    shape = vbs.LlamaShape(32, 4096, 32, 8, 14336, 128256)
+    for world in (2, 4, 8):
+        specs = [vbs.shard_spec("output", shape, r, world) for r in range(world)]
+        assert all(s[0] == shape.vocab // world for s in specs)
+        assert [s[2] for s in specs] == [r * (shape.vocab // world) for r in range(world)]
