@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default=None,
-                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep"],
+                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep", "prefill"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
     ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
@@ -108,6 +108,39 @@ def profile_kernel(args):
                                       "gbs": round(alg / (med * 1e-6) / 1e9, 1),
                                       "frac_of_measured": round(alg / (med * 1e-6) / 1e9 / peak, 3)}), flush=True)
                 del ws
+        return
+    if args.profile == "prefill":
+        # the batched prompt pass: --ctx prompt tokens (chunks of 8 through
+        # the batched matvec) against the same prompt fed one token per step,
+        # both timed with CUDA events on the decoder's stream; --layers and
+        # --vocab cut the model for a small ncu case
+        import models
+        cfg = dict(models.L8B, n_layers=args.layers, vocab=args.vocab)
+        model = vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=2024)
+        prompt = models.splitmix_ints(4096, args.ctx, args.vocab)
+        res = {}
+        for mode in ("batched", "token-by-token"):
+            dec = vbs.Decoder(model, args.ctx + 8, vbs.DEC_NO_PERSIST if args.per_op else 0)
+            if mode == "batched":   # warm-up: buffers, workspaces, first launches
+                dec.prefill(prompt[:8])
+            else:
+                dec.forward(prompt[:8], logits=False)
+            dec.reset()
+            s = torch.cuda.ExternalStream(dec.stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(s)
+            if mode == "batched":
+                dec.prefill(prompt)
+            else:
+                dec.forward(prompt, logits=False)
+            e1.record(s)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            res[mode] = {"ms": round(ms, 2), "tok_s": round(args.ctx / (ms * 1e-3), 1)}
+            dec.close()
+        print(json.dumps({"profile": "prefill", "ctx": args.ctx, "layers": args.layers, "vocab": args.vocab,
+                          "per_op": bool(args.per_op), **res}))
         return
     if args.profile == "decode":
         # the full decode step at position --ctx (the cache rows before it
