@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default=None,
-                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep", "prefill"],
+                    choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep", "prefill",
+                             "upload"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
     ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
@@ -108,6 +109,34 @@ def profile_kernel(args):
                                       "gbs": round(alg / (med * 1e-6) / 1e9, 1),
                                       "frac_of_measured": round(alg / (med * 1e-6) / 1e9 / peak, 3)}), flush=True)
                 del ws
+        return
+    if args.profile == "upload":
+        # direct file -> device upload (vbs_cu_upload_file): a 2 GiB file of
+        # seeded bytes in 64 ranges, read once to warm the page cache, then
+        # timed (wall clock around the call; it returns after every copy)
+        import tempfile
+        import numpy as np
+        n, size = 64, 32 << 20
+        with tempfile.TemporaryDirectory() as td:
+            path = Path(td) / "blob.bin"
+            rng = np.random.default_rng(5)
+            with open(path, "wb") as f:
+                for _ in range(n):
+                    f.write(rng.integers(0, 256, size, dtype=np.uint8).tobytes())
+            bufs = [torch.empty(size, dtype=torch.uint8, device="cuda") for _ in range(n)]
+            torch.cuda.synchronize()
+            ranges = [(i * size, size, b.data_ptr()) for i, b in enumerate(bufs)]
+            res = {}
+            for threads in (1, 4, 8):
+                vbs.upload_file(path, ranges, threads)   # warm: page cache, pinned allocations
+                t0 = time.perf_counter()
+                vbs.upload_file(path, ranges, threads)
+                s = time.perf_counter() - t0
+                res[f"threads_{threads}"] = {"s": round(s, 4), "gb_s": round(n * size / s / 1e9, 2)}
+            ok = bool(np.array_equal(bufs[-1][:4096].cpu().numpy(),
+                                     np.fromfile(path, dtype=np.uint8, count=4096, offset=(n - 1) * size)))
+        print(json.dumps({"profile": "upload", "bytes": n * size, "ranges": n, "page_cache": "warm", "check": ok,
+                          **res}))
         return
     if args.profile == "prefill":
         # the batched prompt pass: --ctx prompt tokens (chunks of 8 through
