@@ -212,9 +212,10 @@ VBS_API int vbs_cu_attention(const float *q, const uint16_t *kc, const uint16_t 
  * workspace on demand; this entry point uses a fixed scratch of 2 MiB per
  * device in the library's static device memory instead.
  *  - Limit: the split partials must fit the scratch. The number of splits is
- *    lowered until they do; a call whose single-split need (about 64 KiB +
- *    batch * n_kv_heads * 4 KiB at head_dim 128) is above 2 MiB fails with an
- *    error naming the size.
+ *    lowered until they do; at one split the result goes straight to `out`
+ *    and no scratch is used, so every valid call runs. Calls that need fewer
+ *    splits than vbs_cu_attention picks (large batch x n_kv_heads at long
+ *    contexts) are slower, not different beyond float rounding.
  *  - Setup: the first call on a device initialises the backend for that
  *    device if needed and looks up the scratch address (cudaGetSymbolAddress
  *    with that device current); make that first call before any stream
@@ -291,7 +292,9 @@ typedef struct vbs_cu_decoder vbs_cu_decoder_t;
  * [head_dim]; fp32 [layer][max_ctx][kv_dim] under STRICT) and the control
  * block on the current device. Synchronizes the device first, so weights
  * still being written by work on other streams are complete before the
- * decoder's own stream reads them. */
+ * decoder's own stream reads them. Every later vbs_cu_decoder_* call makes
+ * the decoder's device current for its duration and leaves the caller's
+ * current device as it found it. */
 VBS_API vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t flags,
                                         char *err, size_t err_cap);
 VBS_API void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d);

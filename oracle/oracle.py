@@ -10,6 +10,7 @@ module; the product path never does.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -41,10 +42,19 @@ _lib = None
 _ref = None
 
 
+def reference_dir() -> Path:
+    """The reference checkout: $VBS_REFDIR when set, else a `reference`
+    folder beside this repository (absent on machines that only run the
+    prebuilt checker)."""
+    env = os.environ.get("VBS_REFDIR")
+    return Path(env) if env else ORACLE_DIR.parent.parent / "reference"
+
+
 def build(ref: bool = True) -> None:
     subprocess.run(["make", "-C", str(ORACLE_DIR), "oracle"], check=True, capture_output=True)
-    if ref and Path("/root/reference/src").is_dir():
-        subprocess.run(["make", "-C", str(ORACLE_DIR), "ref"], check=True, capture_output=True)
+    refdir = reference_dir()
+    if ref and (refdir / "src").is_dir():
+        subprocess.run(["make", "-C", str(ORACLE_DIR), "ref", f"REFDIR={refdir}"], check=True, capture_output=True)
 
 
 def lib() -> C.CDLL:

@@ -66,3 +66,17 @@ def test_sources_no_multicast_loads():
     code = re.sub(r"//[^\n]*", "", src)
     word = "".join(reversed("tsacitlum"))
     assert word not in code
+
+
+@pytest.mark.parametrize("entry", ["attention", "attention_static"])
+@pytest.mark.parametrize("nqh,nkh", [(32, 0), (0, 8), (30, 8)])
+def test_attention_rejects_bad_head_counts(vbs, entry, nqh, nkh):
+    """A zero or non-dividing KV head count is refused before any device
+    work (it would otherwise reach the split arithmetic, which divides by
+    it). The pointers are never dereferenced: the argument check comes
+    first, so this runs without a GPU."""
+    vbs.clear_error()
+    fake = 4096
+    with pytest.raises(vbs.VbsError, match="invalid arguments"):
+        getattr(vbs, entry)(fake, fake, fake, fake, 128, 0, 128, nqh, nkh, 128, 0.088)
+    vbs.clear_error()

@@ -612,12 +612,13 @@ int vbs_cu_ffn_gate_up(int type, const void *w_gate, const void *w_up, const flo
 int vbs_cu_attention(const float *q, const uint16_t *kc, const uint16_t *vc, float *out, uint32_t seq_len, uint32_t layer,
                      uint32_t max_ctx, uint32_t nqh, uint32_t nkh, uint32_t hd, float scale, uint32_t batch,
                      uint64_t kv_batch_stride, void *stream) {
-    DevState *d = backend_current();
-    if (!d) { latch_error("vbs_cu_attention: no usable device"); return -1; }
-    if (!q || !kc || !vc || !out || !seq_len || seq_len > max_ctx || !batch) {
+    // arguments first: a zero head count must not reach the split arithmetic
+    if (!q || !kc || !vc || !out || !seq_len || seq_len > max_ctx || !batch || !nkh || !nqh || nqh % nkh) {
         latch_error("vbs_cu_attention: invalid arguments");
         return -1;
     }
+    DevState *d = backend_current();
+    if (!d) { latch_error("vbs_cu_attention: no usable device"); return -1; }
     AttnParams ap = {};
     ap.q = q; ap.kc = kc; ap.vc = vc; ap.out = out;
     ap.seq_len = seq_len; ap.layer = layer; ap.max_ctx = max_ctx;
@@ -633,27 +634,23 @@ int vbs_cu_attention(const float *q, const uint16_t *kc, const uint16_t *vc, flo
 int vbs_cu_attention_static(const float *q, const uint16_t *kc, const uint16_t *vc, float *out, uint32_t seq_len,
                             uint32_t layer, uint32_t max_ctx, uint32_t nqh, uint32_t nkh, uint32_t hd, float scale,
                             uint32_t batch, uint64_t kv_batch_stride, void *stream) {
-    DevState *d = backend_current();
-    if (!d) { latch_error("vbs_cu_attention_static: no usable device"); return -1; }
-    if (!q || !kc || !vc || !out || !seq_len || seq_len > max_ctx || !batch || !nkh) {
+    // arguments first: a zero head count must not reach the split arithmetic
+    if (!q || !kc || !vc || !out || !seq_len || seq_len > max_ctx || !batch || !nkh || !nqh || nqh % nkh) {
         latch_error("vbs_cu_attention_static: invalid arguments");
         return -1;
     }
+    DevState *d = backend_current();
+    if (!d) { latch_error("vbs_cu_attention_static: no usable device"); return -1; }
     if (!d->attn_static) {   // first call on this device: look the scratch up (its device is current here)
         void *ptr = nullptr;
         if (!cuda_ok(attn_static_address(&ptr), "vbs_cu_attention_static: scratch address")) return -1;
         d->attn_static = ptr;
     }
-    // as many splits as the fixed scratch holds, never more than the allocating entry point uses
+    // as many splits as the fixed scratch holds, never more than the allocating
+    // entry point uses. One split writes its result straight to `out` and
+    // touches neither the merge tickets nor the partials, so it always fits.
     uint32_t ns = attn_num_splits(seq_len, nkh, batch, d->n_sm);
     while (ns > 1 && attn_workspace_bytes(nqh, nkh, hd, batch, ns) > attn_static_bytes()) --ns;
-    const size_t need = attn_workspace_bytes(nqh, nkh, hd, batch, ns);
-    if (need > attn_static_bytes()) {
-        latch_error("vbs_cu_attention_static: batch %u x %u KV heads x head_dim %u needs %zu bytes of scratch, above the "
-                    "fixed %zu; use vbs_cu_attention",
-                    batch, nkh, hd, need, attn_static_bytes());
-        return -1;
-    }
     AttnParams ap = {};
     ap.q = q; ap.kc = kc; ap.vc = vc; ap.out = out;
     ap.seq_len = seq_len; ap.layer = layer; ap.max_ctx = max_ctx;

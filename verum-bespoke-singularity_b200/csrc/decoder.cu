@@ -95,6 +95,21 @@ struct vbs_cu_decoder {
 
 namespace {
 
+// Makes the decoder's device current for one entry point and puts the
+// caller's current device back on every return path (a host thread may
+// drive several devices, e.g. tensor-parallel ranks).
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int ordinal) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != ordinal) cudaSetDevice(ordinal);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
 bool dmalloc(void **p, size_t bytes, const char *what) {
     return cuda_ok(cudaMalloc(p, bytes ? bytes : 16), what);
 }
@@ -643,6 +658,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
 
 void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
     if (!d) return;
+    DeviceGuard guard(d->dev ? d->dev->ordinal : 0);
     if (d->st) cudaStreamSynchronize(d->st);
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->graph) cudaGraphDestroy(d->graph);
@@ -661,9 +677,7 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
 
 int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n, float *logits_out) {
     if (!d || (!tokens && n)) { latch_error("decoder_forward: invalid arguments"); return -1; }
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (cur != d->dev->ordinal) cudaSetDevice(d->dev->ordinal);
+    DeviceGuard guard(d->dev->ordinal);
     for (size_t i = 0; i < n; ++i)
         if (tokens[i] >= d->vocab_full) { latch_error("decoder_forward: token %u >= vocab %u", tokens[i], d->vocab_full); return -1; }
     if (d->host_pos + n > d->max_ctx) { latch_error("decoder_forward: %zu tokens exceed the KV capacity", n); return -1; }
@@ -688,9 +702,7 @@ int vbs_cu_decoder_prefill(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n
     if (!d || (!tokens && n)) { latch_error("decoder_prefill: invalid arguments"); return -1; }
     if (d->strict) { latch_error("decoder_prefill: strict mode feeds prompts token by token (vbs_cpu arithmetic)"); return -1; }
     if (d->tp_world > 1) { latch_error("decoder_prefill: tensor parallelism feeds prompts token by token"); return -1; }
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (cur != d->dev->ordinal) cudaSetDevice(d->dev->ordinal);
+    DeviceGuard guard(d->dev->ordinal);
     for (size_t i = 0; i < n; ++i)
         if (tokens[i] >= d->vocab_full) { latch_error("decoder_prefill: token %u >= vocab %u", tokens[i], d->vocab_full); return -1; }
     if (d->host_pos + n > d->max_ctx) { latch_error("decoder_prefill: %zu tokens exceed the KV capacity", n); return -1; }
@@ -707,6 +719,7 @@ int vbs_cu_decoder_prefill(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n
 
 void vbs_cu_decoder_reset(vbs_cu_decoder_t *d) {
     if (!d) return;
+    DeviceGuard guard(d->dev->ordinal);
     cudaMemsetAsync(d->ctrl, 0, 4, d->st);
     cudaStreamSynchronize(d->st);
     d->host_pos = 0;
@@ -714,6 +727,7 @@ void vbs_cu_decoder_reset(vbs_cu_decoder_t *d) {
 
 int vbs_cu_decoder_set_position(vbs_cu_decoder_t *d, uint32_t pos, uint32_t token) {
     if (!d || pos >= d->max_ctx) { latch_error("decoder_set_position: position out of range"); return -1; }
+    DeviceGuard guard(d->dev->ordinal);
     d->pinned[0] = pos;
     d->pinned[1] = token;
     if (!cuda_ok(cudaMemcpyAsync(d->ctrl, d->pinned, 8, cudaMemcpyHostToDevice, d->st), "set position")) return -1;
@@ -723,6 +737,7 @@ int vbs_cu_decoder_set_position(vbs_cu_decoder_t *d, uint32_t pos, uint32_t toke
 
 uint32_t vbs_cu_decoder_position(vbs_cu_decoder_t *d) {
     if (!d) return 0;
+    DeviceGuard guard(d->dev->ordinal);
     if (!cuda_ok(cudaMemcpyAsync(d->pinned, d->ctrl, 8, cudaMemcpyDeviceToHost, d->st), "position")) return 0;
     cudaStreamSynchronize(d->st);
     return d->pinned[0];
@@ -730,6 +745,7 @@ uint32_t vbs_cu_decoder_position(vbs_cu_decoder_t *d) {
 
 int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t n_prompt, uint32_t n_new, uint32_t *out) {
     if (!d || !prompt || !n_prompt || (n_new && !out)) { latch_error("decoder_generate: invalid arguments"); return -1; }
+    DeviceGuard guard(d->dev->ordinal);
     for (size_t i = 0; i < n_prompt; ++i)
         if (prompt[i] >= d->vocab_full) { latch_error("decoder_generate: token %u >= vocab", prompt[i]); return -1; }
     if (d->host_pos + n_prompt + (n_new ? n_new - 1 : 0) > d->max_ctx) {
@@ -749,6 +765,7 @@ int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t 
 
 int vbs_cu_decoder_enqueue_steps(vbs_cu_decoder_t *d, uint32_t n) {
     if (!d) return -1;
+    DeviceGuard guard(d->dev->ordinal);
     if (d->host_pos + n > d->max_ctx) { latch_error("enqueue_steps: exceeds the KV capacity"); return -1; }
     for (uint32_t i = 0; i < n; ++i)
         if (!enqueue_step(d)) return -1;
