@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-layers", type=int, default=32,
+                    help="--impl reference: layers of the 8B shape (fewer only to check the JSON contract quickly)")
     ap.add_argument("--profile", default=None,
                     choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep", "prefill",
                              "upload"],
@@ -398,23 +400,130 @@ def cpu_decode_sample(n_tokens: float, threads: int):
     return tokens / dt, kind, passes
 
 
+def write_l8b_gguf(path, model=None, n_layers: int = 32) -> None:
+    """The bench's 8B-shaped model (seed 2024) as a GGUF file for the
+    reference CPU path. From the device model's bytes when one is given
+    (the synthesizers are bit-identical), else synthesized on the host
+    cores."""
+    import models
+    cfg = dict(models.L8B, n_layers=n_layers)
+    if model is not None:
+        host = models.host_model_from_device(cfg, model).t
+    else:
+        host = models.host_tensors_parallel(cfg, models.L8B_TYPES, 2024)
+    models.write_model_gguf(path, cfg, host, context_length=8192)
+
+
+def ref_cpu_decode(gguf, n_prompt: int, n_warm: int, n_steps: int) -> dict:
+    """Greedy decode through the reference's own CPU inference path,
+    vbs_cpu_step_ex (src/vbs_cpu.c:572-639), as its vbs-cpu CLI runs it
+    (src/vbs_cpu_main.c:70-86): load (K-quants requantized to Q8_0,
+    src/vbs_cpu.c:312-346), an n_prompt-token prompt, n_warm untimed decode
+    tokens, then n_steps timed decode tokens, each a full step with its
+    logits and the first-maximum argmax. One host thread, as the reference
+    runs (src/vbs_hotpath.c:3-5)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import models
+    import oracle as orc
+    t0 = time.perf_counter()
+    cpu = orc.RefCpu(gguf, n_prompt + n_warm + n_steps + 1)
+    t1 = time.perf_counter()
+    prompt = models.splitmix_ints(4096, n_prompt, models.L8B["vocab"])
+    for i, t in enumerate(prompt):
+        cpu.step(t, i + 1 == len(prompt))
+    t2 = time.perf_counter()
+    tok = cpu.argmax()
+    for _ in range(n_warm):
+        cpu.step(tok)
+        tok = cpu.argmax()
+    t3 = time.perf_counter()
+    for _ in range(n_steps):
+        cpu.step(tok)
+        tok = cpu.argmax()
+    t4 = time.perf_counter()
+    cpu.close()
+    return {"tok_s": n_steps / (t4 - t3), "load_s": t1 - t0, "prompt_s": t2 - t1, "timed_s": t4 - t3,
+            "position": n_prompt + n_warm}
+
+
+def ref_cpu_tiny() -> dict:
+    """BASELINE config 0 end to end through the reference CPU path: the tiny
+    GGUF, its 16 seeded prompt tokens, 64 greedy tokens (the golden run)."""
+    import tempfile
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import models
+    import oracle as orc
+    with tempfile.TemporaryDirectory() as td:
+        path = Path(td) / "tiny.gguf"
+        models.make_tiny_gguf(path)
+        t0 = time.perf_counter()
+        cpu = orc.RefCpu(path, 128)
+        prompt = models.tiny_prompt()
+        for i, t in enumerate(prompt):
+            cpu.step(t, i + 1 == len(prompt))
+        out = []
+        for i in range(models.N_NEW):
+            out.append(cpu.argmax())
+            if i + 1 < models.N_NEW:
+                cpu.step(out[-1])
+        s = time.perf_counter() - t0
+        cpu.close()
+    golden = json.loads((ROOT / "tests" / "golden" / "tiny_greedy.json").read_text())
+    return {"tok_s": (models.N_PROMPT + models.N_NEW - 1) / s, "s": round(s, 4),
+            "tokens_match_golden": out == golden["generated"]}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+REF_PROMPT = 16   # prompt tokens before the reference path's timed decode steps
+
+
 def reference_arm(args, rank):
+    """--impl reference: the reference's own CPU decode path (vbs_cpu, from
+    oracle/_ref, compiled from the reference's sources) on the 8B-shaped
+    model, one decode token per step."""
     if rank != 0:
         return
+    import tempfile
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
     threads = os.cpu_count() or 1
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_decode_sample(0.05, threads)
-    tok_s, kind, passes = cpu_decode_sample(max(1, args.steps) * 0.25, threads)
+    if orc.ref() is None:
+        # the reference was not compiled here: its hot kernel's port over
+        # one token's matvec work per step (the oracle's restatement)
+        tok_s, kind, passes = cpu_decode_sample(max(1, args.steps) * 0.25, threads)
+        sample = f"{passes} passes of the ported matvec_q8_0 over a 14336x4096 Q8_0 matrix, row-sharded"
+        workload, cores, extra = "llama3-8b-shape decode matvec work, ported reference kernel", threads, {}
+    else:
+        with tempfile.TemporaryDirectory() as td:
+            path = Path(td) / "l8b.gguf"
+            write_l8b_gguf(path, n_layers=args.ref_layers)
+            r = ref_cpu_decode(path, REF_PROMPT, min(args.warmup, 2), args.steps)
+        tok_s, kind, cores = r["tok_s"], "reference", 1
+        sample = (f"{args.steps} greedy decode steps of vbs_cpu_step_ex (the reference's CPU path) on the 8B-shaped "
+                  f"GGUF at positions {r['position']}..{r['position'] + args.steps - 1}, after a {REF_PROMPT}-token "
+                  f"prompt and {min(args.warmup, 2)} untimed steps (a 4096-token CPU prefill would take hours); "
+                  f"load {r['load_s']:.0f} s")
+        workload = (f"llama3-8b-shape decode ({args.ref_layers}L, dim 4096, 32/8 heads, ffn 14336, vocab 128256; "
+                    "Q4_K attn+gate/up, Q6_K down/output/embd), reference vbs-cpu path (vbs_cpu_step_ex)")
+        extra = {"tiny_e2e": ref_cpu_tiny()}
     line = {
         "impl": "reference", "metric": "decode tokens/s, Llama-3-8B Q4_K shape", "value": round(tok_s, 4),
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000.0 / tok_s, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
-        "config": {"workload": "llama3-8b-shape decode, reference CPU path (vbs_cpu hot kernel, Q8_0 requant)",
-                   "ctx": args.ctx, "parallelism": f"{threads} host threads"},
-        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tokens/s", "cores": threads, "kind": kind,
-                         "sample": f"{passes} passes of matvec_q8_0 over a 14336x4096 Q8_0 matrix "
-                                   f"(= {args.steps * 0.25:g} tokens of 8B decode matvec work), row-sharded"},
+        "vs_baseline": None, "dtype": "int8-dot/f32 (Q8_0 requant)", "data": "synthetic",
+        "config": {"workload": workload, "ctx": REF_PROMPT if kind == "reference" else args.ctx, "batch": 1,
+                   "parallelism": f"{cores} host thread(s) of {threads}", "cpu_model": cpu_model(), **extra},
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
+                         "sample": sample},
         "e2e": {"value": round(tok_s, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -597,12 +706,26 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        v, kind, passes = cpu_decode_sample(1.0, threads)
-        cpu = {"value": round(v, 4), "unit": "tokens/s", "cores": threads, "kind": kind,
-               "sample": f"{passes} passes of the vbs_cpu hot kernel matvec_q8_0 over a 14336x4096 Q8_0 matrix = "
-                         f"1 token of 8B decode matvec work (K-quants are requantized to Q8_0 by the reference CPU "
-                         f"path), row-sharded over {threads} threads"}
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as orc
+        if orc.ref() is not None:
+            import tempfile
+            with tempfile.TemporaryDirectory() as td:
+                path = Path(td) / "l8b.gguf"
+                write_l8b_gguf(path, model)
+                r = ref_cpu_decode(path, REF_PROMPT, 1, 8)
+            cpu = {"value": round(r["tok_s"], 4), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                   "sample": f"8 greedy decode steps of the reference's vbs_cpu_step_ex on the same 8B-shaped model "
+                             f"(GGUF of these weights; K-quants requantized to Q8_0 by the reference at load) at "
+                             f"positions {r['position']}..{r['position'] + 7}, after a {REF_PROMPT}-token prompt; one "
+                             f"host thread, as the reference runs; {cpu_model()}, {os.cpu_count()} host threads",
+                   "timed_s": round(r["timed_s"], 2)}
+        else:
+            threads = os.cpu_count() or 1
+            v, kind, passes = cpu_decode_sample(1.0, threads)
+            cpu = {"value": round(v, 4), "unit": "tokens/s", "cores": threads, "kind": kind,
+                   "sample": f"{passes} passes of the ported vbs_cpu hot kernel matvec_q8_0 over a 14336x4096 Q8_0 "
+                             f"matrix = 1 token of 8B decode matvec work, row-sharded over {threads} threads"}
     if rank == 0:
         line = {
             "metric": "decode tokens/s, Llama-3-8B Q4_K shape", "value": round(tok_s, 2), "unit": "tokens/s",

@@ -118,6 +118,13 @@ def ref() -> C.CDLL | None:
             "ref_linear_tile": (i32, [_P, i32, _P, _P, u32, u32, u32, u32, i32]),
             "ref_hot_matvec_q8_0": (None, [_P, sz, sz, _P, _P, _P]),
             "ref_hot_matvec_f32": (None, [_P, sz, sz, _P, _P]),
+            # the reference CPU inference path itself (include/vbs_cpu.h:13-24)
+            "vbs_cpu_open": (_P, [C.c_char_p, sz, C.c_char_p, sz]),
+            "vbs_cpu_close": (None, [_P]),
+            "vbs_cpu_reset": (None, [_P]),
+            "vbs_cpu_step_ex": (C.c_bool, [_P, u32, C.c_bool, C.c_char_p, sz]),
+            "vbs_cpu_logits": (_P, [_P]),
+            "vbs_cpu_vocab_size": (sz, [_P]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(L, n)
@@ -169,6 +176,49 @@ def synth_f32(seed: int, rows: int, cols: int, scale: float, row0=0, col0=0, ful
     out = np.empty(rows * cols, dtype=np.float32)
     lib().orc_synth_f32(seed, rows, cols, row0, col0, full_cols or cols, scale, ptr(out))
     return out
+
+
+class RefCpu:
+    """The reference's own CPU inference (vbs_cpu_open / vbs_cpu_step_ex,
+    src/vbs_cpu.c:572-639), loaded from a GGUF file: K-quant weights are
+    requantized to Q8_0 at load (src/vbs_cpu.c:312-346), one host thread.
+    Needs oracle/_ref/libvbsref.so (the reference compiled from its
+    sources)."""
+
+    def __init__(self, path, context: int):
+        R = ref()
+        if R is None:
+            raise FileNotFoundError(f"{REF_LIB} is not built")
+        self.R = R
+        err = C.create_string_buffer(512)
+        self.h = R.vbs_cpu_open(str(path).encode(), context, err, 512)
+        if not self.h:
+            raise RuntimeError(f"vbs_cpu_open: {err.value.decode()}")
+        self.vocab = int(R.vbs_cpu_vocab_size(self.h))
+        self._err = err
+
+    def step(self, token: int, logits: bool = True) -> None:
+        if not self.R.vbs_cpu_step_ex(self.h, token, logits, self._err, 512):
+            raise RuntimeError(f"vbs_cpu_step_ex: {self._err.value.decode()}")
+
+    def logits(self) -> np.ndarray:
+        p = self.R.vbs_cpu_logits(self.h)
+        return np.ctypeslib.as_array(C.cast(p, _f32p), shape=(self.vocab,)).copy()
+
+    def argmax(self) -> int:
+        """First maximum, as src/vbs_cpu_main.c:78-80."""
+        return int(np.argmax(self.logits()))
+
+    def close(self) -> None:
+        if self.h:
+            self.R.vbs_cpu_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ---------------------------------------------------------------------------

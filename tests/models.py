@@ -84,9 +84,36 @@ def host_tensors(cfg: dict, types: dict, seed: int, std: float = 0.02) -> dict:
     return t
 
 
-def write_model_gguf(path, cfg: dict, tensors: dict) -> None:
+def host_tensors_parallel(cfg: dict, types: dict, seed: int, std: float = 0.02, threads: int = 0) -> dict:
+    """host_tensors() with the tensors synthesized on a thread pool (the C
+    synthesizer releases the GIL), for full-size models."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    shape = shape_of(cfg)
+    scale = orc.synth_scale(std)
+    jobs = [("token_embd", "token_embd"), ("output", "output")]
+    for l in range(cfg["n_layers"]):
+        jobs += [(f"blk.{l}.{b}", b) for b in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up",
+                                               "ffn_down")]
+
+    def one(job):
+        name, base = job
+        rows, cols, _, _, _ = vbs.shard_spec(name, shape, 0, 1)
+        ty = types[base]
+        return name, (ty, rows, cols, orc.synth_tensor(ty, vbs.tensor_seed(seed, name), rows, cols, scale))
+
+    with ThreadPoolExecutor(threads or os.cpu_count() or 1) as ex:
+        t = dict(ex.map(one, jobs))
+    t["output_norm"] = (orc.F32, 1, cfg["dim"], np.ones(cfg["dim"], dtype=np.float32))
+    for l in range(cfg["n_layers"]):
+        t[f"blk.{l}.attn_norm"] = (orc.F32, 1, cfg["dim"], np.ones(cfg["dim"], dtype=np.float32))
+        t[f"blk.{l}.ffn_norm"] = (orc.F32, 1, cfg["dim"], np.ones(cfg["dim"], dtype=np.float32))
+    return t
+
+
+def write_model_gguf(path, cfg: dict, tensors: dict, context_length: int = 2048) -> None:
     meta = {"general.architecture": "llama", "general.alignment": 32, "llama.block_count": cfg["n_layers"],
-            "llama.context_length": 2048, "llama.embedding_length": cfg["dim"],
+            "llama.context_length": context_length, "llama.embedding_length": cfg["dim"],
             "llama.feed_forward_length": cfg["ffn"], "llama.attention.head_count": cfg["n_heads"],
             "llama.attention.head_count_kv": cfg["n_kv_heads"], "llama.rope.freq_base": float(cfg["theta"]),
             "llama.attention.layer_norm_rms_epsilon": float(cfg["eps"]), "llama.vocab_size": cfg["vocab"]}
@@ -98,9 +125,25 @@ def write_model_gguf(path, cfg: dict, tensors: dict) -> None:
     for name in order:
         ty, rows, cols, arr = tensors[name]
         dims = [cols] if name.endswith("norm") else [cols, rows]
-        tl.append((name + ".weight", ty, dims, np.ascontiguousarray(arr).view(np.uint8).tobytes()))
+        tl.append((name + ".weight", ty, dims, np.ascontiguousarray(arr).view(np.uint8)))
     vbs.write_gguf(path, meta, tl)
 
 
 def make_tiny_gguf(path) -> None:
     write_model_gguf(path, TINY, host_tensors(TINY, TINY_TYPES, TINY_SEED))
+
+
+def host_model_from_device(cfg: dict, dm) -> "orc.HostModel":
+    """The oracle's host copy of a device model (vbs.DeviceModel): every
+    tensor copied back, matrices cut to their packed size."""
+    host = {}
+    for name, t in dm.tensors.items():
+        arr = t.cpu().numpy()
+        if name.endswith("norm"):
+            host[name] = (orc.F32, 1, cfg["dim"], arr)
+        else:
+            base = name.split(".")[-1]
+            rows, cols, *_ = vbs.shard_spec(name, dm.shape, 0, 1)
+            host[name] = (dm.types[base], rows, cols, arr[:rows * orc.row_bytes(dm.types[base], cols)])
+    return orc.HostModel(cfg, host)
+

@@ -11,7 +11,9 @@ from conftest import ROOT
 
 
 def test_reference_arm_json_line():
-    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1"],
+    # one layer of the 8B shape keeps the GGUF small; the line is the same
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1",
+                          "--ref-layers", "1"],
                          capture_output=True, text=True, timeout=300, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
@@ -25,4 +27,8 @@ def test_reference_arm_json_line():
     assert cb["value"] == d["value"] and cb["unit"] == d["unit"] and cb["cores"] >= 1
     assert cb["kind"] in ("reference", "port") and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert d["config"]["ctx"] == 4096
+    if cb["kind"] == "reference":   # the reference's vbs_cpu path after a short prompt, one thread
+        assert cb["cores"] == 1 and d["config"]["ctx"] > 0 and "vbs_cpu_step_ex" in d["config"]["workload"]
+        assert d["config"]["tiny_e2e"]["tokens_match_golden"] is True
+    else:
+        assert d["config"]["ctx"] == 4096

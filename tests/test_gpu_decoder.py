@@ -67,16 +67,7 @@ def l8b_2layer(gpu, vbs):
 
 
 def _host_model(orc, cfg, dm):
-    host = {}
-    for name, t in dm.tensors.items():
-        arr = t.cpu().numpy()
-        if name.endswith("norm"):
-            host[name] = (orc.F32, 1, cfg["dim"], arr)
-        else:
-            base = name.split(".")[-1]
-            rows, cols, *_ = models.vbs.shard_spec(name, dm.shape, 0, 1)
-            host[name] = (dm.types[base], rows, cols, arr[:rows * orc.row_bytes(dm.types[base], cols)])
-    return orc.HostModel(cfg, host)
+    return models.host_model_from_device(cfg, dm)
 
 
 @pytest.mark.parametrize("path", ["persistent", "per_op"])

@@ -445,9 +445,10 @@ _GG_U32, _GG_F32, _GG_STR, _GG_ARR = 4, 6, 8, 9
 
 
 def write_gguf(path, metadata: dict, tensors: list, alignment: int = 32) -> None:
-    """tensors: [(name, type_id, dims (ne0 = columns first), bytes)].
-    metadata values: int -> u32, float -> f32, str -> string, and a list of
-    one of those -> array (the tokenizer tables of real model files)."""
+    """tensors: [(name, type_id, dims (ne0 = columns first), data)], data
+    any bytes-like buffer (written as is, not copied). metadata values: int
+    -> u32, float -> f32, str -> string, and a list of one of those -> array
+    (the tokenizer tables of real model files)."""
     def s(x: str) -> bytes:
         b = x.encode()
         return struct.pack("<Q", len(b)) + b
@@ -475,8 +476,9 @@ def write_gguf(path, metadata: dict, tensors: list, alignment: int = 32) -> None
             off += pad
         info += s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
         info += struct.pack("<IQ", typ, off)
-        blobs.append(bytes(data))
-        off += len(data)
+        mv = memoryview(data).cast("B")
+        blobs.append(mv)
+        off += mv.nbytes
     head = struct.pack("<4sIQQ", b"GGUF", 3, len(tensors), len(metadata)) + kv + info
     start = (len(head) + alignment - 1) // alignment * alignment
     with open(path, "wb") as f:
