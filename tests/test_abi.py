@@ -80,3 +80,17 @@ def test_attention_rejects_bad_head_counts(vbs, entry, nqh, nkh):
     with pytest.raises(vbs.VbsError, match="invalid arguments"):
         getattr(vbs, entry)(fake, fake, fake, fake, 128, 0, 128, nqh, nkh, 128, 0.088)
     vbs.clear_error()
+
+
+def test_layout_matches_reference_headers():
+    """Every offset and size of the ops-table types in include/vbs_b200.h
+    equals the reference's include/vbs_backend.h (the same printer compiled
+    against each header; oracle/abi_layout.c)."""
+    ours, ref = ROOT / "oracle" / "abi-layout", ROOT / "oracle" / "_ref" / "abi-layout-ref"
+    if not ours.exists():
+        subprocess.run(["make", "-C", str(ROOT / "oracle"), "abi-layout"], check=True, capture_output=True)
+    if not ref.exists():
+        pytest.skip("the reference was not compiled here (oracle/_ref)")
+    a = subprocess.run([str(ours)], capture_output=True, text=True, check=True).stdout
+    b = subprocess.run([str(ref)], capture_output=True, text=True, check=True).stdout
+    assert a.count("\n") >= 30 and a == b
