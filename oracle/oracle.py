@@ -21,8 +21,9 @@ LIB = ORACLE_DIR / "liboracle.so"
 REF_LIB = ORACLE_DIR / "_ref" / "libvbsref.so"
 REF_CPU = ORACLE_DIR / "_ref" / "vbs-cpu"
 
-F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K = 0, 1, 2, 3, 8, 12, 14
-BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K, LNS8 = 0, 1, 2, 3, 8, 12, 14, 40
+BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210),
+         LNS8: (32, 36)}
 
 _P = C.c_void_p
 _u8p = C.POINTER(C.c_uint8)

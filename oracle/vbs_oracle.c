@@ -17,7 +17,7 @@
 int orc_block_elems(int type) {
     switch (type) {
         case ORC_F32: case ORC_F16: return 1;
-        case ORC_Q4_0: case ORC_Q4_1: case ORC_Q8_0: return 32;
+        case ORC_Q4_0: case ORC_Q4_1: case ORC_Q8_0: case ORC_LNS8: return 32;
         case ORC_Q4_K: case ORC_Q6_K: return 256;
         default: return 0;
     }
@@ -32,6 +32,7 @@ int orc_block_bytes(int type) {
         case ORC_Q8_0: return 34;
         case ORC_Q4_K: return 144;
         case ORC_Q6_K: return 210;
+        case ORC_LNS8: return 36;
         default: return 0;
     }
 }
@@ -172,6 +173,15 @@ static void dq_q6_k(const uint8_t *b, float *y) {             /* :316-333 */
     }
 }
 
+/* LNS8 (36 B: 32 u8 log2 values, f32 scale at byte 32): value = 2^q *
+ * scale, src/vbs_host_math.h:111-121 (exp2f of an integer 0..255 is the
+ * exact power of two, +inf from 128 on). */
+static void dq_lns8(const uint8_t *b, float *y) {
+    float s;
+    memcpy(&s, b + 32, 4);
+    for (int i = 0; i < 32; i++) y[i] = ldexpf(1.0f, b[i]) * s;
+}
+
 size_t orc_dequant(int type, const void *src, size_t n_blocks, float *out) {
     const uint8_t *p = (const uint8_t *)src;
     int be = orc_block_elems(type), bb = orc_block_bytes(type);
@@ -187,6 +197,7 @@ size_t orc_dequant(int type, const void *src, size_t n_blocks, float *out) {
             case ORC_Q8_0: dq_q8_0(b, y); break;
             case ORC_Q4_K: dq_q4_k(b, y); break;
             case ORC_Q6_K: dq_q6_k(b, y); break;
+            case ORC_LNS8: dq_lns8(b, y); break;
             default: return 0;
         }
     }

@@ -36,7 +36,7 @@ extern "C" {
 /* GGML type ids used here (include/vbs_gguf.h:13-48 of the reference). */
 enum {
     ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q4_1 = 3, ORC_Q8_0 = 8,
-    ORC_Q4_K = 12, ORC_Q6_K = 14
+    ORC_Q4_K = 12, ORC_Q6_K = 14, ORC_LNS8 = 40
 };
 
 /* Block geometry: elements and bytes per block; 0 for unknown types. */

@@ -264,3 +264,25 @@ def test_kernel_launch_counter_moves(vbs, torch, clean_errors):
     vbs.matvec(12, w.data_ptr(), x.data_ptr(), y.data_ptr(), 1, 256)
     torch.cuda.synchronize()
     assert vbs.kernel_launches() == before + 1
+
+
+def test_lns8_matvec_and_dequant(vbs, orc, torch, clean_errors):
+    """The reference's LNS8 type (value = 2^q * scale; linear tiles only,
+    src/vbs_host_math.h:111-121, :250-255): bit-exact dequant and the
+    portable matvec against the oracle's host math."""
+    rng = np.random.default_rng(40)
+    rows, cols = 37, 512
+    q = rng.integers(0, 128, (rows * cols // 32, 32), dtype=np.uint8)
+    s = (rng.random(rows * cols // 32, dtype=np.float32) * np.float32(2.0 ** -122)).astype(np.float32)
+    w = np.ascontiguousarray(np.concatenate([q, s.view(np.uint8).reshape(-1, 4)], axis=1).reshape(-1))
+    x = rng.standard_normal(cols).astype(np.float32)
+    wd = torch.from_numpy(w).cuda()
+    out = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    vbs.dequant(vbs.LNS8, wd.data_ptr(), out.data_ptr(), rows * cols)
+    y = torch.empty(rows, dtype=torch.float32, device="cuda")
+    vbs.matvec(vbs.LNS8, wd.data_ptr(), torch.from_numpy(x).cuda().data_ptr(), y.data_ptr(), rows, cols)
+    torch.cuda.synchronize()
+    assert (out.cpu().numpy().view(np.uint32) == orc.dequant(orc.LNS8, w).view(np.uint32)).all()
+    want = orc.linear_tile(w, orc.LNS8, x, rows, cols)
+    assert np.abs(y.cpu().numpy() - want).max() <= 1e-3 * np.abs(want).max()
+

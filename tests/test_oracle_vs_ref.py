@@ -46,3 +46,35 @@ def test_linear_tile_offsets_accumulate(orc, t):
         assert R.ref_linear_tile(orc.ptr(w), t, orc.ptr(x), orc.ptr(y1), cols, rows, 64, 5, acc) == 0
         assert orc.lib().orc_linear_tile(orc.ptr(w), t, orc.ptr(x), orc.ptr(y2), cols, rows, 64, 5, acc) == 0
         assert (y1 == y2).all()
+
+
+def _lns8_blocks(rng, nblocks, qmax=128):
+    """LNS8 blocks: 32 log2 values in [0, qmax), then an f32 scale."""
+    q = rng.integers(0, qmax, (nblocks, 32), dtype=np.uint8)
+    s = (rng.random(nblocks, dtype=np.float32) * np.float32(2.0 ** -120)).astype(np.float32)
+    return np.ascontiguousarray(np.concatenate([q, s.view(np.uint8).reshape(nblocks, 4)], axis=1).reshape(-1))
+
+
+def test_lns8_dequant_formula(orc):
+    """value = 2^q * scale (src/vbs_host_math.h:111-121), q >= 128 -> inf."""
+    rng = np.random.default_rng(40)
+    blk = _lns8_blocks(rng, 64, qmax=256)
+    got = orc.dequant(orc.LNS8, blk)
+    q = blk.reshape(64, 36)[:, :32].astype(np.int32)
+    s = blk.reshape(64, 36)[:, 32:].copy().view(np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        # float32 throughout: the exact power 2^q (inf from 128 on, as exp2f), times the scale
+        want = (np.ldexp(np.ones(q.shape, np.float32), q) * s).astype(np.float32).reshape(-1)
+    assert (got.view(np.uint32) == want.view(np.uint32)).all()
+
+
+def test_lns8_linear_tile_matches_reference(orc):
+    R = orc.ref()
+    rng = np.random.default_rng(41)
+    rows, cols = 7, 256
+    w = _lns8_blocks(rng, rows * cols // 32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y1, y2 = np.zeros(rows, np.float32), np.zeros(rows, np.float32)
+    assert R.ref_linear_tile(orc.ptr(w), orc.LNS8, orc.ptr(x), orc.ptr(y1), cols, rows, 0, 0, 0) == 0
+    assert orc.lib().orc_linear_tile(orc.ptr(w), orc.LNS8, orc.ptr(x), orc.ptr(y2), cols, rows, 0, 0, 0) == 0
+    assert (y1 == y2).all()

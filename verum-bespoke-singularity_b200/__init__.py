@@ -24,9 +24,12 @@ PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libvbs_b200.so"
 
 # GGML type ids (include/vbs_gguf.h:13-48 of the reference)
-F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K, Q8_K = 0, 1, 2, 3, 8, 12, 14, 15
-TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q4_1: "Q4_1", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
-BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K, Q8_K, LNS8 = 0, 1, 2, 3, 8, 12, 14, 15, 40
+TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q4_1: "Q4_1", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K",
+              LNS8: "LNS8"}
+# LNS8: the reference's log-scaled type, 32 x u8 log2 values + an f32 scale (value = 2^q * scale)
+BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210),
+         LNS8: (32, 36)}
 
 # op kinds (include/vbs_graph.h:12-24 of the reference)
 (OP_EMBEDDING, OP_LINEAR, OP_NORMALIZE, OP_ATTENTION, OP_ROTARY, OP_ACTIVATION, OP_ELEMENTWISE,

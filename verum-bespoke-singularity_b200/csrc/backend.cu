@@ -186,10 +186,15 @@ constexpr uint32_t kPipeMagic = 0x56425342u;   // "VBSB"
 static bool type_supported(int t) {
     return t == T_F32 || t == T_F16 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K;
 }
+// Weight types of linear tiles: the above plus LNS8, which the reference's
+// bridge dispatches as a linear type (src/vbs_specializer_bridge.c:116-118)
+// but has no embedding for (its self-test expects that refusal,
+// src/vbs_backend_test.c:959-960).
+static bool linear_type_supported(int t) { return type_supported(t) || t == T_LNS8; }
 
 int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
                uint32_t batch, uint32_t flags, cudaStream_t st) {
-    if (!type_supported(type) || !w || !x || !y || !rows || !cols || !batch || cols % (uint32_t)block_elems(type)) {
+    if (!linear_type_supported(type) || !w || !x || !y || !rows || !cols || !batch || cols % (uint32_t)block_elems(type)) {
         latch_error("matvec: invalid arguments (type %d, %ux%u, batch %u)", type, rows, cols, batch);
         return -1;
     }
@@ -314,7 +319,7 @@ static bool ops_copy_to_host(void *dst, const vbs_buffer_t *src, size_t bytes) {
 
 static void *ops_compile_linear_pipeline(vbs_device_t *dev, vbs_ggml_type_t type, char *err, size_t cap) {
     (void)dev;
-    if (!type_supported((int)type)) {
+    if (!linear_type_supported((int)type)) {
         if (err && cap) snprintf(err, cap, "CUDA linear pipeline refusal: no sm_100a kernel for weight type %d", (int)type);
         return nullptr;
     }
@@ -556,7 +561,7 @@ uint64_t vbs_cu_kernel_launches(void) { return g_launches.load(); }
 int vbs_cu_dequant(int type, const void *w, float *out, uint64_t n, void *stream) {
     DevState *d = backend_current();
     if (!d) { latch_error("vbs_cu_dequant: no usable device"); return -1; }
-    if (!type_supported(type) || !w || !out || n % (uint64_t)block_elems(type)) {
+    if (!linear_type_supported(type) || !w || !out || n % (uint64_t)block_elems(type)) {
         latch_error("vbs_cu_dequant: invalid arguments");
         return -1;
     }

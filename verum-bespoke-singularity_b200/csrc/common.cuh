@@ -15,12 +15,13 @@
 namespace vbs {
 
 // GGML type ids (include/vbs_gguf.h:13-48).
-enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+// LNS8 (40) is the reference's own log-scaled 8-bit type (src/vbs_gguf.c:35).
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_LNS8 = 40 };
 
 __host__ __device__ inline int block_elems(int t) {
     switch (t) {
         case T_F32: case T_F16: return 1;
-        case T_Q4_0: case T_Q4_1: case T_Q8_0: return 32;
+        case T_Q4_0: case T_Q4_1: case T_Q8_0: case T_LNS8: return 32;
         case T_Q4_K: case T_Q6_K: return 256;
         default: return 0;
     }
@@ -34,6 +35,7 @@ __host__ __device__ inline int block_bytes(int t) {
         case T_Q8_0: return 34;
         case T_Q4_K: return 144;
         case T_Q6_K: return 210;
+        case T_LNS8: return 36;
         default: return 0;
     }
 }
@@ -157,6 +159,11 @@ __device__ __forceinline__ float dq_elem(int type, const uint8_t *b, int e) {
             int hi = (b[128 + h * 32 + l] >> (q * 2)) & 3;
             float ds = __fmul_rn(f16_exact(ld_u16(b + 208)), (float)(int8_t)b[192 + (e >> 4)]);
             return __fmul_rn(ds, (float)((lo | (hi << 4)) - 32));
+        }
+        case T_LNS8: {   // value = 2^q * scale (src/vbs_host_math.h:111-121); 2^q built exactly, +inf from q = 128
+            const uint32_t q = b[e];
+            const float p2 = q < 128u ? __uint_as_float((q + 127u) << 23) : __uint_as_float(0x7F800000u);
+            return __fmul_rn(p2, __uint_as_float(ld_u16(b + 32) | (ld_u16(b + 34) << 16)));
         }
         default: return 0.0f;
     }

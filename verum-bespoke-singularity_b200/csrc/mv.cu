@@ -555,6 +555,7 @@ cudaError_t mv_generic_launch(int type, const uint8_t *w, const float *x, float 
         case T_Q8_0: VBS_GEN(T_Q8_0); break;
         case T_Q4_K: VBS_GEN(T_Q4_K); break;
         case T_Q6_K: VBS_GEN(T_Q6_K); break;
+        case T_LNS8: VBS_GEN(T_LNS8); break;
         default: return cudaErrorInvalidValue;
     }
 #undef VBS_GEN
