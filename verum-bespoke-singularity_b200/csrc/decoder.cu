@@ -91,6 +91,7 @@ struct vbs_cu_decoder {
     cudaGraphExec_t exec = nullptr;
     uint32_t kernels_per_step = 0;
     uint64_t host_pos = 0;           // host shadow of ctrl[0] (steps enqueued since the last reset)
+    unsigned long long *trace = nullptr;   // step timeline of a VBS_STEP_TRACE profiling build
 };
 
 namespace {
@@ -473,6 +474,12 @@ bool plan_persistent(vbs_cu_decoder *d) {
     p.sync = reinterpret_cast<uint32_t *>(d->step_acc + acc_floats);
     p.ctrl = d->ctrl; p.hist = d->hist; p.hist_cap = d->max_ctx + 1;
     p.err = d->dev->err;
+#ifdef VBS_STEP_TRACE
+    if (!dmalloc((void **)&d->trace, (size_t)d->dev->n_sm * (5 * p.n_layers + 2) * SK_TR_SLOTS * 8, "step trace") ||
+        !cuda_ok(cudaMemset(d->trace, 0, (size_t)d->dev->n_sm * (5 * p.n_layers + 2) * SK_TR_SLOTS * 8), "step trace"))
+        return false;
+    p.trace = d->trace;
+#endif
     d->persist = true;
     return true;
 }
@@ -666,7 +673,7 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
                     d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
                     d->tok_dev, d->attn_work, d->argmax_work, d->step_layers, d->step_acc, d->step_attn, d->step_packed,
                     d->words_mem, d->words_comm, d->pf_x, d->pf_xn, d->pf_q, d->pf_k, d->pf_v, d->pf_att,
-                    d->pf_g, d->pf_u, d->pf_h, d->pf_attn_work};
+                    d->pf_g, d->pf_u, d->pf_h, d->pf_attn_work, d->trace};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->pinned) cudaFreeHost(d->pinned);
@@ -777,6 +784,16 @@ const float *vbs_cu_decoder_logits_device(vbs_cu_decoder_t *d) {
     return d ? (d->tp_world > 1 ? (d->persist ? tp_own_logits() : d->logits_full) : d->logits) : nullptr;
 }
 uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d) { return d ? d->kernels_per_step : 0; }
+#ifdef VBS_STEP_TRACE
+// Profiling builds only: the device address of the last step's timeline,
+// [CTA][op][SK_TR_SLOTS] %globaltimer stamps.
+VBS_API void *vbs_cu_decoder_trace(vbs_cu_decoder_t *d, uint32_t *n_ctas, uint32_t *n_ops) {
+    if (!d || !d->trace) return nullptr;
+    if (n_ctas) *n_ctas = (uint32_t)d->dev->n_sm;
+    if (n_ops) *n_ops = 5 * d->m.n_layers + 2;
+    return d->trace;
+}
+#endif
 uint32_t vbs_cu_decoder_tp_mode(vbs_cu_decoder_t *d) { return !d || d->tp_world == 1 ? 0u : (d->tp_p2p ? 2u : 1u); }
 
 }  // extern "C"

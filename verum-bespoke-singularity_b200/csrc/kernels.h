@@ -228,7 +228,11 @@ struct StepParams {
     // for the logits per step.
     const TpComm *tp;
     uint32_t tp_world, tp_rank, vocab_full;
+    // Timeline of one step, written only by builds with VBS_STEP_TRACE
+    // (a profiling build): per CTA and op, SK_TR_SLOTS %globaltimer stamps.
+    unsigned long long *trace;
 };
+constexpr int SK_TR_SLOTS = 8;   // op start, prologue done, op done, producer first / last issue, 3 spare
 
 // Element (pos, i) of one layer's KV block in the step kernel's cache:
 // [kv head][position][head_dim] with the 16-byte chunk index of each row

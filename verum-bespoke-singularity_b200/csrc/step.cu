@@ -174,6 +174,18 @@ __device__ __forceinline__ SkAttn sk_attn_unit(const StepParams &p, uint32_t seq
     return a;
 }
 
+// Timeline stamps of a profiling build (VBS_STEP_TRACE): slot k of op i of
+// this CTA. Nothing in the product build.
+#ifdef VBS_STEP_TRACE
+__device__ __forceinline__ void sk_stamp(const StepParams &p, uint32_t i, int k) {
+    if (p.trace)
+        p.trace[((size_t)blockIdx.x * (5 * p.n_layers + 2) + i) * SK_TR_SLOTS + k] = global_ns();
+}
+#define SK_STAMP(p, i, k) sk_stamp(p, i, k)
+#else
+#define SK_STAMP(p, i, k) ((void)0)
+#endif
+
 // ---------------------------------------------------------------------------
 // waits
 // ---------------------------------------------------------------------------
@@ -207,23 +219,24 @@ __device__ __forceinline__ void sk_abort(const StepParams &p, uint32_t code) {
 // Grid barrier among the consumer warps of all CTAs: arrive, then wait for
 // `target` arrivals. Returns false, the same value in every consumer thread
 // of the CTA, when this CTA or the grid aborted: thread 0 decides after the
-// first CTA barrier and the second one publishes its decision.
+// first CTA barrier and the second one publishes its decision. The arrival is
+// one release add (it publishes the CTA's writes, which the CTA barrier
+// ordered before it) and the poll an acquire load, with no separate fences:
+// measured 1.6 -> 1.3 us per barrier and a third of the release skew.
 __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t target, volatile int *flag,
                                              volatile int *cta_abort) {
     named_bar_sync(1, SK_CT);
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&p.sync[0], 1u);
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.sync[0]) : "memory");
         bool ok = *cta_abort == 0;
-        const uint64_t t0 = global_ns();
+        uint64_t t0 = 0;
         for (uint32_t it = 1; ok && ld_acquire_gpu(&p.sync[0]) < target; ++it) {
-            __nanosleep(32);
-            if ((it & 15u) == 0) {
+            if ((it & 63u) == 0) {
+                if (it == 64) t0 = global_ns();
                 if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
-                if (global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
+                if (it > 64 && global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
             }
         }
-        __threadfence();
         *flag = ok ? 1 : 0;
     }
     named_bar_sync(1, SK_CT);
@@ -368,6 +381,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
         if (kind == K_ARGMAX) continue;
+        if (lane == 0) SK_STAMP(p, i, 3);
         if (kind == K_ATTN) {
             const SkAttn a = sk_attn_unit(p, seq);
             const uint64_t hb = (((uint64_t)l * p.nkh + a.h) * p.max_ctx) * p.hd;
@@ -383,6 +397,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
                 }
                 sk_issued(r, f, sb, lane);
             }
+            if (lane == 0) SK_STAMP(p, i, 4);
             continue;
         }
         if (kind == K_QKV || kind == K_GU || kind == K_OUT) {   // the norm weight, for every CTA
@@ -409,6 +424,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
             }
             sk_issued(r, f, bytes, lane);
         }
+        if (lane == 0) SK_STAMP(p, i, 4);
     }
     if (!ok) {
         // wait (bounded) for copies still in flight before the CTA may exit
@@ -1098,14 +1114,17 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         }
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
+        if (threadIdx.x == 0) SK_STAMP(p, i, 0);
         if (kind == K_ATTN) {
             if constexpr (HD != 0) sk_attn<HD>(p, l, pos, seq, S, r, sh);
             else if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh);
             else sk_attn<64>(p, l, pos, seq, S, r, sh);
+            if (threadIdx.x == 0) SK_STAMP(p, i, 2);
             continue;
         }
         if (kind == K_ARGMAX) {
             sk_argmax(p, S, pos, tp_base);
+            if (threadIdx.x == 0) SK_STAMP(p, i, 2);
             continue;
         }
         SkMv d = sk_mv_desc(p, kind, l);
@@ -1141,9 +1160,11 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             xq_u = xq_a - (col0 / 32) * (d.type == T_Q6_K ? XQ_PLAIN_STRIDE : XQ_SLOT_STRIDE);   // mv_unit indexes x blocks from column 0
             xf_u = xf_a - (col0 / 32) * 16;
         }
-        if (!work) continue;
+        if (threadIdx.x == 0) SK_STAMP(p, i, 1);
+        if (!work) { if (threadIdx.x == 0) SK_STAMP(p, i, 2); continue; }
         named_bar_sync(1, SK_CT);
         sk_mv_dispatch<HAS_Q4, HAS_Q6, HAS_Q8, TPX>(p, d, S, r, xq_u, xf_u);
+        if (threadIdx.x == 0) SK_STAMP(p, i, 2);
     }
 }
 
