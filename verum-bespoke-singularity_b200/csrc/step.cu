@@ -37,7 +37,8 @@
 //    position applies RoPE to the new key, stores the new K/V row (fp16, the
 //    engine's rounding) into the cache and patches it into its staged copy.
 //    q.K and p.V run on mma.sync m16n8k16 with f16 hi/lo operand splits
-//    (fp32-accurate); the last CTA of a KV head merges the splits.
+//    (fp32-accurate). Each split publishes its partial state on its head's
+//    counter; once all have, the head's splits merge a share each.
 //  * The argmax runs on slices per CTA; the last CTA advances the position
 //    and token in the device control block.
 //
@@ -70,7 +71,8 @@ constexpr uint32_t SK_MAX_SPLITS = 128;
 constexpr int SK_GS = 8;                           // query-head slots per KV head
 constexpr float SK_LAZY = 8.0f;                    // softmax rescale threshold (log2 units)
 // sync words: [0] grid barrier, [1] abort, [2] argmax ticket,
-// [16 + h] attention merge ticket of KV head h, [SK_SLOTS + 2c] argmax slots
+// [16 + h] KV head h's attention splits published in this step (all layers),
+// [SK_SLOTS + 2c] argmax slots
 constexpr uint32_t SK_TICKET0 = 16, SK_MAX_KV = 112, SK_SLOTS = SK_TICKET0 + SK_MAX_KV;
 
 enum : int { K_QKV = 0, K_ATTN = 1, K_O = 2, K_GU = 3, K_DOWN = 4, K_OUT = 5, K_ARGMAX = 6 };
@@ -719,16 +721,18 @@ __device__ __forceinline__ float2 sk_rope(float a, float b, uint32_t d, uint32_t
     return make_float2(a * c - b * s, a * s + b * c);
 }
 
-// The last split of a KV head merges the S partial states [m, l, pad, pad,
-// o[HD]] of each query head in split order: every thread two outputs, all
-// loads of a batch of splits in flight at once (a single round trip for
-// S <= SK_MB), batches combined with the usual rescale.
+// Merges the S partial states [m, l, pad, pad, o[HD]] of a KV head's query
+// heads in split order, for the outputs [e_lo, e_hi) of the G * HD (e_lo,
+// e_hi even): every thread two outputs, all loads of a batch of splits in
+// flight at once (a single round trip for S <= SK_MB), batches combined with
+// the usual rescale.
 constexpr uint32_t SK_MB = 20;
 template <int HD>
-__device__ __noinline__ void sk_attn_merge(const StepParams &p, const SkAttn &a, uint32_t G, const float *parts, float *outp) {
+__device__ __noinline__ void sk_attn_merge(const StepParams &p, const SkAttn &a, uint32_t G, const float *parts, float *outp,
+                                           uint32_t e_lo, uint32_t e_hi) {
     constexpr uint32_t RS = 4 + HD;
     constexpr size_t part_stride = (size_t)SK_GS * RS;
-    for (uint32_t e = 2 * threadIdx.x; e < G * HD; e += 2 * SK_CT) {
+    for (uint32_t e = e_lo + 2 * threadIdx.x; e < e_hi; e += 2 * SK_CT) {
         const uint32_t gg = e / HD, d = e % HD;
         const float *src = parts + gg * RS;
         float M = -INFINITY, L = 0.f, O0 = 0.f, O1 = 0.f;
@@ -961,15 +965,34 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
         }
     }
     if (a.S == 1) return;
-    __threadfence();
+    // Publish this split's state with one release add on the head's counter
+    // (the CTA barrier orders every thread's stores before it; the counter
+    // counts splits over the step's layers, so layer l waits for S * (l + 1)),
+    // wait until every split of the head published, then merge this split's
+    // share of the head's outputs: the S CTAs of a head merge in parallel.
     named_bar_sync(1, SK_CT);
     volatile int *flag = S.sync_flag();
-    if (threadIdx.x == 0) *flag = atomicAdd(&p.sync[SK_TICKET0 + a.h], 1u) == a.S - 1;
+    if (threadIdx.x == 0) {
+        uint32_t *cnt = &p.sync[SK_TICKET0 + a.h];
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+        const uint32_t want = a.S * (l + 1u);
+        bool ok = !*cta_abort;
+        uint64_t t0 = 0;
+        for (uint32_t it = 1; ok && ld_acquire_gpu(cnt) < want; ++it) {
+            if ((it & 63u) == 0) {
+                if (it == 64) t0 = global_ns();
+                if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
+                if (it > 64 && global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
+            }
+        }
+        if (!ok) *cta_abort = 1;
+        *flag = ok ? 1 : 0;
+    }
     named_bar_sync(1, SK_CT);
     if (!*flag) return;
-    __threadfence();
-    sk_attn_merge<HD>(p, a, G, work + (size_t)a.h * SK_MAX_SPLITS * part_stride, outp);
-    if (threadIdx.x == 0) p.sync[SK_TICKET0 + a.h] = 0u;
+    const uint32_t per = ((G * HD + a.S - 1) / a.S + 1) & ~1u;
+    const uint32_t e_lo = min(G * HD, a.split * per), e_hi = min(G * HD, e_lo + per);
+    sk_attn_merge<HD>(p, a, G, work + (size_t)a.h * SK_MAX_SPLITS * part_stride, outp, e_lo, e_hi);
 }
 
 // ---------------------------------------------------------------------------
