@@ -303,4 +303,76 @@ __device__ __forceinline__ void quant_block8(const float v[8], uint32_t u, uint3
     if (u == 0) xf[J] = make_float4(d2, d2 * (float)(half + half_hi), __int_as_float(half), __int_as_float(half_hi));
 }
 
+// quant_block8 for two blocks J[0], J[1] of the same quad at once, their
+// dependent chains (block maxima, shuffles, roundings) interleaved. Block 1
+// is skipped (computed, not stored) when !has1; the quad's four lanes agree
+// on has1, so the shuffles stay uniform.
+template <bool PLAIN>
+__device__ __forceinline__ void quant_block8x2(const float v[2][8], uint32_t u, uint32_t qmask, const uint32_t J[2],
+                                               bool has1, uint8_t *xq, float4 *xf) {
+    float amax[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax[b] = fmaxf(amax[b], fabsf(v[b][i]));
+#pragma unroll
+    for (int b = 0; b < 2; ++b) amax[b] = fmaxf(amax[b], __shfl_xor_sync(qmask, amax[b], 1));
+#pragma unroll
+    for (int b = 0; b < 2; ++b) amax[b] = fmaxf(amax[b], __shfl_xor_sync(qmask, amax[b], 2));
+    constexpr float kMagic = 12582912.0f;
+    constexpr int kMagicBits = 0x4B400000;
+    float d2[2];
+    int sum[2] = {0, 0};
+    uint32_t q1w[2][2], q2w[2][2];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        d2[b] = amax[b] * (1.0f / (127.0f * 254.0f));
+        const float d1 = d2[b] * 254.0f;
+        float r1 = 0.0f, r2 = 0.0f;
+        if (d2[b] > 0.0f) {   // approximate reciprocals, as quant_block8
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r2) : "f"(d2[b]));
+        }
+        uint32_t t1[8], t2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float a = fminf(fmaxf(v[b][i] * r1, -127.0f), 127.0f) + kMagic;
+            const float res = fmaf(-(a - kMagic), d1, v[b][i]);
+            const float c = fminf(fmaxf(res * r2, -127.0f), 127.0f) + kMagic;
+            t1[i] = __float_as_uint(a);
+            t2[i] = __float_as_uint(c);
+            sum[b] += 254 * (__float_as_int(a) - kMagicBits) + (__float_as_int(c) - kMagicBits);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            q1w[b][k] = __byte_perm(__byte_perm(t1[4 * k], t1[4 * k + 1], 0x0040u), __byte_perm(t1[4 * k + 2], t1[4 * k + 3], 0x0040u), 0x5410u);
+            q2w[b][k] = __byte_perm(__byte_perm(t2[4 * k], t2[4 * k + 1], 0x0040u), __byte_perm(t2[4 * k + 2], t2[4 * k + 3], 0x0040u), 0x5410u);
+        }
+    }
+    int half[2], half_hi[2];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) half[b] = sum[b] + __shfl_xor_sync(qmask, sum[b], 1);
+#pragma unroll
+    for (int b = 0; b < 2; ++b) half_hi[b] = __shfl_xor_sync(qmask, half[b], 2);
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        if (b == 1 && !has1) break;
+        uint8_t *blk = xq + (size_t)J[b] * xq_stride<PLAIN>();
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t w = 2 * u + k;
+            if constexpr (PLAIN) {
+                *reinterpret_cast<uint32_t *>(blk + 4 * w) = q1w[b][k];
+                *reinterpret_cast<uint32_t *>(blk + 32 + 4 * w) = q2w[b][k];
+            } else {
+                const uint32_t off = (w & 3) * 16 + (w >> 2) * 4;
+                *reinterpret_cast<uint32_t *>(blk + off) = q1w[b][k];
+                *reinterpret_cast<uint32_t *>(blk + 8 + off) = q2w[b][k];
+            }
+        }
+        if (u == 0)
+            xf[J[b]] = make_float4(d2[b], d2[b] * (float)(half[b] + half_hi[b]), __int_as_float(half[b]), __int_as_float(half_hi[b]));
+    }
+}
+
 }  // namespace vbs

@@ -95,6 +95,7 @@ struct SkMv {
     float *out;             // chunk c's sums at out + c * rows (one writer per element)
     StepMvGeom g;
     int tpw;                // tensor parallelism: 0 local, 1 o/down partial planes to every rank, 2 logits shard to every rank
+    int norm;               // the input was RMSNorm-ed without its scale: multiply the row sums by sk_norm_scale
     uint32_t tp_k;          // exchange index (its slot set is tp_k % 2)
 };
 
@@ -119,7 +120,7 @@ __device__ __forceinline__ SkMv sk_mv_desc(const StepParams &p, int kind, uint32
     const StepLayer &L = p.layers[kind == K_OUT ? 0 : l];
     switch (kind) {
         case K_QKV:
-            d.type = p.t_qkv; d.packed = L.qkv;
+            d.type = p.t_qkv; d.packed = L.qkv; d.norm = 1;
             d.rows = qd + 2 * kvd; d.cols = p.dim; d.out = sk_acc(p, l); d.g = p.geo[STEP_QKV];
             break;
         case K_O:
@@ -127,7 +128,7 @@ __device__ __forceinline__ SkMv sk_mv_desc(const StepParams &p, int kind, uint32
             d.rows = p.dim; d.cols = qd; d.out = sk_acc_o(p, l); d.g = p.geo[STEP_O];
             break;
         case K_GU:
-            d.type = p.t_gu; d.gu = 1; d.packed = L.gu;
+            d.type = p.t_gu; d.gu = 1; d.packed = L.gu; d.norm = 1;
             d.rows = p.ffn; d.cols = p.dim; d.out = sk_acc_h(p, l); d.g = p.geo[STEP_GU];
             break;
         case K_DOWN:
@@ -135,7 +136,7 @@ __device__ __forceinline__ SkMv sk_mv_desc(const StepParams &p, int kind, uint32
             d.rows = p.dim; d.cols = p.ffn; d.out = sk_acc_down(p, l); d.g = p.geo[STEP_DOWN];
             break;
         default:   // K_OUT
-            d.type = p.t_out; d.packed = p.out;
+            d.type = p.t_out; d.packed = p.out; d.norm = 1;
             d.rows = p.vocab; d.cols = p.dim; d.out = sk_logits(p); d.g = p.geo[STEP_OUT];
             break;
     }
@@ -466,6 +467,21 @@ __device__ __forceinline__ void sk_quant(int type, const float v[8], uint32_t u,
                                          float4 *xf) {
     sk_quant(type, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], u, qmask, J, xq, xf);
 }
+// Two blocks J0, J1 of this quad at once (quant_block8x2); J1 only when has1.
+__device__ __noinline__ void sk_quant2(int type, float a0, float a1, float a2, float a3, float a4, float a5, float a6,
+                                       float a7, float b0, float b1, float b2, float b3, float b4, float b5, float b6,
+                                       float b7, uint32_t u, uint32_t qmask, uint32_t J0, uint32_t J1, bool has1,
+                                       uint8_t *xq, float4 *xf) {
+    const float v[2][8] = {{a0, a1, a2, a3, a4, a5, a6, a7}, {b0, b1, b2, b3, b4, b5, b6, b7}};
+    const uint32_t J[2] = {J0, J1};
+    if (type == T_Q6_K) quant_block8x2<true>(v, u, qmask, J, has1, xq, xf);
+    else quant_block8x2<false>(v, u, qmask, J, has1, xq, xf);
+}
+__device__ __forceinline__ void sk_quant2(int type, const float v[2][8], uint32_t u, uint32_t qmask, uint32_t J0,
+                                          uint32_t J1, bool has1, uint8_t *xq, float4 *xf) {
+    sk_quant2(type, v[0][0], v[0][1], v[0][2], v[0][3], v[0][4], v[0][5], v[0][6], v[0][7], v[1][0], v[1][1], v[1][2],
+              v[1][3], v[1][4], v[1][5], v[1][6], v[1][7], u, qmask, J0, J1, has1, xq, xf);
+}
 
 // Elements e..e+7 of the embedding row of `token` (src/vbs_host_math.h:136-142).
 __device__ __noinline__ void sk_embed8(const StepParams &p, uint32_t token, uint32_t e, float *out) {
@@ -477,9 +493,12 @@ __device__ __noinline__ void sk_embed8(const StepParams &p, uint32_t token, uint
 
 // Residual update x += add (or x = the embedding row when add is NULL,
 // src/vbs_host_math.h:136-142), RMSNorm (src/vbs_host_math.h:28-36) with
-// the norm weight, and, when `quant`, the quantized normalized vector. The
-// norm weight arrives as a ring stage of dim floats (the producer issues it
-// ahead of the op's weight stages), so it is never a load on this path.
+// the norm weight, and, when `quant`, the quantized vector. The norm weight
+// arrives as a ring stage of dim floats (the producer issues it ahead of the
+// op's weight stages), so it is never a load on this path. RMSNorm's scalar
+// 1/rms(x) does not wait here: x * w is quantized as it is (the block
+// quantization is scale-free) and the matvec multiplies its row sums by the
+// scale (sk_norm_scale), once every warp's sum of squares is in misc[0..7].
 constexpr int SK_MAXPL = 4;      // partial planes summed by the norm prologue
 
 // WORDS (instances with tensor parallelism): when `want` is not 0 the planes
@@ -545,31 +564,26 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
     ss = warp_sum(ss);
     float *misc = S.misc();
     if ((ctid & 31u) == 0) misc[ctid >> 5] = ss;
-    named_bar_sync(1, SK_CT);
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < SK_NCW; ++w) tot += misc[w];
-    const float scale = 1.0f / sqrtf(tot / (float)p.dim + p.eps);
     // the norm weight stage (long landed by now); released after use
     const int lane = (int)(ctid & 31u);
     volatile int *cta_abort = S.abort_flag();
     const uint32_t nb = p.dim * 4, ws = S.ring + r.place(nb, S.ring_bytes);
     const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
     if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
-    if (quant && got) {
+    static_assert(SK_PB == 2, "the prologue quantizes its two blocks together");
+    if (quant && got && q < nsub) {
+        float v[SK_PB][8];
 #pragma unroll
         for (int r2 = 0; r2 < SK_PB; ++r2) {
             const uint32_t J = q + r2 * (SK_CT / 4);
-            if (J >= nsub) continue;
-            const uint32_t e = J * 32 + 8 * u;
+            const uint32_t e = (J < nsub ? J : q) * 32 + 8 * u;
             const uint4 w0 = lds_u128(ws + e * 4), w1 = lds_u128(ws + e * 4 + 16);
             const float wv[8] = {__uint_as_float(w0.x), __uint_as_float(w0.y), __uint_as_float(w0.z), __uint_as_float(w0.w),
                                  __uint_as_float(w1.x), __uint_as_float(w1.y), __uint_as_float(w1.z), __uint_as_float(w1.w)};
-            float v[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[k] = xv[r2][k] * scale * wv[k];
-            sk_quant(type, v, u, qmask, J, xq, xf);
+            for (int k = 0; k < 8; ++k) v[r2][k] = xv[r2][k] * wv[k];
         }
+        sk_quant2(type, v, u, qmask, q, q + SK_CT / 4, q + SK_CT / 4 < nsub, xq, xf);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(S.empty(r.idx));
@@ -581,20 +595,18 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
 // before any is used.
 template <int NB>
 __device__ __noinline__ void sk_prologue_vec(uint32_t n, int type, const float *src, uint8_t *xq, float4 *xf) {
+    static_assert(NB == 2, "blocks are quantized in pairs");
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = n / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
     for (uint32_t J0 = q; J0 < nsub; J0 += NB * (SK_CT / 4)) {
         float v[NB][8];
+        const uint32_t J1 = J0 + SK_CT / 4;
+        ld8_cg(src + J0 * 32 + 8 * u, v[0]);
+        if (J1 < nsub) ld8_cg(src + J1 * 32 + 8 * u, v[1]);
+        else
 #pragma unroll
-        for (int r = 0; r < NB; ++r) {
-            const uint32_t J = J0 + r * (SK_CT / 4);
-            if (J < nsub) ld8_cg(src + J * 32 + 8 * u, v[r]);
-        }
-#pragma unroll
-        for (int r = 0; r < NB; ++r) {
-            const uint32_t J = J0 + r * (SK_CT / 4);
-            if (J < nsub) sk_quant(type, v[r], u, qmask, J, xq, xf);
-        }
+            for (int k = 0; k < 8; ++k) v[1][k] = 0.0f;
+        sk_quant2(type, v, u, qmask, J0, J1, J1 < nsub, xq, xf);
     }
 }
 
@@ -604,10 +616,22 @@ __device__ __noinline__ void sk_prologue_vec(uint32_t n, int type, const float *
 // stores into its column chunk's plane, or for gate/up rows as
 // SiLU(gate)*up.
 // ---------------------------------------------------------------------------
+// RMSNorm's scale 1/sqrt(mean(x^2) + eps) (src/vbs_host_math.h:28-36) from
+// the warps' sums of squares the norm prologue left in misc[0..7], summed in
+// warp order.
+__device__ __forceinline__ float sk_norm_scale(const StepParams &p, const SkSmem &S) {
+    const float *misc = S.misc();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < SK_NCW; ++w) tot += misc[w];
+    return 1.0f / sqrtf(tot / (float)p.dim + p.eps);
+}
+
 template <int TYPE, bool TPX>
 __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                               uint32_t xq_a, uint32_t xf_a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    const float nscale = d.norm ? sk_norm_scale(p, S) : 1.0f;
     const uint32_t RS = d.g.rs, CK = d.g.ck, SB = 16u * RS;
     volatile int *cta_abort = S.abort_flag();
     float *red = S.red();
@@ -661,12 +685,14 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
                 float va = 0.f;
 #pragma unroll
                 for (int w = 0; w < SK_NCW; ++w) va += b[w * 16 + rr];
+                va *= nscale;
                 const uint32_t row = sk_slot_row(d.gu != 0, tile, rr);
                 if (d.gu) {   // h = SiLU(gate) * up (src/vbs_host_math.h:53-57): slot rr < 8 gate, rr + 8 up
                     if (rr < 8 && row < d.rows) {
                         float vu = 0.f;
 #pragma unroll
                         for (int w = 0; w < SK_NCW; ++w) vu += b[w * 16 + rr + 8];
+                        vu *= nscale;
                         d.out[row] = va / (1.0f + expf(-va)) * vu;
                     }
                 } else if (TPX && row < d.rows && d.tpw) {   // this rank's partial into every rank's region
