@@ -117,6 +117,26 @@ typedef struct vbs_backend_ops {
 } vbs_backend_ops_t;
 #endif /* VBS_BACKEND_H */
 
+#ifndef VBS_ENGINE_H
+/* ---- restated engine control block (include/vbs_engine.h:22-40 of the
+ * reference; layout must not change): the device-resident state of a
+ * generation run, read and written by launch_persistent_kernel. ---- */
+typedef enum {
+    VBS_PGAE_IDLE = 0, VBS_PGAE_PREFILL = 1, VBS_PGAE_GENERATE = 2, VBS_PGAE_EXIT = 3
+} vbs_pgae_state_t;
+#define VBS_PGAE_EOS_NONE ((uint32_t)0xFFFFFFFFu)
+typedef struct {
+    volatile uint32_t state;
+    volatile uint32_t current_token;
+    volatile uint32_t position;
+    volatile uint32_t max_tokens;
+    volatile uint32_t vocab_size;
+    volatile uint32_t eos_token_id;
+    uint64_t generated_tokens_dev;
+    uint64_t logits_dev;
+} vbs_gpu_control_t;
+#endif /* VBS_ENGINE_H */
+
 /* ================================================================== */
 /* 1. Drop-in boundary                                                 */
 /* ================================================================== */
@@ -132,9 +152,10 @@ typedef struct vbs_backend_ops {
  *                  src/vbs_backend_test.c:863), NULL above.
  *  copy_*          synchronous; copy_to_host returns false once an error
  *                  has been latched.
- *  compile_linear_pipeline  F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K;
- *                  refuses every other type with a message.
- *  compile_embed_pipeline   same type set.
+ *  compile_linear_pipeline  F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K and the
+ *                  reference's LNS8; refuses every other type with a message.
+ *  compile_embed_pipeline   the same types without LNS8 (no embedding
+ *                  kernel in the reference either).
  *  compile_primitive_pipeline  EMBEDDING, NORMALIZE, ROTARY, CACHE,
  *                  ATTENTION, ACTIVATION, ELEMENTWISE.
  *  dispatch_linear_tile  both calling conventions: resident weights
@@ -145,7 +166,11 @@ typedef struct vbs_backend_ops {
  *  dispatch_primitive  canonical bridge argument order
  *                  (include/vbs_specializer_bridge.h:44-53); grid/block
  *                  hints are ignored, the backend picks its own launch.
- *  launch_persistent_kernel  NULL (include/vbs_backend.h:94-98). */
+ *  launch_persistent_kernel  (include/vbs_backend.h:94-98, NULL in every
+ *                  reference backend) device-driven greedy generation:
+ *                  `pipeline` is a vbs_cu_decoder_t of a model on `dev`,
+ *                  `control_buffer` a device buffer holding a
+ *                  vbs_gpu_control_t; runs vbs_cu_decoder_run_control. */
 extern VBS_API const vbs_backend_ops_t g_vbs_cuda_backend;
 
 /* Last error message, "ok" when none (include/vbs_backend_select.h:40). */
@@ -323,6 +348,27 @@ VBS_API void vbs_cu_decoder_reset(vbs_cu_decoder_t *d);
  * src/vbs_engine.c:240-327. */
 VBS_API int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t n_prompt, uint32_t n_new,
                             uint32_t *out_tokens);
+
+/* Device-driven greedy generation, the engine's autonomy loop
+ * (src/vbs_engine.c:240-327) with every decision on the device. `control`
+ * is the device address of a vbs_gpu_control_t with state PREFILL or
+ * GENERATE, current_token the next token to feed (the prompt's last, as the
+ * reference's Phase 1 sets it), max_tokens >= 1, vocab_size the decoder's
+ * vocabulary, eos_token_id (VBS_PGAE_EOS_NONE: none) and
+ * generated_tokens_dev (max_tokens uint32 on the device); the decoder holds
+ * the rest of the prompt as context. Each step feeds current_token at the
+ * decoder's position; a one-thread kernel after it takes the step's argmax
+ * (first maximum wins), stops on EOS (not stored) or when max_tokens tokens
+ * are stored, else appends the token to generated_tokens_dev, sets
+ * current_token and position (= tokens generated), exactly as the
+ * reference's loop does; once stopped, state is EXIT and the steps still
+ * queued do nothing. The host only enqueues steps and looks at the stop word
+ * every 16 steps. logits_dev (when not 0) receives the last step's logits
+ * (vocab_size floats). 0 on success; -1 with the error latched for a bad
+ * control block or when max_tokens steps would exceed the KV capacity.
+ * Tensor-parallel decoders are not supported (the engine binds one
+ * device). */
+VBS_API int vbs_cu_decoder_run_control(vbs_cu_decoder_t *d, void *control);
 
 /* Enqueue n decode steps on the decoder's stream that feed each step's
  * argmax back as the next token (no host work between steps); returns

@@ -4,11 +4,13 @@
  * the reference's include/vbs_backend.h (oracle/_ref/abi-layout-ref) and
  * once against this library's include/vbs_b200.h (oracle/abi-layout), so a
  * test can compare every offset and size of the two definitions. The
- * engine calls through these structs (include/vbs_backend.h:24-99), so they
- * must agree field for field.
+ * engine calls through these structs (include/vbs_backend.h:24-99) and
+ * hands launch_persistent_kernel its control block (include/vbs_engine.h:
+ * 31-40), so they must agree field for field.
  */
 #ifdef LAYOUT_OF_REFERENCE
 #include "vbs_backend.h"
+#include "vbs_engine.h"
 #else
 #include "vbs_b200.h"
 #endif
@@ -37,6 +39,12 @@ int main(void) {
     FIELD(vbs_backend_ops_t, compile_primitive_pipeline); FIELD(vbs_backend_ops_t, dispatch_linear_tile);
     FIELD(vbs_backend_ops_t, dispatch_primitive); FIELD(vbs_backend_ops_t, synchronize_device);
     FIELD(vbs_backend_ops_t, launch_persistent_kernel);
+    TYPE(vbs_gpu_control_t);
+    FIELD(vbs_gpu_control_t, state); FIELD(vbs_gpu_control_t, current_token); FIELD(vbs_gpu_control_t, position);
+    FIELD(vbs_gpu_control_t, max_tokens); FIELD(vbs_gpu_control_t, vocab_size); FIELD(vbs_gpu_control_t, eos_token_id);
+    FIELD(vbs_gpu_control_t, generated_tokens_dev); FIELD(vbs_gpu_control_t, logits_dev);
+    printf("VBS_PGAE_GENERATE %d VBS_PGAE_EXIT %d VBS_PGAE_EOS_NONE %u\n", (int)VBS_PGAE_GENERATE, (int)VBS_PGAE_EXIT,
+           (unsigned)VBS_PGAE_EOS_NONE);
     /* enum values the engine passes across the boundary */
     printf("VBS_GGML_TYPE_Q4_K %d VBS_GGML_TYPE_Q6_K %d VBS_GGML_TYPE_Q8_0 %d VBS_GGML_TYPE_F32 %d\n",
            (int)VBS_GGML_TYPE_Q4_K, (int)VBS_GGML_TYPE_Q6_K, (int)VBS_GGML_TYPE_Q8_0, (int)VBS_GGML_TYPE_F32);

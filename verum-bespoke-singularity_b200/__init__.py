@@ -95,8 +95,20 @@ class OpsTable(C.Structure):
         ("dispatch_primitive", C.CFUNCTYPE(C.c_bool, _P_DEV, C.c_void_p, C.POINTER(Arg), C.c_size_t, C.c_size_t,
                                            C.c_size_t)),
         ("synchronize_device", C.CFUNCTYPE(None, _P_DEV)),
-        ("launch_persistent_kernel", C.c_void_p),
+        ("launch_persistent_kernel", C.CFUNCTYPE(C.c_bool, _P_DEV, C.c_void_p, _P_BUF)),
     ]
+
+
+# PGAE states and the control block (include/vbs_engine.h:22-40 of the reference)
+PGAE_IDLE, PGAE_PREFILL, PGAE_GENERATE, PGAE_EXIT = 0, 1, 2, 3
+PGAE_EOS_NONE = 0xFFFFFFFF
+
+
+class GpuControl(C.Structure):
+    """vbs_gpu_control_t: the device-resident state of a generation run."""
+    _fields_ = [("state", C.c_uint32), ("current_token", C.c_uint32), ("position", C.c_uint32),
+                ("max_tokens", C.c_uint32), ("vocab_size", C.c_uint32), ("eos_token_id", C.c_uint32),
+                ("generated_tokens_dev", C.c_uint64), ("logits_dev", C.c_uint64)]
 
 
 class ModelDesc(C.Structure):
@@ -161,6 +173,7 @@ def lib() -> C.CDLL:
         "vbs_cu_decoder_reset": (None, [vp]),
         "vbs_cu_decoder_generate": (i32, [vp, C.POINTER(u32), sz, u32, C.POINTER(u32)]),
         "vbs_cu_decoder_enqueue_steps": (i32, [vp, u32]),
+        "vbs_cu_decoder_run_control": (i32, [vp, vp]),
         "vbs_cu_decoder_set_position": (i32, [vp, u32, u32]),
         "vbs_cu_decoder_position": (u32, [vp]),
         "vbs_cu_decoder_stream": (vp, [vp]),

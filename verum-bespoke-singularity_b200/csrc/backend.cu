@@ -524,6 +524,20 @@ static void ops_synchronize(vbs_device_t *dev) {
     check_device_error(d, 0);
 }
 
+// The reference's Phase 2 hook (include/vbs_backend.h:94-98): `pipeline` is
+// a vbs_cu_decoder_t of a model on `dev`, `control_buffer` holds the
+// engine's vbs_gpu_control_t (include/vbs_engine.h:31-40). Generation runs on
+// the device, steered by that block (vbs_cu_decoder_run_control).
+static bool ops_launch_persistent_kernel(vbs_device_t *dev, void *pipeline, vbs_buffer_t *control) {
+    DevState *d = dev_of(dev);
+    if (!d || !pipeline || !control || !control->internal_handle || control->size < sizeof(vbs_gpu_control_t)) {
+        latch_error("launch_persistent_kernel: needs a device, a decoder and a control buffer of %zu bytes",
+                    sizeof(vbs_gpu_control_t));
+        return false;
+    }
+    return vbs_cu_decoder_run_control(static_cast<vbs_cu_decoder_t *>(pipeline), control->internal_handle) == 0;
+}
+
 const vbs_backend_ops_t g_vbs_cuda_backend = {
     ops_init,
     ops_get_device_count,
@@ -538,7 +552,7 @@ const vbs_backend_ops_t g_vbs_cuda_backend = {
     ops_dispatch_linear_tile,
     ops_dispatch_primitive,
     ops_synchronize,
-    nullptr,
+    ops_launch_persistent_kernel,
 };
 
 // ===========================================================================

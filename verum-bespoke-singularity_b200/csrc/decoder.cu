@@ -48,7 +48,10 @@ struct Layer {
 
 }  // namespace
 
+constexpr uint32_t kDecoderMagic = 0x56424443u;   // "VBDC": a live vbs_cu_decoder
+
 struct vbs_cu_decoder {
+    uint32_t magic = kDecoderMagic;
     vbs_cu_model_t m;
     std::vector<Layer> L;
     uint32_t flags = 0, max_ctx = 0, kv_dim = 0, q_dim = 0, vocab_full = 0;
@@ -551,6 +554,37 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
     return true;
 }
 
+// One step's stop decision of device-driven generation (the engine's loop,
+// src/vbs_engine.c:295-316), one thread, after the step: ctrl[1] holds the
+// step's argmax (first maximum), which the next step feeds. ctrl[2] is the
+// decoder's stop word: once set, later steps (the step kernel) and decisions
+// do nothing.
+__global__ void control_step_kernel(uint32_t *ctrl, vbs_gpu_control_t *gc) {
+    if (ctrl[2]) return;
+    const uint32_t t = ctrl[1];
+    if (gc->eos_token_id != VBS_PGAE_EOS_NONE && t == gc->eos_token_id) {
+        gc->state = VBS_PGAE_EXIT;
+        ctrl[2] = 1u;
+        return;
+    }
+    const uint32_t n = gc->position;
+    reinterpret_cast<uint32_t *>(gc->generated_tokens_dev)[n] = t;
+    gc->position = n + 1u;
+    gc->current_token = t;
+    if (n + 1u >= gc->max_tokens) {
+        gc->state = VBS_PGAE_EXIT;
+        ctrl[2] = 1u;
+    }
+}
+
+// The first token to feed comes from the control block; the stop word starts clear.
+__global__ void control_start_kernel(uint32_t *ctrl, vbs_gpu_control_t *gc) {
+    ctrl[1] = gc->current_token;
+    ctrl[2] = 0u;
+    gc->state = VBS_PGAE_GENERATE;
+    gc->position = 0u;
+}
+
 }  // namespace
 
 extern "C" {
@@ -665,6 +699,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
 
 void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
     if (!d) return;
+    d->magic = 0;
     DeviceGuard guard(d->dev ? d->dev->ordinal : 0);
     if (d->st) cudaStreamSynchronize(d->st);
     if (d->exec) cudaGraphExecDestroy(d->exec);
@@ -768,6 +803,65 @@ int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt, size_t 
             return -1;
     }
     return sync_and_check(d) ? 0 : -1;
+}
+
+int vbs_cu_decoder_run_control(vbs_cu_decoder_t *d, void *control) {
+    if (!d || d->magic != kDecoderMagic || !control) { latch_error("decoder_run_control: invalid decoder or control block"); return -1; }
+    if (d->tp_world > 1) { latch_error("decoder_run_control: tensor-parallel decoders are driven per rank"); return -1; }
+    DeviceGuard guard(d->dev->ordinal);
+    vbs_gpu_control_t gc;
+    if (!cuda_ok(cudaMemcpyAsync(&gc, control, sizeof gc, cudaMemcpyDeviceToHost, d->st), "control block") ||
+        !cuda_ok(cudaStreamSynchronize(d->st), "control block"))
+        return -1;
+    if ((gc.state != VBS_PGAE_PREFILL && gc.state != VBS_PGAE_GENERATE) || !gc.max_tokens || !gc.generated_tokens_dev ||
+        gc.vocab_size != d->vocab_full || gc.current_token >= d->vocab_full) {
+        latch_error("decoder_run_control: control block state %u, max_tokens %u, vocab %u (decoder %u), token %u, "
+                    "tokens buffer %s", gc.state, gc.max_tokens, gc.vocab_size, d->vocab_full, gc.current_token,
+                    gc.generated_tokens_dev ? "set" : "missing");
+        return -1;
+    }
+    if (d->host_pos + gc.max_tokens > d->max_ctx) {
+        latch_error("decoder_run_control: %u steps from position %llu exceed the KV capacity %u", gc.max_tokens,
+                    (unsigned long long)d->host_pos, d->max_ctx);
+        return -1;
+    }
+    auto *gcd = static_cast<vbs_gpu_control_t *>(control);
+    note_launches(1);
+    control_start_kernel<<<1, 1, 0, d->st>>>(d->ctrl, gcd);
+    if (!cuda_ok(cudaGetLastError(), "control start")) return -1;
+    // the persistent step kernel returns at once when the stop word is set,
+    // so steps go out 16 at a time; the per-op and strict steps do not look
+    // at it and go out one at a time
+    const uint32_t chunk = d->persist ? 16u : 1u;
+    uint32_t done = 0;
+    while (done < gc.max_tokens) {
+        const uint32_t n = std::min(chunk, gc.max_tokens - done);
+        for (uint32_t i = 0; i < n; ++i) {
+            if (!enqueue_step(d)) return -1;
+            note_launches(1);
+            control_step_kernel<<<1, 1, 0, d->st>>>(d->ctrl, gcd);
+            if (!cuda_ok(cudaGetLastError(), "control step")) return -1;
+        }
+        done += n;
+        if (!cuda_ok(cudaMemcpyAsync(d->pinned + 2, d->ctrl + 2, 4, cudaMemcpyDeviceToHost, d->st), "stop word") ||
+            !sync_and_check(d))
+            return -1;
+        if (d->pinned[2]) break;
+    }
+    // the decoder's position: steps that ran (the stopped ones did nothing)
+    if (!cuda_ok(cudaMemcpyAsync(d->pinned, d->ctrl, 4, cudaMemcpyDeviceToHost, d->st), "position")) return -1;
+    // the next steps of the decoder run normally
+    if (!cuda_ok(cudaMemsetAsync(d->ctrl + 2, 0, 4, d->st), "stop word")) return -1;
+    if (!sync_and_check(d)) return -1;
+    d->host_pos = d->pinned[0];
+    if (gc.logits_dev) {
+        const float *src = vbs_cu_decoder_logits_device(d);
+        if (!cuda_ok(cudaMemcpyAsync(reinterpret_cast<void *>(gc.logits_dev), src, (size_t)d->vocab_full * 4,
+                                     cudaMemcpyDeviceToDevice, d->st), "logits copy") ||
+            !sync_and_check(d))
+            return -1;
+    }
+    return 0;
 }
 
 int vbs_cu_decoder_enqueue_steps(vbs_cu_decoder_t *d, uint32_t n) {

@@ -1117,6 +1117,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     // read once: the last CTA rewrites the control block at the end of the step
     const uint32_t pos = *reinterpret_cast<const volatile uint32_t *>(p.ctrl);
     const uint32_t token = *reinterpret_cast<const volatile uint32_t *>(p.ctrl + 1);
+    // ctrl[2]: device-driven generation stopped (vbs_cu_decoder_run_control):
+    // this step does nothing, the same decision in every CTA
+    if (*reinterpret_cast<const volatile uint32_t *>(p.ctrl + 2)) return;
     if (pos >= p.max_ctx || token >= (p.tp ? p.vocab_full : p.vocab)) {   // the same decision in every CTA: nothing runs, nothing waits
         if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(p.err, DERR_BAD_ARG);
         return;
