@@ -370,6 +370,18 @@ VBS_API int vbs_cu_decoder_generate(vbs_cu_decoder_t *d, const uint32_t *prompt,
  * device). */
 VBS_API int vbs_cu_decoder_run_control(vbs_cu_decoder_t *d, void *control);
 
+/* Bounded-wait test control (no reference counterpart). Every wait of the
+ * persistent step kernel (mbarriers, grid barriers, exchange words,
+ * attention counters) gives up after wait_ns of global time (1 ms .. 2 s;
+ * 2 s by default), records DERR_TIMEOUT_* in the device error word and
+ * unwinds every CTA; the next synchronising call reports it. drop_op (a step
+ * op index: 5 * layer + {0 QKV, 1 ATTN, 2 O, 3 GU, 4 DOWN}, then 5 * layers
+ * for the output; ~0u: none) makes CTA 0 withhold its arrival at that op's
+ * grid barrier, so the other CTAs' waits run out as they would for a stalled
+ * peer. The decoder launches its step directly afterwards (no graph). 0, or
+ * -1 for a decoder without the persistent step kernel. */
+VBS_API int vbs_cu_decoder_set_wait_test(vbs_cu_decoder_t *d, uint64_t wait_ns, uint32_t drop_op);
+
 /* Enqueue n decode steps on the decoder's stream that feed each step's
  * argmax back as the next token (no host work between steps); returns
  * without synchronising. For timing loops. */

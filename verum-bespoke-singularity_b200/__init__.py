@@ -174,6 +174,7 @@ def lib() -> C.CDLL:
         "vbs_cu_decoder_generate": (i32, [vp, C.POINTER(u32), sz, u32, C.POINTER(u32)]),
         "vbs_cu_decoder_enqueue_steps": (i32, [vp, u32]),
         "vbs_cu_decoder_run_control": (i32, [vp, vp]),
+        "vbs_cu_decoder_set_wait_test": (i32, [vp, u64, u32]),
         "vbs_cu_decoder_set_position": (i32, [vp, u32, u32]),
         "vbs_cu_decoder_position": (u32, [vp]),
         "vbs_cu_decoder_stream": (vp, [vp]),
@@ -425,6 +426,11 @@ class Decoder:
     @property
     def position(self) -> int:
         return int(lib().vbs_cu_decoder_position(self.h))
+
+    def set_wait_test(self, wait_ns: int, drop_op: int = 0xFFFFFFFF) -> None:
+        """Bounded-wait test control: the step kernel's wait limit and an op
+        before whose grid barrier CTA 0 withholds its arrival."""
+        check(lib().vbs_cu_decoder_set_wait_test(self.h, wait_ns, drop_op), "vbs_cu_decoder_set_wait_test")
 
     def enqueue_steps(self, n: int) -> None:
         check(lib().vbs_cu_decoder_enqueue_steps(self.h, n), "vbs_cu_decoder_enqueue_steps")

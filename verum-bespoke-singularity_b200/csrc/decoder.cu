@@ -412,6 +412,8 @@ bool plan_persistent(vbs_cu_decoder *d) {
     p.n_layers = m.n_layers; p.dim = m.dim; p.nqh = m.n_heads; p.nkh = m.n_kv_heads; p.hd = m.head_dim;
     p.ffn = m.ffn; p.vocab = m.vocab; p.max_ctx = d->max_ctx;
     p.eps = m.eps; p.theta = m.theta; p.scale = 1.0f / sqrtf((float)m.head_dim);
+    p.wait_ns = kWaitNs;
+    p.drop_op = ~0u;
     p.t_embd = m.embd_type; p.t_qkv = y0.tq; p.t_o = y0.to; p.t_gu = y0.tgate; p.t_down = y0.tdown; p.t_out = m.out_type;
     p.embd = static_cast<const uint8_t *>(m.embd);
     p.out_norm = m.out_norm;
@@ -861,6 +863,21 @@ int vbs_cu_decoder_run_control(vbs_cu_decoder_t *d, void *control) {
             !sync_and_check(d))
             return -1;
     }
+    return 0;
+}
+
+int vbs_cu_decoder_set_wait_test(vbs_cu_decoder_t *d, uint64_t wait_ns, uint32_t drop_op) {
+    if (!d || d->magic != kDecoderMagic) { latch_error("decoder_set_wait_test: invalid decoder"); return -1; }
+    if (!d->persist) { latch_error("decoder_set_wait_test: the decoder does not run the persistent step kernel"); return -1; }
+    if (wait_ns < 1000000ull || wait_ns > kWaitNs) { latch_error("decoder_set_wait_test: wait limit outside 1 ms .. 2 s"); return -1; }
+    DeviceGuard guard(d->dev->ordinal);
+    if (!cuda_ok(cudaStreamSynchronize(d->st), "decoder_set_wait_test")) return -1;
+    d->sp.wait_ns = wait_ns;
+    d->sp.drop_op = drop_op;
+    // the step graph holds the old parameters: launch directly from now on
+    if (d->exec) { cudaGraphExecDestroy(d->exec); d->exec = nullptr; }
+    if (d->graph) { cudaGraphDestroy(d->graph); d->graph = nullptr; }
+    d->use_graph = false;
     return 0;
 }
 

@@ -228,6 +228,12 @@ struct StepParams {
     // for the logits per step.
     const TpComm *tp;
     uint32_t tp_world, tp_rank, vocab_full;
+    // Bounded waits: every wait of the step gives up after wait_ns of global
+    // time (2 s by default) and records DERR_TIMEOUT_*. A test can shorten
+    // it and name an op (drop_op, else ~0u) before whose grid barrier CTA 0
+    // does not arrive, so the other CTAs' waits run out.
+    uint64_t wait_ns;
+    uint32_t drop_op;
     // Timeline of one step, written only by builds with VBS_STEP_TRACE
     // (a profiling build): per CTA and op, SK_TR_SLOTS %globaltimer stamps.
     unsigned long long *trace;

@@ -42,8 +42,9 @@
 //  * The argmax runs on slices per CTA; the last CTA advances the position
 //    and token in the device control block.
 //
-// Every wait is bounded (2 s of %globaltimer). A timeout sets an abort word
-// that every other wait polls, records the error and unwinds the kernel.
+// Every wait is bounded (p.wait_ns of %globaltimer, 2 s by default). A
+// timeout sets an abort word that every other wait polls, records the error
+// and unwinds the kernel.
 #include "common.cuh"
 #include "kernels.h"
 #include "mv_core.cuh"
@@ -198,13 +199,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
     return v;
 }
 
-// mbarrier phase wait, bounded, giving up early when the grid aborts.
-__device__ __forceinline__ bool sk_wait(uint32_t bar, uint32_t parity, const uint32_t *gabort) {
+// mbarrier phase wait, bounded (p.wait_ns), giving up early when the grid aborts.
+__device__ __forceinline__ bool sk_wait(uint32_t bar, uint32_t parity, const StepParams &p) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63u) == 0 && (*reinterpret_cast<const volatile uint32_t *>(gabort) || global_ns() - t0 > kWaitNs))
+        if ((it & 63u) == 0 && (*reinterpret_cast<const volatile uint32_t *>(p.sync + 1) || global_ns() - t0 > p.wait_ns))
             return false;
     }
 }
@@ -227,17 +228,19 @@ __device__ __forceinline__ void sk_abort(const StepParams &p, uint32_t code) {
 // ordered before it) and the poll an acquire load, with no separate fences:
 // measured 1.6 -> 1.3 us per barrier and a third of the release skew.
 __device__ __forceinline__ bool sk_grid_sync(const StepParams &p, uint32_t target, volatile int *flag,
-                                             volatile int *cta_abort) {
+                                             volatile int *cta_abort, uint32_t op) {
     named_bar_sync(1, SK_CT);
     if (threadIdx.x == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.sync[0]) : "memory");
+        // p.drop_op: a bounded-wait test withholds CTA 0's arrival here
+        if (op != p.drop_op || blockIdx.x != 0)
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.sync[0]) : "memory");
         bool ok = *cta_abort == 0;
         uint64_t t0 = 0;
         for (uint32_t it = 1; ok && ld_acquire_gpu(&p.sync[0]) < target; ++it) {
             if ((it & 63u) == 0) {
                 if (it == 64) t0 = global_ns();
                 if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
-                if (it > 64 && global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
+                if (it > 64 && global_ns() - t0 > p.wait_ns) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
             }
         }
         *flag = ok ? 1 : 0;
@@ -273,7 +276,7 @@ __device__ __forceinline__ void ld_words_sys(const uint64_t *a, uint64_t &x, uin
 // aborted or the wait passed its limit, recording a peer timeout.
 __device__ __noinline__ bool sk_word_give_up(const StepParams &p, uint64_t t0, volatile int *cta_abort) {
     if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { *cta_abort = 1; return true; }
-    if (global_ns() - t0 <= kWaitNs) return false;
+    if (global_ns() - t0 <= p.wait_ns) return false;
     *cta_abort = 1;
     sk_abort(p, DERR_TIMEOUT_PEER);
     return true;
@@ -359,7 +362,7 @@ __device__ __forceinline__ bool sk_reserve(const StepParams &p, const SkSmem &S,
     for (;;) {
         const bool clash = f.held && f.s < o + bytes && o < f.e;
         if (!__any_sync(0xffffffffu, clash) && r.idx - f.tail < SK_NB) return true;
-        if (!sk_wait(S.empty(f.tail), (f.tail / SK_NB) & 1u, p.sync + 1)) {
+        if (!sk_wait(S.empty(f.tail), (f.tail / SK_NB) & 1u, p)) {
             if (lane == 0) sk_abort(p, DERR_TIMEOUT_EMPTY);
             return false;
         }
@@ -431,7 +434,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
     }
     if (!ok) {
         // wait (bounded) for copies still in flight before the CTA may exit
-        for (uint32_t s = f.tail; s < r.idx; ++s) mbar_wait_bounded(S.full(s), (s / SK_NB) & 1u, kWaitNs);
+        for (uint32_t s = f.tail; s < r.idx; ++s) mbar_wait_bounded(S.full(s), (s / SK_NB) & 1u, p.wait_ns);
     }
 }
 
@@ -568,7 +571,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
     const int lane = (int)(ctid & 31u);
     volatile int *cta_abort = S.abort_flag();
     const uint32_t nb = p.dim * 4, ws = S.ring + r.place(nb, S.ring_bytes);
-    const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
+    const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p));
     if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
     static_assert(SK_PB == 2, "the prologue quantizes its two blocks together");
     if (quant && got && q < nsub) {
@@ -642,7 +645,7 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
         sk_unit(d, u, tile, ch);
         // one decision per warp: the MMAs and shuffles below need all 32 lanes
         const uint32_t ms = S.ring + r.place(SB, S.ring_bytes);
-        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
+        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p));
         if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
         float acc[2] = {0.f, 0.f};
         if (got) {
@@ -864,7 +867,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
     for (uint32_t s = 0; s < a.nst; ++s) {
         // one decision per warp: the MMAs and shuffles below need all 32 lanes
         const uint32_t stg = S.ring + r.place(2 * SK_AP * ROWB, S.ring_bytes);
-        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p.sync + 1));
+        const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p));
         if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
         const uint32_t ts = a.t0 + s * SK_AP, tb = ts + 16 * wl;
         if (got && (int)(s & 1) == grp && tb < a.t1) {
@@ -1008,7 +1011,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
             if ((it & 63u) == 0) {
                 if (it == 64) t0 = global_ns();
                 if (*reinterpret_cast<const volatile uint32_t *>(&p.sync[1])) { ok = false; break; }
-                if (it > 64 && global_ns() - t0 > kWaitNs) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
+                if (it > 64 && global_ns() - t0 > p.wait_ns) { sk_abort(p, DERR_TIMEOUT_PEER); ok = false; break; }
             }
         }
         if (!ok) *cta_abort = 1;
@@ -1160,7 +1163,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
                 // the next op only reads exchange words, which it checks one
                 // by one; an abort is taken at the next grid barrier
                 named_bar_sync(1, SK_CT);
-            } else if (!sk_grid_sync(p, (TPX ? ++nsync : i) * gridDim.x, S.sync_flag(), S.abort_flag())) {
+            } else if (!sk_grid_sync(p, (TPX ? ++nsync : i) * gridDim.x, S.sync_flag(), S.abort_flag(), i)) {
                 break;
             }
         }
