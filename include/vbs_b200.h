@@ -310,6 +310,14 @@ typedef struct {
 #define VBS_CU_DEC_WORDS 32u     /* one GPU: run the step kernel's tensor-parallel instance (exchange words in place of
                                     the grid barriers after o_proj and down) over a local area. Same results; slower
                                     on one GPU (every thread polls its words), there to test that instance. */
+#define VBS_CU_DEC_STREAM 64u    /* slice streaming (the reference's slice executor, src/vbs_slice_executor.c:8-107,
+                                    for models above device memory): the per-layer matrices wq..wdown of the model
+                                    description are PINNED HOST pointers (cudaHostAlloc / cudaHostRegister), every
+                                    layer with the first layer's types; embedding, output matrix and norm weights stay
+                                    on the device. Two device slots of one layer each; every step copies each layer
+                                    in (one cudaMemcpyAsync per matrix, its own stream) while the previous layer's
+                                    kernels run. Per-op kernels, one GPU, no strict mode; same results as the same
+                                    model resident with VBS_CU_DEC_NO_PERSIST. */
 
 typedef struct vbs_cu_decoder vbs_cu_decoder_t;
 

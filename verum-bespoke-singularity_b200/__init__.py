@@ -40,6 +40,7 @@ MV_ACCUMULATE, MV_PORTABLE = 1, 2
 DEC_STRICT, DEC_NO_GRAPH, DEC_NO_PDL, DEC_NO_PERSIST = 1, 2, 4, 8
 DEC_TP_NCCL = 16   # tensor parallelism: NCCL all-reduce for the per-layer sums (the reference collective)
 DEC_WORDS = 32     # one GPU: the step kernel's tensor-parallel instance over a local word area (for testing it)
+DEC_STREAM = 64    # slice streaming: per-layer matrices in pinned host memory, copied in per layer (two device slots)
 
 
 class VbsError(RuntimeError):
@@ -312,6 +313,23 @@ class DeviceModel:
         d.vocab_offset = self.tp_rank * (s.vocab // self.tp_world)
         self.desc = d
         return d
+
+
+def streamed_model(model: "DeviceModel") -> "DeviceModel":
+    """The same model with its per-layer matrices moved to pinned host
+    memory, for a VBS_CU_DEC_STREAM decoder (slice streaming); the
+    embedding, output matrix and norm weights stay on the device."""
+    import torch
+    m = DeviceModel(shape=model.shape, types=dict(model.types), tp_rank=model.tp_rank, tp_world=model.tp_world)
+    for name, t in model.tensors.items():
+        if name.startswith("blk.") and not name.endswith("norm"):
+            h = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+            h.copy_(t)
+            m.tensors[name] = h
+        else:
+            m.tensors[name] = t
+    m.make_desc()
+    return m
 
 
 # Per-tensor seeds of synthetic models: a fixed function of the model seed

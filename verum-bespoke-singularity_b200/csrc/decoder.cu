@@ -94,6 +94,17 @@ struct vbs_cu_decoder {
     cudaGraphExec_t exec = nullptr;
     uint32_t kernels_per_step = 0;
     uint64_t host_pos = 0;           // host shadow of ctrl[0] (steps enqueued since the last reset)
+    // slice streaming (VBS_CU_DEC_STREAM): the layers' matrices stay in
+    // pinned host memory (L[l] holds host pointers); each layer is copied
+    // into one of two device slots on its own stream, layer g + 1's copy
+    // overlapping layer g's kernels
+    bool stream = false;
+    cudaStream_t cst = nullptr;              // copy stream
+    uint8_t *slot[2] = {nullptr, nullptr};
+    cudaEvent_t copied[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr};
+    size_t off[7] = {}, slot_bytes = 0;      // per matrix (q k v o gate up down): offset in a slot
+    uint64_t layers_queued = 0;              // layers whose copy has been enqueued
+    uint64_t layers_run = 0;                 // layers whose kernels have been enqueued
     unsigned long long *trace = nullptr;   // step timeline of a VBS_STEP_TRACE profiling build
 };
 
@@ -163,6 +174,62 @@ bool step_matvec(vbs_cu_decoder *d, int type, const uint8_t *w, const float *x, 
                    "decode matvec");
 }
 
+// Bytes of layer matrix k (q k v o gate up down) of a streamed model.
+size_t stream_matrix_bytes(const vbs_cu_decoder *d, const Layer &y, int k) {
+    const vbs_cu_model_t &m = d->m;
+    const uint32_t qd = d->q_dim, kvd = d->kv_dim;
+    switch (k) {
+        case 0: return row_bytes(y.tq, m.dim) * qd;
+        case 1: return row_bytes(y.tk, m.dim) * kvd;
+        case 2: return row_bytes(y.tv, m.dim) * kvd;
+        case 3: return row_bytes(y.to, qd) * m.dim;
+        case 4: return row_bytes(y.tgate, m.dim) * m.ffn;
+        case 5: return row_bytes(y.tup, m.dim) * m.ffn;
+        default: return row_bytes(y.tdown, m.ffn) * m.dim;
+    }
+}
+
+// Enqueues the copy of the next layer (in step order, wrapping to layer 0)
+// into its slot on the copy stream, after the kernels that last read that
+// slot: one cudaMemcpyAsync per matrix, then the slot's `copied` event.
+bool stream_queue_copy(vbs_cu_decoder *d) {
+    const uint64_t g = d->layers_queued;
+    const int sl = (int)(g & 1u);
+    const Layer &y = d->L[g % d->m.n_layers];
+    if (g >= 2 && !cuda_ok(cudaStreamWaitEvent(d->cst, d->done[sl], 0), "stream: slot free")) return false;
+    const uint8_t *src[7] = {y.wq, y.wk, y.wv, y.wo, y.wgate, y.wup, y.wdown};
+    for (int k = 0; k < 7; ++k)
+        if (!cuda_ok(cudaMemcpyAsync(d->slot[sl] + d->off[k], src[k], stream_matrix_bytes(d, y, k), cudaMemcpyHostToDevice,
+                                     d->cst), "stream: layer copy"))
+            return false;
+    if (!cuda_ok(cudaEventRecord(d->copied[sl], d->cst), "stream: copied")) return false;
+    d->layers_queued = g + 1;
+    return true;
+}
+
+// The device view of layer l for the next layer of kernels: waits (on the
+// compute stream) for its copy and queues the copy of the layer after it.
+bool stream_layer(vbs_cu_decoder *d, uint32_t l, Layer &out) {
+    const uint64_t g = d->layers_run;
+    const int sl = (int)(g & 1u);
+    if (d->layers_queued <= g && !stream_queue_copy(d)) return false;
+    if (!cuda_ok(cudaStreamWaitEvent(d->st, d->copied[sl], 0), "stream: wait copy")) return false;
+    out = d->L[l];
+    uint8_t *b = d->slot[sl];
+    out.wq = b + d->off[0]; out.wk = b + d->off[1]; out.wv = b + d->off[2]; out.wo = b + d->off[3];
+    out.wgate = b + d->off[4]; out.wup = b + d->off[5]; out.wdown = b + d->off[6];
+    return true;
+}
+
+// After layer l's kernels: the slot is free once they finish; the next
+// layer's copy goes out now, overlapping them.
+bool stream_layer_done(vbs_cu_decoder *d) {
+    const int sl = (int)(d->layers_run & 1u);
+    if (!cuda_ok(cudaEventRecord(d->done[sl], d->st), "stream: done")) return false;
+    d->layers_run++;
+    return d->layers_queued > d->layers_run || stream_queue_copy(d);
+}
+
 bool enqueue_persistent_step(vbs_cu_decoder *d) {
     // every activation is written once per step; only the barrier and ticket words start at zero
     const size_t sync_bytes = step_sync_words(d->dev->n_sm) * 4;
@@ -186,7 +253,9 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
     const float *pending = nullptr;   // TP over NCCL: partial sum to add into the residual
     bool pending_tp = false;          // TP over peer memory: the exchange to add into the residual
     for (uint32_t l = 0; l < m.n_layers; ++l) {
-        const Layer &ly = d->L[l];
+        Layer streamed;
+        if (d->stream && !stream_layer(d, l, streamed)) return false;
+        const Layer &ly = d->stream ? streamed : d->L[l];
         // ---- 1. norm + QKV + RoPE + KV store ----
         const void *wv[3] = {ly.wq, ly.wk, ly.wv};
         const bool fused = ly.tq == ly.tk && ly.tq == ly.tv && mv_fast_supported(ly.tq, nq + 2 * nk, dim, wv, 3, xr, 0);
@@ -290,6 +359,7 @@ bool enqueue_fast_step(vbs_cu_decoder *d) {
         } else {
             if (!step_matvec(d, ly.tdown, ly.wdown, d->hid, xr, dim, m.ffn, true, nullptr, nullptr, nullptr)) return false;
         }
+        if (d->stream && !stream_layer_done(d)) return false;
     }
     // ---- final norm + output ----
     if (!step_matvec(d, m.out_type, static_cast<const uint8_t *>(m.out), xr, d->logits, m.vocab, dim, false, m.out_norm,
@@ -523,7 +593,9 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
                      "prefill embed"))
             return false;
     for (uint32_t l = 0; l < m.n_layers; ++l) {
-        const Layer &y = d->L[l];
+        Layer streamed;
+        if (d->stream && !stream_layer(d, l, streamed)) return false;
+        const Layer &y = d->stream ? streamed : d->L[l];
         if (!cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.attn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm") ||
             matvec_any(dev, y.tq, y.wq, d->pf_xn, d->pf_q, nq, dim, B, 0, st) ||
             matvec_any(dev, y.tk, y.wk, d->pf_xn, d->pf_k, nk, dim, B, 0, st) ||
@@ -552,6 +624,7 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
             !cuda_ok(silu_mul_launch(d->pf_g, d->pf_u, d->pf_h, B * ffn, st), "prefill silu") ||
             matvec_any(dev, y.tdown, y.wdown, d->pf_h, d->pf_x, dim, ffn, B, VBS_CU_MV_ACCUMULATE, st))
             return false;
+        if (d->stream && !stream_layer_done(d)) return false;
     }
     return true;
 }
@@ -611,8 +684,11 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
     d->m = *m;
     d->flags = flags;
     d->strict = (flags & VBS_CU_DEC_STRICT) != 0;
-    d->use_graph = !(flags & VBS_CU_DEC_NO_GRAPH);
-    d->use_pdl = !(flags & VBS_CU_DEC_NO_PDL) && !d->strict;
+    d->stream = (flags & VBS_CU_DEC_STREAM) != 0;
+    // streamed layers: direct launches around the copy events (no graph, no
+    // programmatic overlap across the event waits)
+    d->use_graph = !(flags & VBS_CU_DEC_NO_GRAPH) && !d->stream;
+    d->use_pdl = !(flags & VBS_CU_DEC_NO_PDL) && !d->strict && !d->stream;
     d->max_ctx = max_ctx;
     d->dev = dev;
     d->kv_dim = m->n_kv_heads * m->head_dim;
@@ -620,6 +696,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
     d->vocab_full = m->vocab_full ? m->vocab_full : m->vocab;
     d->tp_world = tp_world();
     if (d->tp_world > 1 && d->strict) return fail("strict mode runs on one GPU", d);
+    if (d->stream && (d->strict || d->tp_world > 1)) return fail("slice streaming runs the fast per-op step on one GPU", d);
     d->tp_p2p = d->tp_world > 1 && tp_comm() && !(flags & VBS_CU_DEC_TP_NCCL) && m->dim <= TP_DIM_MAX;
     if (d->tp_world == 1 && d->vocab_full != m->vocab) return fail("vocab_full differs from vocab without TP", d);
     if (d->tp_world > 1 && (d->vocab_full != (uint32_t)d->tp_world * m->vocab ||
@@ -652,6 +729,29 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
         if (d->tp_p2p) d->tp_p2p = mv_fast_supported(m->out_type, m->vocab, m->dim, wout, 1, nullptr, 0);
     }
     if (!cuda_ok(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "decoder stream")) return fail("stream", d);
+    if (d->stream) {
+        // matrices of one layer, each 256-byte aligned with 256 zero bytes
+        // after it (the fast kernels may read past a row end); every layer
+        // must have the first layer's types
+        const Layer &y0 = d->L[0];
+        for (const Layer &y : d->L)
+            if (y.tq != y0.tq || y.tk != y0.tk || y.tv != y0.tv || y.to != y0.to || y.tgate != y0.tgate ||
+                y.tup != y0.tup || y.tdown != y0.tdown)
+                return fail("slice streaming: every layer must have the same weight types", d);
+        size_t o = 0;
+        for (int k = 0; k < 7; ++k) {
+            d->off[k] = o;
+            o += (stream_matrix_bytes(d, y0, k) + 256 + 255) & ~(size_t)255;
+        }
+        d->slot_bytes = o;
+        bool sok = cuda_ok(cudaStreamCreateWithFlags(&d->cst, cudaStreamNonBlocking), "copy stream");
+        for (int i = 0; sok && i < 2; ++i)
+            sok = dmalloc((void **)&d->slot[i], d->slot_bytes, "layer slot") &&
+                  cuda_ok(cudaMemset(d->slot[i], 0, d->slot_bytes), "layer slot") &&
+                  cuda_ok(cudaEventCreateWithFlags(&d->copied[i], cudaEventDisableTiming), "event") &&
+                  cuda_ok(cudaEventCreateWithFlags(&d->done[i], cudaEventDisableTiming), "event");
+        if (!sok) return fail("slice streaming buffers", d);
+    }
     const size_t big = std::max<size_t>(std::max<size_t>(m->dim, m->ffn), d->q_dim);
     bool ok = dmalloc((void **)&d->x, m->dim * 4, "x") && dmalloc((void **)&d->x2, m->dim * 4, "x2") &&
               dmalloc((void **)&d->q, d->q_dim * 4, "q") && dmalloc((void **)&d->att, d->q_dim * 4, "att") &&
@@ -669,7 +769,7 @@ vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ct
              dmalloc((void **)&d->xq, big, "xq") && dmalloc((void **)&d->qd, (big / 32 + 1) * 4, "qd");
     } else if (ok) {
         ok = dmalloc((void **)&d->kc, cache_elems * 2, "kv cache") && dmalloc((void **)&d->vc, cache_elems * 2, "kv cache");
-        if (ok && !(flags & VBS_CU_DEC_NO_PERSIST) && (d->tp_world == 1 || d->tp_p2p)) ok = plan_persistent(d);
+        if (ok && !(flags & VBS_CU_DEC_NO_PERSIST) && !d->stream && (d->tp_world == 1 || d->tp_p2p)) ok = plan_persistent(d);
         if (ok) {
             d->n_splits = attn_num_splits(max_ctx, m->n_kv_heads, 1, dev->n_sm);
             const size_t wb = attn_workspace_bytes(m->n_heads, m->n_kv_heads, m->head_dim, 1, d->n_splits);
@@ -713,6 +813,13 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
                     d->pf_g, d->pf_u, d->pf_h, d->pf_attn_work, d->trace};
     for (void *b : bufs)
         if (b) cudaFree(b);
+    if (d->cst) cudaStreamSynchronize(d->cst);
+    for (int i = 0; i < 2; ++i) {
+        if (d->slot[i]) cudaFree(d->slot[i]);
+        if (d->copied[i]) cudaEventDestroy(d->copied[i]);
+        if (d->done[i]) cudaEventDestroy(d->done[i]);
+    }
+    if (d->cst) cudaStreamDestroy(d->cst);
     if (d->pinned) cudaFreeHost(d->pinned);
     if (d->logits_pinned) cudaFreeHost(d->logits_pinned);
     if (d->st) cudaStreamDestroy(d->st);
