@@ -53,11 +53,14 @@ def parse():
                     help="--impl reference: layers of the 8B shape (fewer only to check the JSON contract quickly)")
     ap.add_argument("--profile", default=None,
                     choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep", "prefill",
-                             "upload"],
+                             "upload", "stream"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
     ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
     ap.add_argument("--vocab", type=int, default=128256, help="--profile decode: vocabulary rows")
+    ap.add_argument("--shape", default="8b", choices=["8b", "70b"],
+                    help="--profile decode/timed: the Llama-3-8B mix (BASELINE config 3) or the 70B shape, all Q4_K "
+                         "(config 4)")
     ap.add_argument("--per-op", action="store_true",
                     help="--profile decode: the per-op kernels (one launch per op) instead of the one-launch step")
     return ap.parse_args()
@@ -173,23 +176,67 @@ def profile_kernel(args):
         print(json.dumps({"profile": "prefill", "ctx": args.ctx, "layers": args.layers, "vocab": args.vocab,
                           "per_op": bool(args.per_op), **res}))
         return
-    if args.profile == "decode":
-        # the full decode step at position --ctx (the cache rows before it
-        # are zeros: same bytes and kernels as a prefilled cache), then
-        # --steps graph replays; --layers/--vocab cut the model for a small
-        # ncu case
+    if args.profile == "stream":
+        # slice streaming: the 8B shape's layer matrices in pinned host
+        # memory, copied in layer by layer every step (PCIe-bound), against
+        # the same model resident, per-op kernels, --steps steps each
         import models
         cfg = dict(models.L8B, n_layers=args.layers, vocab=args.vocab)
         model = vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=2024)
+        host = vbs.streamed_model(model)
+        layer_bytes = sum(t.numel() for n, t in host.tensors.items() if n.startswith("blk.0.") and not n.endswith("norm"))
+        res = {}
+        for mode, m, fl in (("streamed", host, vbs.DEC_STREAM), ("resident", model, vbs.DEC_NO_PERSIST)):
+            dec = vbs.Decoder(m, args.ctx + args.steps + 16, fl)
+            dec.forward([1], logits=False)
+            dec.set_position(args.ctx - 1, 1)
+            dec.enqueue_steps(2)
+            torch.cuda.synchronize()
+            s = torch.cuda.ExternalStream(dec.stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            dec.enqueue_steps(args.steps)
+            e1.record(s)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            res[mode] = {"ms_per_step": round(ms, 3), "tok_s": round(1000.0 / ms, 2)}
+            dec.close()
+        gbs = layer_bytes * args.layers / (res["streamed"]["ms_per_step"] * 1e-3) / 1e9
+        print(json.dumps({"profile": "stream", "layers": args.layers, "vocab": args.vocab, "ctx": args.ctx,
+                          "host_bytes_per_step": layer_bytes * args.layers, "h2d_gb_s": round(gbs, 2), **res}))
+        return
+    if args.profile == "decode":
+        # the full decode step at position --ctx (the cache rows before it
+        # are zeros: same bytes and kernels as a prefilled cache), then
+        # --steps graph replays timed with CUDA events; --layers/--vocab cut
+        # the model for a small ncu case; --shape 70b: BASELINE config 4 on
+        # one GPU (39 GB of Q4_K)
+        import models
+        base, types = (models.L70B, models.L70B_TYPES) if args.shape == "70b" else (models.L8B, models.L8B_TYPES)
+        layers = args.layers if args.layers != 32 or args.shape == "8b" else base["n_layers"]
+        cfg = dict(base, n_layers=layers, vocab=args.vocab)
+        model = vbs.synth_llama(models.shape_of(cfg), types, seed=2024)
         dec = vbs.Decoder(model, args.ctx + args.steps + 8, vbs.DEC_NO_PERSIST if args.per_op else 0)
         dec.forward([1], logits=False)
         dec.set_position(args.ctx - 1, 1)
+        dec.enqueue_steps(2)
         torch.cuda.synchronize()
+        s = torch.cuda.ExternalStream(dec.stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
         for i in range(args.steps):
             dec.enqueue_steps(1)
+        e1.record(s)
         torch.cuda.synchronize()
-        print(json.dumps({"profile": "decode", "ctx": args.ctx, "layers": args.layers, "vocab": args.vocab,
-                          "kernels_per_step": dec.kernels_per_step, "steps": args.steps}))
+        ms = e0.elapsed_time(e1) / max(1, args.steps)
+        wbytes = model.weight_bytes() - model.tensors["token_embd"].numel()
+        kv = cfg["n_layers"] * cfg["n_kv_heads"] * (cfg["dim"] // cfg["n_heads"]) * 2 * 2 * (args.ctx + 2)
+        peak, _ = peaks()
+        print(json.dumps({"profile": "decode", "shape": args.shape, "ctx": args.ctx, "layers": cfg["n_layers"],
+                          "vocab": args.vocab, "kernels_per_step": dec.kernels_per_step, "steps": args.steps,
+                          "ms_per_step": round(ms, 4), "tok_s": round(1000.0 / ms, 2),
+                          "bytes_per_step": int(wbytes + kv),
+                          "frac_of_measured": round((wbytes + kv) / (ms * 1e-3) / 1e9 / peak, 4)}))
         dec.close()
         return
     if args.profile == "attention":

@@ -93,7 +93,7 @@ static bool do_init() {
         if (cudaMalloc(&s.err, 256) != cudaSuccess) continue;
         cudaMemset(s.err, 0, 256);
         if (mv_configure() != cudaSuccess || mvb_configure() != cudaSuccess || attn_configure() != cudaSuccess ||
-            step_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
+            step_configure() != cudaSuccess || qgemm_configure() != cudaSuccess) { cudaFree(s.err); s.err = nullptr; continue; }
         vbs_device_t &d = g_devices[g_ndev];
         memset(&d, 0, sizeof(d));
         snprintf(d.name, sizeof(d.name), "%s", pr.name);
@@ -160,6 +160,19 @@ void *attn_workspace(DevState *d, size_t bytes) {
     return d->attn_work;
 }
 
+void *qg_workspace(DevState *d, size_t bytes) {
+    if (d->qg_work_bytes >= bytes) return d->qg_work;
+    if (d->qg_work) {
+        cudaDeviceSynchronize();
+        cudaFree(d->qg_work);
+        d->qg_work = nullptr;
+        d->qg_work_bytes = 0;
+    }
+    if (!cuda_ok(cudaMalloc(&d->qg_work, bytes), "GEMM workspace")) return nullptr;
+    d->qg_work_bytes = bytes;
+    return d->qg_work;
+}
+
 void *mvb_workspace(DevState *d, size_t bytes) {
     if (d->mvb_work_bytes >= bytes) return d->mvb_work;
     if (d->mvb_work) {
@@ -211,6 +224,23 @@ int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y
         p.accumulate = (flags & VBS_CU_MV_ACCUMULATE) ? 1u : 0u;
         p.err = d->err;
         return cuda_ok(mv_fast_launch(type, 0, MV_EPI_STORE, p, d->n_sm, st, false, 0), "matvec launch") ? 0 : -1;
+    }
+    if (batch > 8 && !(flags & VBS_CU_MV_PORTABLE) && qgemm_supported(type, rows, cols, batch) &&
+        !(reinterpret_cast<uintptr_t>(w) & 15)) {
+        // many sequences (prompt chunks, large decode batches): the tcgen05 GEMM
+        QgemmParams p = {};
+        p.w = w;
+        p.rb = row_bytes(type, cols);
+        p.rows = rows;
+        p.cols = cols;
+        p.tokens = batch;
+        p.y = y;
+        p.y_stride = rows;
+        p.accumulate = (flags & VBS_CU_MV_ACCUMULATE) ? 1u : 0u;
+        p.err = d->err;
+        __half *work = static_cast<__half *>(qg_workspace(d, qgemm_workspace_bytes(cols, batch)));
+        if (!work) return -1;
+        return cuda_ok(qgemm_launch(type, p, x, cols, work, d->n_sm, st), "GEMM launch") ? 0 : -1;
     }
     if (batch > 1 && !(flags & VBS_CU_MV_PORTABLE) && mvb_supported(type, rows, cols, batch, w, x)) {
         // batched decode on the tensor cores (mvb.cu)

@@ -17,6 +17,8 @@ struct DevState {
     void *attn_static = nullptr;    // address of the fixed scratch of vbs_cu_attention_static
     void *mvb_work = nullptr;       // chunk planes of the batched matvec
     size_t mvb_work_bytes = 0;
+    void *qg_work = nullptr;        // fp16 copy of X for the tcgen05 GEMM
+    size_t qg_work_bytes = 0;
 };
 
 // Devices usable by this library (sm_100). Index = position in the ops
@@ -39,8 +41,11 @@ bool check_device_error(DevState *d, cudaStream_t st);
 void *attn_workspace(DevState *d, size_t bytes);
 // Grow the device's batched-matvec plane workspace to `bytes`.
 void *mvb_workspace(DevState *d, size_t bytes);
+// Grow the device's GEMM activation workspace to `bytes`.
+void *qg_workspace(DevState *d, size_t bytes);
 // y[b] (+)= W x[b] for b < batch on `st`, through the kernel the shape and
-// type allow (fast, batched tensor-core or portable); flags VBS_CU_MV_*.
+// type allow (fast, batched tensor-core, the tcgen05 GEMM above 8
+// sequences, or portable); flags VBS_CU_MV_*.
 // 0, or -1 with the error latched.
 int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
                uint32_t batch, uint32_t flags, cudaStream_t st);

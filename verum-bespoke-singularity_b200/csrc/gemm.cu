@@ -1,0 +1,282 @@
+// gemm.cu -- quantized-weight GEMM on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in tensor memory), for prompt prefill and
+// batched decode above the batched matvec's 8 sequences.
+//
+//   Y[t][r] (+)= sum_c dequant(W)[r][c] * X[t][c]     t < T tokens, r < N rows
+//
+// The reference has no batched path at all: the engine feeds a prompt one
+// token at a time through forward_token (src/main.c:901-904), every token
+// streaming every weight. Here one CTA owns a tile of 128 weight rows x 128
+// tokens:
+//  * producer warps (128 threads) walk K in steps of 64: thread i dequantizes
+//    row i's 64 weights (the GGUF block decode of src/vbs_dequant.c, rounded
+//    to fp16) and copies token i's 64 activations (fp16, converted once per
+//    call), both into the UMMA canonical K-major layout in shared memory:
+//    8-row x 16-byte core matrices, 128 bytes apart along M/N (SBO), k-chunks
+//    of 8 elements 2 KB apart (LBO);
+//  * one thread issues tcgen05.mma.kind::f16 (M = 128, N = 128, K = 16, four
+//    per stage) into a 128 x 128 fp32 accumulator in tensor memory and
+//    releases each stage with tcgen05.commit on its mbarrier;
+//  * after the last stage the producer warpgroup reads the accumulator back
+//    with tcgen05.ld (warp w owns lanes 32w..32w+31 = rows) and stores Y.
+// Every wait is bounded; a timeout records DERR_TIMEOUT_* and the CTA
+// skips the rest of its tile (tensor memory is always released).
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace vbs {
+
+constexpr int QG_M = 128;            // weight rows per tile (UMMA M)
+constexpr int QG_N = 128;            // tokens per tile (UMMA N)
+constexpr int QG_KT = 64;            // k per stage
+constexpr int QG_NS = 4;             // stages
+constexpr int QG_THREADS = 160;      // 4 producer / epilogue warps + the MMA warp
+constexpr uint32_t QG_A_BYTES = QG_M * QG_KT * 2, QG_B_BYTES = QG_N * QG_KT * 2;
+constexpr uint32_t QG_STAGE = QG_A_BYTES + QG_B_BYTES;
+constexpr uint32_t QG_HDR = 1024;    // barriers + tensor-memory address
+constexpr uint32_t QG_SMEM = QG_HDR + QG_NS * QG_STAGE;
+
+// UMMA shared-memory descriptor, K-major, no swizzle (the canonical layout
+// ((8, m), (8 elements, 2)) : ((16 B, SBO), (2 B, LBO)); addresses and
+// offsets in 16-byte units; version 1 for sm_100).
+__device__ __forceinline__ uint64_t qg_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor of kind::f16: D fp32, A and B fp16, both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t QG_IDESC = (1u << 4) | ((uint32_t)(QG_N >> 3) << 17) | ((uint32_t)(QG_M >> 4) << 24);
+
+__device__ __forceinline__ void qg_mma(uint32_t tmem, uint64_t da, uint64_t db, bool acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(tmem), "l"(da), "l"(db), "r"(QG_IDESC), "r"(acc ? 1u : 0u) : "memory");
+}
+__device__ __forceinline__ void qg_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void qg_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void qg_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void qg_fence_proxy() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 8 consecutive weights e0..e0+7 of one row as fp16x2 words, decoded as
+// src/vbs_dequant.c does (dq_elem) and rounded to fp16.
+template <int TYPE>
+__device__ __forceinline__ uint4 qg_dq8(const uint8_t *row, uint32_t e0) {
+    constexpr int E = TYPE == T_Q8_0 ? 32 : 256, BB = TYPE == T_Q4_K ? 144 : (TYPE == T_Q6_K ? 210 : 34);
+    const uint8_t *blk = row + (uint64_t)(e0 / E) * BB;
+    const uint32_t o = e0 % E;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = dq_elem(TYPE, blk, (int)(o + k));
+    uint4 r;
+    r.x = __half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16);
+    r.y = __half_as_ushort(__float2half_rn(v[2])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[3])) << 16);
+    r.z = __half_as_ushort(__float2half_rn(v[4])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[5])) << 16);
+    r.w = __half_as_ushort(__float2half_rn(v[6])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[7])) << 16);
+    return r;
+}
+
+// Q4_K, the prefill's hot type: row i's 64 weights of one stage are two
+// sub-blocks of one super-block (header and 32 bytes of nibbles), decoded
+// with the reference's operation order ((d*sc)*q - dmin*m, no FMA).
+__device__ __forceinline__ void qg_dq64_q4k(const uint8_t *row, uint32_t k0, uint4 out[8]) {
+    const uint8_t *b = row + (uint64_t)(k0 >> 8) * 144;
+    const uint32_t j0 = (k0 & 255u) >> 5;   // even
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(b));
+    const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(b + 16 + (j0 >> 1) * 32));
+    const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(b + 32 + (j0 >> 1) * 32));
+    const uint8_t *s = reinterpret_cast<const uint8_t *>(&hdr) + 4;
+    int sc[2], mn[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int j = (int)j0 + h;
+        if (j < 4) { sc[h] = s[j] & 63; mn[h] = s[j + 4] & 63; }
+        else { sc[h] = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn[h] = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
+    }
+    const float d = f16_exact(hdr.x & 0xFFFFu), dmin = f16_exact(hdr.x >> 16);
+    const float a0 = __fmul_rn(d, (float)sc[0]), c0 = __fmul_rn(dmin, (float)mn[0]);
+    const float a1 = __fmul_rn(d, (float)sc[1]), c1 = __fmul_rn(dmin, (float)mn[1]);
+    const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    // k 0..31: low nibbles (sub-block j0); k 32..63: high nibbles (j0 + 1)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const bool hi = c >= 4;
+        const float a = hi ? a1 : a0, cc = hi ? c1 : c0;
+        const uint32_t w0 = q[(c & 3) * 2], w1 = q[(c & 3) * 2 + 1];
+        const uint32_t sh = hi ? 4u : 0u;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            v[k] = __fsub_rn(__fmul_rn(a, (float)((w0 >> (8 * k + sh)) & 15u)), cc);
+            v[4 + k] = __fsub_rn(__fmul_rn(a, (float)((w1 >> (8 * k + sh)) & 15u)), cc);
+        }
+        out[c].x = __half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16);
+        out[c].y = __half_as_ushort(__float2half_rn(v[2])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[3])) << 16);
+        out[c].z = __half_as_ushort(__float2half_rn(v[4])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[5])) << 16);
+        out[c].w = __half_as_ushort(__float2half_rn(v[6])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[7])) << 16);
+    }
+}
+
+__device__ __forceinline__ bool qg_wait(uint32_t bar, uint32_t parity) { return mbar_wait_bounded(bar, parity, kWaitNs); }
+
+template <int TYPE>
+__global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t base = smem_u32(smem);
+    const uint32_t full0 = base, empty0 = base + 8 * QG_NS, accb = base + 16 * QG_NS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 512);
+    volatile int *bad = reinterpret_cast<volatile int *>(smem + 520);
+    const uint32_t st0 = base + QG_HDR;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r0 = blockIdx.x * QG_M, t0 = blockIdx.y * QG_N;
+    const uint32_t nk = p.cols / QG_KT;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < QG_NS; ++s) { mbar_init(full0 + 8 * s, 128); mbar_init(empty0 + 8 * s, 1); }
+        mbar_init(accb, 1);
+        *bad = 0;
+        mbar_fence_init();
+    }
+    if (warp == 4) {   // tensor memory: 128 columns of 32-bit accumulators
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(128u) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    qg_fence_before();
+    __syncthreads();
+    qg_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 4) {
+        // ---------------- producers: row i and token i of the tile ----------
+        const uint32_t i = threadIdx.x;
+        const uint32_t row = r0 + i, tok = t0 + i;
+        const uint8_t *wrow = p.w + (uint64_t)min(row, p.rows - 1) * p.rb;
+        const __half *xrow = p.x16 + (uint64_t)tok * p.cols;   // padded to whole tiles of tokens
+        // canonical offsets of row i: core matrix i/8 at SBO = 128 B, row i%8 at 16 B
+        const uint32_t roff = (i >> 3) * 128u + (i & 7u) * 16u;
+        for (uint32_t kt = 0; kt < nk; ++kt) {
+            const uint32_t s = kt % QG_NS;
+            if (kt >= QG_NS && !qg_wait(empty0 + 8 * s, ((kt / QG_NS) - 1) & 1u)) { *bad = 1; break; }
+            if (*bad) break;
+            const uint32_t k0 = kt * QG_KT;
+            const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
+            uint4 wv[8];
+            if (row < p.rows) {
+                if constexpr (TYPE == T_Q4_K) qg_dq64_q4k(wrow, k0, wv);
+                else
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) wv[c] = qg_dq8<TYPE>(wrow, k0 + 8 * c);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) wv[c] = make_uint4(0, 0, 0, 0);
+            }
+            const uint4 *xs = reinterpret_cast<const uint4 *>(xrow + k0);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {   // k-chunk c of 8 elements: LBO = 128 rows x 16 B = 2 KB
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + c * 2048u + roff), "r"(wv[c].x), "r"(wv[c].y),
+                             "r"(wv[c].z), "r"(wv[c].w) : "memory");
+                const uint4 xv = __ldg(xs + c);
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sb + c * 2048u + roff), "r"(xv.x), "r"(xv.y),
+                             "r"(xv.z), "r"(xv.w) : "memory");
+            }
+            qg_fence_proxy();   // the tensor core (async proxy) reads what these generic stores wrote
+            mbar_arrive(full0 + 8 * s);
+        }
+        // ---------------- epilogue: accumulator rows -> Y ------------------
+        const bool ok = !*bad && qg_wait(accb, 0);
+        qg_fence_after();
+        const uint32_t rr = r0 + 32u * warp + lane;
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < QG_N; c0 += 16) {
+            uint32_t v[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                : "r"(tmem + ((32u * warp) << 16) + c0));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (!ok || rr >= p.rows) continue;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t t = t0 + c0 + j;
+                if (t >= p.tokens) break;
+                float *dst = p.y + (uint64_t)t * p.y_stride + rr;
+                const float val = __uint_as_float(v[j]);
+                *dst = p.accumulate ? *dst + val : val;
+            }
+        }
+        if (!ok && lane == 0) dev_flag_error(p.err, DERR_TIMEOUT_FULL);
+    } else if (lane == 0) {
+        // ---------------- MMA issue (one thread) ----------------------------
+        for (uint32_t kt = 0; kt < nk; ++kt) {
+            const uint32_t s = kt % QG_NS;
+            if (!qg_wait(full0 + 8 * s, (kt / QG_NS) & 1u)) { *bad = 1; break; }
+            qg_fence_after();
+            const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < QG_KT / 16; ++ks) {   // K = 16 = two k-chunks per MMA
+                const uint64_t da = qg_desc(sa + ks * 4096u, 2048u, 128u);
+                const uint64_t db = qg_desc(sb + ks * 4096u, 2048u, 128u);
+                qg_mma(tmem, da, db, kt > 0 || ks > 0);
+            }
+            qg_commit(empty0 + 8 * s);   // the stage is free once these MMAs have read it
+        }
+        qg_commit(accb);                 // the accumulator is complete
+    }
+    qg_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        qg_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u) : "memory");
+    }
+}
+
+// fp32 rows [rows x cols] -> fp16 [rows_pad x cols], rows past `rows` zero
+__global__ void qg_to_half_kernel(const float *__restrict__ x, uint64_t xs, __half *__restrict__ out, uint32_t rows,
+                                  uint32_t rows_pad, uint32_t cols) {
+    const uint64_t n = (uint64_t)rows_pad * cols;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(i / cols), c = (uint32_t)(i % cols);
+        out[i] = __float2half_rn(r < rows ? x[(uint64_t)r * xs + c] : 0.0f);
+    }
+}
+
+bool qgemm_supported(int type, uint32_t rows, uint32_t cols, uint32_t tokens) {
+    if (type != T_Q4_K && type != T_Q6_K && type != T_Q8_0) return false;
+    return rows && tokens && cols % QG_KT == 0 && cols % (uint32_t)block_elems(type) == 0;
+}
+
+size_t qgemm_workspace_bytes(uint32_t cols, uint32_t tokens) {
+    return (size_t)((tokens + QG_N - 1) / QG_N) * QG_N * cols * sizeof(__half);
+}
+
+cudaError_t qgemm_configure() {
+    cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(qgemm_kernel<T_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM);
+    return e;
+}
+
+cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, __half *work, int n_sm,
+                         cudaStream_t st) {
+    if (!qgemm_supported(type, p.rows, p.cols, p.tokens) || !work) return cudaErrorInvalidValue;
+    const uint32_t tpad = (p.tokens + QG_N - 1) / QG_N * QG_N;
+    note_launches(2);
+    const uint64_t n = (uint64_t)tpad * p.cols;
+    qg_to_half_kernel<<<(unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 16), 256, 0, st>>>(
+        x, x_stride, work, p.tokens, tpad, p.cols);
+    p.x16 = work;
+    const dim3 grid((p.rows + QG_M - 1) / QG_M, tpad / QG_N);
+    switch (type) {
+        case T_Q4_K: qgemm_kernel<T_Q4_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
+        case T_Q6_K: qgemm_kernel<T_Q6_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
+        default: qgemm_kernel<T_Q8_0><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace vbs

@@ -3,6 +3,7 @@
 // cudaError_t and never synchronises.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stddef.h>
@@ -101,6 +102,24 @@ bool mvb_supported(int type, uint32_t rows, uint32_t cols, uint32_t batch, const
 size_t mvb_workspace_bytes(int type, uint32_t rows, uint32_t cols, uint32_t batch);
 cudaError_t mvb_configure();
 cudaError_t mvb_launch(int type, const MvbParams &p, float *work, int n_sm, cudaStream_t st);
+
+// ---- quantized GEMM on tcgen05 (gemm.cu): Y[t][r] (+)= W[r] . X[t] ----
+struct QgemmParams {
+    const uint8_t *w;           // [rows] packed GGUF rows
+    uint64_t rb;                // packed bytes per row
+    uint32_t rows, cols, tokens;
+    const __half *x16;          // set by the launcher: X in fp16, tokens padded to whole tiles
+    float *y;                   // [tokens][y_stride]
+    uint64_t y_stride;
+    uint32_t accumulate;
+    uint32_t *err;
+};
+bool qgemm_supported(int type, uint32_t rows, uint32_t cols, uint32_t tokens);
+// Device workspace for the fp16 copy of X.
+size_t qgemm_workspace_bytes(uint32_t cols, uint32_t tokens);
+cudaError_t qgemm_configure();
+cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, __half *work, int n_sm,
+                         cudaStream_t st);
 
 // True when the TMA/mma kernel can serve this shape/alignment.
 bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const *w, int nw,
