@@ -337,8 +337,9 @@ VBS_API void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d);
  * copied to logits_out (host, vocab floats; NULL skips the readback). */
 VBS_API int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n_tokens, float *logits_out);
 /* Prompt tokens as context: their KV rows are computed and stored at
- * positions position()..position()+n-1, up to 8 tokens sharing one pass over
- * the weights (batched matvec, causal split-KV attention), no logits. The
+ * positions position()..position()+n-1, up to 128 tokens sharing one pass
+ * over the weights (the tcgen05 GEMM; a last chunk of up to 8 tokens through
+ * the batched matvec; causal split-KV attention), no logits. The
  * next vbs_cu_decoder_forward / generate continues at position()+n; feed
  * the prompt's last token through it to get its logits. The reference feeds
  * prompts one token at a time through forward_token (src/main.c:901-904);

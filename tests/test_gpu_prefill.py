@@ -1,6 +1,6 @@
 """Batched prompt pass (vbs_cu_decoder_prefill) on a B200. The reference
 feeds a prompt one token at a time (src/main.c:901-904); the prefill runs
-up to 8 tokens per pass over the weights and must leave the same KV cache
+up to 128 tokens per pass over the weights (the tcgen05 GEMM) and must leave the same KV cache
 behind, to the kernels' rounding:
 
 * against the oracle fed one token at a time: the logits of the prompt's

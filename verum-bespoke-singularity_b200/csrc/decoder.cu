@@ -30,6 +30,7 @@
 #include "kernels.h"
 #include "tp.h"
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -562,15 +563,21 @@ bool plan_persistent(vbs_cu_decoder *d) {
 // ---------------------------------------------------------------------------
 // prompt chunks: up to PF_CHUNK tokens share one pass over the weights
 // ---------------------------------------------------------------------------
-constexpr uint32_t PF_CHUNK = 8;   // the batched matvec's largest batch
+// Chunks of up to 128 tokens: the matrices go through the tcgen05 GEMM
+// (above 8 tokens) or the batched matvec (the last, short chunk).
+constexpr uint32_t PF_CHUNK = 128;
 
 bool prefill_buffers(vbs_cu_decoder *d) {
     if (d->pf_x) return true;
     const vbs_cu_model_t &m = d->m;
     const size_t B = PF_CHUNK;
-    // the most splits any chunk takes (fewer for larger batches)
+    // the most splits any chunk takes (fewer for larger batches), and the
+    // largest split workspace over the chunk sizes a prompt can end with
     d->pf_splits = attn_num_splits(d->max_ctx, m.n_kv_heads, 1, d->dev->n_sm);
-    const size_t aw = attn_workspace_bytes(m.n_heads, m.n_kv_heads, m.head_dim, PF_CHUNK, d->pf_splits);
+    size_t aw = 0;
+    for (uint32_t b = 1; b <= PF_CHUNK; ++b)
+        aw = std::max(aw, attn_workspace_bytes(m.n_heads, m.n_kv_heads, m.head_dim, b,
+                                               std::min(d->pf_splits, attn_num_splits(d->max_ctx, m.n_kv_heads, b, d->dev->n_sm))));
     return dmalloc((void **)&d->pf_x, B * m.dim * 4, "prefill rows") && dmalloc((void **)&d->pf_xn, B * m.dim * 4, "prefill rows") &&
            dmalloc((void **)&d->pf_q, B * d->q_dim * 4, "prefill rows") && dmalloc((void **)&d->pf_att, B * d->q_dim * 4, "prefill rows") &&
            dmalloc((void **)&d->pf_k, B * d->kv_dim * 4, "prefill rows") && dmalloc((void **)&d->pf_v, B * d->kv_dim * 4, "prefill rows") &&
