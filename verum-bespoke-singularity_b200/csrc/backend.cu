@@ -238,7 +238,7 @@ int matvec_any(DevState *d, int type, const uint8_t *w, const float *x, float *y
         p.y_stride = rows;
         p.accumulate = (flags & VBS_CU_MV_ACCUMULATE) ? 1u : 0u;
         p.err = d->err;
-        __half *work = static_cast<__half *>(qg_workspace(d, qgemm_workspace_bytes(cols, batch)));
+        void *work = qg_workspace(d, qgemm_workspace_bytes(rows, cols, batch, d->n_sm));
         if (!work) return -1;
         return cuda_ok(qgemm_launch(type, p, x, cols, work, d->n_sm, st), "GEMM launch") ? 0 : -1;
     }

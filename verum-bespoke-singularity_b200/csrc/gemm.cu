@@ -121,6 +121,41 @@ __device__ __forceinline__ void qg_dq64_q4k(const uint8_t *row, uint32_t k0, uin
     }
 }
 
+// Q6_K: the 64 weights of stage chunk c (0..3) of a super-block are half
+// h = c / 2, quarters q0 = 2 (c % 2) and q0 + 1: low bits from ql[64 h + 32 (q & 1)
+// + l], high bits from qh[32 h + l], scale byte (e / 16), as
+// src/vbs_dequant.c:316-333 ((d * sc) * (q - 32)). GGUF Q6_K blocks are only
+// 2-byte aligned, so the bytes come in 16-bit loads.
+__device__ __forceinline__ void qg_dq64_q6k(const uint8_t *row, uint32_t k0, uint4 out[8]) {
+    const uint8_t *b = row + (uint64_t)(k0 >> 8) * 210;
+    const uint32_t c = (k0 & 255u) >> 6, h = c >> 1, q0 = 2u * (c & 1u);
+    const unsigned short *ql = reinterpret_cast<const unsigned short *>(b + 64 * h);
+    const unsigned short *qh = reinterpret_cast<const unsigned short *>(b + 128 + 32 * h);
+    const unsigned short *scp = reinterpret_cast<const unsigned short *>(b + 192 + 4 * c);
+    const float d = f16_exact(__ldg(reinterpret_cast<const unsigned short *>(b + 208)));
+    const uint32_t s01 = __ldg(scp), s23 = __ldg(scp + 1);
+    const int scv[4] = {(int)(int8_t)(s01 & 255u), (int)(int8_t)(s01 >> 8), (int)(int8_t)(s23 & 255u), (int)(int8_t)(s23 >> 8)};
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {            // 8 elements i = 8 cc .. 8 cc + 7 of the 64
+        const uint32_t q = q0 + (uint32_t)(cc >> 2), l0 = (uint32_t)(cc & 3) * 8;
+        const float ds = __fmul_rn(d, (float)scv[cc >> 1]);   // element 8 cc + j: scale byte (64 c + 8 cc) / 16
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const uint32_t lw = __ldg(ql + (((q & 1u) * 32u + l0 + j) >> 1)), hw = __ldg(qh + ((l0 + j) >> 1));
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const uint32_t lo = ((lw >> (8 * t)) >> ((q >> 1) * 4)) & 15u, hi = ((hw >> (8 * t)) >> (q * 2)) & 3u;
+                v[j + t] = __fmul_rn(ds, (float)((int)(lo | (hi << 4)) - 32));
+            }
+        }
+        out[cc].x = __half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16);
+        out[cc].y = __half_as_ushort(__float2half_rn(v[2])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[3])) << 16);
+        out[cc].z = __half_as_ushort(__float2half_rn(v[4])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[5])) << 16);
+        out[cc].w = __half_as_ushort(__float2half_rn(v[6])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[7])) << 16);
+    }
+}
+
 __device__ __forceinline__ bool qg_wait(uint32_t bar, uint32_t parity) { return mbar_wait_bounded(bar, parity, kWaitNs); }
 
 template <int TYPE>
@@ -133,7 +168,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     const uint32_t st0 = base + QG_HDR;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t r0 = blockIdx.x * QG_M, t0 = blockIdx.y * QG_N;
-    const uint32_t nk = p.cols / QG_KT;
+    // split-K: this CTA's stages [kb, kb + nk) of the row's K / 64
+    const uint32_t nk_all = p.cols / QG_KT, per = (nk_all + gridDim.z - 1) / gridDim.z;
+    const uint32_t kb = min(nk_all, blockIdx.z * per), nk = min(nk_all, kb + per) - kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < QG_NS; ++s) { mbar_init(full0 + 8 * s, 128); mbar_init(empty0 + 8 * s, 1); }
@@ -162,11 +199,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
             const uint32_t s = kt % QG_NS;
             if (kt >= QG_NS && !qg_wait(empty0 + 8 * s, ((kt / QG_NS) - 1) & 1u)) { *bad = 1; break; }
             if (*bad) break;
-            const uint32_t k0 = kt * QG_KT;
+            const uint32_t k0 = (kb + kt) * QG_KT;
             const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
             uint4 wv[8];
             if (row < p.rows) {
                 if constexpr (TYPE == T_Q4_K) qg_dq64_q4k(wrow, k0, wv);
+                else if constexpr (TYPE == T_Q6_K) qg_dq64_q6k(wrow, k0, wv);
                 else
 #pragma unroll
                     for (int c = 0; c < 8; ++c) wv[c] = qg_dq8<TYPE>(wrow, k0 + 8 * c);
@@ -204,9 +242,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
             for (int j = 0; j < 16; ++j) {
                 const uint32_t t = t0 + c0 + j;
                 if (t >= p.tokens) break;
-                float *dst = p.y + (uint64_t)t * p.y_stride + rr;
-                const float val = __uint_as_float(v[j]);
-                *dst = p.accumulate ? *dst + val : val;
+                const float val = nk ? __uint_as_float(v[j]) : 0.0f;
+                if (gridDim.z > 1) {   // split-K: this split's plane, summed in split order by qg_reduce_kernel
+                    p.planes[((uint64_t)blockIdx.z * p.tokens + t) * p.rows + rr] = val;
+                } else {
+                    float *dst = p.y + (uint64_t)t * p.y_stride + rr;
+                    *dst = p.accumulate ? *dst + val : val;
+                }
             }
         }
         if (!ok && lane == 0) dev_flag_error(p.err, DERR_TIMEOUT_FULL);
@@ -225,13 +267,26 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
             }
             qg_commit(empty0 + 8 * s);   // the stage is free once these MMAs have read it
         }
-        qg_commit(accb);                 // the accumulator is complete
+        qg_commit(accb);                 // the accumulator is complete (no stage: nothing to wait for)
     }
     qg_fence_before();
     __syncthreads();
     if (warp == 4) {
         qg_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u) : "memory");
+    }
+}
+
+// Split-K: Y[t][r] (+)= sum over splits z in order of planes[z][t][r].
+__global__ void qg_reduce_kernel(const float *__restrict__ planes, uint32_t nz, uint32_t tokens, uint32_t rows,
+                                 float *__restrict__ y, uint64_t ys, uint32_t accumulate) {
+    const uint64_t n = (uint64_t)tokens * rows;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        float v = planes[i];
+        for (uint32_t z = 1; z < nz; ++z) v += planes[(uint64_t)z * n + i];
+        const uint32_t t = (uint32_t)(i / rows), r = (uint32_t)(i % rows);
+        float *dst = y + (uint64_t)t * ys + r;
+        *dst = accumulate ? *dst + v : v;
     }
 }
 
@@ -250,8 +305,18 @@ bool qgemm_supported(int type, uint32_t rows, uint32_t cols, uint32_t tokens) {
     return rows && tokens && cols % QG_KT == 0 && cols % (uint32_t)block_elems(type) == 0;
 }
 
-size_t qgemm_workspace_bytes(uint32_t cols, uint32_t tokens) {
-    return (size_t)((tokens + QG_N - 1) / QG_N) * QG_N * cols * sizeof(__half);
+// K splits for a grid of `tiles` output tiles: enough CTAs to cover the
+// SMs, at least 8 stages of 64 per split.
+static uint32_t qg_splits(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm) {
+    const uint32_t tiles = ((rows + QG_M - 1) / QG_M) * ((tokens + QG_N - 1) / QG_N);
+    uint32_t z = std::max(1u, (uint32_t)n_sm / std::max(1u, tiles));
+    return std::max(1u, std::min(z, cols / QG_KT / 8u));
+}
+
+size_t qgemm_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm) {
+    const size_t x16 = ((size_t)((tokens + QG_N - 1) / QG_N) * QG_N * cols * sizeof(__half) + 255) & ~(size_t)255;
+    const uint32_t z = qg_splits(rows, cols, tokens, n_sm);
+    return x16 + (z > 1 ? (size_t)z * tokens * rows * sizeof(float) : 0);
 }
 
 cudaError_t qgemm_configure() {
@@ -261,20 +326,28 @@ cudaError_t qgemm_configure() {
     return e;
 }
 
-cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, __half *work, int n_sm,
+cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, void *work, int n_sm,
                          cudaStream_t st) {
     if (!qgemm_supported(type, p.rows, p.cols, p.tokens) || !work) return cudaErrorInvalidValue;
     const uint32_t tpad = (p.tokens + QG_N - 1) / QG_N * QG_N;
-    note_launches(2);
+    const uint32_t z = qg_splits(p.rows, p.cols, p.tokens, n_sm);
+    note_launches(z > 1 ? 3 : 2);
     const uint64_t n = (uint64_t)tpad * p.cols;
+    __half *x16 = static_cast<__half *>(work);
     qg_to_half_kernel<<<(unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 16), 256, 0, st>>>(
-        x, x_stride, work, p.tokens, tpad, p.cols);
-    p.x16 = work;
-    const dim3 grid((p.rows + QG_M - 1) / QG_M, tpad / QG_N);
+        x, x_stride, x16, p.tokens, tpad, p.cols);
+    p.x16 = x16;
+    p.planes = reinterpret_cast<float *>(static_cast<uint8_t *>(work) + ((n * sizeof(__half) + 255) & ~(size_t)255));
+    const dim3 grid((p.rows + QG_M - 1) / QG_M, tpad / QG_N, z);
     switch (type) {
         case T_Q4_K: qgemm_kernel<T_Q4_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
         case T_Q6_K: qgemm_kernel<T_Q6_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
         default: qgemm_kernel<T_Q8_0><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
+    }
+    if (z > 1) {
+        const uint64_t m = (uint64_t)p.tokens * p.rows;
+        qg_reduce_kernel<<<(unsigned)std::min<uint64_t>((m + 255) / 256, (uint64_t)n_sm * 8), 256, 0, st>>>(
+            p.planes, z, p.tokens, p.rows, p.y, p.y_stride, p.accumulate);
     }
     return cudaGetLastError();
 }

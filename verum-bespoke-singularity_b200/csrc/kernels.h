@@ -109,16 +109,17 @@ struct QgemmParams {
     uint64_t rb;                // packed bytes per row
     uint32_t rows, cols, tokens;
     const __half *x16;          // set by the launcher: X in fp16, tokens padded to whole tiles
+    float *planes;              // set by the launcher: split-K partial planes [split][tokens][rows]
     float *y;                   // [tokens][y_stride]
     uint64_t y_stride;
     uint32_t accumulate;
     uint32_t *err;
 };
 bool qgemm_supported(int type, uint32_t rows, uint32_t cols, uint32_t tokens);
-// Device workspace for the fp16 copy of X.
-size_t qgemm_workspace_bytes(uint32_t cols, uint32_t tokens);
+// Device workspace: the fp16 copy of X, then the split-K planes.
+size_t qgemm_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm);
 cudaError_t qgemm_configure();
-cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, __half *work, int n_sm,
+cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, void *work, int n_sm,
                          cudaStream_t st);
 
 // True when the TMA/mma kernel can serve this shape/alignment.
