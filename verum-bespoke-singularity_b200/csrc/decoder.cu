@@ -563,9 +563,10 @@ bool plan_persistent(vbs_cu_decoder *d) {
 // ---------------------------------------------------------------------------
 // prompt chunks: up to PF_CHUNK tokens share one pass over the weights
 // ---------------------------------------------------------------------------
-// Chunks of up to 128 tokens: the matrices go through the tcgen05 GEMM
-// (above 8 tokens) or the batched matvec (the last, short chunk).
-constexpr uint32_t PF_CHUNK = 128;
+// Chunks of up to 256 tokens (one GEMM tile of tokens): the matrices go
+// through the tcgen05 GEMM (above 8 tokens) or the batched matvec (the
+// last, short chunk).
+constexpr uint32_t PF_CHUNK = 256;
 
 bool prefill_buffers(vbs_cu_decoder *d) {
     if (d->pf_x) return true;
@@ -594,11 +595,10 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
     const uint32_t dim = m.dim, nq = d->q_dim, nk = d->kv_dim, ffn = m.ffn, hd = m.head_dim;
     const int layout = d->persist ? 2 : 1;   // the cache layout of the decoder's steps
     DevState *dev = d->dev;
-    for (uint32_t b = 0; b < B; ++b)
-        if (!cuda_ok(embed_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), tok + b, 0, d->vocab_full,
-                                  d->pf_x + (size_t)b * dim, dim, dev->err, st, false),
-                     "prefill embed"))
-            return false;
+    if (!cuda_ok(embed_rows_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), tok, B, d->vocab_full, d->pf_x, dim,
+                                   dev->err, st),
+                 "prefill embed"))
+        return false;
     for (uint32_t l = 0; l < m.n_layers; ++l) {
         Layer streamed;
         if (d->stream && !stream_layer(d, l, streamed)) return false;

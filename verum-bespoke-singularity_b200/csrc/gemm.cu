@@ -6,19 +6,21 @@
 //
 // The reference has no batched path at all: the engine feeds a prompt one
 // token at a time through forward_token (src/main.c:901-904), every token
-// streaming every weight. Here one CTA owns a tile of 128 weight rows x 128
+// streaming every weight. Here one CTA owns a tile of 128 weight rows x 256
 // tokens:
-//  * producer warps (128 threads) walk K in steps of 64: thread i dequantizes
-//    row i's 64 weights (the GGUF block decode of src/vbs_dequant.c, rounded
-//    to fp16) and copies token i's 64 activations (fp16, converted once per
-//    call), both into the UMMA canonical K-major layout in shared memory:
-//    8-row x 16-byte core matrices, 128 bytes apart along M/N (SBO), k-chunks
-//    of 8 elements 2 KB apart (LBO);
-//  * one thread issues tcgen05.mma.kind::f16 (M = 128, N = 128, K = 16, four
-//    per stage) into a 128 x 128 fp32 accumulator in tensor memory and
+//  * producer warps (256 threads) walk K in steps of 64: threads 2r and
+//    2r + 1 dequantize row r's 64 weights, 32 each (the GGUF block decode of
+//    src/vbs_dequant.c, rounded to fp16), and thread i copies token i's 64
+//    activations (fp16, converted once per call), all into the UMMA
+//    canonical K-major layout in shared memory: 8-row x 16-byte core
+//    matrices 128 bytes apart along M/N (SBO), k-chunks of 8 elements one
+//    operand-height x 16 bytes apart (LBO);
+//  * one thread issues tcgen05.mma.kind::f16 (M = 128, N = 256, K = 16, four
+//    per stage) into a 128 x 256 fp32 accumulator in tensor memory and
 //    releases each stage with tcgen05.commit on its mbarrier;
-//  * after the last stage the producer warpgroup reads the accumulator back
-//    with tcgen05.ld (warp w owns lanes 32w..32w+31 = rows) and stores Y.
+//  * after the last stage the producer warps read the accumulator back with
+//    tcgen05.ld (warp w: lanes 32 (w % 4).. = rows, columns 128 (w / 4).. =
+//    tokens) and store Y (split-K: a plane per split, summed in order).
 // Every wait is bounded; a timeout records DERR_TIMEOUT_* and the CTA
 // skips the rest of its tile (tensor memory is always released).
 #include "common.cuh"
@@ -29,10 +31,11 @@
 namespace vbs {
 
 constexpr int QG_M = 128;            // weight rows per tile (UMMA M)
-constexpr int QG_N = 128;            // tokens per tile (UMMA N)
+constexpr int QG_N = 256;            // tokens per tile (UMMA N)
 constexpr int QG_KT = 64;            // k per stage
 constexpr int QG_NS = 4;             // stages
-constexpr int QG_THREADS = 160;      // 4 producer / epilogue warps + the MMA warp
+constexpr int QG_PT = 256;           // producer / epilogue threads
+constexpr int QG_THREADS = QG_PT + 32;   // + the MMA warp
 constexpr uint32_t QG_A_BYTES = QG_M * QG_KT * 2, QG_B_BYTES = QG_N * QG_KT * 2;
 constexpr uint32_t QG_STAGE = QG_A_BYTES + QG_B_BYTES;
 constexpr uint32_t QG_HDR = 1024;    // barriers + tensor-memory address
@@ -80,44 +83,38 @@ __device__ __forceinline__ uint4 qg_dq8(const uint8_t *row, uint32_t e0) {
     return r;
 }
 
-// Q4_K, the prefill's hot type: row i's 64 weights of one stage are two
-// sub-blocks of one super-block (header and 32 bytes of nibbles), decoded
-// with the reference's operation order ((d*sc)*q - dmin*m, no FMA).
-__device__ __forceinline__ void qg_dq64_q4k(const uint8_t *row, uint32_t k0, uint4 out[8]) {
+__device__ __forceinline__ uint32_t qg_h2(float a, float b) {
+    return __half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+
+// Q4_K, the prefill's hot type: the 64 weights of a stage are sub-blocks j0
+// and j0 + 1 of one super-block (the low and the high nibbles of the same 32
+// bytes); `half` picks one, decoded with the reference's operation order
+// ((d*sc)*q - dmin*m, no FMA).
+__device__ __forceinline__ void qg_dq32_q4k(const uint8_t *row, uint32_t k0, uint32_t half, uint4 out[4]) {
     const uint8_t *b = row + (uint64_t)(k0 >> 8) * 144;
-    const uint32_t j0 = (k0 & 255u) >> 5;   // even
+    const uint32_t j0 = (k0 & 255u) >> 5, j = j0 + half;   // j0 even
     const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(b));
     const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(b + 16 + (j0 >> 1) * 32));
     const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(b + 32 + (j0 >> 1) * 32));
     const uint8_t *s = reinterpret_cast<const uint8_t *>(&hdr) + 4;
-    int sc[2], mn[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int j = (int)j0 + h;
-        if (j < 4) { sc[h] = s[j] & 63; mn[h] = s[j + 4] & 63; }
-        else { sc[h] = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn[h] = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
-    }
+    int sc, mn;
+    if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
+    else { sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
     const float d = f16_exact(hdr.x & 0xFFFFu), dmin = f16_exact(hdr.x >> 16);
-    const float a0 = __fmul_rn(d, (float)sc[0]), c0 = __fmul_rn(dmin, (float)mn[0]);
-    const float a1 = __fmul_rn(d, (float)sc[1]), c1 = __fmul_rn(dmin, (float)mn[1]);
+    const float a = __fmul_rn(d, (float)sc), c = __fmul_rn(dmin, (float)mn);
     const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    // k 0..31: low nibbles (sub-block j0); k 32..63: high nibbles (j0 + 1)
+    const uint32_t sh = half ? 4u : 0u;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const bool hi = c >= 4;
-        const float a = hi ? a1 : a0, cc = hi ? c1 : c0;
-        const uint32_t w0 = q[(c & 3) * 2], w1 = q[(c & 3) * 2 + 1];
-        const uint32_t sh = hi ? 4u : 0u;
+    for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t w0 = q[2 * cc], w1 = q[2 * cc + 1];
         float v[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            v[k] = __fsub_rn(__fmul_rn(a, (float)((w0 >> (8 * k + sh)) & 15u)), cc);
-            v[4 + k] = __fsub_rn(__fmul_rn(a, (float)((w1 >> (8 * k + sh)) & 15u)), cc);
+            v[k] = __fsub_rn(__fmul_rn(a, (float)((w0 >> (8 * k + sh)) & 15u)), c);
+            v[4 + k] = __fsub_rn(__fmul_rn(a, (float)((w1 >> (8 * k + sh)) & 15u)), c);
         }
-        out[c].x = __half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16);
-        out[c].y = __half_as_ushort(__float2half_rn(v[2])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[3])) << 16);
-        out[c].z = __half_as_ushort(__float2half_rn(v[4])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[5])) << 16);
-        out[c].w = __half_as_ushort(__float2half_rn(v[6])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[7])) << 16);
+        out[cc] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
     }
 }
 
@@ -126,7 +123,7 @@ __device__ __forceinline__ void qg_dq64_q4k(const uint8_t *row, uint32_t k0, uin
 // + l], high bits from qh[32 h + l], scale byte (e / 16), as
 // src/vbs_dequant.c:316-333 ((d * sc) * (q - 32)). GGUF Q6_K blocks are only
 // 2-byte aligned, so the bytes come in 16-bit loads.
-__device__ __forceinline__ void qg_dq64_q6k(const uint8_t *row, uint32_t k0, uint4 out[8]) {
+__device__ __forceinline__ void qg_dq32_q6k(const uint8_t *row, uint32_t k0, uint32_t half, uint4 out[4]) {
     const uint8_t *b = row + (uint64_t)(k0 >> 8) * 210;
     const uint32_t c = (k0 & 255u) >> 6, h = c >> 1, q0 = 2u * (c & 1u);
     const unsigned short *ql = reinterpret_cast<const unsigned short *>(b + 64 * h);
@@ -136,7 +133,8 @@ __device__ __forceinline__ void qg_dq64_q6k(const uint8_t *row, uint32_t k0, uin
     const uint32_t s01 = __ldg(scp), s23 = __ldg(scp + 1);
     const int scv[4] = {(int)(int8_t)(s01 & 255u), (int)(int8_t)(s01 >> 8), (int)(int8_t)(s23 & 255u), (int)(int8_t)(s23 >> 8)};
 #pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {            // 8 elements i = 8 cc .. 8 cc + 7 of the 64
+    for (int c4 = 0; c4 < 4; ++c4) {            // 8 elements i = 8 cc .. 8 cc + 7 of the 64
+        const int cc = c4 + 4 * (int)half;
         const uint32_t q = q0 + (uint32_t)(cc >> 2), l0 = (uint32_t)(cc & 3) * 8;
         const float ds = __fmul_rn(d, (float)scv[cc >> 1]);   // element 8 cc + j: scale byte (64 c + 8 cc) / 16
         float v[8];
@@ -149,10 +147,7 @@ __device__ __forceinline__ void qg_dq64_q6k(const uint8_t *row, uint32_t k0, uin
                 v[j + t] = __fmul_rn(ds, (float)((int)(lo | (hi << 4)) - 32));
             }
         }
-        out[cc].x = __half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16);
-        out[cc].y = __half_as_ushort(__float2half_rn(v[2])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[3])) << 16);
-        out[cc].z = __half_as_ushort(__float2half_rn(v[4])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[5])) << 16);
-        out[cc].w = __half_as_ushort(__float2half_rn(v[6])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[7])) << 16);
+        out[c4] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
     }
 }
 
@@ -173,13 +168,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     const uint32_t kb = min(nk_all, blockIdx.z * per), nk = min(nk_all, kb + per) - kb;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < QG_NS; ++s) { mbar_init(full0 + 8 * s, 128); mbar_init(empty0 + 8 * s, 1); }
+        for (int s = 0; s < QG_NS; ++s) { mbar_init(full0 + 8 * s, QG_PT); mbar_init(empty0 + 8 * s, 1); }
         mbar_init(accb, 1);
         *bad = 0;
         mbar_fence_init();
     }
-    if (warp == 4) {   // tensor memory: 128 columns of 32-bit accumulators
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(128u) : "memory");
+    if (warp == QG_PT / 32) {   // tensor memory: QG_N columns of 32-bit accumulators
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)QG_N) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     qg_fence_before();
@@ -187,38 +182,42 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     qg_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {
-        // ---------------- producers: row i and token i of the tile ----------
-        const uint32_t i = threadIdx.x;
-        const uint32_t row = r0 + i, tok = t0 + i;
+    if (warp < QG_PT / 32) {
+        // ------- producers: half `wh` of weight row wr, and token i -------
+        const uint32_t i = threadIdx.x, wr = i >> 1, wh = i & 1u;
+        const uint32_t row = r0 + wr, tok = t0 + i;
         const uint8_t *wrow = p.w + (uint64_t)min(row, p.rows - 1) * p.rb;
         const __half *xrow = p.x16 + (uint64_t)tok * p.cols;   // padded to whole tiles of tokens
-        // canonical offsets of row i: core matrix i/8 at SBO = 128 B, row i%8 at 16 B
-        const uint32_t roff = (i >> 3) * 128u + (i & 7u) * 16u;
+        // canonical offsets: core matrix r/8 at SBO = 128 B, row r%8 at 16 B
+        const uint32_t aoff = (wr >> 3) * 128u + (wr & 7u) * 16u, boff = (i >> 3) * 128u + (i & 7u) * 16u;
         for (uint32_t kt = 0; kt < nk; ++kt) {
             const uint32_t s = kt % QG_NS;
             if (kt >= QG_NS && !qg_wait(empty0 + 8 * s, ((kt / QG_NS) - 1) & 1u)) { *bad = 1; break; }
             if (*bad) break;
             const uint32_t k0 = (kb + kt) * QG_KT;
             const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
-            uint4 wv[8];
+            uint4 wv[4];
             if (row < p.rows) {
-                if constexpr (TYPE == T_Q4_K) qg_dq64_q4k(wrow, k0, wv);
-                else if constexpr (TYPE == T_Q6_K) qg_dq64_q6k(wrow, k0, wv);
+                if constexpr (TYPE == T_Q4_K) qg_dq32_q4k(wrow, k0, wh, wv);
+                else if constexpr (TYPE == T_Q6_K) qg_dq32_q6k(wrow, k0, wh, wv);
                 else
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) wv[c] = qg_dq8<TYPE>(wrow, k0 + 8 * c);
+                    for (int c = 0; c < 4; ++c) wv[c] = qg_dq8<TYPE>(wrow, k0 + 32 * wh + 8 * c);
             } else {
 #pragma unroll
-                for (int c = 0; c < 8; ++c) wv[c] = make_uint4(0, 0, 0, 0);
+                for (int c = 0; c < 4; ++c) wv[c] = make_uint4(0, 0, 0, 0);
             }
+            // A: k-chunks 4 wh .. 4 wh + 3 of row wr, LBO = 128 rows x 16 B
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + (4 * wh + c) * (QG_M * 16u) + aoff),
+                             "r"(wv[c].x), "r"(wv[c].y), "r"(wv[c].z), "r"(wv[c].w) : "memory");
+            // B: all 8 k-chunks of token i, LBO = 256 tokens x 16 B
             const uint4 *xs = reinterpret_cast<const uint4 *>(xrow + k0);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {   // k-chunk c of 8 elements: LBO = 128 rows x 16 B = 2 KB
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + c * 2048u + roff), "r"(wv[c].x), "r"(wv[c].y),
-                             "r"(wv[c].z), "r"(wv[c].w) : "memory");
+            for (int c = 0; c < 8; ++c) {
                 const uint4 xv = __ldg(xs + c);
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sb + c * 2048u + roff), "r"(xv.x), "r"(xv.y),
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sb + c * (QG_N * 16u) + boff), "r"(xv.x), "r"(xv.y),
                              "r"(xv.z), "r"(xv.w) : "memory");
             }
             qg_fence_proxy();   // the tensor core (async proxy) reads what these generic stores wrote
@@ -227,15 +226,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         // ---------------- epilogue: accumulator rows -> Y ------------------
         const bool ok = !*bad && qg_wait(accb, 0);
         qg_fence_after();
-        const uint32_t rr = r0 + 32u * warp + lane;
+        const uint32_t rr = r0 + 32u * (warp & 3) + lane;
 #pragma unroll 1
-        for (uint32_t c0 = 0; c0 < QG_N; c0 += 16) {
+        for (uint32_t c0 = (warp >> 2) * (QG_N / 2); c0 < (warp >> 2) * (QG_N / 2) + QG_N / 2; c0 += 16) {
             uint32_t v[16];
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-                : "r"(tmem + ((32u * warp) << 16) + c0));
+                : "r"(tmem + ((32u * (warp & 3)) << 16) + c0));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             if (!ok || rr >= p.rows) continue;
 #pragma unroll
@@ -261,8 +260,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
             const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
 #pragma unroll
             for (int ks = 0; ks < QG_KT / 16; ++ks) {   // K = 16 = two k-chunks per MMA
-                const uint64_t da = qg_desc(sa + ks * 4096u, 2048u, 128u);
-                const uint64_t db = qg_desc(sb + ks * 4096u, 2048u, 128u);
+                const uint64_t da = qg_desc(sa + ks * (2 * QG_M * 16u), QG_M * 16u, 128u);
+                const uint64_t db = qg_desc(sb + ks * (2 * QG_N * 16u), QG_N * 16u, 128u);
                 qg_mma(tmem, da, db, kt > 0 || ks > 0);
             }
             qg_commit(empty0 + 8 * s);   // the stage is free once these MMAs have read it
@@ -271,9 +270,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     }
     qg_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == QG_PT / 32) {
         qg_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)QG_N) : "memory");
     }
 }
 

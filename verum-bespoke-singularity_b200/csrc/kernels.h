@@ -145,6 +145,9 @@ cudaError_t dequant_launch(int type, const uint8_t *w, float *out, uint64_t n_el
 // and writes zeros.
 cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, uint32_t token, uint32_t rows,
                          float *out, uint32_t dim, uint32_t *err, cudaStream_t st, bool pdl);
+// n rows: out[b] = the embedding row of tokens_dev[b] (prompt chunks)
+cudaError_t embed_rows_launch(int type, const uint8_t *w, const uint32_t *tokens_dev, uint32_t n, uint32_t rows,
+                              float *out, uint32_t dim, uint32_t *err, cudaStream_t st);
 cudaError_t rmsnorm_launch(const float *in, const float *w, float *out, uint32_t n, float eps, cudaStream_t st);
 // rope/cache store take the position from ctrl[0] when ctrl != NULL.
 cudaError_t rope_launch(float *x, uint32_t pos, const uint32_t *ctrl, uint32_t head_dim, uint32_t n_heads, float theta,

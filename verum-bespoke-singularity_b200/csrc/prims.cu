@@ -46,6 +46,32 @@ cudaError_t embed_launch(int type, const uint8_t *w, const uint32_t *token_dev, 
     return cudaLaunchKernelEx(&cfg, embed_kernel, type, w, token_dev, token, rows, out, dim, err);
 }
 
+// n embedding rows at once (prompt chunks): block (x, b) covers part of the
+// row of tokens_dev[b]; out is [n][dim].
+__global__ void embed_rows_kernel(int type, const uint8_t *__restrict__ w, const uint32_t *__restrict__ tokens_dev,
+                                  uint32_t rows, float *__restrict__ out, uint32_t dim, uint32_t *err) {
+    const uint32_t tok = tokens_dev[blockIdx.y];
+    float *o = out + (uint64_t)blockIdx.y * dim;
+    if (tok >= rows) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(err, DERR_BAD_ARG);
+        for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x) o[e] = 0.0f;
+        return;
+    }
+    const int E = block_elems(type), BB = block_bytes(type);
+    const uint8_t *row = w + (uint64_t)tok * row_bytes(type, dim);
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x)
+        o[e] = dq_elem(type, row + (uint64_t)(e / E) * BB, (int)(e % E));
+}
+
+cudaError_t embed_rows_launch(int type, const uint8_t *w, const uint32_t *tokens_dev, uint32_t n, uint32_t rows,
+                              float *out, uint32_t dim, uint32_t *err, cudaStream_t st) {
+    if (!block_elems(type) || dim % block_elems(type) || !n) return cudaErrorInvalidValue;
+    note_launches(1);
+    embed_rows_kernel<<<dim3(std::max(1u, std::min(16u, (dim + 255) / 256)), n), 256, 0, st>>>(type, w, tokens_dev, rows,
+                                                                                                out, dim, err);
+    return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm with double accumulation (src/vbs_host_math.h:28-36)
 // ---------------------------------------------------------------------------
