@@ -53,7 +53,7 @@ def parse():
                     help="--impl reference: layers of the 8B shape (fewer only to check the JSON contract quickly)")
     ap.add_argument("--profile", default=None,
                     choices=["ffn_gate_up", "down", "output", "qkv_like", "attention", "decode", "sweep", "prefill",
-                             "upload", "stream"],
+                             "upload", "stream", "timeline"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
     ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
@@ -66,11 +66,110 @@ def parse():
     return ap.parse_args()
 
 
+TIMELINE_LIB = ROOT / "verum-bespoke-singularity_b200" / "libvbs_b200_trace.so"
+
+
+def profile_timeline(args):
+    """Where a step kernel's time goes, op by op: the profiling build of the
+    library (`make -C verum-bespoke-singularity_b200 trace`) stamps
+    %globaltimer per CTA at each op's start (after its grid barrier), at the
+    end of its prologue and at its end, and the producer warp's first and
+    last stage issue. One step at position --ctx - 1, three times; the last
+    one's per-op figures, medians over CTAs, averaged over the middle layers
+    (1 .. L-2) per op kind, in microseconds:
+      span      last CTA's end of the previous op -> last CTA's end of this op
+      barrier   last CTA's end of the previous op -> first CTA's start
+      prologue  start -> prologue done (norm, x quantization)
+      body      prologue done (ATTN: start) -> end
+      prod_lead consumer start - producer's last issue for the op (> 0: the
+                op's weights were all in flight before its consumers began)
+    and the phases inside (medians over CTAs of thread 0's stamps): the norm
+    prologue's loads and sum of squares, its wait for the norm weight stage
+    and its quantization; attention's q/KV setup, stage loop, partial store,
+    wait for the head's other splits and merge."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    import vbs_b200 as vbs
+    import models
+    if not TIMELINE_LIB.exists():
+        raise SystemExit(f"{TIMELINE_LIB} is not built: make -C {TIMELINE_LIB.parent} trace")
+    vbs.LIB_PATH = TIMELINE_LIB
+    L = vbs.lib()
+    L.vbs_cu_decoder_trace.restype = C.c_void_p
+    L.vbs_cu_decoder_trace.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]
+    torch.cuda.set_device(0)
+    if not vbs.ops().init():
+        raise SystemExit(vbs.last_error())
+    nl = args.layers
+    cfg = dict(models.L8B, n_layers=nl, vocab=args.vocab)
+    model = vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=2024)
+    dec = vbs.Decoder(model, args.ctx + 64)
+    dec.forward([1], logits=False)
+    dec.set_position(args.ctx - 1, 1)
+    dec.enqueue_steps(4)
+    torch.cuda.synchronize()
+    kinds = ["QKV", "ATTN", "O", "GU", "DOWN"]
+    ops_t = vbs.ops()
+    s = torch.cuda.ExternalStream(dec.stream)
+    for rep in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        dec.enqueue_steps(1)
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        nc, no = C.c_uint32(), C.c_uint32()
+        ptr = L.vbs_cu_decoder_trace(dec.h, C.byref(nc), C.byref(no))
+        n = nc.value * no.value * 8
+        host = np.zeros(n, np.uint64)
+        buf = vbs.Buffer()
+        buf.internal_handle, buf.size = ptr, n * 8
+        assert ops_t.copy_to_host(host.ctypes.data, C.byref(buf), n * 8), vbs.last_error()
+    raw = host.reshape(nc.value, no.value, 8)
+    T = raw.astype(np.int64)
+    T -= T[:, 0, 0].min()
+
+    def phase(i, a, b):   # median over the CTAs that stamped both
+        ok = (raw[:, i, a] > 0) & (raw[:, i, b] > 0)
+        return float(np.median(T[ok, i, b] - T[ok, i, a])) / 1e3 if ok.any() else 0.0
+
+    per_op, prev_end = [], 0
+    for i in range(no.value):
+        st, pro, en, pf, pl = (T[:, i, k] for k in range(5))
+        k = kinds[i % 5] if i < 5 * nl else ("OUT", "ARGMAX")[i - 5 * nl]
+        normed = k not in ("ATTN", "ARGMAX")
+        r = {"op": k, "i": i, "span": (en.max() - prev_end) / 1e3, "barrier": (st.min() - prev_end) / 1e3 if i else 0.0,
+             "prologue": float(np.median(pro - st)) / 1e3 if normed else 0.0,
+             "body": float(np.median(en - (pro if normed else st))) / 1e3,
+             "prod_lead": float(np.median(st - pl)) / 1e3 if k != "ARGMAX" else 0.0}
+        if k in ("QKV", "GU", "OUT"):
+            r.update(pro_sums=phase(i, 0, 5), pro_weight=phase(i, 5, 6), pro_quant=phase(i, 6, 7))
+        if k == "ATTN":
+            r.update(setup=phase(i, 0, 1), stages=phase(i, 1, 5), partial=phase(i, 5, 6), wait=phase(i, 6, 7),
+                     merge=phase(i, 7, 2))
+        per_op.append(r)
+        prev_end = en.max()
+    table = {}
+    for r in per_op:
+        if r["op"] not in kinds or 5 <= r["i"] < 5 * (nl - 1):
+            table.setdefault(r["op"], []).append(r)
+    out = {k: {f: round(float(np.mean([r[f] for r in v])), 2) for f in v[0] if f not in ("op", "i")}
+           for k, v in table.items()}
+    layer_us = sum(out[k]["span"] for k in kinds)
+    print(json.dumps({"profile": "timeline", "ctx": args.ctx, "layers": nl, "vocab": args.vocab, "event_ms": round(ms, 4),
+                      "traced_us": round(prev_end / 1e3, 1), "layer_us": round(layer_us, 2), "per_op_us": out}))
+    dec.close()
+
+
 def profile_kernel(args):
     """Standalone launches of one hot kernel at its Llama-3-8B shape. Four
     weight sets rotate so no launch finds its weights in L2."""
     import torch
     import vbs_b200 as vbs
+    if args.profile == "timeline":   # loads the profiling build instead of the product library
+        profile_timeline(args)
+        return
     torch.cuda.set_device(0)
     if not vbs.ops().init():
         raise SystemExit(vbs.last_error())
@@ -144,8 +243,8 @@ def profile_kernel(args):
                           **res}))
         return
     if args.profile == "prefill":
-        # the batched prompt pass: --ctx prompt tokens (chunks of 8 through
-        # the batched matvec) against the same prompt fed one token per step,
+        # the batched prompt pass: --ctx prompt tokens (chunks of 256 through
+        # the tcgen05 GEMM) against the same prompt fed one token per step,
         # both timed with CUDA events on the decoder's stream; --layers and
         # --vocab cut the model for a small ncu case
         import models

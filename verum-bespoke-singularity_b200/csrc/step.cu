@@ -509,7 +509,7 @@ constexpr int SK_MAXPL = 4;      // partial planes summed by the norm prologue
 template <bool WORDS>
 __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSmem &S, SkRing &r, float *x,
                                                  const void *add, uint32_t nadd, uint32_t want, uint32_t token,
-                                                 bool quant, int type, uint8_t *xq, float4 *xf) {
+                                                 bool quant, int type, uint8_t *xq, float4 *xf, uint32_t op) {
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = p.dim / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
     float xv[SK_PB][8];
@@ -565,6 +565,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
         for (int k = 0; k < 8; ++k) ss = fmaf(xv[r][k], xv[r][k], ss);
     }
     ss = warp_sum(ss);
+    if (ctid == 0) SK_STAMP(p, op, 5);
     float *misc = S.misc();
     if ((ctid & 31u) == 0) misc[ctid >> 5] = ss;
     // the norm weight stage (long landed by now); released after use
@@ -573,6 +574,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
     const uint32_t nb = p.dim * 4, ws = S.ring + r.place(nb, S.ring_bytes);
     const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p));
     if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
+    if (ctid == 0) SK_STAMP(p, op, 6);
     static_assert(SK_PB == 2, "the prologue quantizes its two blocks together");
     if (quant && got && q < nsub) {
         float v[SK_PB][8];
@@ -588,6 +590,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
         }
         sk_quant2(type, v, u, qmask, q, q + SK_CT / 4, q + SK_CT / 4 < nsub, xq, xf);
     }
+    if (ctid == 0) SK_STAMP(p, op, 7);
     __syncwarp();
     if (lane == 0) mbar_arrive(S.empty(r.idx));
     r.advance(nb);
@@ -800,7 +803,7 @@ __device__ __noinline__ void sk_attn_merge(const StepParams &p, const SkAttn &a,
 
 template <int HD>
 __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_t pos, uint32_t seq, const SkSmem &S, SkRing &r,
-                        float *sh) {
+                        float *sh, uint32_t op) {
     constexpr int RS = 4 + HD;                 // state row [m, l, pad, pad, o[HD]]
     constexpr uint32_t ROWB = HD * 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -857,6 +860,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
         }
         named_bar_sync(1, SK_CT);
     }
+    if (threadIdx.x == 0) SK_STAMP(p, op, 1);
     const uint32_t a_lane = a_base + (lane & 15) * ASTR + (lane >> 4) * 16;
 
     float o[HD / 8][4];
@@ -948,6 +952,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
     }
 
     // warp states -> shared memory, merge over the 8 warps
+    if (threadIdx.x == 0) SK_STAMP(p, op, 5);
     lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
     lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
     if ((uint32_t)g < G) {
@@ -1000,6 +1005,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
     // wait until every split of the head published, then merge this split's
     // share of the head's outputs: the S CTAs of a head merge in parallel.
     named_bar_sync(1, SK_CT);
+    if (threadIdx.x == 0) SK_STAMP(p, op, 6);
     volatile int *flag = S.sync_flag();
     if (threadIdx.x == 0) {
         uint32_t *cnt = &p.sync[SK_TICKET0 + a.h];
@@ -1018,6 +1024,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
         *flag = ok ? 1 : 0;
     }
     named_bar_sync(1, SK_CT);
+    if (threadIdx.x == 0) SK_STAMP(p, op, 7);
     if (!*flag) return;
     const uint32_t per = ((G * HD + a.S - 1) / a.S + 1) & ~1u;
     const uint32_t e_lo = min(G * HD, a.split * per), e_hi = min(G * HD, e_lo + per);
@@ -1171,9 +1178,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         const int kind = sk_kind(i, p.n_layers, l);
         if (threadIdx.x == 0) SK_STAMP(p, i, 0);
         if (kind == K_ATTN) {
-            if constexpr (HD != 0) sk_attn<HD>(p, l, pos, seq, S, r, sh);
-            else if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh);
-            else sk_attn<64>(p, l, pos, seq, S, r, sh);
+            if constexpr (HD != 0) sk_attn<HD>(p, l, pos, seq, S, r, sh, i);
+            else if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh, i);
+            else sk_attn<64>(p, l, pos, seq, S, r, sh, i);
             if (threadIdx.x == 0) SK_STAMP(p, i, 2);
             continue;
         }
@@ -1204,7 +1211,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
                 nadd *= p.tp->world;
                 want = k + 1u;
             }
-            sk_prologue_norm<TPX>(p, S, r, x, planes, nadd, want, token, work, d.type, xq, xf);
+            sk_prologue_norm<TPX>(p, S, r, x, planes, nadd, want, token, work, d.type, xq, xf, i);
         } else if (kind == K_O) {
             if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
         } else if (work) {   // K_DOWN: only the column chunks of this CTA's units
