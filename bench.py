@@ -83,10 +83,13 @@ def profile_timeline(args):
       body      prologue done (ATTN: start) -> end
       prod_lead consumer start - producer's last issue for the op (> 0: the
                 op's weights were all in flight before its consumers began)
-    and the phases inside (medians over CTAs of thread 0's stamps): the norm
+    and the phases inside (medians over CTAs of thread 0's stamps): the
+    prologue's first instruction after the barrier (pro_entry), the norm
     prologue's loads and sum of squares, its wait for the norm weight stage
-    and its quantization; attention's q/KV setup, stage loop, partial store,
-    wait for the head's other splits and merge."""
+    and its quantization; attention's q/KV setup, first and last stage
+    arrival, stage loop, partial store, wait for the head's other splits and
+    merge; and l2_probe, one dependent L2 load of the op's input timed right
+    after the prologue (attention: after the merge)."""
     import ctypes as C
     import numpy as np
     import torch
@@ -97,7 +100,7 @@ def profile_timeline(args):
     vbs.LIB_PATH = TIMELINE_LIB
     L = vbs.lib()
     L.vbs_cu_decoder_trace.restype = C.c_void_p
-    L.vbs_cu_decoder_trace.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]
+    L.vbs_cu_decoder_trace.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]
     torch.cuda.set_device(0)
     if not vbs.ops().init():
         raise SystemExit(vbs.last_error())
@@ -119,14 +122,14 @@ def profile_timeline(args):
         e1.record(s)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
-        nc, no = C.c_uint32(), C.c_uint32()
-        ptr = L.vbs_cu_decoder_trace(dec.h, C.byref(nc), C.byref(no))
-        n = nc.value * no.value * 8
+        nc, no, ns = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        ptr = L.vbs_cu_decoder_trace(dec.h, C.byref(nc), C.byref(no), C.byref(ns))
+        n = nc.value * no.value * ns.value
         host = np.zeros(n, np.uint64)
         buf = vbs.Buffer()
         buf.internal_handle, buf.size = ptr, n * 8
         assert ops_t.copy_to_host(host.ctypes.data, C.byref(buf), n * 8), vbs.last_error()
-    raw = host.reshape(nc.value, no.value, 8)
+    raw = host.reshape(nc.value, no.value, ns.value)
     T = raw.astype(np.int64)
     T -= T[:, 0, 0].min()
 
@@ -144,10 +147,13 @@ def profile_timeline(args):
              "body": float(np.median(en - (pro if normed else st))) / 1e3,
              "prod_lead": float(np.median(st - pl)) / 1e3 if k != "ARGMAX" else 0.0}
         if k in ("QKV", "GU", "OUT"):
-            r.update(pro_sums=phase(i, 0, 5), pro_weight=phase(i, 5, 6), pro_quant=phase(i, 6, 7))
+            r.update(pro_entry=phase(i, 0, 8), pro_sums=phase(i, 8, 5), pro_weight=phase(i, 5, 6),
+                     pro_quant=phase(i, 6, 7), l2_probe=phase(i, 9, 10))
+        if k in ("O", "DOWN"):
+            r.update(pro_entry=phase(i, 0, 8), l2_probe=phase(i, 9, 10))
         if k == "ATTN":
-            r.update(setup=phase(i, 0, 1), stages=phase(i, 1, 5), partial=phase(i, 5, 6), wait=phase(i, 6, 7),
-                     merge=phase(i, 7, 2))
+            r.update(setup=phase(i, 0, 1), first_stage=phase(i, 1, 8), last_stage=phase(i, 1, 9), stages=phase(i, 1, 5),
+                     partial=phase(i, 5, 6), wait=phase(i, 6, 7), merge=phase(i, 7, 2), l2_probe=phase(i, 10, 11))
         per_op.append(r)
         prev_end = en.max()
     table = {}

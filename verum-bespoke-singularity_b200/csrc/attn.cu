@@ -513,12 +513,179 @@ static cudaError_t attn_simt_go(const AttnParams &p, uint32_t n_splits, cudaStre
     return cudaLaunchKernelEx(&cfg, attn_simt_kernel<HD, DPL, GMAX>, p, n_splits);
 }
 
+// ---------------------------------------------------------------------------
+// Causal prompt-chunk attention (prefill): CTA = (kv head, 8 consecutive
+// query tokens). Query token b of the chunk attends positions
+// 0 .. seq_len + b - 1 (seq_step 1). Every KV tile of 64 positions is
+// staged once per CTA and serves all 8 tokens of all G query heads of the
+// group: warp w computes query head kvh * G + w for the 8 tokens.
+//  * A rows: token r (0..7) as fp16(q), row r + 8 as the fp16 remainder, so
+//    the products are exact to ~2^-22 relative as in attn_mma_kernel; P is
+//    split the same way for p.V, and the two halves are summed in fp32.
+//  * No split of the positions, so no merge: the CTA writes the outputs.
+// The decode kernel, used for chunks before, is one CTA per token and
+// re-reads the whole context for each of a chunk's tokens.
+// ---------------------------------------------------------------------------
+constexpr uint32_t APF_TOK = 8, APF_SP = 64, APF_NST = 3;
+template <int HD> struct AttnPf {
+    static constexpr uint32_t RSB = HD * 2 + 16;       // padded row: conflict-free ldmatrix
+    static constexpr uint32_t STAGE = 2 * APF_SP * RSB;  // K rows then V rows
+    static constexpr uint32_t SMEM = APF_NST * STAGE;
+    static constexpr int CPR = HD * 2 / 16;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(ATTN_GS * 32, 1) attn_prefill_kernel(const AttnParams p) {
+    using C = AttnPf<HD>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t kvh = blockIdx.x, b0 = blockIdx.y * APF_TOK;
+    const uint32_t G = p.nqh / p.nkh, nthr = blockDim.x;
+    const KvSlice kv = attn_slice(p, 0, kvh);
+    const uint32_t blast = min(b0 + APF_TOK, p.batch) - 1;   // the CTA's last real token
+    uint32_t t1 = p.seq_len + blast;                          // positions any of its tokens sees
+    if (t1 > p.max_ctx) {
+        if (threadIdx.x == 0) dev_flag_error(p.err, DERR_BAD_ARG);
+        return;
+    }
+    const uint32_t nch = (t1 + APF_SP - 1) / APF_SP;
+    const uint32_t sbase = smem_u32(smem);
+
+    auto issue = [&](uint32_t c) {
+        const uint32_t slot = sbase + (c % APF_NST) * C::STAGE;
+        const uint32_t pb = c * APF_SP;
+        for (uint32_t i = threadIdx.x; i < 2 * APF_SP * C::CPR; i += nthr) {
+            const uint32_t isv = i / (APF_SP * C::CPR), r = (i / C::CPR) % APF_SP, ch = i % C::CPR;
+            const uint32_t t = pb + r;
+            const bool ok = t < t1;
+            const uint32_t tr = ok ? t : 0u;
+            const uint32_t cs = p.swz ? (ch ^ (tr & 7u)) : ch;
+            const uint16_t *src = (isv ? kv.v : kv.k) + (uint64_t)tr * kv.ps + cs * 8;
+            cp_async16(slot + (isv * APF_SP + r) * C::RSB + ch * 16, src, ok ? 16u : 0u);
+        }
+    };
+
+    // q of token b0 + g, head kvh * G + warp: rows g = fp16(q), g + 8 = remainder
+    const int g = lane >> 2, qd = 2 * (lane & 3);
+    const uint32_t tok = b0 + g;
+    const bool tok_ok = tok < p.batch;
+    const uint32_t lim = p.seq_len + (tok_ok ? tok : blast);   // this row's positions: t < lim
+    const float qscale = p.scale * 1.4426950408889634f;
+    uint32_t qa[HD / 16][4];
+    {
+        const float *qh = p.q + (size_t)(tok_ok ? tok : blast) * p.nqh * HD + (size_t)(kvh * G + warp) * HD;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float2 v = tok_ok ? *reinterpret_cast<const float2 *>(qh + 16 * kk + 8 * h + qd) : make_float2(0.f, 0.f);
+                split_h2(v.x * qscale, v.y * qscale, qa[kk][2 * h], qa[kk][2 * h + 1]);
+            }
+        }
+    }
+#pragma unroll
+    for (uint32_t c = 0; c < APF_NST - 1; ++c) {
+        if (c < nch) issue(c);
+        cp_async_commit();
+    }
+    float o[HD / 8][4];
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float mrun = -INFINITY, lrun = 0.f;
+
+    for (uint32_t c = 0; c < nch; ++c) {
+        if (c + APF_NST - 1 < nch) issue(c + APF_NST - 1);
+        cp_async_commit();
+        cp_async_wait<APF_NST - 1>();
+        __syncthreads();
+        const uint32_t kst = sbase + (c % APF_NST) * C::STAGE, vst = kst + APF_SP * C::RSB;
+        const uint32_t tb = c * APF_SP;
+        // scores: 8 blocks of 8 positions; rows g (hi) and g + 8 (lo) summed
+        float sc[APF_SP / 8][2];
+#pragma unroll
+        for (int j = 0; j < (int)APF_SP / 8; ++j) {
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; kk += 2) {
+                uint32_t b0r, b1r, b2r, b3r;
+                ldsm_x4(kst + (8 * j + (lane & 7)) * C::RSB + (16 * kk + 8 * (lane >> 3)) * 2, b0r, b1r, b2r, b3r);
+                mma_f16_acc(s4, qa[kk], b0r, b1r);
+                mma_f16_acc(s4, qa[kk + 1], b2r, b3r);
+            }
+            const uint32_t pq = tb + 8 * j + qd;
+            sc[j][0] = pq < lim ? s4[0] + s4[2] : -INFINITY;
+            sc[j][1] = pq + 1 < lim ? s4[1] + s4[3] : -INFINITY;
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < (int)APF_SP / 8; ++j) mx = fmaxf(mx, fmaxf(sc[j][0], sc[j][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (mx > mrun + ATTN_LAZY) {   // the first tile always holds position 0 of every row
+            const float r = exp2f(mrun - mx);
+            lrun *= r;
+#pragma unroll
+            for (int n = 0; n < HD / 8; ++n) { o[n][0] *= r; o[n][1] *= r; o[n][2] *= r; o[n][3] *= r; }
+            mrun = mx;
+        }
+#pragma unroll
+        for (int kc = 0; kc < (int)APF_SP / 16; ++kc) {
+            const float p0 = exp2f(sc[2 * kc][0] - mrun), p1 = exp2f(sc[2 * kc][1] - mrun);
+            const float p2 = exp2f(sc[2 * kc + 1][0] - mrun), p3 = exp2f(sc[2 * kc + 1][1] - mrun);
+            lrun += (p0 + p1) + (p2 + p3);
+            uint32_t pa[4];
+            split_h2(p0, p1, pa[0], pa[1]);
+            split_h2(p2, p3, pa[2], pa[3]);
+#pragma unroll
+            for (int n = 0; n < HD / 8; n += 2) {
+                uint32_t b0r, b1r, b2r, b3r;
+                ldsm_x4_trans(vst + (16 * kc + (lane & 7) + 8 * ((lane >> 3) & 1)) * C::RSB + (8 * n + 8 * (lane >> 4)) * 2,
+                              b0r, b1r, b2r, b3r);
+                mma_f16_acc(o[n], pa, b0r, b1r);
+                mma_f16_acc(o[n + 1], pa, b2r, b3r);
+            }
+        }
+        __syncthreads();
+    }
+    lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
+    lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
+    if (tok_ok) {
+        const float il = 1.0f / lrun;
+        float *dst = p.out + (size_t)tok * p.nqh * HD + (size_t)(kvh * G + warp) * HD;
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n)
+            *reinterpret_cast<float2 *>(dst + 8 * n + qd) = make_float2((o[n][0] + o[n][2]) * il, (o[n][1] + o[n][3]) * il);
+    }
+}
+
+bool attn_prefill_supported(const AttnParams &p) {
+    return (p.hd == 64 || p.hd == 128) && p.head_major && p.nkh && p.nqh % p.nkh == 0 && p.nqh / p.nkh >= 1 &&
+           p.nqh / p.nkh <= (uint32_t)ATTN_GS && p.seq_step == 1 && p.batch && !p.seq_dev && p.kv_batch_stride == 0;
+}
+
+cudaError_t attn_prefill_launch(const AttnParams &p, cudaStream_t st) {
+    if (!attn_prefill_supported(p)) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(p.kc) | reinterpret_cast<uintptr_t>(p.vc) | reinterpret_cast<uintptr_t>(p.q) |
+         reinterpret_cast<uintptr_t>(p.out)) & 15)
+        return cudaErrorInvalidValue;
+    note_launches(1);
+    const dim3 grid(p.nkh, (p.batch + APF_TOK - 1) / APF_TOK);
+    const uint32_t threads = 32 * (p.nqh / p.nkh);
+    if (p.hd == 128) attn_prefill_kernel<128><<<grid, threads, AttnPf<128>::SMEM, st>>>(p);
+    else attn_prefill_kernel<64><<<grid, threads, AttnPf<64>::SMEM, st>>>(p);
+    return cudaGetLastError();
+}
+
 cudaError_t attn_configure() {
     cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnMma<32>::SMEM);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnMma<64>::SMEM);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnMma<128>::SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnPf<64>::SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnPf<128>::SMEM);
     return e;
 }
 

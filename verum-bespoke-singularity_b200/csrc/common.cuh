@@ -223,6 +223,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
         ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
+// The same with an L2 cache policy (createpolicy), e.g. evict_first for a
+// stream that is read once, so it does not displace what is read again.
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // Programmatic dependent launch: wait for the upstream grid's memory, and
 // allow the downstream grid to start its prologue. Both are no-ops when the
 // launch carries no programmatic dependency.

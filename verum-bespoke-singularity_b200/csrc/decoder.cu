@@ -623,7 +623,8 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
         ap.work = d->pf_attn_work;
         ap.err = dev->err;
         const uint32_t ns = std::min(d->pf_splits, attn_num_splits(p0 + B, m.n_kv_heads, B, dev->n_sm));
-        if (!cuda_ok(attn_launch(ap, ns, st, false), "prefill attention") ||
+        if (!cuda_ok(attn_prefill_supported(ap) ? attn_prefill_launch(ap, st) : attn_launch(ap, ns, st, false),
+                     "prefill attention") ||
             matvec_any(dev, y.to, y.wo, d->pf_att, d->pf_x, dim, nq, B, VBS_CU_MV_ACCUMULATE, st) ||
             !cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.ffn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm") ||
             matvec_any(dev, y.tgate, y.wgate, d->pf_xn, d->pf_g, ffn, dim, B, 0, st) ||
@@ -1012,10 +1013,11 @@ uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d) { return d ? d->ke
 #ifdef VBS_STEP_TRACE
 // Profiling builds only: the device address of the last step's timeline,
 // [CTA][op][SK_TR_SLOTS] %globaltimer stamps.
-VBS_API void *vbs_cu_decoder_trace(vbs_cu_decoder_t *d, uint32_t *n_ctas, uint32_t *n_ops) {
+VBS_API void *vbs_cu_decoder_trace(vbs_cu_decoder_t *d, uint32_t *n_ctas, uint32_t *n_ops, uint32_t *n_slots) {
     if (!d || !d->trace) return nullptr;
     if (n_ctas) *n_ctas = (uint32_t)d->dev->n_sm;
     if (n_ops) *n_ops = 5 * d->m.n_layers + 2;
+    if (n_slots) *n_slots = SK_TR_SLOTS;
     return d->trace;
 }
 #endif

@@ -190,6 +190,11 @@ size_t attn_workspace_bytes(uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t ba
 uint32_t attn_num_splits(uint32_t seq_len_hint, uint32_t nkh, uint32_t batch, int n_sm);
 cudaError_t attn_launch(const AttnParams &p, uint32_t n_splits, cudaStream_t st, bool pdl);
 cudaError_t attn_configure();
+// Causal attention of a prompt chunk (seq_step 1, head-major cache, hd 64 or
+// 128, one sequence): query token b attends positions < seq_len + b. One CTA
+// per (kv head, 8 tokens), no position splits and no workspace.
+bool attn_prefill_supported(const AttnParams &p);
+cudaError_t attn_prefill_launch(const AttnParams &p, cudaStream_t st);
 // The fixed per-device scratch of vbs_cu_attention_static: its size, and its
 // address on the current device.
 size_t attn_static_bytes();
@@ -261,7 +266,9 @@ struct StepParams {
     // (a profiling build): per CTA and op, SK_TR_SLOTS %globaltimer stamps.
     unsigned long long *trace;
 };
-constexpr int SK_TR_SLOTS = 8;   // op start, prologue done, op done, producer first / last issue, 3 spare
+// Slots: 0 op start, 1 prologue done, 2 op done, 3/4 producer first / last
+// issue, 5..15 phases inside the op (bench.py --profile timeline names them).
+constexpr int SK_TR_SLOTS = 16;
 
 // Element (pos, i) of one layer's KV block in the step kernel's cache:
 // [kv head][position][head_dim] with the 16-byte chunk index of each row

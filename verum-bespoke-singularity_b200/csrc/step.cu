@@ -185,9 +185,20 @@ __device__ __forceinline__ void sk_stamp(const StepParams &p, uint32_t i, int k)
     if (p.trace)
         p.trace[((size_t)blockIdx.x * (5 * p.n_layers + 2) + i) * SK_TR_SLOTS + k] = global_ns();
 }
+// The same, taken only once v has arrived (v feeds an instruction issued
+// before the clock is read): the latency of the load that produced v.
+__device__ __forceinline__ void sk_stamp_after(const StepParams &p, uint32_t i, int k, float v) {
+    uint64_t t;
+    asm volatile("{\n .reg .pred q;\n setp.nan.f32 q, %1, %1;\n mov.u64 %0, %%globaltimer;\n @q mov.u64 %0, 0;\n}"
+                 : "=l"(t) : "f"(v) : "memory");
+    if (p.trace) p.trace[((size_t)blockIdx.x * (5 * p.n_layers + 2) + i) * SK_TR_SLOTS + k] = t;
+}
 #define SK_STAMP(p, i, k) sk_stamp(p, i, k)
+// One dependent L2 load of src by this thread, timed into slots k, k + 1.
+#define SK_PROBE(p, i, k, src) do { SK_STAMP(p, i, k); sk_stamp_after(p, i, (k) + 1, __ldcg(src)); } while (0)
 #else
 #define SK_STAMP(p, i, k) ((void)0)
+#define SK_PROBE(p, i, k, src) ((void)0)
 #endif
 
 // ---------------------------------------------------------------------------
@@ -383,6 +394,9 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
     SkRing r;
     SkInflight f;
     bool ok = true;
+    // weights and KV rows are read once per step: first out of L2, so the
+    // activations, the norm weights and the kernel's code stay in it
+    const uint64_t once = l2_policy_evict_first();
     for (uint32_t i = 0; i < nops && ok; ++i) {
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
@@ -398,8 +412,8 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
                 if (lane == 0) {
                     const uint32_t dst = S.ring + r.off;
                     mbar_arrive_expect_tx(S.full(r.idx), 2 * bytes);
-                    bulk_g2s(dst, p.kc + hb + (uint64_t)t * p.hd, bytes, S.full(r.idx));
-                    bulk_g2s(dst + SK_AP * rowb, p.vc + hb + (uint64_t)t * p.hd, bytes, S.full(r.idx));
+                    bulk_g2s_hint(dst, p.kc + hb + (uint64_t)t * p.hd, bytes, S.full(r.idx), once);
+                    bulk_g2s_hint(dst + SK_AP * rowb, p.vc + hb + (uint64_t)t * p.hd, bytes, S.full(r.idx), once);
                 }
                 sk_issued(r, f, sb, lane);
             }
@@ -426,7 +440,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
             sk_unit(d, u, tile, ch);
             if (lane == 0) {
                 mbar_arrive_expect_tx(S.full(r.idx), bytes);
-                bulk_g2s(S.ring + r.off, d.packed + (uint64_t)(tile * d.g.nch + ch) * bytes, bytes, S.full(r.idx));
+                bulk_g2s_hint(S.ring + r.off, d.packed + (uint64_t)(tile * d.g.nch + ch) * bytes, bytes, S.full(r.idx), once);
             }
             sk_issued(r, f, bytes, lane);
         }
@@ -512,6 +526,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
                                                  bool quant, int type, uint8_t *xq, float4 *xf, uint32_t op) {
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = p.dim / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
+    if (ctid == 0) SK_STAMP(p, op, 8);
     float xv[SK_PB][8];
     // add = nadd planes of dim partial sums, summed in plane order
 #pragma unroll
@@ -591,6 +606,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
         sk_quant2(type, v, u, qmask, q, q + SK_CT / 4, q + SK_CT / 4 < nsub, xq, xf);
     }
     if (ctid == 0) SK_STAMP(p, op, 7);
+    if (ctid == 0 && add) SK_PROBE(p, op, 9, static_cast<const float *>(add) + 8 * nadd);
     __syncwarp();
     if (lane == 0) mbar_arrive(S.empty(r.idx));
     r.advance(nb);
@@ -873,6 +889,8 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
         const uint32_t stg = S.ring + r.place(2 * SK_AP * ROWB, S.ring_bytes);
         const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p));
         if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
+        if (threadIdx.x == 0 && s == 0) SK_STAMP(p, op, 8);
+        if (threadIdx.x == 0 && s + 1 == a.nst) SK_STAMP(p, op, 9);
         const uint32_t ts = a.t0 + s * SK_AP, tb = ts + 16 * wl;
         if (got && (int)(s & 1) == grp && tb < a.t1) {
             const uint32_t kst = stg + 16 * wl * ROWB;
@@ -1029,6 +1047,7 @@ __device__ __forceinline__ void sk_attn(const StepParams &p, uint32_t l, uint32_
     const uint32_t per = ((G * HD + a.S - 1) / a.S + 1) & ~1u;
     const uint32_t e_lo = min(G * HD, a.split * per), e_hi = min(G * HD, e_lo + per);
     sk_attn_merge<HD>(p, a, G, work + (size_t)a.h * SK_MAX_SPLITS * part_stride, outp, e_lo, e_hi);
+    if (threadIdx.x == 0) SK_PROBE(p, op, 10, work + (size_t)a.h * SK_MAX_SPLITS * part_stride + 4);
 }
 
 // ---------------------------------------------------------------------------
@@ -1213,12 +1232,16 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             }
             sk_prologue_norm<TPX>(p, S, r, x, planes, nadd, want, token, work, d.type, xq, xf, i);
         } else if (kind == K_O) {
+            if (threadIdx.x == 0) SK_STAMP(p, i, 8);
             if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
+            if (threadIdx.x == 0) SK_PROBE(p, i, 9, p.att + 64);
         } else if (work) {   // K_DOWN: only the column chunks of this CTA's units
             const uint32_t c_lo = u0 / d.g.ntiles, c_hi = (u1 - 1) / d.g.ntiles;
             const uint32_t col0 = c_lo * d.g.ck, col1 = min(d.cols, (c_hi + 1) * d.g.ck);
             const float *hp = sk_acc_h(p, l) + col0;
+            if (threadIdx.x == 0) SK_STAMP(p, i, 8);
             sk_prologue_vec<2>(col1 - col0, d.type, hp, xq, xf);
+            if (threadIdx.x == 0) SK_PROBE(p, i, 9, hp + 64);
             xq_u = xq_a - (col0 / 32) * (d.type == T_Q6_K ? XQ_PLAIN_STRIDE : XQ_SLOT_STRIDE);   // mv_unit indexes x blocks from column 0
             xf_u = xf_a - (col0 / 32) * 16;
         }
