@@ -10,8 +10,10 @@
 // tokens:
 //  * producer warps (256 threads) walk K in steps of 64: threads 2r and
 //    2r + 1 dequantize row r's 64 weights, 32 each (the GGUF block decode of
-//    src/vbs_dequant.c, rounded to fp16), and thread i copies token i's 64
-//    activations (fp16, converted once per call), all into the UMMA
+//    src/vbs_dequant.c, rounded to fp16; the raw bytes are fetched two
+//    stages ahead into registers), and thread i copies token i's 64
+//    activations (fp16, converted once per call; cp.async, one stage
+//    ahead), all into the UMMA
 //    canonical K-major layout in shared memory: 8-row x 16-byte core
 //    matrices 128 bytes apart along M/N (SBO), k-chunks of 8 elements one
 //    operand-height x 16 bytes apart (LBO);
@@ -87,67 +89,96 @@ __device__ __forceinline__ uint32_t qg_h2(float a, float b) {
     return __half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
 }
 
-// Q4_K, the prefill's hot type: the 64 weights of a stage are sub-blocks j0
-// and j0 + 1 of one super-block (the low and the high nibbles of the same 32
-// bytes); `half` picks one, decoded with the reference's operation order
-// ((d*sc)*q - dmin*m, no FMA).
-__device__ __forceinline__ void qg_dq32_q4k(const uint8_t *row, uint32_t k0, uint32_t half, uint4 out[4]) {
-    const uint8_t *b = row + (uint64_t)(k0 >> 8) * 144;
-    const uint32_t j0 = (k0 & 255u) >> 5, j = j0 + half;   // j0 even
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(b));
-    const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(b + 16 + (j0 >> 1) * 32));
-    const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(b + 32 + (j0 >> 1) * 32));
-    const uint8_t *s = reinterpret_cast<const uint8_t *>(&hdr) + 4;
-    int sc, mn;
-    if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
-    else { sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
-    const float d = f16_exact(hdr.x & 0xFFFFu), dmin = f16_exact(hdr.x >> 16);
-    const float a = __fmul_rn(d, (float)sc), c = __fmul_rn(dmin, (float)mn);
-    const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    const uint32_t sh = half ? 4u : 0u;
+__device__ __forceinline__ uint32_t lo_word(const uint32_t (&w)[8], int i) { return w[i]; }
+
+// The producers fetch a stage's raw weight bytes two stages before they
+// decode them (QgRaw in registers), so the loads' latency overlaps the
+// decode and the shared-memory stores of the stages in between.
+template <int TYPE> struct QgRaw { uint32_t k0; };
+template <> struct QgRaw<T_Q4_K> { uint4 hdr, q0, q1; uint32_t k0; };
+template <> struct QgRaw<T_Q6_K> { uint32_t ql[8], qh[8], sc, d, k0; };
+
+// 32 bytes at a 2-byte aligned address, as 8 words: 9 aligned words and a
+// funnel shift (the 4 bytes past the range lie inside the same Q6_K block).
+__device__ __forceinline__ void qg_ld32_a2(const uint8_t *ptr, uint32_t out[8]) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(reinterpret_cast<uintptr_t>(ptr) & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(ptr) & 3u) * 8u;
+    uint32_t v[9];
 #pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-        const uint32_t w0 = q[2 * cc], w1 = q[2 * cc + 1];
-        float v[8];
+    for (int i = 0; i < 9; ++i) v[i] = __ldg(w + i);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            v[k] = __fsub_rn(__fmul_rn(a, (float)((w0 >> (8 * k + sh)) & 15u)), c);
-            v[4 + k] = __fsub_rn(__fmul_rn(a, (float)((w1 >> (8 * k + sh)) & 15u)), c);
-        }
-        out[cc] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
+    for (int i = 0; i < 8; ++i) out[i] = __funnelshift_r(v[i], v[i + 1], sh);
+}
+
+template <int TYPE>
+__device__ __forceinline__ void qg_fetch(const uint8_t *row, uint32_t k0, uint32_t half, QgRaw<TYPE> &r) {
+    r.k0 = k0;
+    if constexpr (TYPE == T_Q4_K) {
+        const uint8_t *b = row + (uint64_t)(k0 >> 8) * 144;
+        const uint32_t j0 = (k0 & 255u) >> 5;
+        r.hdr = __ldg(reinterpret_cast<const uint4 *>(b));
+        r.q0 = __ldg(reinterpret_cast<const uint4 *>(b + 16 + (j0 >> 1) * 32));
+        r.q1 = __ldg(reinterpret_cast<const uint4 *>(b + 32 + (j0 >> 1) * 32));
+    } else if constexpr (TYPE == T_Q6_K) {
+        const uint8_t *b = row + (uint64_t)(k0 >> 8) * 210;
+        const uint32_t c = (k0 & 255u) >> 6, h = c >> 1;
+        qg_ld32_a2(b + 64 * h + 32 * half, r.ql);   // quarter q = 2 (c % 2) + half: ql bytes 32 (q % 2) ..
+        qg_ld32_a2(b + 128 + 32 * h, r.qh);
+        r.sc = __ldg(reinterpret_cast<const unsigned short *>(b + 192 + 4 * c + 2 * half));
+        r.d = __ldg(reinterpret_cast<const unsigned short *>(b + 208));
     }
 }
 
-// Q6_K: the 64 weights of stage chunk c (0..3) of a super-block are half
-// h = c / 2, quarters q0 = 2 (c % 2) and q0 + 1: low bits from ql[64 h + 32 (q & 1)
-// + l], high bits from qh[32 h + l], scale byte (e / 16), as
-// src/vbs_dequant.c:316-333 ((d * sc) * (q - 32)). GGUF Q6_K blocks are only
-// 2-byte aligned, so the bytes come in 16-bit loads.
-__device__ __forceinline__ void qg_dq32_q6k(const uint8_t *row, uint32_t k0, uint32_t half, uint4 out[4]) {
-    const uint8_t *b = row + (uint64_t)(k0 >> 8) * 210;
-    const uint32_t c = (k0 & 255u) >> 6, h = c >> 1, q0 = 2u * (c & 1u);
-    const unsigned short *ql = reinterpret_cast<const unsigned short *>(b + 64 * h);
-    const unsigned short *qh = reinterpret_cast<const unsigned short *>(b + 128 + 32 * h);
-    const unsigned short *scp = reinterpret_cast<const unsigned short *>(b + 192 + 4 * c);
-    const float d = f16_exact(__ldg(reinterpret_cast<const unsigned short *>(b + 208)));
-    const uint32_t s01 = __ldg(scp), s23 = __ldg(scp + 1);
-    const int scv[4] = {(int)(int8_t)(s01 & 255u), (int)(int8_t)(s01 >> 8), (int)(int8_t)(s23 & 255u), (int)(int8_t)(s23 >> 8)};
+// The 32 weights `half` of the stage from its raw bytes, decoded with the
+// reference's operation order (src/vbs_dequant.c: Q4_K (d*sc)*q - dmin*m,
+// Q6_K (d*sc)*(q-32), no FMA) and rounded to fp16. Q4_K: the stage is
+// sub-blocks j0 and j0 + 1 of a super-block, the low and the high nibbles of
+// the same 32 bytes. Q6_K: stage chunk c of a super-block is half h = c / 2,
+// quarters 2 (c % 2) and 2 (c % 2) + 1; low bits from ql, high bits from qh,
+// one scale byte per 16 weights.
+template <int TYPE>
+__device__ __forceinline__ void qg_decode(const uint8_t *row, const QgRaw<TYPE> &r, uint32_t half, uint4 out[4]) {
+    if constexpr (TYPE == T_Q4_K) {
+        const uint32_t j = ((r.k0 & 255u) >> 5) + half;
+        const uint8_t *s = reinterpret_cast<const uint8_t *>(&r.hdr) + 4;
+        int sc, mn;
+        if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
+        else { sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
+        const float d = f16_exact(r.hdr.x & 0xFFFFu), dmin = f16_exact(r.hdr.x >> 16);
+        const float a = __fmul_rn(d, (float)sc), c = __fmul_rn(dmin, (float)mn);
+        const uint32_t q[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
+        const uint32_t sh = half ? 4u : 0u;
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {            // 8 elements i = 8 cc .. 8 cc + 7 of the 64
-        const int cc = c4 + 4 * (int)half;
-        const uint32_t q = q0 + (uint32_t)(cc >> 2), l0 = (uint32_t)(cc & 3) * 8;
-        const float ds = __fmul_rn(d, (float)scv[cc >> 1]);   // element 8 cc + j: scale byte (64 c + 8 cc) / 16
-        float v[8];
+        for (int cc = 0; cc < 4; ++cc) {
+            const uint32_t w0 = q[2 * cc], w1 = q[2 * cc + 1];
+            float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-            const uint32_t lw = __ldg(ql + (((q & 1u) * 32u + l0 + j) >> 1)), hw = __ldg(qh + ((l0 + j) >> 1));
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                const uint32_t lo = ((lw >> (8 * t)) >> ((q >> 1) * 4)) & 15u, hi = ((hw >> (8 * t)) >> (q * 2)) & 3u;
-                v[j + t] = __fmul_rn(ds, (float)((int)(lo | (hi << 4)) - 32));
+            for (int k = 0; k < 4; ++k) {
+                v[k] = __fsub_rn(__fmul_rn(a, (float)((w0 >> (8 * k + sh)) & 15u)), c);
+                v[4 + k] = __fsub_rn(__fmul_rn(a, (float)((w1 >> (8 * k + sh)) & 15u)), c);
             }
+            out[cc] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
         }
-        out[c4] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
+    } else if constexpr (TYPE == T_Q6_K) {
+        const uint32_t c = (r.k0 & 255u) >> 6, q = 2u * (c & 1u) + half;
+        const float d = f16_exact(r.d);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {   // elements 8 c4 .. 8 c4 + 7 of this half
+            const float ds = __fmul_rn(d, (float)(int)(int8_t)((r.sc >> (8 * (c4 >> 1))) & 255u));
+            const uint32_t l0 = lo_word(r.ql, 2 * c4), l1 = lo_word(r.ql, 2 * c4 + 1);
+            const uint32_t h0 = lo_word(r.qh, 2 * c4), h1 = lo_word(r.qh, 2 * c4 + 1);
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const uint32_t lw = t < 4 ? l0 : l1, hw = t < 4 ? h0 : h1, bsh = 8u * (t & 3);
+                const uint32_t lo = ((lw >> bsh) >> ((q >> 1) * 4)) & 15u, hi = ((hw >> bsh) >> (q * 2)) & 3u;
+                v[t] = __fmul_rn(ds, (float)((int)(lo | (hi << 4)) - 32));
+            }
+            out[c4] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
+        }
+    } else {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) out[cc] = qg_dq8<TYPE>(row, r.k0 + 32 * half + 8 * cc);
     }
 }
 
@@ -190,19 +221,33 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         const __half *xrow = p.x16 + (uint64_t)tok * p.cols;   // padded to whole tiles of tokens
         // canonical offsets: core matrix r/8 at SBO = 128 B, row r%8 at 16 B
         const uint32_t aoff = (wr >> 3) * 128u + (wr & 7u) * 16u, boff = (i >> 3) * 128u + (i & 7u) * 16u;
-        for (uint32_t kt = 0; kt < nk; ++kt) {
-            const uint32_t s = kt % QG_NS;
-            if (kt >= QG_NS && !qg_wait(empty0 + 8 * s, ((kt / QG_NS) - 1) & 1u)) { *bad = 1; break; }
-            if (*bad) break;
-            const uint32_t k0 = (kb + kt) * QG_KT;
-            const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
+        // token i's 64 activations of stage kt into its slot: cp.async, one
+        // stage ahead, waited for (this thread's own copies) before the
+        // stage is declared full
+        auto put_b = [&](uint32_t kt) {
+            const uint32_t sb = st0 + (kt % QG_NS) * QG_STAGE + QG_A_BYTES;
+            const __half *src = xrow + (kb + kt) * QG_KT;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) cp_async16(sb + c * (QG_N * 16u) + boff, src + 8 * c);
+        };
+        auto fetch = [&](uint32_t kt, QgRaw<TYPE> &rw) {
+            if (kt < nk && row < p.rows) qg_fetch<TYPE>(wrow, (kb + kt) * QG_KT, wh, rw);
+        };
+        // one stage: the next stage's activations go out (its slot freed
+        // first), this stage's weights are decoded from rw, rw is refilled
+        // with the raw bytes of the stage after next
+        auto stage = [&](uint32_t kt, QgRaw<TYPE> &rw) -> bool {
+            if (kt + 1 < nk) {
+                const uint32_t s1 = (kt + 1) % QG_NS;
+                if (kt + 1 >= QG_NS && !qg_wait(empty0 + 8 * s1, (((kt + 1) / QG_NS) - 1) & 1u)) return false;
+                if (*bad) return false;
+                put_b(kt + 1);
+            }
+            cp_async_commit();
+            const uint32_t sa = st0 + (kt % QG_NS) * QG_STAGE;
             uint4 wv[4];
             if (row < p.rows) {
-                if constexpr (TYPE == T_Q4_K) qg_dq32_q4k(wrow, k0, wh, wv);
-                else if constexpr (TYPE == T_Q6_K) qg_dq32_q6k(wrow, k0, wh, wv);
-                else
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) wv[c] = qg_dq8<TYPE>(wrow, k0 + 32 * wh + 8 * c);
+                qg_decode<TYPE>(wrow, rw, wh, wv);
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) wv[c] = make_uint4(0, 0, 0, 0);
@@ -212,17 +257,22 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
             for (int c = 0; c < 4; ++c)
                 asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + (4 * wh + c) * (QG_M * 16u) + aoff),
                              "r"(wv[c].x), "r"(wv[c].y), "r"(wv[c].z), "r"(wv[c].w) : "memory");
-            // B: all 8 k-chunks of token i, LBO = 256 tokens x 16 B
-            const uint4 *xs = reinterpret_cast<const uint4 *>(xrow + k0);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint4 xv = __ldg(xs + c);
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sb + c * (QG_N * 16u) + boff), "r"(xv.x), "r"(xv.y),
-                             "r"(xv.z), "r"(xv.w) : "memory");
-            }
-            qg_fence_proxy();   // the tensor core (async proxy) reads what these generic stores wrote
-            mbar_arrive(full0 + 8 * s);
+            fetch(kt + 2, rw);
+            cp_async_wait<1>();   // this stage's activations have landed
+            qg_fence_proxy();     // the tensor core (async proxy) reads what the generic stores and copies wrote
+            mbar_arrive(full0 + 8 * (kt % QG_NS));
+            return true;
+        };
+        QgRaw<TYPE> ra, rb;
+        fetch(0, ra);
+        fetch(1, rb);
+        if (nk) put_b(0);
+        cp_async_commit();
+        for (uint32_t kt = 0; kt < nk; kt += 2) {
+            if (!stage(kt, ra)) { *bad = 1; break; }
+            if (kt + 1 < nk && !stage(kt + 1, rb)) { *bad = 1; break; }
         }
+        cp_async_wait<0>();
         // ---------------- epilogue: accumulator rows -> Y ------------------
         const bool ok = !*bad && qg_wait(accb, 0);
         qg_fence_after();
