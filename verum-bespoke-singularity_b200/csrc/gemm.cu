@@ -36,7 +36,8 @@ constexpr int QG_M = 128;            // weight rows per tile (UMMA M)
 constexpr int QG_N = 256;            // tokens per tile (UMMA N)
 constexpr int QG_KT = 64;            // k per stage
 constexpr int QG_NS = 4;             // stages
-constexpr int QG_PT = 256;           // producer / epilogue threads
+constexpr int QG_PT = 512;           // producer / epilogue threads: 4 per weight row, 2 per token
+constexpr uint32_t QG_PARTS = QG_PT / QG_M;   // threads per weight row, 16 of its 64 stage weights each
 constexpr int QG_THREADS = QG_PT + 32;   // + the MMA warp
 constexpr uint32_t QG_A_BYTES = QG_M * QG_KT * 2, QG_B_BYTES = QG_N * QG_KT * 2;
 constexpr uint32_t QG_STAGE = QG_A_BYTES + QG_B_BYTES;
@@ -85,45 +86,57 @@ __device__ __forceinline__ uint4 qg_dq8(const uint8_t *row, uint32_t e0) {
     return r;
 }
 
+// a, b rounded to fp16 (round to nearest even), a in the low half: one
+// paired conversion.
 __device__ __forceinline__ uint32_t qg_h2(float a, float b) {
-    return __half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// Byte k of w as an exact float: 2^23 + byte by a byte permute, minus 2^23
+// (no integer-to-float conversion).
+__device__ __forceinline__ float qg_byte_f(uint32_t w, uint32_t k) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | k)) - 8388608.0f;
 }
 
-__device__ __forceinline__ uint32_t lo_word(const uint32_t (&w)[8], int i) { return w[i]; }
+__device__ __forceinline__ uint32_t lo_word(const uint32_t (&w)[4], int i) { return w[i]; }
 
-// The producers fetch a stage's raw weight bytes two stages before they
+// The producers fetch a stage's raw weight bytes QgDepth stages before they
 // decode them (QgRaw in registers), so the loads' latency overlaps the
 // decode and the shared-memory stores of the stages in between.
+// A thread's share of a stage is part pi (0..3) of its row's 64 weights:
+// half h = pi / 2 (Q4_K: the low or high nibbles; Q6_K: the first or second
+// 32 values), and within it the 16 weights of k-chunks 2 (pi % 2), +1.
 template <int TYPE> struct QgRaw { uint32_t k0; };
-template <> struct QgRaw<T_Q4_K> { uint4 hdr, q0, q1; uint32_t k0; };
-template <> struct QgRaw<T_Q6_K> { uint32_t ql[8], qh[8], sc, d, k0; };
+template <> struct QgRaw<T_Q4_K> { uint4 hdr, q; uint32_t k0; };
+template <> struct QgRaw<T_Q6_K> { uint32_t ql[4], qh[4], sc, d, k0; };
+template <int TYPE> struct QgDepth { static constexpr int D = TYPE == T_Q4_K ? 4 : 2; };   // within 120 registers
 
-// 32 bytes at a 2-byte aligned address, as 8 words: 9 aligned words and a
-// funnel shift (the 4 bytes past the range lie inside the same Q6_K block).
-__device__ __forceinline__ void qg_ld32_a2(const uint8_t *ptr, uint32_t out[8]) {
+// 16 bytes at a 2-byte aligned address, as 4 words: 5 aligned words and a
+// funnel shift (the bytes past the range lie inside the same Q6_K block).
+__device__ __forceinline__ void qg_ld16_a2(const uint8_t *ptr, uint32_t out[4]) {
     const uint32_t *w = reinterpret_cast<const uint32_t *>(reinterpret_cast<uintptr_t>(ptr) & ~(uintptr_t)3);
     const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(ptr) & 3u) * 8u;
-    uint32_t v[9];
+    uint32_t v[5];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) v[i] = __ldg(w + i);
+    for (int i = 0; i < 5; ++i) v[i] = __ldg(w + i);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) out[i] = __funnelshift_r(v[i], v[i + 1], sh);
+    for (int i = 0; i < 4; ++i) out[i] = __funnelshift_r(v[i], v[i + 1], sh);
 }
 
 template <int TYPE>
-__device__ __forceinline__ void qg_fetch(const uint8_t *row, uint32_t k0, uint32_t half, QgRaw<TYPE> &r) {
+__device__ __forceinline__ void qg_fetch(const uint8_t *row, uint32_t k0, uint32_t pi, QgRaw<TYPE> &r) {
     r.k0 = k0;
+    const uint32_t half = pi >> 1, part = pi & 1u;
     if constexpr (TYPE == T_Q4_K) {
         const uint8_t *b = row + (uint64_t)(k0 >> 8) * 144;
         const uint32_t j0 = (k0 & 255u) >> 5;
         r.hdr = __ldg(reinterpret_cast<const uint4 *>(b));
-        r.q0 = __ldg(reinterpret_cast<const uint4 *>(b + 16 + (j0 >> 1) * 32));
-        r.q1 = __ldg(reinterpret_cast<const uint4 *>(b + 32 + (j0 >> 1) * 32));
+        r.q = __ldg(reinterpret_cast<const uint4 *>(b + 16 + (j0 >> 1) * 32 + 16 * part));
     } else if constexpr (TYPE == T_Q6_K) {
         const uint8_t *b = row + (uint64_t)(k0 >> 8) * 210;
         const uint32_t c = (k0 & 255u) >> 6, h = c >> 1;
-        qg_ld32_a2(b + 64 * h + 32 * half, r.ql);   // quarter q = 2 (c % 2) + half: ql bytes 32 (q % 2) ..
-        qg_ld32_a2(b + 128 + 32 * h, r.qh);
+        qg_ld16_a2(b + 64 * h + 32 * half + 16 * part, r.ql);   // quarter q = 2 (c % 2) + half: ql bytes 32 (q % 2) ..
+        qg_ld16_a2(b + 128 + 32 * h + 16 * part, r.qh);
         r.sc = __ldg(reinterpret_cast<const unsigned short *>(b + 192 + 4 * c + 2 * half));
         r.d = __ldg(reinterpret_cast<const unsigned short *>(b + 208));
     }
@@ -137,7 +150,8 @@ __device__ __forceinline__ void qg_fetch(const uint8_t *row, uint32_t k0, uint32
 // quarters 2 (c % 2) and 2 (c % 2) + 1; low bits from ql, high bits from qh,
 // one scale byte per 16 weights.
 template <int TYPE>
-__device__ __forceinline__ void qg_decode(const uint8_t *row, const QgRaw<TYPE> &r, uint32_t half, uint4 out[4]) {
+__device__ __forceinline__ void qg_decode(const uint8_t *row, const QgRaw<TYPE> &r, uint32_t pi, uint4 out[2]) {
+    const uint32_t half = pi >> 1, part = pi & 1u;
     if constexpr (TYPE == T_Q4_K) {
         const uint32_t j = ((r.k0 & 255u) >> 5) + half;
         const uint8_t *s = reinterpret_cast<const uint8_t *>(&r.hdr) + 4;
@@ -146,39 +160,41 @@ __device__ __forceinline__ void qg_decode(const uint8_t *row, const QgRaw<TYPE> 
         else { sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
         const float d = f16_exact(r.hdr.x & 0xFFFFu), dmin = f16_exact(r.hdr.x >> 16);
         const float a = __fmul_rn(d, (float)sc), c = __fmul_rn(dmin, (float)mn);
-        const uint32_t q[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
+        const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
         const uint32_t sh = half ? 4u : 0u;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-            const uint32_t w0 = q[2 * cc], w1 = q[2 * cc + 1];
+        for (int cc = 0; cc < 2; ++cc) {
+            const uint32_t w0 = (q[2 * cc] >> sh) & 0x0F0F0F0Fu, w1 = (q[2 * cc + 1] >> sh) & 0x0F0F0F0Fu;
             float v[8];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                v[k] = __fsub_rn(__fmul_rn(a, (float)((w0 >> (8 * k + sh)) & 15u)), c);
-                v[4 + k] = __fsub_rn(__fmul_rn(a, (float)((w1 >> (8 * k + sh)) & 15u)), c);
+                v[k] = __fsub_rn(__fmul_rn(a, qg_byte_f(w0, k)), c);
+                v[4 + k] = __fsub_rn(__fmul_rn(a, qg_byte_f(w1, k)), c);
             }
             out[cc] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
         }
     } else if constexpr (TYPE == T_Q6_K) {
         const uint32_t c = (r.k0 & 255u) >> 6, q = 2u * (c & 1u) + half;
         const float d = f16_exact(r.d);
+        const float ds = __fmul_rn(d, (float)(int)(int8_t)((r.sc >> (8 * part)) & 255u));   // one scale per 16 weights
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {   // elements 8 c4 .. 8 c4 + 7 of this half
-            const float ds = __fmul_rn(d, (float)(int)(int8_t)((r.sc >> (8 * (c4 >> 1))) & 255u));
-            const uint32_t l0 = lo_word(r.ql, 2 * c4), l1 = lo_word(r.ql, 2 * c4 + 1);
-            const uint32_t h0 = lo_word(r.qh, 2 * c4), h1 = lo_word(r.qh, 2 * c4 + 1);
+        for (int c4 = 0; c4 < 2; ++c4) {   // elements 16 part + 8 c4 .. + 7 of this half
+            // four 6-bit values per word: low nibbles from ql, two high bits from qh
+            const uint32_t lsh = (q >> 1) * 4, hsh = q * 2;
+            const uint32_t e0 = ((lo_word(r.ql, 2 * c4) >> lsh) & 0x0F0F0F0Fu) | (((lo_word(r.qh, 2 * c4) >> hsh) & 0x03030303u) << 4);
+            const uint32_t e1 = ((lo_word(r.ql, 2 * c4 + 1) >> lsh) & 0x0F0F0F0Fu) |
+                                (((lo_word(r.qh, 2 * c4 + 1) >> hsh) & 0x03030303u) << 4);
             float v[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const uint32_t lw = t < 4 ? l0 : l1, hw = t < 4 ? h0 : h1, bsh = 8u * (t & 3);
-                const uint32_t lo = ((lw >> bsh) >> ((q >> 1) * 4)) & 15u, hi = ((hw >> bsh) >> (q * 2)) & 3u;
-                v[t] = __fmul_rn(ds, (float)((int)(lo | (hi << 4)) - 32));
+            for (int t = 0; t < 4; ++t) {
+                v[t] = __fmul_rn(ds, qg_byte_f(e0, t) - 32.0f);
+                v[4 + t] = __fmul_rn(ds, qg_byte_f(e1, t) - 32.0f);
             }
             out[c4] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
         }
     } else {
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) out[cc] = qg_dq8<TYPE>(row, r.k0 + 32 * half + 8 * cc);
+        for (int cc = 0; cc < 2; ++cc) out[cc] = qg_dq8<TYPE>(row, r.k0 + 32 * half + 16 * part + 8 * cc);
     }
 }
 
@@ -188,7 +204,7 @@ template <int TYPE>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t base = smem_u32(smem);
-    const uint32_t full0 = base, empty0 = base + 8 * QG_NS, accb = base + 16 * QG_NS;
+    const uint32_t full0 = base, empty0 = base + 8 * QG_NS, accb = base + 16 * QG_NS, bfull0 = accb + 8;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 512);
     volatile int *bad = reinterpret_cast<volatile int *>(smem + 520);
     const uint32_t st0 = base + QG_HDR;
@@ -199,7 +215,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     const uint32_t kb = min(nk_all, blockIdx.z * per), nk = min(nk_all, kb + per) - kb;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < QG_NS; ++s) { mbar_init(full0 + 8 * s, QG_PT); mbar_init(empty0 + 8 * s, 1); }
+        // full: one arrival per producer warp (A); bfull: the B copy's bytes
+        for (int s = 0; s < QG_NS; ++s) {
+            mbar_init(full0 + 8 * s, QG_PT / 32);
+            mbar_init(empty0 + 8 * s, 1);
+            mbar_init(bfull0 + 8 * s, 1);
+        }
         mbar_init(accb, 1);
         *bad = 0;
         mbar_fence_init();
@@ -214,71 +235,84 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     const uint32_t tmem = *tmem_slot;
 
     if (warp < QG_PT / 32) {
-        // ------- producers: half `wh` of weight row wr, and token i -------
-        const uint32_t i = threadIdx.x, wr = i >> 1, wh = i & 1u;
-        const uint32_t row = r0 + wr, tok = t0 + i;
+        // ---- producers: part wh of weight row wr ----
+        const uint32_t i = threadIdx.x, wr = i / QG_PARTS, wh = i % QG_PARTS;
+        const uint32_t row = r0 + wr;
         const uint8_t *wrow = p.w + (uint64_t)min(row, p.rows - 1) * p.rb;
-        const __half *xrow = p.x16 + (uint64_t)tok * p.cols;   // padded to whole tiles of tokens
+        // this token tile's activations, already in the B layout: a stage is
+        // QG_B_BYTES contiguous bytes
+        const uint8_t *xtile = reinterpret_cast<const uint8_t *>(p.x16) + (uint64_t)blockIdx.y * (p.cols / 8) * QG_N * 16u;
         // canonical offsets: core matrix r/8 at SBO = 128 B, row r%8 at 16 B
-        const uint32_t aoff = (wr >> 3) * 128u + (wr & 7u) * 16u, boff = (i >> 3) * 128u + (i & 7u) * 16u;
-        // token i's 64 activations of stage kt into its slot: cp.async, one
-        // stage ahead, waited for (this thread's own copies) before the
-        // stage is declared full
+        const uint32_t aoff = (wr >> 3) * 128u + (wr & 7u) * 16u;
+        // the B operand of stage kt: one bulk copy (no multicast) by thread 0,
+        // two stages ahead, completing on the stage's bfull barrier
+        uint32_t b_issued = 0;   // stages whose B copy thread 0 issued
         auto put_b = [&](uint32_t kt) {
-            const uint32_t sb = st0 + (kt % QG_NS) * QG_STAGE + QG_A_BYTES;
-            const __half *src = xrow + (kb + kt) * QG_KT;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) cp_async16(sb + c * (QG_N * 16u) + boff, src + 8 * c);
+            if (i == 0) {
+                const uint32_t s = kt % QG_NS;
+                mbar_arrive_expect_tx(bfull0 + 8 * s, QG_B_BYTES);
+                bulk_g2s(st0 + s * QG_STAGE + QG_A_BYTES, xtile + (uint64_t)(kb + kt) * QG_B_BYTES, QG_B_BYTES, bfull0 + 8 * s);
+            }
+            b_issued = kt + 1;
         };
         auto fetch = [&](uint32_t kt, QgRaw<TYPE> &rw) {
             if (kt < nk && row < p.rows) qg_fetch<TYPE>(wrow, (kb + kt) * QG_KT, wh, rw);
         };
-        // one stage: the next stage's activations go out (its slot freed
-        // first), this stage's weights are decoded from rw, rw is refilled
-        // with the raw bytes of the stage after next
+        // one stage: the activations of the stage after next go out (their
+        // slot freed first), this stage's weights are decoded from rw, rw is
+        // refilled with the raw bytes of stage kt + D
         auto stage = [&](uint32_t kt, QgRaw<TYPE> &rw) -> bool {
-            if (kt + 1 < nk) {
-                const uint32_t s1 = (kt + 1) % QG_NS;
-                if (kt + 1 >= QG_NS && !qg_wait(empty0 + 8 * s1, (((kt + 1) / QG_NS) - 1) & 1u)) return false;
-                if (*bad) return false;
-                put_b(kt + 1);
+            if (kt + 2 < nk) {   // warp-uniform decision: the warp arrives as one below
+                const uint32_t s2 = (kt + 2) % QG_NS;
+                const bool freed = kt + 2 < QG_NS || qg_wait(empty0 + 8 * s2, (((kt + 2) / QG_NS) - 1) & 1u);
+                if (!__all_sync(0xffffffffu, freed && !*bad)) return false;
+                put_b(kt + 2);
             }
-            cp_async_commit();
             const uint32_t sa = st0 + (kt % QG_NS) * QG_STAGE;
-            uint4 wv[4];
+            uint4 wv[2];
             if (row < p.rows) {
                 qg_decode<TYPE>(wrow, rw, wh, wv);
             } else {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) wv[c] = make_uint4(0, 0, 0, 0);
+                wv[0] = wv[1] = make_uint4(0, 0, 0, 0);
             }
-            // A: k-chunks 4 wh .. 4 wh + 3 of row wr, LBO = 128 rows x 16 B
+            // A: k-chunks 2 wh, 2 wh + 1 of row wr (part wh = half * 2 + part:
+            // chunk 4 half + 2 part), LBO = 128 rows x 16 B
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + (4 * wh + c) * (QG_M * 16u) + aoff),
+            for (int c = 0; c < 2; ++c)
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + (2 * wh + c) * (QG_M * 16u) + aoff),
                              "r"(wv[c].x), "r"(wv[c].y), "r"(wv[c].z), "r"(wv[c].w) : "memory");
-            fetch(kt + 2, rw);
-            cp_async_wait<1>();   // this stage's activations have landed
-            qg_fence_proxy();     // the tensor core (async proxy) reads what the generic stores and copies wrote
-            mbar_arrive(full0 + 8 * (kt % QG_NS));
+            fetch(kt + QgDepth<TYPE>::D, rw);
+            qg_fence_proxy();     // the tensor core (async proxy) reads what the generic stores wrote
+            __syncwarp();         // every lane's stores and fence before the warp's one arrival
+            if (lane == 0) mbar_arrive(full0 + 8 * (kt % QG_NS));
             return true;
         };
-        QgRaw<TYPE> ra, rb;
-        fetch(0, ra);
-        fetch(1, rb);
-        if (nk) put_b(0);
-        cp_async_commit();
-        for (uint32_t kt = 0; kt < nk; kt += 2) {
-            if (!stage(kt, ra)) { *bad = 1; break; }
-            if (kt + 1 < nk && !stage(kt + 1, rb)) { *bad = 1; break; }
+        constexpr int D = QgDepth<TYPE>::D;
+        QgRaw<TYPE> raw[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) fetch(d, raw[d]);
+        if (nk > 0) put_b(0);   // slots 0 and 1 start free
+        if (nk > 1) put_b(1);
+        for (uint32_t kt = 0; kt < nk && !*bad; kt += D) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                if (kt + d < nk && !stage(kt + d, raw[d])) { *bad = 1; break; }
+            }
         }
-        cp_async_wait<0>();
+        if (*bad && i == 0) {
+            // copies may still be landing in slots nobody will read: wait
+            // (bounded) for the newest one of every slot (older ones were
+            // consumed before their slot was reused) before the CTA can exit
+            for (uint32_t kt = b_issued > (uint32_t)QG_NS ? b_issued - QG_NS : 0; kt < b_issued; ++kt)
+                qg_wait(bfull0 + 8 * (kt % QG_NS), (kt / QG_NS) & 1u);
+        }
         // ---------------- epilogue: accumulator rows -> Y ------------------
         const bool ok = !*bad && qg_wait(accb, 0);
         qg_fence_after();
+        constexpr uint32_t CW = QG_N / (QG_PT / 128);   // columns per warp of a lane quadrant
         const uint32_t rr = r0 + 32u * (warp & 3) + lane;
 #pragma unroll 1
-        for (uint32_t c0 = (warp >> 2) * (QG_N / 2); c0 < (warp >> 2) * (QG_N / 2) + QG_N / 2; c0 += 16) {
+        for (uint32_t c0 = (warp >> 2) * CW; c0 < (warp >> 2) * CW + CW; c0 += 16) {
             uint32_t v[16];
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -305,7 +339,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         // ---------------- MMA issue (one thread) ----------------------------
         for (uint32_t kt = 0; kt < nk; ++kt) {
             const uint32_t s = kt % QG_NS;
-            if (!qg_wait(full0 + 8 * s, (kt / QG_NS) & 1u)) { *bad = 1; break; }
+            if (!qg_wait(full0 + 8 * s, (kt / QG_NS) & 1u) || !qg_wait(bfull0 + 8 * s, (kt / QG_NS) & 1u)) { *bad = 1; break; }
             qg_fence_after();
             const uint32_t sa = st0 + s * QG_STAGE, sb = sa + QG_A_BYTES;
 #pragma unroll
@@ -321,6 +355,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     qg_fence_before();
     __syncthreads();
     if (warp == QG_PT / 32) {
+        // every MMA this CTA issued has completed (the final commit) before
+        // its tensor memory goes back; bounded like every other wait
+        if (lane == 0) qg_wait(accb, 0);
+        __syncwarp();
         qg_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)QG_N) : "memory");
     }
@@ -340,12 +378,22 @@ __global__ void qg_reduce_kernel(const float *__restrict__ planes, uint32_t nz, 
 }
 
 // fp32 rows [rows x cols] -> fp16 [rows_pad x cols], rows past `rows` zero
+// The activations as fp16 in the B operand's shared-memory layout, so one
+// bulk copy moves a stage: [token tile][k-chunk of 8][QG_N tokens][8],
+// tokens past `rows` zero. Each thread converts 8 consecutive values.
 __global__ void qg_to_half_kernel(const float *__restrict__ x, uint64_t xs, __half *__restrict__ out, uint32_t rows,
                                   uint32_t rows_pad, uint32_t cols) {
-    const uint64_t n = (uint64_t)rows_pad * cols;
+    const uint32_t nch = cols / 8;
+    const uint64_t n = (uint64_t)rows_pad * nch;   // 16-byte pieces
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint32_t r = (uint32_t)(i / cols), c = (uint32_t)(i % cols);
-        out[i] = __float2half_rn(r < rows ? x[(uint64_t)r * xs + c] : 0.0f);
+        const uint32_t tt = (uint32_t)(i % QG_N), g = (uint32_t)((i / QG_N) % nch), y = (uint32_t)(i / ((uint64_t)QG_N * nch));
+        const uint32_t r = y * QG_N + tt;
+        uint4 h = make_uint4(0, 0, 0, 0);
+        if (r < rows) {   // scalar loads: x may be only 4-byte aligned
+            const float *src = x + (uint64_t)r * xs + 8 * g;
+            h = make_uint4(qg_h2(src[0], src[1]), qg_h2(src[2], src[3]), qg_h2(src[4], src[5]), qg_h2(src[6], src[7]));
+        }
+        reinterpret_cast<uint4 *>(out)[i] = h;
     }
 }
 
@@ -383,7 +431,7 @@ cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_str
     note_launches(z > 1 ? 3 : 2);
     const uint64_t n = (uint64_t)tpad * p.cols;
     __half *x16 = static_cast<__half *>(work);
-    qg_to_half_kernel<<<(unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 16), 256, 0, st>>>(
+    qg_to_half_kernel<<<(unsigned)std::min<uint64_t>((n / 8 + 255) / 256, (uint64_t)n_sm * 16), 256, 0, st>>>(
         x, x_stride, x16, p.tokens, tpad, p.cols);
     p.x16 = x16;
     p.planes = reinterpret_cast<float *>(static_cast<uint8_t *>(work) + ((n * sizeof(__half) + 255) & ~(size_t)255));
