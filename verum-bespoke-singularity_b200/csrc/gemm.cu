@@ -167,9 +167,12 @@ __device__ __forceinline__ void qg_decode(const uint8_t *row, const QgRaw<TYPE> 
             const uint32_t w0 = (q[2 * cc] >> sh) & 0x0F0F0F0Fu, w1 = (q[2 * cc + 1] >> sh) & 0x0F0F0F0Fu;
             float v[8];
 #pragma unroll
+            // a = d*sc has at most 17 significant bits and q at most 4, so
+            // a*q is exact in fp32 and the FMA rounds once, as the
+            // reference's fmul then fsub does
             for (int k = 0; k < 4; ++k) {
-                v[k] = __fsub_rn(__fmul_rn(a, qg_byte_f(w0, k)), c);
-                v[4 + k] = __fsub_rn(__fmul_rn(a, qg_byte_f(w1, k)), c);
+                v[k] = __fmaf_rn(a, qg_byte_f(w0, k), -c);
+                v[4 + k] = __fmaf_rn(a, qg_byte_f(w1, k), -c);
             }
             out[cc] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
         }
@@ -186,9 +189,9 @@ __device__ __forceinline__ void qg_decode(const uint8_t *row, const QgRaw<TYPE> 
                                 (((lo_word(r.qh, 2 * c4 + 1) >> hsh) & 0x03030303u) << 4);
             float v[8];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                v[t] = __fmul_rn(ds, qg_byte_f(e0, t) - 32.0f);
-                v[4 + t] = __fmul_rn(ds, qg_byte_f(e1, t) - 32.0f);
+            for (int t = 0; t < 4; ++t) {   // q - 32 exactly: (2^23 + q) - (2^23 + 32)
+                v[t] = __fmul_rn(ds, __uint_as_float(__byte_perm(e0, 0x4B000000u, 0x7440u | t)) - 8388640.0f);
+                v[4 + t] = __fmul_rn(ds, __uint_as_float(__byte_perm(e1, 0x4B000000u, 0x7440u | t)) - 8388640.0f);
             }
             out[c4] = make_uint4(qg_h2(v[0], v[1]), qg_h2(v[2], v[3]), qg_h2(v[4], v[5]), qg_h2(v[6], v[7]));
         }
