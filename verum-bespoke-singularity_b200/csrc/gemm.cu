@@ -8,20 +8,20 @@
 // token at a time through forward_token (src/main.c:901-904), every token
 // streaming every weight. Here one CTA owns a tile of 128 weight rows x 256
 // tokens:
-//  * producer warps (256 threads) walk K in steps of 64: threads 2r and
-//    2r + 1 dequantize row r's 64 weights, 32 each (the GGUF block decode of
-//    src/vbs_dequant.c, rounded to fp16; the raw bytes are fetched two
-//    stages ahead into registers), and thread i copies token i's 64
-//    activations (fp16, converted once per call; cp.async, one stage
-//    ahead), all into the UMMA
-//    canonical K-major layout in shared memory: 8-row x 16-byte core
-//    matrices 128 bytes apart along M/N (SBO), k-chunks of 8 elements one
-//    operand-height x 16 bytes apart (LBO);
+//  * producer warps (512 threads) walk K in steps of 64: threads 4r..4r+3
+//    dequantize row r's 64 weights, 16 each (the GGUF block decode of
+//    src/vbs_dequant.c, rounded to fp16; the raw bytes are fetched two to
+//    four stages ahead into registers) into the UMMA canonical K-major
+//    layout in shared memory: 8-row x 16-byte core matrices 128 bytes apart
+//    along M/N (SBO), k-chunks of 8 elements one operand-height x 16 bytes
+//    apart (LBO);
+//  * a loader warp moves each stage's activations with one bulk copy: they
+//    were converted to fp16 once per call, already in that layout;
 //  * one thread issues tcgen05.mma.kind::f16 (M = 128, N = 256, K = 16, four
 //    per stage) into a 128 x 256 fp32 accumulator in tensor memory and
 //    releases each stage with tcgen05.commit on its mbarrier;
 //  * after the last stage the producer warps read the accumulator back with
-//    tcgen05.ld (warp w: lanes 32 (w % 4).. = rows, columns 128 (w / 4).. =
+//    tcgen05.ld (warp w: lanes 32 (w % 4).. = rows, columns 64 (w / 4).. =
 //    tokens) and store Y (split-K: a plane per split, summed in order).
 // Every wait is bounded; a timeout records DERR_TIMEOUT_* and the CTA
 // skips the rest of its tile (tensor memory is always released).
@@ -38,7 +38,7 @@ constexpr int QG_KT = 64;            // k per stage
 constexpr int QG_NS = 4;             // stages
 constexpr int QG_PT = 512;           // producer / epilogue threads: 4 per weight row, 2 per token
 constexpr uint32_t QG_PARTS = QG_PT / QG_M;   // threads per weight row, 16 of its 64 stage weights each
-constexpr int QG_THREADS = QG_PT + 32;   // + the MMA warp
+constexpr int QG_THREADS = QG_PT + 64;   // + the MMA warp + the activation loader warp
 constexpr uint32_t QG_A_BYTES = QG_M * QG_KT * 2, QG_B_BYTES = QG_N * QG_KT * 2;
 constexpr uint32_t QG_STAGE = QG_A_BYTES + QG_B_BYTES;
 constexpr uint32_t QG_HDR = 1024;    // barriers + tensor-memory address
@@ -242,36 +242,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         const uint32_t i = threadIdx.x, wr = i / QG_PARTS, wh = i % QG_PARTS;
         const uint32_t row = r0 + wr;
         const uint8_t *wrow = p.w + (uint64_t)min(row, p.rows - 1) * p.rb;
-        // this token tile's activations, already in the B layout: a stage is
-        // QG_B_BYTES contiguous bytes
-        const uint8_t *xtile = reinterpret_cast<const uint8_t *>(p.x16) + (uint64_t)blockIdx.y * (p.cols / 8) * QG_N * 16u;
         // canonical offsets: core matrix r/8 at SBO = 128 B, row r%8 at 16 B
         const uint32_t aoff = (wr >> 3) * 128u + (wr & 7u) * 16u;
-        // the B operand of stage kt: one bulk copy (no multicast) by thread 0,
-        // two stages ahead, completing on the stage's bfull barrier
-        uint32_t b_issued = 0;   // stages whose B copy thread 0 issued
-        auto put_b = [&](uint32_t kt) {
-            if (i == 0) {
-                const uint32_t s = kt % QG_NS;
-                mbar_arrive_expect_tx(bfull0 + 8 * s, QG_B_BYTES);
-                bulk_g2s(st0 + s * QG_STAGE + QG_A_BYTES, xtile + (uint64_t)(kb + kt) * QG_B_BYTES, QG_B_BYTES, bfull0 + 8 * s);
-            }
-            b_issued = kt + 1;
-        };
         auto fetch = [&](uint32_t kt, QgRaw<TYPE> &rw) {
             if (kt < nk && row < p.rows) qg_fetch<TYPE>(wrow, (kb + kt) * QG_KT, wh, rw);
         };
-        // one stage: the activations of the stage after next go out (their
-        // slot freed first), this stage's weights are decoded from rw, rw is
-        // refilled with the raw bytes of stage kt + D
+        // one stage: once the slot is free, this stage's weights are decoded
+        // from rw, and rw is refilled with the raw bytes of stage kt + D
         auto stage = [&](uint32_t kt, QgRaw<TYPE> &rw) -> bool {
-            if (kt + 2 < nk) {   // warp-uniform decision: the warp arrives as one below
-                const uint32_t s2 = (kt + 2) % QG_NS;
-                const bool freed = kt + 2 < QG_NS || qg_wait(empty0 + 8 * s2, (((kt + 2) / QG_NS) - 1) & 1u);
-                if (!__all_sync(0xffffffffu, freed && !*bad)) return false;
-                put_b(kt + 2);
-            }
-            const uint32_t sa = st0 + (kt % QG_NS) * QG_STAGE;
+            const uint32_t s0 = kt % QG_NS;   // warp-uniform decision: the warp arrives as one below
+            const bool freed = kt < QG_NS || qg_wait(empty0 + 8 * s0, ((kt / QG_NS) - 1) & 1u);
+            if (!__all_sync(0xffffffffu, freed && !*bad)) return false;
+            const uint32_t sa = st0 + s0 * QG_STAGE;
             uint4 wv[2];
             if (row < p.rows) {
                 qg_decode<TYPE>(wrow, rw, wh, wv);
@@ -294,20 +276,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         QgRaw<TYPE> raw[D];
 #pragma unroll
         for (int d = 0; d < D; ++d) fetch(d, raw[d]);
-        if (nk > 0) put_b(0);   // slots 0 and 1 start free
-        if (nk > 1) put_b(1);
         for (uint32_t kt = 0; kt < nk && !*bad; kt += D) {
 #pragma unroll
             for (int d = 0; d < D; ++d) {
                 if (kt + d < nk && !stage(kt + d, raw[d])) { *bad = 1; break; }
             }
-        }
-        if (*bad && i == 0) {
-            // copies may still be landing in slots nobody will read: wait
-            // (bounded) for the newest one of every slot (older ones were
-            // consumed before their slot was reused) before the CTA can exit
-            for (uint32_t kt = b_issued > (uint32_t)QG_NS ? b_issued - QG_NS : 0; kt < b_issued; ++kt)
-                qg_wait(bfull0 + 8 * (kt % QG_NS), (kt / QG_NS) & 1u);
         }
         // ---------------- epilogue: accumulator rows -> Y ------------------
         const bool ok = !*bad && qg_wait(accb, 0);
@@ -338,6 +311,29 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
             }
         }
         if (!ok && lane == 0) dev_flag_error(p.err, DERR_TIMEOUT_FULL);
+    } else if (warp == QG_PT / 32 + 1) {
+        // -------- activation loader: the B operand of every stage, one bulk
+        // copy (no multicast) per stage, as soon as its slot is free --------
+        if (lane == 0) {
+            // this token tile's activations, already in the B layout: a stage
+            // is QG_B_BYTES contiguous bytes
+            const uint8_t *xtile = reinterpret_cast<const uint8_t *>(p.x16) + (uint64_t)blockIdx.y * (p.cols / 8) * QG_N * 16u;
+            uint32_t issued = 0;
+            for (uint32_t kt = 0; kt < nk; ++kt) {
+                const uint32_t s = kt % QG_NS;
+                if ((kt >= QG_NS && !qg_wait(empty0 + 8 * s, ((kt / QG_NS) - 1) & 1u)) || *bad) { *bad = 1; break; }
+                mbar_arrive_expect_tx(bfull0 + 8 * s, QG_B_BYTES);
+                bulk_g2s(st0 + s * QG_STAGE + QG_A_BYTES, xtile + (uint64_t)(kb + kt) * QG_B_BYTES, QG_B_BYTES, bfull0 + 8 * s);
+                issued = kt + 1;
+            }
+            if (*bad) {
+                // copies may still be landing in slots nobody will read: wait
+                // (bounded) for the newest one of every slot (older ones were
+                // consumed before their slot was reused) before the CTA exits
+                for (uint32_t kt = issued > (uint32_t)QG_NS ? issued - QG_NS : 0; kt < issued; ++kt)
+                    qg_wait(bfull0 + 8 * (kt % QG_NS), (kt / QG_NS) & 1u);
+            }
+        }
     } else if (lane == 0) {
         // ---------------- MMA issue (one thread) ----------------------------
         for (uint32_t kt = 0; kt < nk; ++kt) {
