@@ -746,7 +746,13 @@ def main():
     prefill_s = time.perf_counter() - t0
 
     stream = torch.cuda.ExternalStream(dec.stream)
-    dec.enqueue_steps(args.warmup)
+    # Under tensor parallelism the last warm-up step is enqueued after the
+    # barrier, just before the start event: it cannot finish on any rank
+    # before every rank's exchange words arrived, so it lines the ranks up
+    # on the device and the host-side skew of their launches stays out of
+    # the timed steps.
+    aligned = 1 if dist and args.warmup > 0 else 0
+    dec.enqueue_steps(args.warmup - aligned)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -756,12 +762,14 @@ def main():
         time.sleep(0.3)
         torch.cuda.synchronize()
         clk.mark()
+        if aligned:
+            dec.enqueue_steps(1)
         ev0.record(stream)
         dec.enqueue_steps(args.steps)
         ev1.record(stream)
         torch.cuda.synchronize()
         clk.stop()
-    launches = vbs.kernel_launches() - l0
+    launches = vbs.kernel_launches() - l0 - aligned * dec.kernels_per_step
     ms = ev0.elapsed_time(ev1)
     if dist:
         t = torch.tensor([ms], dtype=torch.float64)
