@@ -43,7 +43,8 @@ constexpr uint32_t MB_MAXST = 16;
 constexpr uint32_t MB_SMEM = 227u * 1024u;
 // shared memory: barriers [0, 256) | abort 256 | red [MB_NCW warps][16 rows][8 seqs] fp32 at 1024 |
 // x fp16 [8][ck] | group sums [8][ck/16] fp32 | ring
-constexpr uint32_t MB_RED = 1024, MB_X = MB_RED + MB_NCW * 16 * MB_B * 4;
+constexpr uint32_t MB_NU = 4;                      // tiles whose row sums share one pair of consumer barriers
+constexpr uint32_t MB_RED = 1024, MB_X = MB_RED + MB_NU * MB_NCW * 16 * MB_B * 4;
 
 struct MbGeom {
     uint32_t ck, rs, nstage, stage0, nch, xs_off;
@@ -96,14 +97,39 @@ __device__ __forceinline__ void mb_q6_pairs(uint32_t v, uint32_t &p02, uint32_t 
     p13 = *reinterpret_cast<const uint32_t *>(&hb);
 }
 
-// One warp, 16 rows (stage rows g, g+8 at rowA/rowB, pads pa/pb), one
-// 256-column super-block at chunk column e (x at xh, group sums at xs).
-// acc: rows g, g+8 x sequences 2t, 2t+1.
+// This lane's B fragments of one 256-column super-block (8 sequences), held
+// in registers for every tile of the launch: a warp always works on the
+// same super-block of the chunk, so x is read from shared memory once.
+template <int TYPE> struct MbX;
+template <> struct MbX<T_Q4_K> { uint4 xv[8]; const float2 *xg; };   // per sub-block: x words; its group sums in shared memory
+template <> struct MbX<T_Q6_K> { uint2 xv[16]; };                 // per (half, 16-column part, quarter)
+
 template <int TYPE>
-__device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t pa, uint32_t pb, uint32_t e, uint32_t xh,
-                                        uint32_t ck, uint32_t xstride, const float *xs, int lane, float acc[4]) {
+__device__ __forceinline__ void mb_xfrag(uint32_t e, uint32_t xh, uint32_t xstride, const float *xs, int lane, MbX<TYPE> &f) {
     const int g = lane >> 2, t = lane & 3;
     const uint32_t xrow = xh + (uint32_t)g * xstride;   // this lane's B column is sequence g
+    if constexpr (TYPE == T_Q4_K) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) f.xv[s] = lds_u128(xrow + (e + 32 * s + 8 * t) * 2);
+        f.xg = reinterpret_cast<const float2 *>(xs + (e >> 5) * MB_B + 2 * t);   // [group][sequence]: + s * MB_B / 2
+    } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int l = 0; l < 2; ++l)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    f.xv[(h * 2 + l) * 4 + q] = lds_u64(xrow + (e + 128 * h + 32 * q + 4 * t + 16 * l) * 2);
+    }
+}
+
+// One warp, 16 rows (stage rows g, g+8 at rowA/rowB, pads pa/pb), one
+// 256-column super-block at chunk column e, x fragments in registers.
+// acc: rows g, g+8 x sequences 2t, 2t+1.
+template <int TYPE>
+__device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t pa, uint32_t pb, uint32_t e,
+                                        const MbX<TYPE> &xf, int lane, float acc[4]) {
+    const int t = lane & 3;
     if constexpr (TYPE == T_Q4_K) {
         const uint32_t sa = rowA + (e >> 8) * 144, sb = rowB + (e >> 8) * 144;
         const uint4 hA = lds_u128(sa), hB = lds_u128(sb);
@@ -128,7 +154,7 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
 #pragma unroll
             for (int hi = 0; hi < 2; ++hi) {
                 const int s = 2 * j + hi;
-                const uint4 xv = lds_u128(xrow + (e + 32 * s + 8 * t) * 2);
+                const uint4 xv = xf.xv[s];
                 float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {   // weights 8t+4hf .. +3
@@ -137,8 +163,7 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
                     mb_nib_pairs(hf ? wB.y : wB.x, 4 * hi, a[1], a[3]);
                     mma_f16_acc(c, a, hf ? xv.z : xv.x, hf ? xv.w : xv.y);
                 }
-                const uint32_t grp = (e >> 5) + s;   // group sums [group][8 sequences]
-                const float2 xg = *reinterpret_cast<const float2 *>(xs + grp * MB_B + 2 * t);
+                const float2 xg = xf.xg[s * (MB_B / 2)];   // the sub-block's x sums, sequences 2t, 2t+1
                 const float x0 = xg.x, x1 = xg.y;
                 acc[0] += dsc[0][s] * c[0] - dmm[0][s] * x0;
                 acc[1] += dsc[0][s] * c[1] - dmm[0][s] * x1;
@@ -165,7 +190,7 @@ __device__ __forceinline__ void mb_unit(uint32_t rowA, uint32_t rowB, uint32_t p
                     uint32_t a[4];
                     mb_q6_pairs(vA, a[0], a[2]);
                     mb_q6_pairs(vB, a[1], a[3]);
-                    const uint2 xv = lds_u64(xrow + (e + 128 * h + 32 * q + o) * 2);
+                    const uint2 xv = xf.xv[(h * 2 + (l0 >> 4)) * 4 + q];
                     float c[4] = {0.f, 0.f, 0.f, 0.f};
                     mma_f16_acc(c, a, xv.x, xv.y);
                     const uint32_t is = 8 * h + 2 * q + (l0 >> 4);
@@ -285,6 +310,11 @@ __global__ void __launch_bounds__(MB_THREADS, 1) mvb_kernel(const MvbParams p, c
     }
 
     const int g = lane >> 2, t = lane & 3;
+    // chunks are at most MB_CK = MB_NCW * 256 columns: one super-block per warp
+    const uint32_t e = (uint32_t)warp * 256u;
+    const bool has_e = e < ncol;
+    MbX<TYPE> xf;
+    if (has_e) mb_xfrag<TYPE>(e, xh, geo.xstride, xs, lane, xf);
     uint32_t slot = 0, round = 0;
     for (uint32_t tile = t0; tile < t1; ++tile) {
         bool ok = !*abort_flag;
@@ -301,31 +331,36 @@ __global__ void __launch_bounds__(MB_THREADS, 1) mvb_kernel(const MvbParams p, c
                 pa = (uint32_t)(reinterpret_cast<uintptr_t>(p.w + (uint64_t)ra * p.rb + boff) & 15);
                 pb = (uint32_t)(reinterpret_cast<uintptr_t>(p.w + (uint64_t)rb * p.rb + boff) & 15);
             }
-            for (uint32_t e = (uint32_t)warp * 256u; e < ncol; e += MB_NCW * 256u)
-                mb_unit<TYPE>(rowA, rowB, pa, pb, e, xh, geo.ck, geo.xstride, xs, lane, acc);
+            if (has_e) mb_unit<TYPE>(rowA, rowB, pa, pb, e, xf, lane, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(slot));
         if (++slot == nstage) { slot = 0; ++round; }
-        // rows g, g+8 x sequences 2t, 2t+1 -> the warps' sum, in warp order
-        float *rw = red + warp * 16 * MB_B;
+        // rows g, g+8 x sequences 2t, 2t+1 -> the warps' sum, in warp order,
+        // for MB_NU tiles at a time behind one pair of consumer barriers
+        const uint32_t k = (tile - t0) % MB_NU;
+        float *rw = red + (k * MB_NCW + warp) * 16 * MB_B;
         rw[g * MB_B + 2 * t] = acc[0];
         rw[g * MB_B + 2 * t + 1] = acc[1];
         rw[(g + 8) * MB_B + 2 * t] = acc[2];
         rw[(g + 8) * MB_B + 2 * t + 1] = acc[3];
-        named_bar_sync(1, MB_NCW * 32);
-        if (threadIdx.x < 16 * MB_B && !*abort_flag) {
-            const uint32_t rr = threadIdx.x / MB_B, b = threadIdx.x % MB_B, row = tile * 16 + rr;
-            float v = 0.f;
+        if (k == MB_NU - 1 || tile + 1 == t1) {
+            named_bar_sync(1, MB_NCW * 32);
+            static_assert(MB_NU * 16 * MB_B <= MB_NCW * 32, "one thread per buffered (tile, row, sequence)");
+            const uint32_t j = threadIdx.x / (16 * MB_B), rr = (threadIdx.x / MB_B) % 16, b = threadIdx.x % MB_B;
+            const uint32_t tj = tile - k + j, row = tj * 16 + rr;
+            if (j <= k && !*abort_flag) {
+                float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < MB_NCW; ++w) v += red[(w * 16 + rr) * MB_B + b];
-            if (b < p.batch && row < p.rows) {
-                float *dst = p.y_plane ? p.y_plane + ((uint64_t)blockIdx.y * p.batch + b) * p.rows + row
-                                       : p.y + (uint64_t)b * p.y_stride + row;
-                *dst = (p.accumulate && !p.y_plane) ? *dst + v : v;
+                for (int w = 0; w < MB_NCW; ++w) v += red[((j * MB_NCW + w) * 16 + rr) * MB_B + b];
+                if (b < p.batch && row < p.rows) {
+                    float *dst = p.y_plane ? p.y_plane + ((uint64_t)blockIdx.y * p.batch + b) * p.rows + row
+                                           : p.y + (uint64_t)b * p.y_stride + row;
+                    *dst = (p.accumulate && !p.y_plane) ? *dst + v : v;
+                }
             }
+            named_bar_sync(1, MB_NCW * 32);
         }
-        named_bar_sync(1, MB_NCW * 32);
     }
 }
 
