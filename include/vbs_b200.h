@@ -337,7 +337,7 @@ VBS_API void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d);
  * copied to logits_out (host, vocab floats; NULL skips the readback). */
 VBS_API int vbs_cu_decoder_forward(vbs_cu_decoder_t *d, const uint32_t *tokens, size_t n_tokens, float *logits_out);
 /* Prompt tokens as context: their KV rows are computed and stored at
- * positions position()..position()+n-1, up to 256 tokens sharing one pass
+ * positions position()..position()+n-1, up to 512 tokens sharing one pass
  * over the weights (the tcgen05 GEMM; a last chunk of up to 8 tokens through
  * the batched matvec; causal split-KV attention), no logits. The
  * next vbs_cu_decoder_forward / generate continues at position()+n; feed

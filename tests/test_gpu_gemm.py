@@ -4,8 +4,8 @@ memory), which serves vbs_cu_matvec above 8 sequences: prompt chunks and
 large decode batches. Every sequence's output against the reference's
 double-accumulated host math (vbs_host_linear_tile), for Q4_K, Q6_K and
 Q8_0, ragged row tiles (rows not a multiple of 128) and ragged token tiles
-(batches not a multiple of 256, the tile of tokens), with and without
-accumulation.
+(batches not a multiple of 512, the tokens of one CTA, and batches over
+two such tiles), with and without accumulation.
 
 Tolerance: the tensor cores take fp16 operands, so each weight and each
 activation carries one fp16 rounding (2^-11 relative); 2e-3 of
@@ -27,7 +27,7 @@ def torch(gpu):
 
 
 @pytest.mark.parametrize("t", [12, 14, 8])
-@pytest.mark.parametrize("rows,cols,B", [(512, 4096, 128), (300, 1024, 200), (128, 256, 17), (1000, 4096, 9), (256, 2048, 300)])
+@pytest.mark.parametrize("rows,cols,B", [(512, 4096, 128), (300, 1024, 200), (128, 256, 17), (1000, 4096, 9), (256, 2048, 300), (128, 1024, 600)])
 def test_gemm_matches_host_math(vbs, orc, torch, t, rows, cols, B, clean_errors):
     rb = orc.row_bytes(t, cols)
     w = torch.empty(rows * rb + 256, dtype=torch.uint8, device="cuda")

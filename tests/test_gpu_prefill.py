@@ -1,14 +1,14 @@
 """Batched prompt pass (vbs_cu_decoder_prefill) on a B200. The reference
 feeds a prompt one token at a time (src/main.c:901-904); the prefill runs
-up to 256 tokens per pass over the weights (the tcgen05 GEMM) and must leave the same KV cache
+up to 512 tokens per pass over the weights (the tcgen05 GEMM) and must leave the same KV cache
 behind, to the kernels' rounding:
 
 * against the oracle fed one token at a time: the logits of the prompt's
   last token and of teacher-forced steps after it (which attend to every
   prefilled row), for both cache layouts (persistent and per-op decoders);
-* against the same decoder fed token by token, over 300 positions that
-  cross a chunk boundary (and end on a short chunk through the batched
-  matvec), and in two prefill calls;
+* against the same decoder fed token by token, over 556 positions that
+  cross a 512-token chunk boundary (and end on a short chunk through the
+  batched matvec), and in two prefill calls;
 * refused, with the reason, where it does not apply.
 """
 import numpy as np
@@ -62,13 +62,13 @@ def test_prefill_vs_engine_oracle(vbs, orc, l8b_2layer, path, clean_errors):
 
 def test_prefill_matches_token_by_token(vbs, l8b_2layer, clean_errors):
     _, dm = l8b_2layer
-    toks = models.splitmix_ints(6, 300, 4096)
-    a, b, c = vbs.Decoder(dm, 512), vbs.Decoder(dm, 512), vbs.Decoder(dm, 512)
+    toks = models.splitmix_ints(6, 556, 4096)
+    a, b, c = vbs.Decoder(dm, 1024), vbs.Decoder(dm, 1024), vbs.Decoder(dm, 1024)
     lb = b.forward(toks)
     assert _rel(a.forward_prompt(toks), lb) <= 2e-3
     c.prefill(toks[:37])               # two calls: positions carry over
-    c.prefill(toks[37:-1])             # chunks of 256 and 6
-    assert c.position == 299
+    c.prefill(toks[37:-1])             # chunks of 512 and 6
+    assert c.position == 555
     assert _rel(c.forward(toks[-1:]), lb) <= 2e-3
     for t in (1, 2, 3):
         want = b.forward([t])

@@ -563,10 +563,10 @@ bool plan_persistent(vbs_cu_decoder *d) {
 // ---------------------------------------------------------------------------
 // prompt chunks: up to PF_CHUNK tokens share one pass over the weights
 // ---------------------------------------------------------------------------
-// Chunks of up to 256 tokens (one GEMM tile of tokens): the matrices go
+// Chunks of up to 512 tokens (one GEMM tile of tokens): the matrices go
 // through the tcgen05 GEMM (above 8 tokens) or the batched matvec (the
 // last, short chunk).
-constexpr uint32_t PF_CHUNK = 256;
+constexpr uint32_t PF_CHUNK = 512;
 
 bool prefill_buffers(vbs_cu_decoder *d) {
     if (d->pf_x) return true;

@@ -6,8 +6,9 @@
 //
 // The reference has no batched path at all: the engine feeds a prompt one
 // token at a time through forward_token (src/main.c:901-904), every token
-// streaming every weight. Here one CTA owns a tile of 128 weight rows x 256
-// tokens:
+// streaming every weight. Here one CTA owns a tile of 128 weight rows x 512
+// tokens (two activation tiles of 256), so each weight is decoded once for
+// 512 tokens:
 //  * producer warps (512 threads) walk K in steps of 64: threads 4r..4r+3
 //    dequantize row r's 64 weights, 16 each (the GGUF block decode of
 //    src/vbs_dequant.c, rounded to fp16; the raw bytes are fetched two to
@@ -18,10 +19,11 @@
 //  * a loader warp moves each stage's activations with one bulk copy: they
 //    were converted to fp16 once per call, already in that layout;
 //  * one thread issues tcgen05.mma.kind::f16 (M = 128, N = 256, K = 16, four
-//    per stage) into a 128 x 256 fp32 accumulator in tensor memory and
-//    releases each stage with tcgen05.commit on its mbarrier;
+//    per stage and activation tile) into two 128 x 256 fp32 accumulators in
+//    tensor memory (all 512 columns) and releases each stage with
+//    tcgen05.commit on its mbarrier;
 //  * after the last stage the producer warps read the accumulator back with
-//    tcgen05.ld (warp w: lanes 32 (w % 4).. = rows, columns 64 (w / 4).. =
+//    tcgen05.ld (warp w: lanes 32 (w % 4).. = rows, columns 128 (w / 4).. =
 //    tokens) and store Y (split-K: a plane per split, summed in order).
 // Every wait is bounded; a timeout records DERR_TIMEOUT_* and the CTA
 // skips the rest of its tile (tensor memory is always released).
@@ -33,14 +35,16 @@
 namespace vbs {
 
 constexpr int QG_M = 128;            // weight rows per tile (UMMA M)
-constexpr int QG_N = 256;            // tokens per tile (UMMA N)
+constexpr int QG_N = 256;            // tokens per MMA (UMMA N) and per activation tile
+constexpr int QG_NT = 2;             // activation tiles per CTA: each weight decoded once for 512 tokens
+constexpr int QG_TT = QG_N * QG_NT;  // tokens per CTA
 constexpr int QG_KT = 64;            // k per stage
-constexpr int QG_NS = 4;             // stages
+constexpr int QG_NS = 2;             // stages (80 KB each)
 constexpr int QG_PT = 512;           // producer / epilogue threads: 4 per weight row, 2 per token
 constexpr uint32_t QG_PARTS = QG_PT / QG_M;   // threads per weight row, 16 of its 64 stage weights each
 constexpr int QG_THREADS = QG_PT + 64;   // + the MMA warp + the activation loader warp
 constexpr uint32_t QG_A_BYTES = QG_M * QG_KT * 2, QG_B_BYTES = QG_N * QG_KT * 2;
-constexpr uint32_t QG_STAGE = QG_A_BYTES + QG_B_BYTES;
+constexpr uint32_t QG_STAGE = QG_A_BYTES + QG_NT * QG_B_BYTES;
 constexpr uint32_t QG_HDR = 1024;    // barriers + tensor-memory address
 constexpr uint32_t QG_SMEM = QG_HDR + QG_NS * QG_STAGE;
 
@@ -212,7 +216,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
     volatile int *bad = reinterpret_cast<volatile int *>(smem + 520);
     const uint32_t st0 = base + QG_HDR;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t r0 = blockIdx.x * QG_M, t0 = blockIdx.y * QG_N;
+    const uint32_t r0 = blockIdx.x * QG_M, t0 = blockIdx.y * QG_TT;
     // split-K: this CTA's stages [kb, kb + nk) of the row's K / 64
     const uint32_t nk_all = p.cols / QG_KT, per = (nk_all + gridDim.z - 1) / gridDim.z;
     const uint32_t kb = min(nk_all, blockIdx.z * per), nk = min(nk_all, kb + per) - kb;
@@ -228,8 +232,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         *bad = 0;
         mbar_fence_init();
     }
-    if (warp == QG_PT / 32) {   // tensor memory: QG_N columns of 32-bit accumulators
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)QG_N) : "memory");
+    if (warp == QG_PT / 32) {   // tensor memory: QG_TT columns of 32-bit accumulators (all 512)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)QG_TT) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     qg_fence_before();
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         // ---------------- epilogue: accumulator rows -> Y ------------------
         const bool ok = !*bad && qg_wait(accb, 0);
         qg_fence_after();
-        constexpr uint32_t CW = QG_N / (QG_PT / 128);   // columns per warp of a lane quadrant
+        constexpr uint32_t CW = QG_TT / (QG_PT / 128);   // columns per warp of a lane quadrant
         const uint32_t rr = r0 + 32u * (warp & 3) + lane;
 #pragma unroll 1
         for (uint32_t c0 = (warp >> 2) * CW; c0 < (warp >> 2) * CW + CW; c0 += 16) {
@@ -317,13 +321,17 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         if (lane == 0) {
             // this token tile's activations, already in the B layout: a stage
             // is QG_B_BYTES contiguous bytes
-            const uint8_t *xtile = reinterpret_cast<const uint8_t *>(p.x16) + (uint64_t)blockIdx.y * (p.cols / 8) * QG_N * 16u;
+            const uint64_t tile_bytes = (uint64_t)(p.cols / 8) * QG_N * 16u;
+            const uint8_t *xtile = reinterpret_cast<const uint8_t *>(p.x16) + (uint64_t)blockIdx.y * QG_NT * tile_bytes;
             uint32_t issued = 0;
             for (uint32_t kt = 0; kt < nk; ++kt) {
                 const uint32_t s = kt % QG_NS;
                 if ((kt >= QG_NS && !qg_wait(empty0 + 8 * s, ((kt / QG_NS) - 1) & 1u)) || *bad) { *bad = 1; break; }
-                mbar_arrive_expect_tx(bfull0 + 8 * s, QG_B_BYTES);
-                bulk_g2s(st0 + s * QG_STAGE + QG_A_BYTES, xtile + (uint64_t)(kb + kt) * QG_B_BYTES, QG_B_BYTES, bfull0 + 8 * s);
+                mbar_arrive_expect_tx(bfull0 + 8 * s, QG_NT * QG_B_BYTES);
+#pragma unroll
+                for (int n = 0; n < QG_NT; ++n)   // activation tile n of this CTA's tokens
+                    bulk_g2s(st0 + s * QG_STAGE + QG_A_BYTES + n * QG_B_BYTES,
+                             xtile + n * tile_bytes + (uint64_t)(kb + kt) * QG_B_BYTES, QG_B_BYTES, bfull0 + 8 * s);
                 issued = kt + 1;
             }
             if (*bad) {
@@ -344,8 +352,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
 #pragma unroll
             for (int ks = 0; ks < QG_KT / 16; ++ks) {   // K = 16 = two k-chunks per MMA
                 const uint64_t da = qg_desc(sa + ks * (2 * QG_M * 16u), QG_M * 16u, 128u);
-                const uint64_t db = qg_desc(sb + ks * (2 * QG_N * 16u), QG_N * 16u, 128u);
-                qg_mma(tmem, da, db, kt > 0 || ks > 0);
+#pragma unroll
+                for (int n = 0; n < QG_NT; ++n) {   // accumulator n: tensor-memory columns 256 n ..
+                    const uint64_t db = qg_desc(sb + n * QG_B_BYTES + ks * (2 * QG_N * 16u), QG_N * 16u, 128u);
+                    qg_mma(tmem + n * QG_N, da, db, kt > 0 || ks > 0);
+                }
             }
             qg_commit(empty0 + 8 * s);   // the stage is free once these MMAs have read it
         }
@@ -359,7 +370,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(QgemmParams p) {
         if (lane == 0) qg_wait(accb, 0);
         __syncwarp();
         qg_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)QG_N) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)QG_TT) : "memory");
     }
 }
 
@@ -404,13 +415,13 @@ bool qgemm_supported(int type, uint32_t rows, uint32_t cols, uint32_t tokens) {
 // K splits for a grid of `tiles` output tiles: enough CTAs to cover the
 // SMs, at least 8 stages of 64 per split.
 static uint32_t qg_splits(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm) {
-    const uint32_t tiles = ((rows + QG_M - 1) / QG_M) * ((tokens + QG_N - 1) / QG_N);
+    const uint32_t tiles = ((rows + QG_M - 1) / QG_M) * ((tokens + QG_TT - 1) / QG_TT);
     uint32_t z = std::max(1u, (uint32_t)n_sm / std::max(1u, tiles));
     return std::max(1u, std::min(z, cols / QG_KT / 8u));
 }
 
 size_t qgemm_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm) {
-    const size_t x16 = ((size_t)((tokens + QG_N - 1) / QG_N) * QG_N * cols * sizeof(__half) + 255) & ~(size_t)255;
+    const size_t x16 = ((size_t)((tokens + QG_TT - 1) / QG_TT) * QG_TT * cols * sizeof(__half) + 255) & ~(size_t)255;
     const uint32_t z = qg_splits(rows, cols, tokens, n_sm);
     return x16 + (z > 1 ? (size_t)z * tokens * rows * sizeof(float) : 0);
 }
@@ -425,7 +436,7 @@ cudaError_t qgemm_configure() {
 cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, void *work, int n_sm,
                          cudaStream_t st) {
     if (!qgemm_supported(type, p.rows, p.cols, p.tokens) || !work) return cudaErrorInvalidValue;
-    const uint32_t tpad = (p.tokens + QG_N - 1) / QG_N * QG_N;
+    const uint32_t tpad = (p.tokens + QG_TT - 1) / QG_TT * QG_TT;
     const uint32_t z = qg_splits(p.rows, p.cols, p.tokens, n_sm);
     note_launches(z > 1 ? 3 : 2);
     const uint64_t n = (uint64_t)tpad * p.cols;
@@ -434,7 +445,7 @@ cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_str
         x, x_stride, x16, p.tokens, tpad, p.cols);
     p.x16 = x16;
     p.planes = reinterpret_cast<float *>(static_cast<uint8_t *>(work) + ((n * sizeof(__half) + 255) & ~(size_t)255));
-    const dim3 grid((p.rows + QG_M - 1) / QG_M, tpad / QG_N, z);
+    const dim3 grid((p.rows + QG_M - 1) / QG_M, tpad / QG_TT, z);
     switch (type) {
         case T_Q4_K: qgemm_kernel<T_Q4_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
         case T_Q6_K: qgemm_kernel<T_Q6_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
