@@ -173,6 +173,28 @@ void *qg_workspace(DevState *d, size_t bytes) {
     return d->qg_work;
 }
 
+bool gemm_x16_ok(int type, const void *w, uint32_t rows, uint32_t cols, uint32_t batch) {
+    return batch > 8 && qgemm_supported(type, rows, cols, batch) && !(reinterpret_cast<uintptr_t>(w) & 15);
+}
+
+int gemm_x16(DevState *d, int type, const void *w, const __half *x16, float *y, uint32_t rows, uint32_t cols,
+             uint32_t batch, uint32_t flags, cudaStream_t st) {
+    QgemmParams p = {};
+    p.w = static_cast<const uint8_t *>(w);
+    p.rb = row_bytes(type, cols);
+    p.rows = rows;
+    p.cols = cols;
+    p.tokens = batch;
+    p.y = y;
+    p.y_stride = rows;
+    p.accumulate = (flags & VBS_CU_MV_ACCUMULATE) ? 1u : 0u;
+    p.err = d->err;
+    void *planes = nullptr;
+    const size_t pb = qgemm_planes_bytes(rows, cols, batch, d->n_sm);
+    if (pb && !(planes = qg_workspace(d, pb))) return -1;
+    return cuda_ok(qgemm_launch_x16(type, p, x16, planes, d->n_sm, st), "GEMM launch") ? 0 : -1;
+}
+
 void *mvb_workspace(DevState *d, size_t bytes) {
     if (d->mvb_work_bytes >= bytes) return d->mvb_work;
     if (d->mvb_work) {

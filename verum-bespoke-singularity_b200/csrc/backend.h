@@ -2,6 +2,7 @@
 // (backend.cu) and the decode program (decoder.cu).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stddef.h>
@@ -43,6 +44,11 @@ void *attn_workspace(DevState *d, size_t bytes);
 void *mvb_workspace(DevState *d, size_t bytes);
 // Grow the device's GEMM activation workspace to `bytes`.
 void *qg_workspace(DevState *d, size_t bytes);
+// Prompt chunks: one matrix on activations already converted by
+// qgemm_to_half (one input, several matrices). gemm_x16_ok: the GEMM takes it.
+bool gemm_x16_ok(int type, const void *w, uint32_t rows, uint32_t cols, uint32_t batch);
+int gemm_x16(DevState *d, int type, const void *w, const __half *x16, float *y, uint32_t rows, uint32_t cols,
+             uint32_t batch, uint32_t flags, cudaStream_t st);
 // y[b] (+)= W x[b] for b < batch on `st`, through the kernel the shape and
 // type allow (fast, batched tensor-core, the tcgen05 GEMM above 8
 // sequences, or portable); flags VBS_CU_MV_*.

@@ -90,6 +90,7 @@ struct vbs_cu_decoder {
     float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_att = nullptr,
           *pf_g = nullptr, *pf_u = nullptr, *pf_h = nullptr;
     void *pf_attn_work = nullptr;
+    __half *pf_x16 = nullptr;   // a prompt chunk's normed rows as GEMM activations (fp16, tile layout)
     uint32_t pf_splits = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -584,6 +585,7 @@ bool prefill_buffers(vbs_cu_decoder *d) {
            dmalloc((void **)&d->pf_k, B * d->kv_dim * 4, "prefill rows") && dmalloc((void **)&d->pf_v, B * d->kv_dim * 4, "prefill rows") &&
            dmalloc((void **)&d->pf_g, B * m.ffn * 4, "prefill rows") && dmalloc((void **)&d->pf_u, B * m.ffn * 4, "prefill rows") &&
            dmalloc((void **)&d->pf_h, B * m.ffn * 4, "prefill rows") && dmalloc(&d->pf_attn_work, aw, "prefill attention") &&
+           dmalloc((void **)&d->pf_x16, qgemm_x16_bytes(PF_CHUNK, m.dim), "prefill fp16 rows") &&
            cuda_ok(cudaMemset(d->pf_attn_work, 0, aw), "prefill attention");
 }
 
@@ -603,11 +605,22 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
         Layer streamed;
         if (d->stream && !stream_layer(d, l, streamed)) return false;
         const Layer &y = d->stream ? streamed : d->L[l];
-        if (!cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.attn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm") ||
-            matvec_any(dev, y.tq, y.wq, d->pf_xn, d->pf_q, nq, dim, B, 0, st) ||
-            matvec_any(dev, y.tk, y.wk, d->pf_xn, d->pf_k, nk, dim, B, 0, st) ||
-            matvec_any(dev, y.tv, y.wv, d->pf_xn, d->pf_v, nk, dim, B, 0, st) ||
-            !cuda_ok(pf_rope_store_launch(d->pf_q, d->pf_k, d->pf_v, d->kc, d->vc, B, p0, l, d->max_ctx, m.n_heads,
+        // one input, several matrices: through the GEMM, its activations are
+        // converted once (q, k, v here; gate, up below)
+        const bool qkv16 = gemm_x16_ok(y.tq, y.wq, nq, dim, B) && gemm_x16_ok(y.tk, y.wk, nk, dim, B) &&
+                           gemm_x16_ok(y.tv, y.wv, nk, dim, B);
+        const bool gu16 = gemm_x16_ok(y.tgate, y.wgate, ffn, dim, B) && gemm_x16_ok(y.tup, y.wup, ffn, dim, B);
+        if (!cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.attn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm"))
+            return false;
+        if (qkv16 ? (!cuda_ok(qgemm_to_half(d->pf_xn, dim, d->pf_x16, B, dim, dev->n_sm, st), "prefill fp16 rows") ||
+                     gemm_x16(dev, y.tq, y.wq, d->pf_x16, d->pf_q, nq, dim, B, 0, st) ||
+                     gemm_x16(dev, y.tk, y.wk, d->pf_x16, d->pf_k, nk, dim, B, 0, st) ||
+                     gemm_x16(dev, y.tv, y.wv, d->pf_x16, d->pf_v, nk, dim, B, 0, st))
+                  : (matvec_any(dev, y.tq, y.wq, d->pf_xn, d->pf_q, nq, dim, B, 0, st) ||
+                     matvec_any(dev, y.tk, y.wk, d->pf_xn, d->pf_k, nk, dim, B, 0, st) ||
+                     matvec_any(dev, y.tv, y.wv, d->pf_xn, d->pf_v, nk, dim, B, 0, st)))
+            return false;
+        if (!cuda_ok(pf_rope_store_launch(d->pf_q, d->pf_k, d->pf_v, d->kc, d->vc, B, p0, l, d->max_ctx, m.n_heads,
                                           m.n_kv_heads, hd, m.theta, layout, st),
                      "prefill rope/kv store"))
             return false;
@@ -627,8 +640,11 @@ bool prefill_chunk(vbs_cu_decoder *d, const uint32_t *tok, uint32_t B, uint32_t 
                      "prefill attention") ||
             matvec_any(dev, y.to, y.wo, d->pf_att, d->pf_x, dim, nq, B, VBS_CU_MV_ACCUMULATE, st) ||
             !cuda_ok(pf_rmsnorm_rows_launch(d->pf_x, y.ffn_norm, d->pf_xn, B, dim, m.eps, st), "prefill norm") ||
-            matvec_any(dev, y.tgate, y.wgate, d->pf_xn, d->pf_g, ffn, dim, B, 0, st) ||
-            matvec_any(dev, y.tup, y.wup, d->pf_xn, d->pf_u, ffn, dim, B, 0, st) ||
+            (gu16 ? (!cuda_ok(qgemm_to_half(d->pf_xn, dim, d->pf_x16, B, dim, dev->n_sm, st), "prefill fp16 rows") ||
+                     gemm_x16(dev, y.tgate, y.wgate, d->pf_x16, d->pf_g, ffn, dim, B, 0, st) ||
+                     gemm_x16(dev, y.tup, y.wup, d->pf_x16, d->pf_u, ffn, dim, B, 0, st))
+                  : (matvec_any(dev, y.tgate, y.wgate, d->pf_xn, d->pf_g, ffn, dim, B, 0, st) ||
+                     matvec_any(dev, y.tup, y.wup, d->pf_xn, d->pf_u, ffn, dim, B, 0, st))) ||
             !cuda_ok(silu_mul_launch(d->pf_g, d->pf_u, d->pf_h, B * ffn, st), "prefill silu") ||
             matvec_any(dev, y.tdown, y.wdown, d->pf_h, d->pf_x, dim, ffn, B, VBS_CU_MV_ACCUMULATE, st))
             return false;
@@ -818,7 +834,7 @@ void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d) {
                     d->gate, d->up, d->tmp, d->scores, d->xq, d->qd, d->kc, d->vc, d->kcf, d->vcf, d->ctrl, d->hist,
                     d->tok_dev, d->attn_work, d->argmax_work, d->step_layers, d->step_acc, d->step_attn, d->step_packed,
                     d->words_mem, d->words_comm, d->pf_x, d->pf_xn, d->pf_q, d->pf_k, d->pf_v, d->pf_att,
-                    d->pf_g, d->pf_u, d->pf_h, d->pf_attn_work, d->trace};
+                    d->pf_g, d->pf_u, d->pf_h, d->pf_attn_work, d->pf_x16, d->trace};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->cst) cudaStreamSynchronize(d->cst);

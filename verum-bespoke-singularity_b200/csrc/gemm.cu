@@ -420,10 +420,10 @@ static uint32_t qg_splits(uint32_t rows, uint32_t cols, uint32_t tokens, int n_s
     return std::max(1u, std::min(z, cols / QG_KT / 8u));
 }
 
+size_t qgemm_x16_bytes(uint32_t tokens, uint32_t cols);
+size_t qgemm_planes_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm);
 size_t qgemm_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm) {
-    const size_t x16 = ((size_t)((tokens + QG_TT - 1) / QG_TT) * QG_TT * cols * sizeof(__half) + 255) & ~(size_t)255;
-    const uint32_t z = qg_splits(rows, cols, tokens, n_sm);
-    return x16 + (z > 1 ? (size_t)z * tokens * rows * sizeof(float) : 0);
+    return qgemm_x16_bytes(tokens, cols) + qgemm_planes_bytes(rows, cols, tokens, n_sm);
 }
 
 cudaError_t qgemm_configure() {
@@ -433,18 +433,33 @@ cudaError_t qgemm_configure() {
     return e;
 }
 
-cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, void *work, int n_sm,
-                         cudaStream_t st) {
-    if (!qgemm_supported(type, p.rows, p.cols, p.tokens) || !work) return cudaErrorInvalidValue;
+size_t qgemm_x16_bytes(uint32_t tokens, uint32_t cols) {
+    return ((size_t)((tokens + QG_TT - 1) / QG_TT) * QG_TT * cols * sizeof(__half) + 255) & ~(size_t)255;
+}
+size_t qgemm_planes_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm) {
+    const uint32_t z = qg_splits(rows, cols, tokens, n_sm);
+    return z > 1 ? (size_t)z * tokens * rows * sizeof(float) : 0;
+}
+
+cudaError_t qgemm_to_half(const float *x, uint64_t x_stride, __half *x16, uint32_t tokens, uint32_t cols, int n_sm,
+                          cudaStream_t st) {
+    if (!tokens || cols % QG_KT || !x16) return cudaErrorInvalidValue;
+    const uint32_t tpad = (tokens + QG_TT - 1) / QG_TT * QG_TT;
+    const uint64_t n = (uint64_t)tpad * cols;
+    note_launches(1);
+    qg_to_half_kernel<<<(unsigned)std::min<uint64_t>((n / 8 + 255) / 256, (uint64_t)n_sm * 16), 256, 0, st>>>(
+        x, x_stride, x16, tokens, tpad, cols);
+    return cudaGetLastError();
+}
+
+cudaError_t qgemm_launch_x16(int type, QgemmParams p, const __half *x16, void *planes, int n_sm, cudaStream_t st) {
+    if (!qgemm_supported(type, p.rows, p.cols, p.tokens) || !x16) return cudaErrorInvalidValue;
     const uint32_t tpad = (p.tokens + QG_TT - 1) / QG_TT * QG_TT;
     const uint32_t z = qg_splits(p.rows, p.cols, p.tokens, n_sm);
-    note_launches(z > 1 ? 3 : 2);
-    const uint64_t n = (uint64_t)tpad * p.cols;
-    __half *x16 = static_cast<__half *>(work);
-    qg_to_half_kernel<<<(unsigned)std::min<uint64_t>((n / 8 + 255) / 256, (uint64_t)n_sm * 16), 256, 0, st>>>(
-        x, x_stride, x16, p.tokens, tpad, p.cols);
+    if (z > 1 && !planes) return cudaErrorInvalidValue;
+    note_launches(z > 1 ? 2 : 1);
     p.x16 = x16;
-    p.planes = reinterpret_cast<float *>(static_cast<uint8_t *>(work) + ((n * sizeof(__half) + 255) & ~(size_t)255));
+    p.planes = static_cast<float *>(planes);
     const dim3 grid((p.rows + QG_M - 1) / QG_M, tpad / QG_TT, z);
     switch (type) {
         case T_Q4_K: qgemm_kernel<T_Q4_K><<<grid, QG_THREADS, QG_SMEM, st>>>(p); break;
@@ -457,6 +472,15 @@ cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_str
             p.planes, z, p.tokens, p.rows, p.y, p.y_stride, p.accumulate);
     }
     return cudaGetLastError();
+}
+
+cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, void *work, int n_sm,
+                         cudaStream_t st) {
+    if (!qgemm_supported(type, p.rows, p.cols, p.tokens) || !work) return cudaErrorInvalidValue;
+    __half *x16 = static_cast<__half *>(work);
+    const cudaError_t e = qgemm_to_half(x, x_stride, x16, p.tokens, p.cols, n_sm, st);
+    if (e != cudaSuccess) return e;
+    return qgemm_launch_x16(type, p, x16, static_cast<uint8_t *>(work) + qgemm_x16_bytes(p.tokens, p.cols), n_sm, st);
 }
 
 }  // namespace vbs

@@ -121,6 +121,15 @@ size_t qgemm_workspace_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int 
 cudaError_t qgemm_configure();
 cudaError_t qgemm_launch(int type, QgemmParams p, const float *x, uint64_t x_stride, void *work, int n_sm,
                          cudaStream_t st);
+// The same in two parts, for callers that feed one input to several
+// matrices: the activations converted once (fp16, in the operand's tile
+// layout, qgemm_x16_bytes), then any number of GEMMs on them (planes: the
+// split-K workspace, qgemm_planes_bytes; may be NULL when that is 0).
+size_t qgemm_x16_bytes(uint32_t tokens, uint32_t cols);
+size_t qgemm_planes_bytes(uint32_t rows, uint32_t cols, uint32_t tokens, int n_sm);
+cudaError_t qgemm_to_half(const float *x, uint64_t x_stride, __half *x16, uint32_t tokens, uint32_t cols, int n_sm,
+                          cudaStream_t st);
+cudaError_t qgemm_launch_x16(int type, QgemmParams p, const __half *x16, void *planes, int n_sm, cudaStream_t st);
 
 // True when the TMA/mma kernel can serve this shape/alignment.
 bool mv_fast_supported(int type, uint32_t rows, uint32_t cols, const void *const *w, int nw,
