@@ -88,8 +88,9 @@ def profile_timeline(args):
     prologue's loads and sum of squares, its wait for the norm weight stage
     and its quantization; attention's q/KV setup, first and last stage
     arrival, stage loop, partial store, wait for the head's other splits and
-    merge; and l2_probe, one dependent L2 load of the op's input timed right
-    after the prologue (attention: after the merge)."""
+    merge; l2_probe, one dependent L2 load of the op's input timed right
+    after the prologue (attention: after the merge); and stamp, two stamps
+    back to back (what one stamp costs)."""
     import ctypes as C
     import numpy as np
     import torch
@@ -151,6 +152,9 @@ def profile_timeline(args):
                      pro_quant=phase(i, 6, 7), l2_probe=phase(i, 9, 10))
         if k in ("O", "DOWN"):
             r.update(pro_entry=phase(i, 0, 8), l2_probe=phase(i, 9, 10))
+        r.update(stamp=phase(i, 0, 11))
+        if k not in ("ATTN", "ARGMAX"):
+            r.update(param=phase(i, 11, 12), layer_ptr=phase(i, 11, 13))
         if k == "ATTN":
             r.update(setup=phase(i, 0, 1), first_stage=phase(i, 1, 8), last_stage=phase(i, 1, 9), stages=phase(i, 1, 5),
                      partial=phase(i, 5, 6), wait=phase(i, 6, 7), merge=phase(i, 7, 2), l2_probe=phase(i, 10, 11))

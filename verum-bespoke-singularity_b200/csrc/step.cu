@@ -64,7 +64,8 @@ constexpr uint32_t SK_REG_LAUNCH = 168, SK_REG_CONSUMER = 232, SK_REG_PRODUCER =
 static_assert(SK_CT * SK_REG_CONSUMER + 128 * SK_REG_PRODUCER <= SK_THREADS * SK_REG_LAUNCH, "register split");
 constexpr uint32_t SK_NB = 8;                      // stages in flight at most (full/empty barrier pairs)
 constexpr uint32_t SK_NU = 8;                      // matvec units per row-sum batch
-constexpr uint32_t SK_RED = 2048;                  // row-sum batches: [2][SK_NU][8 warps][16 rows] floats
+constexpr uint32_t SK_PRM = 2048;                  // the launch's StepParams, copied once per launch
+constexpr uint32_t SK_RED = 3072;                  // row-sum batches: [2][SK_NU][8 warps][16 rows] floats
 constexpr uint32_t SK_HDR = SK_RED + 2 * SK_NU * 8 * 16 * 4;   // barriers, flags, row-sum batches
 constexpr uint32_t SK_SMEM = 227u * 1024u;
 constexpr uint32_t SK_AP = 64;                     // attention positions per stage
@@ -152,9 +153,10 @@ __host__ __device__ __forceinline__ uint32_t sk_slot_row(bool gu, uint32_t tile,
 }
 
 // This CTA's contiguous share [u0, u1) of U units.
+// (U * gridDim.x < 2^32: U is at most a few hundred thousand units.)
 __device__ __forceinline__ void sk_range(uint32_t U, uint32_t &u0, uint32_t &u1) {
-    u0 = (uint32_t)(((uint64_t)blockIdx.x * U) / gridDim.x);
-    u1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * U) / gridDim.x);
+    u0 = blockIdx.x * U / gridDim.x;
+    u1 = (blockIdx.x + 1) * U / gridDim.x;
 }
 
 struct SkAttn {
@@ -335,7 +337,7 @@ struct SkSmem {
     __device__ float *misc() const { return reinterpret_cast<float *>(ptr + 1024); }            // 256 floats
     __device__ float *red() const { return reinterpret_cast<float *>(ptr + SK_RED); }          // [2][SK_NU][8][16]
 };
-static_assert(16 * SK_NB <= 256 && SK_HDR % 1024 == 0, "shared-memory header");
+static_assert(16 * SK_NB <= 256 && SK_HDR % 1024 == 0 && sizeof(StepParams) <= SK_RED - SK_PRM, "shared-memory header");
 
 // Position in the stage sequence, walked identically by the producer and the
 // consumers. Stages take their own size from a ring of bytes (a stage never
@@ -1134,23 +1136,33 @@ __device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uin
 // and its instruction fetch is otherwise a bottleneck). TPX instances add
 // the tensor-parallel exchanges; the one-GPU instances carry none of it.
 template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX>
-__global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p) {
+__global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p_in) {
     static_assert(65536 / SK_THREADS / 8 * 8 >= SK_REG_LAUNCH, "launch register count");
     extern __shared__ __align__(1024) uint8_t smem[];
+    // Every op reads the parameters right after a grid barrier, when the
+    // constant cache has long lost them (an L2 round trip per dependent
+    // read): they are read from shared memory instead, copied once here.
+    {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&p_in);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(smem + SK_PRM);
+        for (uint32_t k = threadIdx.x; k < sizeof(StepParams) / 4; k += blockDim.x) dst[k] = src[k];
+    }
+    const StepParams &p = *reinterpret_cast<const StepParams *>(smem + SK_PRM);
+    static_assert(sizeof(StepParams) % 4 == 0, "parameter copy by words");
     SkSmem S;
     S.ptr = smem;
     S.base = smem_u32(smem);
-    S.ring = S.base + p.ring_off;
-    S.ring_bytes = p.ring_bytes;
+    S.ring = S.base + p_in.ring_off;
+    S.ring_bytes = p_in.ring_bytes;
     const int warp = threadIdx.x >> 5;
     // read once: the last CTA rewrites the control block at the end of the step
-    const uint32_t pos = *reinterpret_cast<const volatile uint32_t *>(p.ctrl);
-    const uint32_t token = *reinterpret_cast<const volatile uint32_t *>(p.ctrl + 1);
+    const uint32_t pos = *reinterpret_cast<const volatile uint32_t *>(p_in.ctrl);
+    const uint32_t token = *reinterpret_cast<const volatile uint32_t *>(p_in.ctrl + 1);
     // ctrl[2]: device-driven generation stopped (vbs_cu_decoder_run_control):
     // this step does nothing, the same decision in every CTA
-    if (*reinterpret_cast<const volatile uint32_t *>(p.ctrl + 2)) return;
-    if (pos >= p.max_ctx || token >= (p.tp ? p.vocab_full : p.vocab)) {   // the same decision in every CTA: nothing runs, nothing waits
-        if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(p.err, DERR_BAD_ARG);
+    if (*reinterpret_cast<const volatile uint32_t *>(p_in.ctrl + 2)) return;
+    if (pos >= p_in.max_ctx || token >= (p_in.tp ? p_in.vocab_full : p_in.vocab)) {   // the same decision in every CTA: nothing runs, nothing waits
+        if (blockIdx.x == 0 && threadIdx.x == 0) dev_flag_error(p_in.err, DERR_BAD_ARG);
         return;
     }
     const uint32_t seq = pos + 1;
@@ -1196,6 +1208,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         uint32_t l;
         const int kind = sk_kind(i, p.n_layers, l);
         if (threadIdx.x == 0) SK_STAMP(p, i, 0);
+        if (threadIdx.x == 0) SK_STAMP(p, i, 11);   // back to back: the cost of a stamp itself
         if (kind == K_ATTN) {
             if constexpr (HD != 0) sk_attn<HD>(p, l, pos, seq, S, r, sh, i);
             else if (p.hd == 128) sk_attn<128>(p, l, pos, seq, S, r, sh, i);
@@ -1209,6 +1222,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             continue;
         }
         SkMv d = sk_mv_desc(p, kind, l);
+#ifdef VBS_STEP_TRACE
+        if (threadIdx.x == 0) {   // when a parameter-block value, then the layer's pointer, is in hand
+            sk_stamp_after(p, i, 12, __uint_as_float(d.g.ntiles | 1u));
+            sk_stamp_after(p, i, 13, __uint_as_float((uint32_t)reinterpret_cast<uintptr_t>(d.packed) | 1u));
+        }
+#endif
         if (TPX && p.tp && (kind == K_O || kind == K_DOWN || kind == K_OUT)) {
             d.tpw = kind == K_OUT ? 2 : 1;
             d.tp_k = sk_tp_index(p, tp_base, kind, l);
