@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--shape", default="8b", choices=["8b", "70b"],
                     help="--profile decode/timed: the Llama-3-8B mix (BASELINE config 3) or the 70B shape, all Q4_K "
                          "(config 4)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="--profile decode: sequences decoded in lockstep (the batch decoder when above 1)")
     ap.add_argument("--per-op", action="store_true",
                     help="--profile decode: the per-op kernels (one launch per op) instead of the one-launch step")
     return ap.parse_args()
@@ -325,9 +327,15 @@ def profile_kernel(args):
         layers = args.layers if args.layers != 32 or args.shape == "8b" else base["n_layers"]
         cfg = dict(base, n_layers=layers, vocab=args.vocab)
         model = vbs.synth_llama(models.shape_of(cfg), types, seed=2024)
-        dec = vbs.Decoder(model, args.ctx + args.steps + 8, vbs.DEC_NO_PERSIST if args.per_op else 0)
-        dec.forward([1], logits=False)
-        dec.set_position(args.ctx - 1, 1)
+        B = max(1, args.batch)
+        if B > 1:   # B sequences in lockstep: each step B tokens
+            dec = vbs.BatchDecoder(model, args.ctx + args.steps + 8, B)
+            dec.step(list(range(1, B + 1)), logits=False)
+            dec.set_position(args.ctx - 1, list(range(1, B + 1)))
+        else:
+            dec = vbs.Decoder(model, args.ctx + args.steps + 8, vbs.DEC_NO_PERSIST if args.per_op else 0)
+            dec.forward([1], logits=False)
+            dec.set_position(args.ctx - 1, 1)
         dec.enqueue_steps(2)
         torch.cuda.synchronize()
         s = torch.cuda.ExternalStream(dec.stream)
@@ -339,11 +347,12 @@ def profile_kernel(args):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / max(1, args.steps)
         wbytes = model.weight_bytes() - model.tensors["token_embd"].numel()
-        kv = cfg["n_layers"] * cfg["n_kv_heads"] * (cfg["dim"] // cfg["n_heads"]) * 2 * 2 * (args.ctx + 2)
+        kv = B * cfg["n_layers"] * cfg["n_kv_heads"] * (cfg["dim"] // cfg["n_heads"]) * 2 * 2 * (args.ctx + 2)
         peak, _ = peaks()
         print(json.dumps({"profile": "decode", "shape": args.shape, "ctx": args.ctx, "layers": cfg["n_layers"],
-                          "vocab": args.vocab, "kernels_per_step": dec.kernels_per_step, "steps": args.steps,
-                          "ms_per_step": round(ms, 4), "tok_s": round(1000.0 / ms, 2),
+                          "vocab": args.vocab, "batch": B,
+                          "kernels_per_step": dec.kernels_per_step if B == 1 else None, "steps": args.steps,
+                          "ms_per_step": round(ms, 4), "tok_s": round(B * 1000.0 / ms, 2),
                           "bytes_per_step": int(wbytes + kv),
                           "frac_of_measured": round((wbytes + kv) / (ms * 1e-3) / 1e9 / peak, 4)}))
         dec.close()

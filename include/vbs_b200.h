@@ -398,6 +398,37 @@ VBS_API int vbs_cu_decoder_enqueue_steps(vbs_cu_decoder_t *d, uint32_t n_steps);
 VBS_API int vbs_cu_decoder_set_position(vbs_cu_decoder_t *d, uint32_t pos, uint32_t token);
 VBS_API uint32_t vbs_cu_decoder_position(vbs_cu_decoder_t *d);
 VBS_API void *vbs_cu_decoder_stream(vbs_cu_decoder_t *d);
+
+/* ---- batched decode: B sequences in lockstep (no reference counterpart) ----
+ * The reference's engine decodes one sequence (src/vbs_engine.c:240-327);
+ * every step streams every weight for one token. This decoder steps B
+ * sequences together, all at the same position, one token each per step,
+ * with the per-op kernels: each weight is read once per step for B tokens
+ * (the batched tensor-core matvec up to 8 sequences, the tcgen05 GEMM
+ * above). Each sequence has its own fp16 KV cache, head-major
+ * [layer][kv head][max_ctx][head_dim]; its logits equal a one-sequence
+ * decoder fed the same tokens, to the kernels' rounding. One GPU; the
+ * model description as for vbs_cu_decoder_create (vocab_full = vocab). */
+typedef struct vbs_cu_batch_decoder vbs_cu_batch_decoder_t;
+/* batch 1..64 sequences; allocates B KV caches of max_ctx positions. */
+VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t batch,
+                                                            char *err, size_t err_cap);
+VBS_API void vbs_cu_batch_decoder_destroy(vbs_cu_batch_decoder_t *d);
+/* One step at position(): tokens (host, B ids; NULL feeds the previous
+ * step's argmax of every sequence), then logits_out (host, B x vocab floats)
+ * and next_tokens (host, B ids: each sequence's argmax, first maximum wins)
+ * when not NULL. Synchronizes. 0, or -1 with the error latched. */
+VBS_API int vbs_cu_batch_decoder_step(vbs_cu_batch_decoder_t *d, const uint32_t *tokens, float *logits_out,
+                                      uint32_t *next_tokens);
+/* n_steps greedy steps enqueued on the decoder's stream, each feeding the
+ * previous argmaxes; returns without synchronizing. For timing loops. */
+VBS_API int vbs_cu_batch_decoder_enqueue_steps(vbs_cu_batch_decoder_t *d, uint32_t n_steps);
+/* Moves every sequence to position pos (the cache rows before it stay as
+ * they are) and, when tokens is not NULL, sets the next tokens (host, B). */
+VBS_API int vbs_cu_batch_decoder_set_position(vbs_cu_batch_decoder_t *d, uint32_t pos, const uint32_t *tokens);
+VBS_API uint32_t vbs_cu_batch_decoder_position(vbs_cu_batch_decoder_t *d);
+VBS_API void vbs_cu_batch_decoder_reset(vbs_cu_batch_decoder_t *d);
+VBS_API void *vbs_cu_batch_decoder_stream(vbs_cu_batch_decoder_t *d);
 VBS_API const float *vbs_cu_decoder_logits_device(vbs_cu_decoder_t *d);
 /* Kernels one decode step launches. */
 VBS_API uint32_t vbs_cu_decoder_kernels_per_step(vbs_cu_decoder_t *d);

@@ -179,6 +179,14 @@ def lib() -> C.CDLL:
         "vbs_cu_decoder_set_position": (i32, [vp, u32, u32]),
         "vbs_cu_decoder_position": (u32, [vp]),
         "vbs_cu_decoder_stream": (vp, [vp]),
+        "vbs_cu_batch_decoder_create": (vp, [C.POINTER(ModelDesc), u32, u32, C.c_char_p, sz]),
+        "vbs_cu_batch_decoder_destroy": (None, [vp]),
+        "vbs_cu_batch_decoder_step": (i32, [vp, C.POINTER(u32), C.POINTER(f32), C.POINTER(u32)]),
+        "vbs_cu_batch_decoder_enqueue_steps": (i32, [vp, u32]),
+        "vbs_cu_batch_decoder_set_position": (i32, [vp, u32, C.POINTER(u32)]),
+        "vbs_cu_batch_decoder_position": (u32, [vp]),
+        "vbs_cu_batch_decoder_reset": (None, [vp]),
+        "vbs_cu_batch_decoder_stream": (vp, [vp]),
         "vbs_cu_decoder_logits_device": (vp, [vp]),
         "vbs_cu_decoder_kernels_per_step": (u32, [vp]),
         "vbs_cu_decoder_tp_mode": (u32, [vp]),
@@ -414,8 +422,8 @@ class Decoder:
         return out
 
     def prefill(self, tokens) -> None:
-        """The tokens as context (KV rows only, chunks of 8 through the
-        batched kernels); the next forward continues after them."""
+        """The tokens as context (KV rows only, chunks of up to 512 through
+        the tcgen05 GEMM); the next forward continues after them."""
         arr = (C.c_uint32 * max(len(tokens), 1))(*tokens)
         check(lib().vbs_cu_decoder_prefill(self.h, arr, len(tokens)), "vbs_cu_decoder_prefill")
 
@@ -469,6 +477,60 @@ class Decoder:
     def close(self) -> None:
         if self.h:
             lib().vbs_cu_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class BatchDecoder:
+    """vbs_cu_batch_decoder_t: `batch` sequences decoded in lockstep, one
+    token each per step at the same position."""
+
+    def __init__(self, model: DeviceModel, max_ctx: int, batch: int):
+        self.model = model
+        desc = model.desc or model.make_desc()
+        err = C.create_string_buffer(512)
+        self.h = lib().vbs_cu_batch_decoder_create(C.byref(desc), max_ctx, batch, err, 512)
+        if not self.h:
+            raise VbsError(f"vbs_cu_batch_decoder_create: {err.value.decode()}")
+        self.batch, self.max_ctx, self.vocab = batch, max_ctx, model.shape.vocab
+
+    def step(self, tokens=None, logits: bool = True):
+        """One step; tokens: one id per sequence (None: the previous argmaxes).
+        Returns (logits [batch][vocab] or None, next tokens)."""
+        import numpy as np
+        arr = (C.c_uint32 * self.batch)(*[int(t) for t in tokens]) if tokens is not None else None
+        out = np.empty((self.batch, self.vocab), dtype=np.float32) if logits else None
+        nxt = (C.c_uint32 * self.batch)()
+        check(lib().vbs_cu_batch_decoder_step(self.h, arr, out.ctypes.data_as(C.POINTER(C.c_float)) if logits else None,
+                                               nxt), "vbs_cu_batch_decoder_step")
+        return out, list(nxt)
+
+    def enqueue_steps(self, n: int) -> None:
+        check(lib().vbs_cu_batch_decoder_enqueue_steps(self.h, n), "vbs_cu_batch_decoder_enqueue_steps")
+
+    def set_position(self, pos: int, tokens=None) -> None:
+        arr = (C.c_uint32 * self.batch)(*[int(t) for t in tokens]) if tokens is not None else None
+        check(lib().vbs_cu_batch_decoder_set_position(self.h, pos, arr), "vbs_cu_batch_decoder_set_position")
+
+    @property
+    def position(self) -> int:
+        return int(lib().vbs_cu_batch_decoder_position(self.h))
+
+    def reset(self) -> None:
+        lib().vbs_cu_batch_decoder_reset(self.h)
+
+    @property
+    def stream(self) -> int:
+        return int(lib().vbs_cu_batch_decoder_stream(self.h) or 0)
+
+    def close(self) -> None:
+        if self.h:
+            lib().vbs_cu_batch_decoder_destroy(self.h)
             self.h = None
 
     def __del__(self):

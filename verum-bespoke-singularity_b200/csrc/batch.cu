@@ -1,0 +1,270 @@
+// batch.cu -- B sequences decoded in lockstep (batched decode).
+//
+// The reference's engine has one sequence and no batch dimension: every
+// decode step streams every weight for one token (src/vbs_specializer.c:
+// 231-359). Serving B sequences together reads each weight once for B
+// tokens, which is where the batched matvec (B <= 8, csrc/mvb.cu) and the
+// tcgen05 GEMM (B > 8, csrc/gemm.cu) earn their keep. Each step here takes
+// one token per sequence, all at the same position, through the per-op
+// kernels:
+//   embedding rows -> per layer: row RMSNorm, Q/K/V for B rows, RoPE and
+//   the KV store into each sequence's own head-major cache, split-KV
+//   attention over B sequences (one cache stride apart), o_proj + residual,
+//   RMSNorm, gate/up, SiLU*up, down + residual -> output norm, logits
+//   [B][vocab], per-sequence argmax (first maximum) fed back as the next
+//   tokens.
+// The op order and the arithmetic of every op are those of the one-sequence
+// per-op decoder, so each sequence's logits match a one-sequence decoder
+// fed the same tokens to the kernels' rounding.
+#include "backend.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "vbs_b200.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+using namespace vbs;
+
+namespace {
+
+constexpr uint32_t kBatchMagic = 0x56424254u;   // "VBBT": a live batch decoder
+constexpr uint32_t kBatchMax = 64;              // sequences per decoder
+
+struct BLayer {
+    const float *attn_norm, *ffn_norm;
+    const uint8_t *wq, *wk, *wv, *wo, *wgate, *wup, *wdown;
+    int tq, tk, tv, to, tgate, tup, tdown;
+};
+
+// Makes `ordinal` current for the scope and restores the caller's device.
+struct BatchDeviceGuard {
+    int prev = -1;
+    explicit BatchDeviceGuard(int ordinal) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != ordinal) cudaSetDevice(ordinal);
+    }
+    ~BatchDeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T> bool balloc(T **p, size_t bytes, const char *what) {
+    return cuda_ok(cudaMalloc(reinterpret_cast<void **>(p), bytes ? bytes : 16), what);
+}
+
+}  // namespace
+
+struct vbs_cu_batch_decoder {
+    uint32_t magic = kBatchMagic;
+    vbs_cu_model_t m;
+    std::vector<BLayer> L;
+    DevState *dev = nullptr;
+    cudaStream_t st = nullptr;
+    uint32_t B = 0, max_ctx = 0, q_dim = 0, kv_dim = 0, splits = 1, pos = 0;
+    uint64_t seq_stride = 0;   // cache elements per sequence: [layer][kv head][max_ctx][head_dim]
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
+          *u = nullptr, *h = nullptr, *logits = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    uint32_t *tok = nullptr;   // [B] the tokens the next step feeds (device)
+    void *attn_work = nullptr, *argmax_work = nullptr;
+};
+
+namespace {
+
+bool bd_valid(const vbs_cu_batch_decoder *d) { return d && d->magic == kBatchMagic; }
+
+// One lockstep step at position d->pos: feeds d->tok, leaves the logits in
+// d->logits and the argmax of every sequence in d->tok.
+bool bd_step(vbs_cu_batch_decoder *d) {
+    if (d->pos >= d->max_ctx) {
+        latch_error("batch decoder: position %u reaches the KV capacity %u", d->pos, d->max_ctx);
+        return false;
+    }
+    const vbs_cu_model_t &m = d->m;
+    cudaStream_t st = d->st;
+    DevState *dev = d->dev;
+    const uint32_t B = d->B, dim = m.dim, nq = d->q_dim, nk = d->kv_dim, ffn = m.ffn, hd = m.head_dim;
+    if (!cuda_ok(embed_rows_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->tok, B, m.vocab, d->x, dim,
+                                   dev->err, st),
+                 "batch embed"))
+        return false;
+    for (uint32_t l = 0; l < m.n_layers; ++l) {
+        const BLayer &y = d->L[l];
+        if (!cuda_ok(pf_rmsnorm_rows_launch(d->x, y.attn_norm, d->xn, B, dim, m.eps, st), "batch norm") ||
+            matvec_any(dev, y.tq, y.wq, d->xn, d->q, nq, dim, B, 0, st) ||
+            matvec_any(dev, y.tk, y.wk, d->xn, d->k, nk, dim, B, 0, st) ||
+            matvec_any(dev, y.tv, y.wv, d->xn, d->v, nk, dim, B, 0, st) ||
+            !cuda_ok(rope_store_seqs_launch(d->q, d->k, d->v, d->kc, d->vc, B, d->seq_stride, d->pos, l, d->max_ctx,
+                                            m.n_heads, m.n_kv_heads, hd, m.theta, st),
+                     "batch rope/kv store"))
+            return false;
+        AttnParams ap = {};
+        ap.q = d->q; ap.kc = d->kc; ap.vc = d->vc; ap.out = d->att;
+        ap.seq_len = d->pos + 1; ap.seq_step = 0;
+        ap.layer = l; ap.max_ctx = d->max_ctx;
+        ap.nqh = m.n_heads; ap.nkh = m.n_kv_heads; ap.hd = hd;
+        ap.scale = 1.0f / sqrtf((float)hd);
+        ap.batch = B; ap.kv_batch_stride = d->seq_stride;
+        ap.head_major = 1; ap.swz = 0;
+        ap.work = d->attn_work;
+        ap.err = dev->err;
+        const uint32_t ns = std::min(d->splits, attn_num_splits(d->pos + 1, m.n_kv_heads, B, dev->n_sm));
+        if (!cuda_ok(attn_launch(ap, ns, st, false), "batch attention") ||
+            matvec_any(dev, y.to, y.wo, d->att, d->x, dim, nq, B, VBS_CU_MV_ACCUMULATE, st) ||
+            !cuda_ok(pf_rmsnorm_rows_launch(d->x, y.ffn_norm, d->xn, B, dim, m.eps, st), "batch norm") ||
+            matvec_any(dev, y.tgate, y.wgate, d->xn, d->g, ffn, dim, B, 0, st) ||
+            matvec_any(dev, y.tup, y.wup, d->xn, d->u, ffn, dim, B, 0, st) ||
+            !cuda_ok(silu_mul_launch(d->g, d->u, d->h, B * ffn, st), "batch silu") ||
+            matvec_any(dev, y.tdown, y.wdown, d->h, d->x, dim, ffn, B, VBS_CU_MV_ACCUMULATE, st))
+            return false;
+    }
+    if (!cuda_ok(pf_rmsnorm_rows_launch(d->x, m.out_norm, d->xn, B, dim, m.eps, st), "batch output norm") ||
+        matvec_any(dev, m.out_type, static_cast<const uint8_t *>(m.out), d->xn, d->logits, m.vocab, dim, B, 0, st))
+        return false;
+    for (uint32_t b = 0; b < B; ++b)   // first maximum wins (src/vbs_cpu_main.c:78-80)
+        if (!cuda_ok(argmax_launch(d->logits + (size_t)b * m.vocab, m.vocab, d->tok + b, nullptr, nullptr, 0, d->argmax_work,
+                                   st, false),
+                     "batch argmax"))
+            return false;
+    ++d->pos;
+    return true;
+}
+
+bool bd_sync(vbs_cu_batch_decoder *d) {
+    return cuda_ok(cudaStreamSynchronize(d->st), "batch decoder") && check_device_error(d->dev, d->st);
+}
+
+}  // namespace
+
+extern "C" {
+
+VBS_API void vbs_cu_batch_decoder_destroy(vbs_cu_batch_decoder_t *d) {
+    if (!bd_valid(d)) return;
+    d->magic = 0;
+    BatchDeviceGuard guard(d->dev ? d->dev->ordinal : 0);
+    if (d->st) cudaStreamSynchronize(d->st);
+    void *bufs[] = {d->x, d->xn, d->q, d->k, d->v, d->att, d->g, d->u, d->h, d->logits, d->kc, d->vc, d->tok,
+                    d->attn_work, d->argmax_work};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    if (d->st) cudaStreamDestroy(d->st);
+    delete d;
+}
+
+VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t batch,
+                                                            char *err, size_t err_cap) {
+    auto fail = [&](const char *why, vbs_cu_batch_decoder *d) -> vbs_cu_batch_decoder_t * {
+        if (err && err_cap) snprintf(err, err_cap, "%s", why);
+        latch_error("batch decoder: %s", why);
+        if (d) vbs_cu_batch_decoder_destroy(d);
+        return nullptr;
+    };
+    if (!m || !m->n_layers || !m->dim || !m->n_heads || !m->n_kv_heads || m->n_heads % m->n_kv_heads || !m->head_dim ||
+        m->head_dim % 8 || !m->ffn || !m->vocab || !m->embd || !m->out || !m->out_norm || !max_ctx)
+        return fail("invalid model description", nullptr);
+    if (!batch || batch > kBatchMax) return fail("batch must be 1..64 sequences", nullptr);
+    if (m->vocab_full && m->vocab_full != m->vocab) return fail("one GPU: vocab_full must equal vocab", nullptr);
+    DevState *dev = backend_current();
+    if (!dev) return fail("no usable sm_100 device is current", nullptr);
+    BatchDeviceGuard guard(dev->ordinal);
+    // weights written by work still in flight on other streams must be
+    // complete before this decoder's own stream reads them
+    if (!cuda_ok(cudaDeviceSynchronize(), "batch decoder create: pending work")) return fail("device error", nullptr);
+    vbs_cu_batch_decoder *d = new vbs_cu_batch_decoder();
+    d->m = *m;
+    d->dev = dev;
+    d->B = batch;
+    d->max_ctx = max_ctx;
+    d->q_dim = m->n_heads * m->head_dim;
+    d->kv_dim = m->n_kv_heads * m->head_dim;
+    d->seq_stride = (uint64_t)m->n_layers * max_ctx * d->kv_dim;
+    d->L.resize(m->n_layers);
+    for (uint32_t l = 0; l < m->n_layers; ++l) {
+        BLayer &y = d->L[l];
+        y.attn_norm = m->attn_norm[l];
+        y.ffn_norm = m->ffn_norm[l];
+        y.wq = static_cast<const uint8_t *>(m->wq[l]);
+        y.wk = static_cast<const uint8_t *>(m->wk[l]);
+        y.wv = static_cast<const uint8_t *>(m->wv[l]);
+        y.wo = static_cast<const uint8_t *>(m->wo[l]);
+        y.wgate = static_cast<const uint8_t *>(m->wgate[l]);
+        y.wup = static_cast<const uint8_t *>(m->wup[l]);
+        y.wdown = static_cast<const uint8_t *>(m->wdown[l]);
+        y.tq = m->tq[l]; y.tk = m->tk[l]; y.tv = m->tv[l]; y.to = m->to[l];
+        y.tgate = m->tgate[l]; y.tup = m->tup[l]; y.tdown = m->tdown[l];
+    }
+    const size_t B = batch, kv_bytes = B * d->seq_stride * sizeof(uint16_t);
+    d->splits = attn_num_splits(max_ctx, m->n_kv_heads, batch, dev->n_sm);
+    const size_t aw = attn_workspace_bytes(m->n_heads, m->n_kv_heads, m->head_dim, batch, d->splits);
+    if (!cuda_ok(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "batch decoder stream") ||
+        !balloc(&d->x, B * m->dim * 4, "batch rows") || !balloc(&d->xn, B * m->dim * 4, "batch rows") ||
+        !balloc(&d->q, B * d->q_dim * 4, "batch rows") || !balloc(&d->k, B * d->kv_dim * 4, "batch rows") ||
+        !balloc(&d->v, B * d->kv_dim * 4, "batch rows") || !balloc(&d->att, B * d->q_dim * 4, "batch rows") ||
+        !balloc(&d->g, B * m->ffn * 4, "batch rows") || !balloc(&d->u, B * m->ffn * 4, "batch rows") ||
+        !balloc(&d->h, B * m->ffn * 4, "batch rows") || !balloc(&d->logits, B * m->vocab * 4, "batch logits") ||
+        !balloc(&d->kc, kv_bytes, "batch KV cache") || !balloc(&d->vc, kv_bytes, "batch KV cache") ||
+        !balloc(&d->tok, B * 4, "batch tokens") || !balloc(&d->attn_work, aw, "batch attention") ||
+        !balloc(&d->argmax_work, argmax_workspace_bytes(), "batch argmax") ||
+        !cuda_ok(cudaMemsetAsync(d->attn_work, 0, aw, d->st), "batch attention") ||
+        !cuda_ok(cudaMemsetAsync(d->argmax_work, 0, argmax_workspace_bytes(), d->st), "batch argmax") ||
+        !cuda_ok(cudaMemsetAsync(d->kc, 0, kv_bytes, d->st), "batch KV cache") ||
+        !cuda_ok(cudaMemsetAsync(d->vc, 0, kv_bytes, d->st), "batch KV cache") ||
+        !cuda_ok(cudaMemsetAsync(d->tok, 0, B * 4, d->st), "batch tokens") || !bd_sync(d))
+        return fail("device allocation failed", d);
+    return d;
+}
+
+VBS_API int vbs_cu_batch_decoder_step(vbs_cu_batch_decoder_t *d, const uint32_t *tokens, float *logits_out,
+                                      uint32_t *next_tokens) {
+    if (!bd_valid(d)) { latch_error("batch decoder step: invalid decoder"); return -1; }
+    BatchDeviceGuard guard(d->dev->ordinal);
+    if (tokens) {
+        for (uint32_t b = 0; b < d->B; ++b)
+            if (tokens[b] >= d->m.vocab) { latch_error("batch decoder step: token %u >= vocab", tokens[b]); return -1; }
+        if (!cuda_ok(cudaMemcpyAsync(d->tok, tokens, (size_t)d->B * 4, cudaMemcpyHostToDevice, d->st), "batch tokens"))
+            return -1;
+    }
+    if (!bd_step(d)) return -1;
+    if (logits_out && !cuda_ok(cudaMemcpyAsync(logits_out, d->logits, (size_t)d->B * d->m.vocab * 4,
+                                               cudaMemcpyDeviceToHost, d->st), "batch logits"))
+        return -1;
+    if (next_tokens &&
+        !cuda_ok(cudaMemcpyAsync(next_tokens, d->tok, (size_t)d->B * 4, cudaMemcpyDeviceToHost, d->st), "batch tokens"))
+        return -1;
+    return bd_sync(d) ? 0 : -1;
+}
+
+VBS_API int vbs_cu_batch_decoder_enqueue_steps(vbs_cu_batch_decoder_t *d, uint32_t n_steps) {
+    if (!bd_valid(d)) { latch_error("batch decoder: invalid decoder"); return -1; }
+    BatchDeviceGuard guard(d->dev->ordinal);
+    for (uint32_t i = 0; i < n_steps; ++i)
+        if (!bd_step(d)) return -1;
+    return 0;
+}
+
+VBS_API int vbs_cu_batch_decoder_set_position(vbs_cu_batch_decoder_t *d, uint32_t pos, const uint32_t *tokens) {
+    if (!bd_valid(d) || pos >= d->max_ctx) { latch_error("batch decoder: invalid decoder or position"); return -1; }
+    BatchDeviceGuard guard(d->dev->ordinal);
+    if (tokens) {
+        for (uint32_t b = 0; b < d->B; ++b)
+            if (tokens[b] >= d->m.vocab) { latch_error("batch decoder: token %u >= vocab", tokens[b]); return -1; }
+        if (!cuda_ok(cudaMemcpyAsync(d->tok, tokens, (size_t)d->B * 4, cudaMemcpyHostToDevice, d->st), "batch tokens") ||
+            !bd_sync(d))
+            return -1;
+    }
+    d->pos = pos;
+    return 0;
+}
+
+VBS_API uint32_t vbs_cu_batch_decoder_position(vbs_cu_batch_decoder_t *d) { return bd_valid(d) ? d->pos : 0u; }
+VBS_API void vbs_cu_batch_decoder_reset(vbs_cu_batch_decoder_t *d) {
+    if (bd_valid(d)) d->pos = 0;
+}
+VBS_API void *vbs_cu_batch_decoder_stream(vbs_cu_batch_decoder_t *d) { return bd_valid(d) ? d->st : nullptr; }
+
+}  // extern "C"

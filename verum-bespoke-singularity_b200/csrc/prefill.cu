@@ -40,7 +40,9 @@ cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, 
     return cudaGetLastError();
 }
 
-// Chunk row b sits at position p0 + b: RoPE on its query heads in place and
+// Row b sits at position p0 + b * pos_step (a prompt chunk: step 1; B
+// sequences decoded in lockstep: step 0, each with its own cache seq_stride
+// elements after the previous one): RoPE on its query heads in place and
 // on its key heads (adjacent pairs, src/vbs_host_math.h:38-51, the rounding
 // of rope_kernel), then its key and value rows go into the cache as fp16
 // with the engine's rounding (src/vbs_host_math.h:150-159) in `layout`:
@@ -49,8 +51,10 @@ cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, 
 __global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const float *k, const float *v, uint16_t *kc,
                                                             uint16_t *vc, uint32_t p0, uint32_t layer, uint32_t max_ctx,
                                                             uint32_t nqh, uint32_t nkh, uint32_t hd, float theta,
-                                                            int layout) {
-    const uint32_t b = blockIdx.x, pos = p0 + b, half = hd / 2, kv_dim = nkh * hd;
+                                                            int layout, uint32_t pos_step, uint64_t seq_stride) {
+    const uint32_t b = blockIdx.x, pos = p0 + b * pos_step, half = hd / 2, kv_dim = nkh * hd;
+    kc += b * seq_stride;
+    vc += b * seq_stride;
     float *qb = q + (size_t)b * nqh * hd;
     const float *kb = k + (size_t)b * kv_dim, *vb = v + (size_t)b * kv_dim;
     auto rope = [&](float a, float c2, uint32_t i, float &o0, float &o1) {
@@ -91,7 +95,17 @@ cudaError_t pf_rope_store_launch(float *q, const float *k, const float *v, uint1
     if (!hd || hd % 2 || p0 + rows > max_ctx || layout < 0 || layout > 2 || (layout == 2 && hd != 64 && hd != 128))
         return cudaErrorInvalidValue;
     note_launches(1);
-    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, k, v, kc, vc, p0, layer, max_ctx, nqh, nkh, hd, theta, layout);
+    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, k, v, kc, vc, p0, layer, max_ctx, nqh, nkh, hd, theta, layout, 1u, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t rope_store_seqs_launch(float *q, const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t seqs,
+                                   uint64_t seq_stride, uint32_t pos, uint32_t layer, uint32_t max_ctx, uint32_t nqh,
+                                   uint32_t nkh, uint32_t hd, float theta, cudaStream_t st) {
+    if (!seqs) return cudaSuccess;
+    if (!hd || hd % 2 || pos >= max_ctx) return cudaErrorInvalidValue;
+    note_launches(1);
+    pf_rope_store_kernel<<<seqs, 256, 0, st>>>(q, k, v, kc, vc, pos, layer, max_ctx, nqh, nkh, hd, theta, 1, 0u, seq_stride);
     return cudaGetLastError();
 }
 
