@@ -15,7 +15,10 @@
 //   tokens.
 // The op order and the arithmetic of every op are those of the one-sequence
 // per-op decoder, so each sequence's logits match a one-sequence decoder
-// fed the same tokens to the kernels' rounding.
+// fed the same tokens to the kernels' rounding. The position lives on the
+// device (RoPE, the KV store and attention read it; the step's last kernel
+// advances it), so after one direct step, which sizes every workspace, a
+// step is captured once as a CUDA graph and replayed.
 #include "backend.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -71,20 +74,23 @@ struct vbs_cu_batch_decoder {
           *u = nullptr, *h = nullptr, *logits = nullptr;
     uint16_t *kc = nullptr, *vc = nullptr;
     uint32_t *tok = nullptr;   // [B] the tokens the next step feeds (device)
+    uint32_t *pos_dev = nullptr;   // the position of the next step (device)
     void *attn_work = nullptr, *argmax_work = nullptr;
+    bool warm = false;         // a direct step ran: every workspace has its final size
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
 };
 
 namespace {
 
 bool bd_valid(const vbs_cu_batch_decoder *d) { return d && d->magic == kBatchMagic; }
 
-// One lockstep step at position d->pos: feeds d->tok, leaves the logits in
-// d->logits and the argmax of every sequence in d->tok.
-bool bd_step(vbs_cu_batch_decoder *d) {
-    if (d->pos >= d->max_ctx) {
-        latch_error("batch decoder: position %u reaches the KV capacity %u", d->pos, d->max_ctx);
-        return false;
-    }
+__global__ void bd_advance_kernel(uint32_t *pos_dev) { ++*pos_dev; }
+
+// The kernels of one lockstep step at position *pos_dev: feeds d->tok,
+// leaves the logits in d->logits and the argmax of every sequence in
+// d->tok, advances *pos_dev.
+bool bd_record(vbs_cu_batch_decoder *d) {
     const vbs_cu_model_t &m = d->m;
     cudaStream_t st = d->st;
     DevState *dev = d->dev;
@@ -99,13 +105,13 @@ bool bd_step(vbs_cu_batch_decoder *d) {
             matvec_any(dev, y.tq, y.wq, d->xn, d->q, nq, dim, B, 0, st) ||
             matvec_any(dev, y.tk, y.wk, d->xn, d->k, nk, dim, B, 0, st) ||
             matvec_any(dev, y.tv, y.wv, d->xn, d->v, nk, dim, B, 0, st) ||
-            !cuda_ok(rope_store_seqs_launch(d->q, d->k, d->v, d->kc, d->vc, B, d->seq_stride, d->pos, l, d->max_ctx,
+            !cuda_ok(rope_store_seqs_launch(d->q, d->k, d->v, d->kc, d->vc, B, d->seq_stride, d->pos_dev, l, d->max_ctx,
                                             m.n_heads, m.n_kv_heads, hd, m.theta, st),
                      "batch rope/kv store"))
             return false;
         AttnParams ap = {};
         ap.q = d->q; ap.kc = d->kc; ap.vc = d->vc; ap.out = d->att;
-        ap.seq_len = d->pos + 1; ap.seq_step = 0;
+        ap.seq_dev = d->pos_dev; ap.seq_step = 0;   // positions <= *pos_dev
         ap.layer = l; ap.max_ctx = d->max_ctx;
         ap.nqh = m.n_heads; ap.nkh = m.n_kv_heads; ap.hd = hd;
         ap.scale = 1.0f / sqrtf((float)hd);
@@ -113,8 +119,7 @@ bool bd_step(vbs_cu_batch_decoder *d) {
         ap.head_major = 1; ap.swz = 0;
         ap.work = d->attn_work;
         ap.err = dev->err;
-        const uint32_t ns = std::min(d->splits, attn_num_splits(d->pos + 1, m.n_kv_heads, B, dev->n_sm));
-        if (!cuda_ok(attn_launch(ap, ns, st, false), "batch attention") ||
+        if (!cuda_ok(attn_launch(ap, d->splits, st, false), "batch attention") ||
             matvec_any(dev, y.to, y.wo, d->att, d->x, dim, nq, B, VBS_CU_MV_ACCUMULATE, st) ||
             !cuda_ok(pf_rmsnorm_rows_launch(d->x, y.ffn_norm, d->xn, B, dim, m.eps, st), "batch norm") ||
             matvec_any(dev, y.tgate, y.wgate, d->xn, d->g, ffn, dim, B, 0, st) ||
@@ -131,6 +136,36 @@ bool bd_step(vbs_cu_batch_decoder *d) {
                                    st, false),
                      "batch argmax"))
             return false;
+    note_launches(1);
+    bd_advance_kernel<<<1, 1, 0, st>>>(d->pos_dev);
+    return cuda_ok(cudaGetLastError(), "batch position");
+}
+
+// One step: the first directly (it sizes the workspaces), then a graph of
+// one step, captured once and replayed.
+bool bd_step(vbs_cu_batch_decoder *d) {
+    if (d->pos >= d->max_ctx) {
+        latch_error("batch decoder: position %u reaches the KV capacity %u", d->pos, d->max_ctx);
+        return false;
+    }
+    if (!d->warm) {
+        if (!bd_record(d)) return false;
+        d->warm = true;
+    } else {
+        if (!d->exec) {
+            if (!cuda_ok(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal), "batch capture")) return false;
+            const bool ok = bd_record(d);
+            cudaGraph_t g = nullptr;
+            const cudaError_t e = cudaStreamEndCapture(d->st, &g);
+            if (!ok || !cuda_ok(e, "batch capture")) {
+                if (g) cudaGraphDestroy(g);
+                return false;
+            }
+            d->graph = g;
+            if (!cuda_ok(cudaGraphInstantiate(&d->exec, d->graph, 0), "batch graph")) return false;
+        }
+        if (!cuda_ok(cudaGraphLaunch(d->exec, d->st), "batch graph launch")) return false;
+    }
     ++d->pos;
     return true;
 }
@@ -148,8 +183,10 @@ VBS_API void vbs_cu_batch_decoder_destroy(vbs_cu_batch_decoder_t *d) {
     d->magic = 0;
     BatchDeviceGuard guard(d->dev ? d->dev->ordinal : 0);
     if (d->st) cudaStreamSynchronize(d->st);
+    if (d->exec) cudaGraphExecDestroy(d->exec);
+    if (d->graph) cudaGraphDestroy(d->graph);
     void *bufs[] = {d->x, d->xn, d->q, d->k, d->v, d->att, d->g, d->u, d->h, d->logits, d->kc, d->vc, d->tok,
-                    d->attn_work, d->argmax_work};
+                    d->pos_dev, d->attn_work, d->argmax_work};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->st) cudaStreamDestroy(d->st);
@@ -208,13 +245,15 @@ VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t
         !balloc(&d->g, B * m->ffn * 4, "batch rows") || !balloc(&d->u, B * m->ffn * 4, "batch rows") ||
         !balloc(&d->h, B * m->ffn * 4, "batch rows") || !balloc(&d->logits, B * m->vocab * 4, "batch logits") ||
         !balloc(&d->kc, kv_bytes, "batch KV cache") || !balloc(&d->vc, kv_bytes, "batch KV cache") ||
-        !balloc(&d->tok, B * 4, "batch tokens") || !balloc(&d->attn_work, aw, "batch attention") ||
+        !balloc(&d->tok, B * 4, "batch tokens") || !balloc(&d->pos_dev, 4, "batch position") ||
+        !balloc(&d->attn_work, aw, "batch attention") ||
         !balloc(&d->argmax_work, argmax_workspace_bytes(), "batch argmax") ||
         !cuda_ok(cudaMemsetAsync(d->attn_work, 0, aw, d->st), "batch attention") ||
         !cuda_ok(cudaMemsetAsync(d->argmax_work, 0, argmax_workspace_bytes(), d->st), "batch argmax") ||
         !cuda_ok(cudaMemsetAsync(d->kc, 0, kv_bytes, d->st), "batch KV cache") ||
         !cuda_ok(cudaMemsetAsync(d->vc, 0, kv_bytes, d->st), "batch KV cache") ||
-        !cuda_ok(cudaMemsetAsync(d->tok, 0, B * 4, d->st), "batch tokens") || !bd_sync(d))
+        !cuda_ok(cudaMemsetAsync(d->tok, 0, B * 4, d->st), "batch tokens") ||
+        !cuda_ok(cudaMemsetAsync(d->pos_dev, 0, 4, d->st), "batch position") || !bd_sync(d))
         return fail("device allocation failed", d);
     return d;
 }
@@ -257,13 +296,17 @@ VBS_API int vbs_cu_batch_decoder_set_position(vbs_cu_batch_decoder_t *d, uint32_
             !bd_sync(d))
             return -1;
     }
+    if (!cuda_ok(cudaMemcpyAsync(d->pos_dev, &pos, 4, cudaMemcpyHostToDevice, d->st), "batch position") || !bd_sync(d))
+        return -1;
     d->pos = pos;
     return 0;
 }
 
 VBS_API uint32_t vbs_cu_batch_decoder_position(vbs_cu_batch_decoder_t *d) { return bd_valid(d) ? d->pos : 0u; }
 VBS_API void vbs_cu_batch_decoder_reset(vbs_cu_batch_decoder_t *d) {
-    if (bd_valid(d)) d->pos = 0;
+    if (!bd_valid(d)) return;
+    BatchDeviceGuard guard(d->dev->ordinal);
+    if (cuda_ok(cudaMemsetAsync(d->pos_dev, 0, 4, d->st), "batch position") && bd_sync(d)) d->pos = 0;
 }
 VBS_API void *vbs_cu_batch_decoder_stream(vbs_cu_batch_decoder_t *d) { return bd_valid(d) ? d->st : nullptr; }
 

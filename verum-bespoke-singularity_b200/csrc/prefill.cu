@@ -51,8 +51,9 @@ cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, 
 __global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const float *k, const float *v, uint16_t *kc,
                                                             uint16_t *vc, uint32_t p0, uint32_t layer, uint32_t max_ctx,
                                                             uint32_t nqh, uint32_t nkh, uint32_t hd, float theta,
-                                                            int layout, uint32_t pos_step, uint64_t seq_stride) {
-    const uint32_t b = blockIdx.x, pos = p0 + b * pos_step, half = hd / 2, kv_dim = nkh * hd;
+                                                            int layout, uint32_t pos_step, uint64_t seq_stride,
+                                                            const uint32_t *pos_dev) {
+    const uint32_t b = blockIdx.x, pos = (pos_dev ? *pos_dev : p0) + b * pos_step, half = hd / 2, kv_dim = nkh * hd;
     kc += b * seq_stride;
     vc += b * seq_stride;
     float *qb = q + (size_t)b * nqh * hd;
@@ -95,17 +96,19 @@ cudaError_t pf_rope_store_launch(float *q, const float *k, const float *v, uint1
     if (!hd || hd % 2 || p0 + rows > max_ctx || layout < 0 || layout > 2 || (layout == 2 && hd != 64 && hd != 128))
         return cudaErrorInvalidValue;
     note_launches(1);
-    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, k, v, kc, vc, p0, layer, max_ctx, nqh, nkh, hd, theta, layout, 1u, 0);
+    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, k, v, kc, vc, p0, layer, max_ctx, nqh, nkh, hd, theta, layout, 1u, 0,
+                                               nullptr);
     return cudaGetLastError();
 }
 
 cudaError_t rope_store_seqs_launch(float *q, const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t seqs,
-                                   uint64_t seq_stride, uint32_t pos, uint32_t layer, uint32_t max_ctx, uint32_t nqh,
-                                   uint32_t nkh, uint32_t hd, float theta, cudaStream_t st) {
+                                   uint64_t seq_stride, const uint32_t *pos_dev, uint32_t layer, uint32_t max_ctx,
+                                   uint32_t nqh, uint32_t nkh, uint32_t hd, float theta, cudaStream_t st) {
     if (!seqs) return cudaSuccess;
-    if (!hd || hd % 2 || pos >= max_ctx) return cudaErrorInvalidValue;
+    if (!hd || hd % 2 || !pos_dev) return cudaErrorInvalidValue;
     note_launches(1);
-    pf_rope_store_kernel<<<seqs, 256, 0, st>>>(q, k, v, kc, vc, pos, layer, max_ctx, nqh, nkh, hd, theta, 1, 0u, seq_stride);
+    pf_rope_store_kernel<<<seqs, 256, 0, st>>>(q, k, v, kc, vc, 0u, layer, max_ctx, nqh, nkh, hd, theta, 1, 0u, seq_stride,
+                                               pos_dev);
     return cudaGetLastError();
 }
 
