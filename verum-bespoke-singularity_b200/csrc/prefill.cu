@@ -16,9 +16,11 @@ namespace vbs {
 
 // RMSNorm of `rows` rows of n floats, one CTA per row, with the arithmetic
 // of rmsnorm_kernel (src/vbs_host_math.h:28-36: sum of squares in double).
-__global__ void __launch_bounds__(256) pf_rmsnorm_rows_kernel(const float *__restrict__ in, const float *__restrict__ w,
-                                                              float *__restrict__ out, uint32_t n, float eps) {
-    __shared__ double part[8];
+// 256 threads per row for prompt chunks; 1024 when there are few rows (a
+// decode batch), so the few CTAs still cover a row in a short loop.
+__global__ void __launch_bounds__(1024) pf_rmsnorm_rows_kernel(const float *__restrict__ in, const float *__restrict__ w,
+                                                               float *__restrict__ out, uint32_t n, float eps) {
+    __shared__ double part[32];
     const float *x = in + (size_t)blockIdx.x * n;
     float *y = out + (size_t)blockIdx.x * n;
     double ss = 0.0;
@@ -27,7 +29,7 @@ __global__ void __launch_bounds__(256) pf_rmsnorm_rows_kernel(const float *__res
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
     __syncthreads();
     double tot = 0.0;
-    for (int k = 0; k < 8; ++k) tot += part[k];
+    for (uint32_t k = 0; k < blockDim.x / 32; ++k) tot += part[k];
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tot / (double)n), eps)));
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
 }
@@ -36,7 +38,7 @@ cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, 
                                    cudaStream_t st) {
     if (!rows || !n) return cudaSuccess;
     note_launches(1);
-    pf_rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(in, w, out, n, eps);
+    pf_rmsnorm_rows_kernel<<<rows, rows < 64 ? 1024 : 256, 0, st>>>(in, w, out, n, eps);
     return cudaGetLastError();
 }
 
@@ -64,7 +66,7 @@ __global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const floa
         o0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(c2, s));
         o1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(c2, c));
     };
-    for (uint32_t t = threadIdx.x; t < (nqh + nkh) * half; t += blockDim.x) {
+    for (uint32_t t = threadIdx.x + blockIdx.y * blockDim.x; t < (nqh + nkh) * half; t += blockDim.x * gridDim.y) {
         const bool isq = t < nqh * half;
         const uint32_t u = isq ? t : t - nqh * half, h = u / half, i = 2 * (u % half);
         if (isq) {
@@ -107,8 +109,9 @@ cudaError_t rope_store_seqs_launch(float *q, const float *k, const float *v, uin
     if (!seqs) return cudaSuccess;
     if (!hd || hd % 2 || !pos_dev) return cudaErrorInvalidValue;
     note_launches(1);
-    pf_rope_store_kernel<<<seqs, 256, 0, st>>>(q, k, v, kc, vc, 0u, layer, max_ctx, nqh, nkh, hd, theta, 1, 0u, seq_stride,
-                                               pos_dev);
+    // few rows: each row's items over 8 CTAs
+    pf_rope_store_kernel<<<dim3(seqs, seqs < 64 ? 8 : 1), 256, 0, st>>>(q, k, v, kc, vc, 0u, layer, max_ctx, nqh, nkh, hd,
+                                                                         theta, 1, 0u, seq_stride, pos_dev);
     return cudaGetLastError();
 }
 
