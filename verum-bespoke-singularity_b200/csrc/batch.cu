@@ -67,6 +67,10 @@ struct vbs_cu_batch_decoder {
     vbs_cu_model_t m;
     std::vector<BLayer> L;
     DevState *dev = nullptr;
+    // The device's state with workspaces of this decoder's own: its graph
+    // holds their addresses, which the device-wide ones (regrown by other
+    // callers) would not keep.
+    DevState own;
     cudaStream_t st = nullptr;
     uint32_t B = 0, max_ctx = 0, q_dim = 0, kv_dim = 0, splits = 1, pos = 0;
     uint64_t seq_stride = 0;   // cache elements per sequence: [layer][kv head][max_ctx][head_dim]
@@ -93,7 +97,7 @@ __global__ void bd_advance_kernel(uint32_t *pos_dev) { ++*pos_dev; }
 bool bd_record(vbs_cu_batch_decoder *d) {
     const vbs_cu_model_t &m = d->m;
     cudaStream_t st = d->st;
-    DevState *dev = d->dev;
+    DevState *dev = &d->own;
     const uint32_t B = d->B, dim = m.dim, nq = d->q_dim, nk = d->kv_dim, ffn = m.ffn, hd = m.head_dim;
     if (!cuda_ok(embed_rows_launch(m.embd_type, static_cast<const uint8_t *>(m.embd), d->tok, B, m.vocab, d->x, dim,
                                    dev->err, st),
@@ -186,7 +190,7 @@ VBS_API void vbs_cu_batch_decoder_destroy(vbs_cu_batch_decoder_t *d) {
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->graph) cudaGraphDestroy(d->graph);
     void *bufs[] = {d->x, d->xn, d->q, d->k, d->v, d->att, d->g, d->u, d->h, d->logits, d->kc, d->vc, d->tok,
-                    d->pos_dev, d->attn_work, d->argmax_work};
+                    d->pos_dev, d->attn_work, d->argmax_work, d->own.mvb_work, d->own.qg_work};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->st) cudaStreamDestroy(d->st);
@@ -215,6 +219,13 @@ VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t
     vbs_cu_batch_decoder *d = new vbs_cu_batch_decoder();
     d->m = *m;
     d->dev = dev;
+    d->own = *dev;
+    d->own.attn_work = nullptr;
+    d->own.attn_work_bytes = 0;
+    d->own.mvb_work = nullptr;
+    d->own.mvb_work_bytes = 0;
+    d->own.qg_work = nullptr;
+    d->own.qg_work_bytes = 0;
     d->B = batch;
     d->max_ctx = max_ctx;
     d->q_dim = m->n_heads * m->head_dim;
