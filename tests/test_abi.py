@@ -82,6 +82,27 @@ def test_attention_rejects_bad_head_counts(vbs, entry, nqh, nkh):
     vbs.clear_error()
 
 
+def test_batch_decoder_refuses_bad_arguments(vbs):
+    """vbs_cu_batch_decoder_create checks the model description and the
+    batch size before it touches a device, so the refusals run without a
+    GPU: no description, and a batch of 0 or above 64 sequences."""
+    import ctypes as C
+    L = vbs.lib()
+    err = C.create_string_buffer(256)
+    vbs.clear_error()
+    assert not L.vbs_cu_batch_decoder_create(None, 64, 8, err, 256)
+    assert b"invalid model description" in err.value
+    desc = vbs.ModelDesc(n_layers=1, dim=64, n_heads=2, n_kv_heads=1, head_dim=32, ffn=128, vocab=16,
+                         embd=16, out=16, out_norm=16)
+    for bad in (0, 65):
+        vbs.clear_error()
+        assert not L.vbs_cu_batch_decoder_create(C.byref(desc), 64, bad, err, 256)
+        assert b"batch must be" in err.value
+        assert "batch" in vbs.last_error()
+    vbs.clear_error()
+    assert L.vbs_cu_batch_decoder_position(None) == 0   # an invalid handle is refused, not dereferenced
+
+
 def test_layout_matches_reference_headers():
     """Every offset and size of the ops-table types in include/vbs_b200.h
     equals the reference's include/vbs_backend.h (the same printer compiled
