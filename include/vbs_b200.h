@@ -410,7 +410,10 @@ VBS_API void *vbs_cu_decoder_stream(vbs_cu_decoder_t *d);
  * decoder fed the same tokens, to the kernels' rounding. One GPU; the
  * model description as for vbs_cu_decoder_create (vocab_full = vocab). */
 typedef struct vbs_cu_batch_decoder vbs_cu_batch_decoder_t;
-/* batch 1..64 sequences; allocates B KV caches of max_ctx positions. */
+/* batch 1..64 sequences; allocates B KV caches of max_ctx positions and
+ * copies [wq; wk; wv] and [wgate; wup] of every layer into one matrix each
+ * (when their types agree), so later changes to those weights are not
+ * seen. */
 VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t batch,
                                                             char *err, size_t err_cap);
 VBS_API void vbs_cu_batch_decoder_destroy(vbs_cu_batch_decoder_t *d);

@@ -41,7 +41,21 @@ struct BLayer {
     const float *attn_norm, *ffn_norm;
     const uint8_t *wq, *wk, *wv, *wo, *wgate, *wup, *wdown;
     int tq, tk, tv, to, tgate, tup, tdown;
+    // the decoder's own copies of [wq; wk; wv] and [wgate; wup] as one
+    // matrix each (NULL when the types differ): one launch per group
+    uint8_t *wqkv, *wgu;
 };
+
+// h[b][i] = SiLU(gu[b][i]) * gu[b][ffn + i] (src/vbs_host_math.h:53-57, the
+// expression of silu_mul_kernel), rows of the fused gate|up projection.
+__global__ void bd_silu_rows_kernel(const float *__restrict__ gu, float *__restrict__ h, uint32_t rows, uint32_t ffn) {
+    const uint64_t n = (uint64_t)rows * ffn;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t b = t / ffn, i = t % ffn;
+        const float g = gu[b * 2 * ffn + i], u = gu[b * 2 * ffn + ffn + i];
+        h[t] = g / (1.0f + expf(-g)) * u;
+    }
+}
 
 // Makes `ordinal` current for the scope and restores the caller's device.
 struct BatchDeviceGuard {
@@ -76,6 +90,7 @@ struct vbs_cu_batch_decoder {
     uint64_t seq_stride = 0;   // cache elements per sequence: [layer][kv head][max_ctx][head_dim]
     float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
           *u = nullptr, *h = nullptr, *logits = nullptr;
+    float *qkv = nullptr;      // [B][q_dim + 2 kv_dim]: the fused projection's rows (g holds [B][2 ffn])
     uint16_t *kc = nullptr, *vc = nullptr;
     uint32_t *tok = nullptr;   // [B] the tokens the next step feeds (device)
     uint32_t *pos_dev = nullptr;   // the position of the next step (device)
@@ -105,13 +120,21 @@ bool bd_record(vbs_cu_batch_decoder *d) {
         return false;
     for (uint32_t l = 0; l < m.n_layers; ++l) {
         const BLayer &y = d->L[l];
-        if (!cuda_ok(pf_rmsnorm_rows_launch(d->x, y.attn_norm, d->xn, B, dim, m.eps, st), "batch norm") ||
-            matvec_any(dev, y.tq, y.wq, d->xn, d->q, nq, dim, B, 0, st) ||
-            matvec_any(dev, y.tk, y.wk, d->xn, d->k, nk, dim, B, 0, st) ||
-            matvec_any(dev, y.tv, y.wv, d->xn, d->v, nk, dim, B, 0, st) ||
-            !cuda_ok(rope_store_seqs_launch(d->q, d->k, d->v, d->kc, d->vc, B, d->seq_stride, d->pos_dev, l, d->max_ctx,
-                                            m.n_heads, m.n_kv_heads, hd, m.theta, st),
-                     "batch rope/kv store"))
+        const uint32_t nqkv = nq + 2 * nk;
+        if (!cuda_ok(pf_rmsnorm_rows_launch(d->x, y.attn_norm, d->xn, B, dim, m.eps, st), "batch norm"))
+            return false;
+        if (y.wqkv ? (matvec_any(dev, y.tq, y.wqkv, d->xn, d->qkv, nqkv, dim, B, 0, st) ||
+                      !cuda_ok(rope_store_seqs_launch(d->qkv, d->q, nqkv, d->qkv + nq, d->qkv + nq + nk, nqkv, d->kc,
+                                                      d->vc, B, d->seq_stride, d->pos_dev, l, d->max_ctx, m.n_heads,
+                                                      m.n_kv_heads, hd, m.theta, st),
+                               "batch rope/kv store"))
+                   : (matvec_any(dev, y.tq, y.wq, d->xn, d->q, nq, dim, B, 0, st) ||
+                      matvec_any(dev, y.tk, y.wk, d->xn, d->k, nk, dim, B, 0, st) ||
+                      matvec_any(dev, y.tv, y.wv, d->xn, d->v, nk, dim, B, 0, st) ||
+                      !cuda_ok(rope_store_seqs_launch(d->q, d->q, nq, d->k, d->v, nk, d->kc, d->vc, B, d->seq_stride,
+                                                      d->pos_dev, l, d->max_ctx, m.n_heads, m.n_kv_heads, hd, m.theta,
+                                                      st),
+                               "batch rope/kv store")))
             return false;
         AttnParams ap = {};
         ap.q = d->q; ap.kc = d->kc; ap.vc = d->vc; ap.out = d->att;
@@ -125,12 +148,20 @@ bool bd_record(vbs_cu_batch_decoder *d) {
         ap.err = dev->err;
         if (!cuda_ok(attn_launch(ap, d->splits, st, false), "batch attention") ||
             matvec_any(dev, y.to, y.wo, d->att, d->x, dim, nq, B, VBS_CU_MV_ACCUMULATE, st) ||
-            !cuda_ok(pf_rmsnorm_rows_launch(d->x, y.ffn_norm, d->xn, B, dim, m.eps, st), "batch norm") ||
-            matvec_any(dev, y.tgate, y.wgate, d->xn, d->g, ffn, dim, B, 0, st) ||
-            matvec_any(dev, y.tup, y.wup, d->xn, d->u, ffn, dim, B, 0, st) ||
-            !cuda_ok(silu_mul_launch(d->g, d->u, d->h, B * ffn, st), "batch silu") ||
-            matvec_any(dev, y.tdown, y.wdown, d->h, d->x, dim, ffn, B, VBS_CU_MV_ACCUMULATE, st))
+            !cuda_ok(pf_rmsnorm_rows_launch(d->x, y.ffn_norm, d->xn, B, dim, m.eps, st), "batch norm"))
             return false;
+        if (y.wgu) {
+            if (matvec_any(dev, y.tgate, y.wgu, d->xn, d->g, 2 * ffn, dim, B, 0, st)) return false;
+            note_launches(1);
+            bd_silu_rows_kernel<<<std::min<uint32_t>((B * ffn + 255) / 256, (uint32_t)dev->n_sm * 8), 256, 0, st>>>(
+                d->g, d->h, B, ffn);
+            if (!cuda_ok(cudaGetLastError(), "batch silu")) return false;
+        } else if (matvec_any(dev, y.tgate, y.wgate, d->xn, d->g, ffn, dim, B, 0, st) ||
+                   matvec_any(dev, y.tup, y.wup, d->xn, d->u, ffn, dim, B, 0, st) ||
+                   !cuda_ok(silu_mul_launch(d->g, d->u, d->h, B * ffn, st), "batch silu")) {
+            return false;
+        }
+        if (matvec_any(dev, y.tdown, y.wdown, d->h, d->x, dim, ffn, B, VBS_CU_MV_ACCUMULATE, st)) return false;
     }
     if (!cuda_ok(pf_rmsnorm_rows_launch(d->x, m.out_norm, d->xn, B, dim, m.eps, st), "batch output norm") ||
         matvec_any(dev, m.out_type, static_cast<const uint8_t *>(m.out), d->xn, d->logits, m.vocab, dim, B, 0, st))
@@ -189,7 +220,11 @@ VBS_API void vbs_cu_batch_decoder_destroy(vbs_cu_batch_decoder_t *d) {
     if (d->st) cudaStreamSynchronize(d->st);
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->graph) cudaGraphDestroy(d->graph);
-    void *bufs[] = {d->x, d->xn, d->q, d->k, d->v, d->att, d->g, d->u, d->h, d->logits, d->kc, d->vc, d->tok,
+    for (BLayer &y : d->L) {
+        if (y.wqkv) cudaFree(y.wqkv);
+        if (y.wgu) cudaFree(y.wgu);
+    }
+    void *bufs[] = {d->x, d->xn, d->q, d->k, d->v, d->att, d->g, d->u, d->h, d->logits, d->qkv, d->kc, d->vc, d->tok,
                     d->pos_dev, d->attn_work, d->argmax_work, d->own.mvb_work, d->own.qg_work};
     for (void *b : bufs)
         if (b) cudaFree(b);
@@ -245,6 +280,30 @@ VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t
         y.wdown = static_cast<const uint8_t *>(m->wdown[l]);
         y.tq = m->tq[l]; y.tk = m->tk[l]; y.tv = m->tv[l]; y.to = m->to[l];
         y.tgate = m->tgate[l]; y.tup = m->tup[l]; y.tdown = m->tdown[l];
+        y.wqkv = y.wgu = nullptr;
+    }
+    // [wq; wk; wv] and [wgate; wup] copied once into one matrix each (same
+    // type, same width: the rows simply follow one another), 256 bytes of
+    // zero tail as the matvec kernels may read past a row end
+    for (uint32_t l = 0; l < m->n_layers; ++l) {
+        BLayer &y = d->L[l];
+        if (y.tq == y.tk && y.tq == y.tv) {
+            const size_t rb = row_bytes(y.tq, m->dim), nq = (size_t)d->q_dim * rb, nk = (size_t)d->kv_dim * rb;
+            if (!balloc(&y.wqkv, nq + 2 * nk + 256, "batch fused q/k/v") ||
+                !cuda_ok(cudaMemset(y.wqkv + nq + 2 * nk, 0, 256), "batch fused q/k/v") ||
+                !cuda_ok(cudaMemcpy(y.wqkv, y.wq, nq, cudaMemcpyDeviceToDevice), "batch fused q/k/v") ||
+                !cuda_ok(cudaMemcpy(y.wqkv + nq, y.wk, nk, cudaMemcpyDeviceToDevice), "batch fused q/k/v") ||
+                !cuda_ok(cudaMemcpy(y.wqkv + nq + nk, y.wv, nk, cudaMemcpyDeviceToDevice), "batch fused q/k/v"))
+                return fail("device allocation failed", d);
+        }
+        if (y.tgate == y.tup) {
+            const size_t half = (size_t)m->ffn * row_bytes(y.tgate, m->dim);
+            if (!balloc(&y.wgu, 2 * half + 256, "batch fused gate/up") ||
+                !cuda_ok(cudaMemset(y.wgu + 2 * half, 0, 256), "batch fused gate/up") ||
+                !cuda_ok(cudaMemcpy(y.wgu, y.wgate, half, cudaMemcpyDeviceToDevice), "batch fused gate/up") ||
+                !cuda_ok(cudaMemcpy(y.wgu + half, y.wup, half, cudaMemcpyDeviceToDevice), "batch fused gate/up"))
+                return fail("device allocation failed", d);
+        }
     }
     const size_t B = batch, kv_bytes = B * d->seq_stride * sizeof(uint16_t);
     d->splits = attn_num_splits(max_ctx, m->n_kv_heads, batch, dev->n_sm);
@@ -253,7 +312,8 @@ VBS_API vbs_cu_batch_decoder_t *vbs_cu_batch_decoder_create(const vbs_cu_model_t
         !balloc(&d->x, B * m->dim * 4, "batch rows") || !balloc(&d->xn, B * m->dim * 4, "batch rows") ||
         !balloc(&d->q, B * d->q_dim * 4, "batch rows") || !balloc(&d->k, B * d->kv_dim * 4, "batch rows") ||
         !balloc(&d->v, B * d->kv_dim * 4, "batch rows") || !balloc(&d->att, B * d->q_dim * 4, "batch rows") ||
-        !balloc(&d->g, B * m->ffn * 4, "batch rows") || !balloc(&d->u, B * m->ffn * 4, "batch rows") ||
+        !balloc(&d->g, B * 2 * m->ffn * 4, "batch rows") || !balloc(&d->u, B * m->ffn * 4, "batch rows") ||
+        !balloc(&d->qkv, B * (d->q_dim + 2 * d->kv_dim) * 4, "batch rows") ||
         !balloc(&d->h, B * m->ffn * 4, "batch rows") || !balloc(&d->logits, B * m->vocab * 4, "batch logits") ||
         !balloc(&d->kc, kv_bytes, "batch KV cache") || !balloc(&d->vc, kv_bytes, "batch KV cache") ||
         !balloc(&d->tok, B * 4, "batch tokens") || !balloc(&d->pos_dev, 4, "batch position") ||

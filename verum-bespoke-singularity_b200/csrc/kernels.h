@@ -175,10 +175,12 @@ cudaError_t pf_rope_store_launch(float *q, const float *k, const float *v, uint1
                                  float theta, int layout, cudaStream_t st);
 // B sequences in lockstep (batch.cu): row b at position *pos_dev (read on
 // the device, so a captured step replays at every position), its K/V into
-// the head-major cache starting seq_stride * b elements in.
-cudaError_t rope_store_seqs_launch(float *q, const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t seqs,
-                                   uint64_t seq_stride, const uint32_t *pos_dev, uint32_t layer, uint32_t max_ctx,
-                                   uint32_t nqh, uint32_t nkh, uint32_t hd, float theta, cudaStream_t st);
+// the head-major cache starting seq_stride * b elements in. Input rows qs
+// (queries) and ks (keys, values) floats apart; RoPE'd queries to q_out.
+cudaError_t rope_store_seqs_launch(const float *q_in, float *q_out, uint32_t qs, const float *k, const float *v,
+                                   uint32_t ks, uint16_t *kc, uint16_t *vc, uint32_t seqs, uint64_t seq_stride,
+                                   const uint32_t *pos_dev, uint32_t layer, uint32_t max_ctx, uint32_t nqh, uint32_t nkh,
+                                   uint32_t hd, float theta, cudaStream_t st);
 
 // Split-KV GQA decode attention. seq_len from `seq_dev` (+1) when non-NULL,
 // else `seq_len`. `work` holds the split partials and merge counters:

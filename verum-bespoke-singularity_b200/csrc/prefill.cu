@@ -50,16 +50,20 @@ cudaError_t pf_rmsnorm_rows_launch(const float *in, const float *w, float *out, 
 // with the engine's rounding (src/vbs_host_math.h:150-159) in `layout`:
 // 0 engine order, 1 head-major, 2 head-major with the step kernel's chunk
 // swizzle. One CTA per row.
-__global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const float *k, const float *v, uint16_t *kc,
-                                                            uint16_t *vc, uint32_t p0, uint32_t layer, uint32_t max_ctx,
-                                                            uint32_t nqh, uint32_t nkh, uint32_t hd, float theta,
-                                                            int layout, uint32_t pos_step, uint64_t seq_stride,
-                                                            const uint32_t *pos_dev) {
-    const uint32_t b = blockIdx.x, pos = (pos_dev ? *pos_dev : p0) + b * pos_step, half = hd / 2, kv_dim = nkh * hd;
+// q_in rows are qs floats apart, k and v rows ks apart (separate buffers,
+// or the q|k|v rows of one fused projection); the RoPE'd queries go to q_out
+// rows of nqh * hd (which may be q_in itself).
+__global__ void __launch_bounds__(256) pf_rope_store_kernel(const float *q_in, float *q_out, uint32_t qs, const float *k,
+                                                            const float *v, uint32_t ks, uint16_t *kc, uint16_t *vc,
+                                                            uint32_t p0, uint32_t layer, uint32_t max_ctx, uint32_t nqh,
+                                                            uint32_t nkh, uint32_t hd, float theta, int layout,
+                                                            uint32_t pos_step, uint64_t seq_stride, const uint32_t *pos_dev) {
+    const uint32_t b = blockIdx.x, pos = (pos_dev ? *pos_dev : p0) + b * pos_step, half = hd / 2;
     kc += b * seq_stride;
     vc += b * seq_stride;
-    float *qb = q + (size_t)b * nqh * hd;
-    const float *kb = k + (size_t)b * kv_dim, *vb = v + (size_t)b * kv_dim;
+    const float *qi = q_in + (size_t)b * qs;
+    float *qb = q_out + (size_t)b * nqh * hd;
+    const float *kb = k + (size_t)b * ks, *vb = v + (size_t)b * ks;
     auto rope = [&](float a, float c2, uint32_t i, float &o0, float &o1) {
         const float ang = __fmul_rn((float)pos, powf(theta, __fdiv_rn(-(float)i, (float)hd)));
         const float c = cosf(ang), s = sinf(ang);
@@ -70,11 +74,11 @@ __global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const floa
         const bool isq = t < nqh * half;
         const uint32_t u = isq ? t : t - nqh * half, h = u / half, i = 2 * (u % half);
         if (isq) {
-            float *p = qb + (size_t)h * hd + i;
+            const float *src = qi + (size_t)h * hd + i;
             float o0, o1;
-            rope(p[0], p[1], i, o0, o1);
-            p[0] = o0;
-            p[1] = o1;
+            rope(src[0], src[1], i, o0, o1);
+            qb[(size_t)h * hd + i] = o0;
+            qb[(size_t)h * hd + i + 1] = o1;
             continue;
         }
         if (pos >= max_ctx) continue;   // the host checks capacity; never write past the cache
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(256) pf_rope_store_kernel(float *q, const floa
         rope(kb[local], kb[local + 1], i, k0, k1);
         // dims i, i+1 (i even) are adjacent in every layout: same 16-byte chunk
         const uint64_t at = layout == 2 ? kv_index_swz(layer, pos, local, max_ctx, nkh, hd)
-                                        : kv_index(layout == 1, layer, pos, local, max_ctx, kv_dim, hd);
+                                        : kv_index(layout == 1, layer, pos, local, max_ctx, nkh * hd, hd);
         kc[at] = f32_to_f16_kv(k0);
         kc[at + 1] = f32_to_f16_kv(k1);
         vc[at] = f32_to_f16_kv(vb[local]);
@@ -98,20 +102,21 @@ cudaError_t pf_rope_store_launch(float *q, const float *k, const float *v, uint1
     if (!hd || hd % 2 || p0 + rows > max_ctx || layout < 0 || layout > 2 || (layout == 2 && hd != 64 && hd != 128))
         return cudaErrorInvalidValue;
     note_launches(1);
-    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, k, v, kc, vc, p0, layer, max_ctx, nqh, nkh, hd, theta, layout, 1u, 0,
-                                               nullptr);
+    pf_rope_store_kernel<<<rows, 256, 0, st>>>(q, q, nqh * hd, k, v, nkh * hd, kc, vc, p0, layer, max_ctx, nqh, nkh, hd,
+                                               theta, layout, 1u, 0, nullptr);
     return cudaGetLastError();
 }
 
-cudaError_t rope_store_seqs_launch(float *q, const float *k, const float *v, uint16_t *kc, uint16_t *vc, uint32_t seqs,
-                                   uint64_t seq_stride, const uint32_t *pos_dev, uint32_t layer, uint32_t max_ctx,
-                                   uint32_t nqh, uint32_t nkh, uint32_t hd, float theta, cudaStream_t st) {
+cudaError_t rope_store_seqs_launch(const float *q_in, float *q_out, uint32_t qs, const float *k, const float *v,
+                                   uint32_t ks, uint16_t *kc, uint16_t *vc, uint32_t seqs, uint64_t seq_stride,
+                                   const uint32_t *pos_dev, uint32_t layer, uint32_t max_ctx, uint32_t nqh, uint32_t nkh,
+                                   uint32_t hd, float theta, cudaStream_t st) {
     if (!seqs) return cudaSuccess;
     if (!hd || hd % 2 || !pos_dev) return cudaErrorInvalidValue;
     note_launches(1);
     // few rows: each row's items over 8 CTAs
-    pf_rope_store_kernel<<<dim3(seqs, seqs < 64 ? 8 : 1), 256, 0, st>>>(q, k, v, kc, vc, 0u, layer, max_ctx, nqh, nkh, hd,
-                                                                         theta, 1, 0u, seq_stride, pos_dev);
+    pf_rope_store_kernel<<<dim3(seqs, seqs < 64 ? 8 : 1), 256, 0, st>>>(q_in, q_out, qs, k, v, ks, kc, vc, 0u, layer, max_ctx,
+                                                                         nqh, nkh, hd, theta, 1, 0u, seq_stride, pos_dev);
     return cudaGetLastError();
 }
 
