@@ -739,8 +739,8 @@ def main():
     dec = vbs.Decoder(model, max_ctx)
     kps = dec.kernels_per_step
     prompt = models.splitmix_ints(4096, args.ctx, shape.vocab)
-    # the context: one GPU takes the batched prefill (chunks of 8 tokens per
-    # pass over the weights), tensor parallelism one token per step like
+    # the context: one GPU takes the batched prefill (chunks of 512 tokens
+    # per pass over the weights), tensor parallelism one token per step like
     # the engine; either way the timed steps below start at position ctx
     prefill_mode = "token-by-token"
     torch.cuda.synchronize()

@@ -2,11 +2,12 @@
 //
 // The reference feeds a prompt one token at a time through forward_token
 // (src/main.c:901-904), so every prompt token streams all weights once.
-// The decoder's prefill instead takes the prompt in chunks of up to 8
-// tokens: the matrices run through the batched matvec (one weight pass per
-// chunk), attention is the split-KV kernel with a causal step per query,
-// and the two kernels here do the row-wise rest: RMSNorm of each chunk row
-// and RoPE plus the fp16 KV store at the rows' positions.
+// The decoder's prefill instead takes the prompt in chunks of up to 512
+// tokens: the matrices run through the tcgen05 GEMM (one weight pass per
+// chunk), attention is the query-tiled causal kernel, and the kernels here
+// do the row-wise rest: RMSNorm of each chunk row, and RoPE plus the fp16
+// KV store at the rows' positions. The batch decoder (batch.cu) uses the
+// same two for its B sequences at one position.
 #include "common.cuh"
 #include "kernels.h"
 
