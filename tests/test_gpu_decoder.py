@@ -7,7 +7,8 @@
   the reference's GPU backends implement; teacher-forced so one near-tie
   cannot end the comparison.
 * An 8B-width model (two Llama-3-8B layers, Q4_K/Q6_K, vocab cut to 4096)
-  against the same oracle.
+  against the same oracle; two Llama-3-70B layers and a 6144-wide model,
+  wider than one stage, through the step kernel.
 * Graph replay, plain launches and PDL give identical bits; the on-device
   greedy loop equals the host-driven one.
 """
@@ -130,6 +131,43 @@ def test_tp_instance_on_one_gpu_identical(vbs, l8b_2layer, clean_errors):
     assert a.generate([11, 12, 13], 24) == b.generate([11, 12, 13], 24)
     a.close()
     b.close()
+
+
+# Models wider than one stage's 4096-column chunk: the step kernel streams
+# their rows as chunks in consecutive stages (sums accumulated, written
+# whole), splits the down projection into up to 7 chunk planes and runs the
+# norm prologue in passes. 70B width (8 query heads per KV head), and 6144
+# (6 per KV head), whose second row chunk and second prologue pass are
+# half-full.
+WIDE = {
+    "70b": dict(models.L70B, n_layers=2, vocab=4096),
+    "w6144": dict(n_layers=2, dim=6144, n_heads=48, n_kv_heads=8, ffn=16384, vocab=4096, eps=1e-5, theta=500000.0),
+}
+
+
+@pytest.fixture(scope="module", params=sorted(WIDE))
+def wide_2layer(request, gpu, vbs):
+    cfg = WIDE[request.param]
+    return cfg, vbs.synth_llama(models.shape_of(cfg), models.L70B_TYPES, seed=71)
+
+
+def test_wide_model_vs_engine_oracle(vbs, orc, wide_2layer, clean_errors):
+    """The persistent step kernel on a model above 4096 columns against
+    the oracle, then against the per-op kernels over 200 positions
+    (attention over several splits, 8 and 6 query heads per KV head)."""
+    cfg, dm = wide_2layer
+    st = orc.OrcState(_host_model(orc, cfg, dm), 256, 1)
+    dec = vbs.Decoder(dm, 256)
+    assert dec.kernels_per_step == 1
+    _teacher_forced(dec, st, [17, 2044, 5], 2e-3)
+    ref = vbs.Decoder(dm, 256, vbs.DEC_NO_PERSIST)
+    ref.forward([17, 2044, 5])
+    toks = models.splitmix_ints(23, 200, 4096)
+    for i in range(0, 200, 50):
+        la, lb = dec.forward(toks[i:i + 50]), ref.forward(toks[i:i + 50])
+        assert np.abs(la - lb).max() <= 1e-3 * np.abs(lb).max(), i
+    dec.close()
+    ref.close()
 
 
 HD64 = dict(n_layers=2, dim=1024, n_heads=16, n_kv_heads=4, ffn=2816, vocab=2048, eps=1e-5, theta=10000.0)

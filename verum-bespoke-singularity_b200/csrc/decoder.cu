@@ -515,6 +515,13 @@ bool plan_persistent(vbs_cu_decoder *d) {
                  bg = step_packed_bytes(p, STEP_GU), bd = step_packed_bytes(p, STEP_DOWN),
                  bout = step_packed_bytes(p, STEP_OUT);
     const size_t per_layer = bq + bo + bg + bd;
+    {   // the repacked copy sits beside the GGUF weights (the per-op and
+        // prefill kernels read those): without room for both plus 1 GiB of
+        // headroom the per-op path stays in use
+        size_t free_b = 0, total_b = 0;
+        if (!cuda_ok(cudaMemGetInfo(&free_b, &total_b), "memory info")) return false;
+        if (per_layer * m.n_layers + bout + (1ull << 30) > free_b) return true;
+    }
     if (!dmalloc((void **)&d->step_packed, per_layer * m.n_layers + bout, "repacked weights")) return false;
     std::vector<StepLayer> hl(m.n_layers);
     for (uint32_t l = 0; l < m.n_layers; ++l) {

@@ -27,8 +27,10 @@
 //    (plain stores, one writer per element) into its chunk's plane of
 //    partial sums; the reader adds the planes in chunk order, so the sums
 //    are deterministic and nothing needs clearing between steps. Only the
-//    down projection is split into column chunks; every other matvec has
-//    one chunk.
+//    down projection is split into column chunk planes. Every other matvec
+//    keeps whole rows: wider than one stage (the 70B shape's 8192 columns),
+//    a tile's row chunks are consecutive stages of one CTA and its row sums
+//    accumulate across them.
 //  * What follows a matvec in the reference (residual add, RMSNorm, SiLU,
 //    RoPE) is applied by the NEXT op as it reads the complete sums: every
 //    CTA keeps its own copy of the residual stream x in shared memory and
@@ -157,6 +159,24 @@ __host__ __device__ __forceinline__ uint32_t sk_slot_row(bool gu, uint32_t tile,
 __device__ __forceinline__ void sk_range(uint32_t U, uint32_t &u0, uint32_t &u1) {
     u0 = blockIdx.x * U / gridDim.x;
     u1 = (blockIdx.x + 1) * U / gridDim.x;
+}
+
+// Stages per row unit. A matrix wider than one stage's column chunk is
+// either split into chunk planes (the down projection: chunk-major units,
+// the reader adds the planes) or, every other op, streamed as row chunks:
+// a tile's chunks are consecutive stages whose row sums accumulate, and the
+// sums are written once, whole (what SiLU, RoPE and the argmax need).
+__device__ __forceinline__ uint32_t sk_row_stages(const SkMv &d) { return d.chunk_major ? 1u : d.g.nch; }
+
+// This CTA's units of op d, whole tiles when a tile spans several stages
+// (only in the WIDE kernel instances: elsewhere every such op has whole
+// rows in one stage). The producer and the consumers walk the same range.
+template <bool WIDE>
+__device__ __forceinline__ void sk_mv_range(const SkMv &d, uint32_t &u0, uint32_t &u1) {
+    const uint32_t rs = WIDE ? sk_row_stages(d) : 1u;
+    sk_range(d.g.ntiles * d.g.nch / rs, u0, u1);
+    u0 *= rs;
+    u1 *= rs;
 }
 
 struct SkAttn {
@@ -390,6 +410,7 @@ __device__ __forceinline__ void sk_issued(SkRing &r, SkInflight &f, uint32_t byt
     r.advance(bytes);
 }
 
+template <bool WIDE>
 __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S, uint32_t seq) {
     const int lane = threadIdx.x & 31;
     const uint32_t nops = 5 * p.n_layers + 2;
@@ -435,7 +456,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
         const SkMv d = sk_mv_desc(p, kind, l);
         const uint32_t bytes = 16u * d.g.rs;
         uint32_t u0, u1;
-        sk_range(d.g.ntiles * d.g.nch, u0, u1);
+        sk_mv_range<WIDE>(d, u0, u1);
         for (uint32_t u = u0; u < u1; ++u) {
             if (!sk_reserve(p, S, r, f, bytes, lane)) { ok = false; break; }
             uint32_t tile, ch;
@@ -462,7 +483,7 @@ __device__ __forceinline__ void sk_producer(const StepParams &p, const SkSmem &S
 // issued before the first is used: while the weight stream saturates the
 // memory system every dependent round trip costs microseconds.
 // ---------------------------------------------------------------------------
-constexpr int SK_PB = 2;        // blocks per thread in the norm prologue (dim <= 4096)
+constexpr int SK_PB = 2;        // blocks per thread and pass in the norm prologue (one pass to dim 4096)
 
 __device__ __forceinline__ void ld8_cg(const float *src, float v[8]) {
     const float4 a = __ldcg(reinterpret_cast<const float4 *>(src)), b = __ldcg(reinterpret_cast<const float4 *>(src + 4));
@@ -521,19 +542,28 @@ __device__ __noinline__ void sk_embed8(const StepParams &p, uint32_t token, uint
 constexpr int SK_MAXPL = 4;      // partial planes summed by the norm prologue
 
 // WORDS (instances with tensor parallelism): when `want` is not 0 the planes
-// are exchange words carrying it.
-template <bool WORDS>
+// are exchange words carrying it. WIDE: widths above 4096, in passes of
+// SK_PB blocks per thread, the quantizer reading each pass's x back from
+// shared memory; without it one pass with x in registers.
+constexpr uint32_t SK_PSTEP = SK_PB * (SK_CT / 4);   // blocks per prologue pass
+template <bool WORDS, bool WIDE>
 __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSmem &S, SkRing &r, float *x,
                                                  const void *add, uint32_t nadd, uint32_t want, uint32_t token,
                                                  bool quant, int type, uint8_t *xq, float4 *xf, uint32_t op) {
     const uint32_t ctid = threadIdx.x, q = ctid >> 2, u = ctid & 3u, nsub = p.dim / 32;
     const uint32_t qmask = 0xFu << ((ctid & 31u) & ~3u);
+    constexpr uint32_t PSTEP = SK_PSTEP;
+    const uint32_t npass = WIDE ? (nsub + PSTEP - 1) / PSTEP : 1u;
     if (ctid == 0) SK_STAMP(p, op, 8);
     float xv[SK_PB][8];
+    float ss = 0.f;
+#pragma unroll 1
+    for (uint32_t pass = 0; pass < npass; ++pass) {
+    const uint32_t qp = q + pass * PSTEP;
     // add = nadd planes of dim partial sums, summed in plane order
 #pragma unroll
     for (int r = 0; r < SK_PB; ++r) {
-        const uint32_t J = q + r * (SK_CT / 4);
+        const uint32_t J = qp + r * (SK_CT / 4);
         if (J < nsub) {
             const uint32_t e = J * 32 + 8 * u;
             if (add) {
@@ -559,10 +589,9 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
             }
         }
     }
-    float ss = 0.f;
 #pragma unroll
     for (int r = 0; r < SK_PB; ++r) {
-        const uint32_t J = q + r * (SK_CT / 4);
+        const uint32_t J = qp + r * (SK_CT / 4);
         if (J >= nsub) continue;
         const uint32_t e = J * 32 + 8 * u;
         float4 *xs = reinterpret_cast<float4 *>(x + e);
@@ -581,6 +610,7 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
 #pragma unroll
         for (int k = 0; k < 8; ++k) ss = fmaf(xv[r][k], xv[r][k], ss);
     }
+    }
     ss = warp_sum(ss);
     if (ctid == 0) SK_STAMP(p, op, 5);
     float *misc = S.misc();
@@ -593,19 +623,27 @@ __device__ __forceinline__ void sk_prologue_norm(const StepParams &p, const SkSm
     if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
     if (ctid == 0) SK_STAMP(p, op, 6);
     static_assert(SK_PB == 2, "the prologue quantizes its two blocks together");
-    if (quant && got && q < nsub) {
+#pragma unroll 1
+    for (uint32_t pass = 0; quant && got && pass < npass; ++pass) {
+        const uint32_t qp = q + pass * PSTEP;
+        if (qp >= nsub) break;
         float v[SK_PB][8];
 #pragma unroll
         for (int r2 = 0; r2 < SK_PB; ++r2) {
-            const uint32_t J = q + r2 * (SK_CT / 4);
-            const uint32_t e = (J < nsub ? J : q) * 32 + 8 * u;
+            const uint32_t J = qp + r2 * (SK_CT / 4);
+            const uint32_t e = (J < nsub ? J : qp) * 32 + 8 * u;
+            if (WIDE) {   // this thread's x of this pass, as it stored it above
+                const float4 o0 = reinterpret_cast<const float4 *>(x + e)[0], o1 = reinterpret_cast<const float4 *>(x + e)[1];
+                xv[r2][0] = o0.x; xv[r2][1] = o0.y; xv[r2][2] = o0.z; xv[r2][3] = o0.w;
+                xv[r2][4] = o1.x; xv[r2][5] = o1.y; xv[r2][6] = o1.z; xv[r2][7] = o1.w;
+            }
             const uint4 w0 = lds_u128(ws + e * 4), w1 = lds_u128(ws + e * 4 + 16);
             const float wv[8] = {__uint_as_float(w0.x), __uint_as_float(w0.y), __uint_as_float(w0.z), __uint_as_float(w0.w),
                                  __uint_as_float(w1.x), __uint_as_float(w1.y), __uint_as_float(w1.z), __uint_as_float(w1.w)};
 #pragma unroll
             for (int k = 0; k < 8; ++k) v[r2][k] = xv[r2][k] * wv[k];
         }
-        sk_quant2(type, v, u, qmask, q, q + SK_CT / 4, q + SK_CT / 4 < nsub, xq, xf);
+        sk_quant2(type, v, u, qmask, qp, qp + SK_CT / 4, qp + SK_CT / 4 < nsub, xq, xf);
     }
     if (ctid == 0) SK_STAMP(p, op, 7);
     if (ctid == 0 && add) SK_PROBE(p, op, 9, static_cast<const float *>(add) + 8 * nadd);
@@ -651,7 +689,7 @@ __device__ __forceinline__ float sk_norm_scale(const StepParams &p, const SkSmem
     return 1.0f / sqrtf(tot / (float)p.dim + p.eps);
 }
 
-template <int TYPE, bool TPX>
+template <int TYPE, bool TPX, bool WIDE>
 __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                               uint32_t xq_a, uint32_t xf_a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
@@ -659,8 +697,11 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
     const uint32_t RS = d.g.rs, CK = d.g.ck, SB = 16u * RS;
     volatile int *cta_abort = S.abort_flag();
     float *red = S.red();
+    const uint32_t RC = WIDE ? sk_row_stages(d) : 1u;
     uint32_t u0, u1;
-    sk_range(d.g.ntiles * d.g.nch, u0, u1);
+    sk_mv_range<WIDE>(d, u0, u1);
+    float acc[2] = {0.f, 0.f};   // WIDE: carried over a tile's row chunks
+    uint32_t k = 0, ub = u0;     // WIDE: row units finished; first unit of the current batch
     for (uint32_t u = u0; u < u1; ++u) {
         uint32_t tile, ch;
         sk_unit(d, u, tile, ch);
@@ -668,7 +709,7 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
         const uint32_t ms = S.ring + r.place(SB, S.ring_bytes);
         const bool got = __all_sync(0xffffffffu, !*cta_abort && sk_wait(S.full(r.idx), r.parity(), p));
         if (!got && lane == 0 && !*cta_abort) { *cta_abort = 1; sk_abort(p, DERR_TIMEOUT_FULL); }
-        float acc[2] = {0.f, 0.f};
+        if constexpr (!WIDE) acc[0] = acc[1] = 0.f;
         if (got) {
             const uint32_t c0 = ch * CK, c1 = min(d.cols, c0 + CK);
             // packed rows start 16-byte aligned in the stage: no alignment pads
@@ -682,6 +723,7 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
         __syncwarp();
         if (lane == 0) mbar_arrive(S.empty(r.idx));
         r.advance(SB);
+        if (WIDE && ch + 1 < RC) continue;   // the tile's next row chunk adds to the same sums
         // the unit's row sums: over the thread columns here, then over the
         // warps for a batch of SK_NU units at once: each warp leaves its 16
         // partials in the batch buffer, and after one consumer barrier the
@@ -693,18 +735,24 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
             acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 1);
             acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], 2);
         }
-        const uint32_t k = u - u0, slot = k % SK_NU;
-        float *batch = red + ((k / SK_NU) & 1u) * (SK_NU * SK_NCW * 16);
+        const uint32_t kk = WIDE ? k : u - u0, slot = kk % SK_NU;
+        if (WIDE && slot == 0) ub = u + 1 - RC;
+        float *batch = red + ((kk / SK_NU) & 1u) * (SK_NU * SK_NCW * 16);
         if ((lane & 3) == 0) {
             batch[(slot * SK_NCW + warp) * 16 + g] = acc[0];
             batch[(slot * SK_NCW + warp) * 16 + g + 8] = acc[1];
+        }
+        if constexpr (WIDE) {
+            ++k;
+            acc[0] = acc[1] = 0.f;
         }
         if (slot == SK_NU - 1 || u + 1 == u1) {
             named_bar_sync(1, SK_CT);
             const uint32_t n = slot + 1, j = threadIdx.x >> 4, rr = threadIdx.x & 15u;
             if (j < n && !*cta_abort) {
                 uint32_t tile, ch;
-                sk_unit(d, u - slot + j, tile, ch);
+                // WIDE: chunk 0 of a row-chunked tile, whose sums are whole
+                sk_unit(d, WIDE ? ub + j * RC : u - slot + j, tile, ch);
                 const float *b = batch + j * SK_NCW * 16;
                 float va = 0.f;
 #pragma unroll
@@ -740,12 +788,12 @@ __device__ __forceinline__ void sk_mv_consume(const StepParams &p, const SkMv &d
 
 // Types the kernel instance carries code for: a compile-time list (a
 // specialized instance) or all three (TQ4 = TQ6 = TQ8 = true).
-template <bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX>
+template <bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX, bool WIDE>
 __device__ __forceinline__ void sk_mv_dispatch(const StepParams &p, const SkMv &d, const SkSmem &S, SkRing &r,
                                                uint32_t xq_a, uint32_t xf_a) {
-    if constexpr (HAS_Q4) if (d.type == T_Q4_K) { sk_mv_consume<T_Q4_K, TPX>(p, d, S, r, xq_a, xf_a); return; }
-    if constexpr (HAS_Q6) if (d.type == T_Q6_K) { sk_mv_consume<T_Q6_K, TPX>(p, d, S, r, xq_a, xf_a); return; }
-    if constexpr (HAS_Q8) if (d.type == T_Q8_0) { sk_mv_consume<T_Q8_0, TPX>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q4) if (d.type == T_Q4_K) { sk_mv_consume<T_Q4_K, TPX, WIDE>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q6) if (d.type == T_Q6_K) { sk_mv_consume<T_Q6_K, TPX, WIDE>(p, d, S, r, xq_a, xf_a); return; }
+    if constexpr (HAS_Q8) if (d.type == T_Q8_0) { sk_mv_consume<T_Q8_0, TPX, WIDE>(p, d, S, r, xq_a, xf_a); return; }
 }
 
 // ---------------------------------------------------------------------------
@@ -1135,7 +1183,7 @@ __device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uin
 // the code their model uses (a kernel that runs every op of a step is large,
 // and its instruction fetch is otherwise a bottleneck). TPX instances add
 // the tensor-parallel exchanges; the one-GPU instances carry none of it.
-template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX>
+template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX, bool WIDE>
 __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p_in) {
     static_assert(65536 / SK_THREADS / 8 * 8 >= SK_REG_LAUNCH, "launch register count");
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -1177,7 +1225,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
     __syncthreads();
     if (warp >= SK_NCW) {   // producer warpgroup
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(SK_REG_PRODUCER));
-        if (warp == SK_NCW) sk_producer(p, S, seq);
+        if (warp == SK_NCW) sk_producer<WIDE>(p, S, seq);
         return;
     }
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(SK_REG_CONSUMER));
@@ -1233,7 +1281,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
             d.tp_k = sk_tp_index(p, tp_base, kind, l);
         }
         uint32_t u0, u1;
-        sk_range(d.g.ntiles * d.g.nch, u0, u1);
+        sk_mv_range<WIDE>(d, u0, u1);
         const bool work = u1 > u0;
         uint32_t xq_u = xq_a, xf_u = xf_a;   // shared addresses of x block 0 for mv_unit
         if (kind == K_QKV || kind == K_GU || kind == K_OUT) {
@@ -1249,7 +1297,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
                 nadd *= p.tp->world;
                 want = k + 1u;
             }
-            sk_prologue_norm<TPX>(p, S, r, x, planes, nadd, want, token, work, d.type, xq, xf, i);
+            sk_prologue_norm<TPX, WIDE>(p, S, r, x, planes, nadd, want, token, work, d.type, xq, xf, i);
         } else if (kind == K_O) {
             if (threadIdx.x == 0) SK_STAMP(p, i, 8);
             if (work) sk_prologue_vec<2>(d.cols, d.type, p.att, xq, xf);
@@ -1267,7 +1315,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_consta
         if (threadIdx.x == 0) SK_STAMP(p, i, 1);
         if (!work) { if (threadIdx.x == 0) SK_STAMP(p, i, 2); continue; }
         named_bar_sync(1, SK_CT);
-        sk_mv_dispatch<HAS_Q4, HAS_Q6, HAS_Q8, TPX>(p, d, S, r, xq_u, xf_u);
+        sk_mv_dispatch<HAS_Q4, HAS_Q6, HAS_Q8, TPX, WIDE>(p, d, S, r, xq_u, xf_u);
         if (threadIdx.x == 0) SK_STAMP(p, i, 2);
     }
 }
@@ -1316,7 +1364,8 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
     }
     if (!block_elems(p.t_embd) || p.dim % (uint32_t)block_elems(p.t_embd)) return no("embedding type");
     if (p.dim % 32 || qd % 32 || p.ffn % 32) return no("widths must be multiples of 32");
-    if (p.dim > (uint32_t)(SK_CT / 4) * 32 * SK_PB) return no("model width above the prologue's register budget");
+    if (p.dim > 16384) return no("model width above 16384");
+    if (p.tp && p.dim > SK_PSTEP * 32) return no("tensor parallelism: model width above 4096");
     // shared memory: header | x | quantized x (or attention states) | ring.
     // The down projection quantizes only its CTA's (at most two) column
     // chunks; the chunk size is fixed first from a provisional ring.
@@ -1353,13 +1402,15 @@ bool step_plan(StepParams &p, int n_sm, char *why, size_t cap) {
         gg.nch = (cols[k] + ck - 1) / ck;
         gg.ntiles = (rows[k] + (k == STEP_GU ? 7 : 15)) / (k == STEP_GU ? 8 : 16);   // gate/up: 8 rows of each
         slot = std::max(slot, SL * gg.rs);
-        if (k != STEP_DOWN && gg.nch != 1) return no("rows of this width do not fit one stage");
+        // row chunks across stages (sk_row_stages); the tensor-parallel
+        // exchange addresses one plane per rank, so it takes whole rows only
+        if (k != STEP_DOWN && gg.nch != 1 && p.tp) return no("rows of this width do not fit one stage");
         if (gg.ck > 4096) return no("stage chunks above 4096 columns");
     }
     {   // down: chunk-major units, every CTA within at most two chunks
         const StepMvGeom &gd = p.geo[STEP_DOWN];
         const uint64_t U = (uint64_t)gd.ntiles * gd.nch;
-        if (gd.nch > (uint32_t)SK_MAXPL) return no("too many column chunks in the down projection");
+        if (gd.nch > (uint32_t)(p.tp ? SK_MAXPL : 4 * SK_MAXPL)) return no("too many column chunks in the down projection");
         if (p.tp && (uint64_t)gd.nch * p.dim > TP_DIM_MAX) return no("down partial planes exceed the exchange slots");
         if ((U + n_sm - 1) / n_sm > gd.ntiles) return no("down projection units per CTA exceed a chunk");
         plan_smem(gd.ck);
@@ -1453,15 +1504,24 @@ static bool sk_is_q4k_only(const StepParams &p) {
     return p.hd == 128 && p.t_qkv == T_Q4_K && p.t_o == T_Q4_K && p.t_gu == T_Q4_K && p.t_down == T_Q4_K &&
            p.t_out == T_Q4_K;
 }
+// Models whose norm prologue takes more than one pass, or with rows (other
+// than the down projection's) spread over several stages: the WIDE instances.
+static bool sk_is_wide(const StepParams &p) {
+    if (p.dim > SK_PSTEP * 32) return true;
+    for (int k = 0; k < 5; ++k)
+        if (k != STEP_DOWN && p.geo[k].nch > 1) return true;
+    return false;
+}
 
-template <int HD, bool A, bool B, bool C, bool T> static cudaError_t sk_attr() {
-    return cudaFuncSetAttribute(step_kernel<HD, A, B, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+template <int HD, bool A, bool B, bool C, bool T, bool W> static cudaError_t sk_attr() {
+    return cudaFuncSetAttribute(step_kernel<HD, A, B, C, T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
 }
 
 cudaError_t step_configure() {
-    const cudaError_t es[] = {sk_attr<0, true, true, true, false>(), sk_attr<128, true, true, false, false>(),
-                              sk_attr<128, true, false, false, false>(), sk_attr<0, true, true, true, true>(),
-                              sk_attr<128, true, true, false, true>()};
+    const cudaError_t es[] = {sk_attr<0, true, true, true, false, false>(), sk_attr<128, true, true, false, false, false>(),
+                              sk_attr<128, true, false, false, false, false>(), sk_attr<0, true, true, true, true, false>(),
+                              sk_attr<128, true, true, false, true, false>(), sk_attr<0, true, true, true, false, true>(),
+                              sk_attr<128, true, false, false, false, true>()};
     for (cudaError_t e : es)
         if (e != cudaSuccess) return e;
     return cudaSuccess;
@@ -1479,14 +1539,20 @@ cudaError_t step_launch(const StepParams &p, int n_sm, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     note_launches(1);
-    // tensor-parallel instances carry the exchange code; the one-GPU ones do not
+    // tensor-parallel instances carry the exchange code; the one-GPU ones do
+    // not. Models wider than 4096 have instances of their own (row chunks,
+    // prologue passes), so the others carry none of that code.
     if (p.tp) {
-        if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false, true>, p);
-        return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, true>, p);
+        if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false, true, false>, p);
+        return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, true, false>, p);
     }
-    if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false, false>, p);
-    if (sk_is_q4k_only(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, false, false, false>, p);
-    return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, false>, p);
+    if (sk_is_wide(p)) {
+        if (sk_is_q4k_only(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, false, false, false, true>, p);
+        return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, false, true>, p);
+    }
+    if (sk_is_8b_mix(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, true, false, false, false>, p);
+    if (sk_is_q4k_only(p)) return cudaLaunchKernelEx(&cfg, step_kernel<128, true, false, false, false, false>, p);
+    return cudaLaunchKernelEx(&cfg, step_kernel<0, true, true, true, false, false>, p);
 }
 
 }  // namespace vbs
