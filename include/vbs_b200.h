@@ -327,7 +327,14 @@ typedef struct vbs_cu_decoder vbs_cu_decoder_t;
  * still being written by work on other streams are complete before the
  * decoder's own stream reads them. Every later vbs_cu_decoder_* call makes
  * the decoder's device current for its duration and leaves the caller's
- * current device as it found it. */
+ * current device as it found it.
+ * Steps run as one persistent kernel launch when the model fits that
+ * kernel's plan and its repacked weight copy fits in device memory with
+ * 1 GiB to spare. The plan wants one weight type per op (Q4_K, Q6_K or
+ * Q8_0), head_dim 64 or 128, 1 to 8 query heads per KV head and a width of
+ * at most 16384 (4096 under tensor parallelism). Otherwise steps run as
+ * per-op kernels. vbs_cu_decoder_kernels_per_step() returns 1 for the
+ * persistent kernel. */
 VBS_API vbs_cu_decoder_t *vbs_cu_decoder_create(const vbs_cu_model_t *m, uint32_t max_ctx, uint32_t flags,
                                         char *err, size_t err_cap);
 VBS_API void vbs_cu_decoder_destroy(vbs_cu_decoder_t *d);
