@@ -56,10 +56,10 @@ def parse():
                              "upload", "stream", "timeline"],
                     help="run only this kernel on its 8B shape, --steps launches over rotating weight sets "
                          "(a small case for ncu); prints per-launch times")
-    ap.add_argument("--layers", type=int, default=32, help="--profile decode: layers of the 8B shape")
+    ap.add_argument("--layers", type=int, default=32, help="--profile decode/timeline: layers of the model")
     ap.add_argument("--vocab", type=int, default=128256, help="--profile decode: vocabulary rows")
     ap.add_argument("--shape", default="8b", choices=["8b", "70b"],
-                    help="--profile decode/timed: the Llama-3-8B mix (BASELINE config 3) or the 70B shape, all Q4_K "
+                    help="--profile decode/timeline: the Llama-3-8B mix (BASELINE config 3) or the 70B shape, all Q4_K "
                          "(config 4)")
     ap.add_argument("--batch", type=int, default=1,
                     help="--profile decode: sequences decoded in lockstep (the batch decoder when above 1)")
@@ -108,8 +108,9 @@ def profile_timeline(args):
     if not vbs.ops().init():
         raise SystemExit(vbs.last_error())
     nl = args.layers
-    cfg = dict(models.L8B, n_layers=nl, vocab=args.vocab)
-    model = vbs.synth_llama(models.shape_of(cfg), models.L8B_TYPES, seed=2024)
+    base, types = (models.L70B, models.L70B_TYPES) if args.shape == "70b" else (models.L8B, models.L8B_TYPES)
+    cfg = dict(base, n_layers=nl, vocab=args.vocab)
+    model = vbs.synth_llama(models.shape_of(cfg), types, seed=2024)
     dec = vbs.Decoder(model, args.ctx + 64)
     dec.forward([1], logits=False)
     dec.set_position(args.ctx - 1, 1)
@@ -169,7 +170,8 @@ def profile_timeline(args):
     out = {k: {f: round(float(np.mean([r[f] for r in v])), 2) for f in v[0] if f not in ("op", "i")}
            for k, v in table.items()}
     layer_us = sum(out[k]["span"] for k in kinds)
-    print(json.dumps({"profile": "timeline", "ctx": args.ctx, "layers": nl, "vocab": args.vocab, "event_ms": round(ms, 4),
+    print(json.dumps({"profile": "timeline", "shape": args.shape, "ctx": args.ctx, "layers": nl, "vocab": args.vocab,
+                      "event_ms": round(ms, 4),
                       "traced_us": round(prev_end / 1e3, 1), "layer_us": round(layer_us, 2), "per_op_us": out}))
     dec.close()
 
