@@ -1183,6 +1183,9 @@ __device__ __noinline__ void sk_argmax(const StepParams &p, const SkSmem &S, uin
 // the code their model uses (a kernel that runs every op of a step is large,
 // and its instruction fetch is otherwise a bottleneck). TPX instances add
 // the tensor-parallel exchanges; the one-GPU instances carry none of it.
+// WIDE instances add row chunks across stages and the multi-pass norm
+// prologue for models wider than 4096; the others carry none of that (one
+// kernel with both paths ran the 8B shape 3% slower).
 template <int HD, bool HAS_Q4, bool HAS_Q6, bool HAS_Q8, bool TPX, bool WIDE>
 __global__ void __launch_bounds__(SK_THREADS, 1) step_kernel(const __grid_constant__ StepParams p_in) {
     static_assert(65536 / SK_THREADS / 8 * 8 >= SK_REG_LAUNCH, "launch register count");
